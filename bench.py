@@ -1,0 +1,425 @@
+#!/usr/bin/env python
+"""Benchmark of the Q4_0 MoE-FFN path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode16]
+    python bench.py --impl reference ...      # the reference's CPU algorithm
+
+Workloads (seeded synthetic data; expert/router weights N(0, 0.02) -> Q4_0,
+activations N(0, 1); norm weights, router_scale and per_expert_scale = 1):
+  decode16  (default) continuous-batch decode, M=16 independent tokens through
+            one 128-expert top-8 MoE layer (d=2816, F=704) with router, LOD,
+            post-norm, plus the dense Q4_0 projections q [2816->4096],
+            k, v [2816->1024], o [4096->2816] on the same 16 tokens.
+  decode1   M=1 decode through the MoE layer.
+  block256  one 256-token diffusion block through the MoE layer.
+A step is one pass of the path over one batch.  Weights of `--layers`
+distinct layers are cycled step by step so every step streams its experts
+from HBM (4 layers x 476 MB >> 126 MB L2).
+
+Multi-GPU: one process per GPU (torchrun); every rank runs its own batch
+against its own replica of the layers (data-parallel replicas, no
+collective on the data path); `value` is the whole-job token rate and
+timing is the max over ranks of CUDA-event time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "llm-mojo_b200"))
+sys.path.insert(1, os.path.join(ROOT, "oracle"))  # CPU baseline leg only
+
+D, F, E, K = 2816, 704, 128, 8
+GU_BYTES = 2 * F * D // 2 + 2 * F * D // 32 * 4   # 2,478,080 per expert
+DN_BYTES = D * F // 2 + D * F // 32 * 4           # 1,239,040 per expert
+ROUTER_BYTES = E * D // 2 + E * D // 32 * 4       # 225,280
+DENSE = [("q", D, 4096), ("k", D, 1024), ("v", D, 1024), ("o", 4096, D)]
+WORKLOADS = {"decode16": 16, "decode1": 1, "block256": 256}
+METRIC = "moe_layer_tokens_per_s"
+
+
+def q4_bytes(c_in, c_out):
+    return c_out * c_in // 2 + c_out * c_in // 32 * 4
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.06)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ----------------------------------------------------------------- CPU leg
+def host_layer(seed: int):
+    """Layer weights built on the CPU with the oracle's quantizer (no GPU code)."""
+    import numpy as np
+    import oracle as O
+    rng = np.random.default_rng(seed)
+    w = dict(d=D, F=F, E=E, top_k=K)
+    rf = rng.standard_normal((E, D), dtype=np.float32) * np.float32(0.02)
+    w["router_p"], w["router_s"], _ = O.quantize_q4_0(rf)
+    gp, gs, dp, ds = [], [], [], []
+    for _ in range(E):
+        p, s, _ = O.quantize_q4_0(rng.standard_normal(2 * F * D, dtype=np.float32) * np.float32(0.02))
+        gp.append(p)
+        gs.append(s)
+        p, s, _ = O.quantize_q4_0(rng.standard_normal(D * F, dtype=np.float32) * np.float32(0.02))
+        dp.append(p)
+        ds.append(s)
+    w["gu_p"], w["gu_s"] = np.concatenate(gp), np.concatenate(gs)
+    w["dn_p"], w["dn_s"] = np.concatenate(dp), np.concatenate(ds)
+    for k in ("router_scale", "pre_norm_w", "post_norm_w"):
+        w[k] = np.ones(D, np.float32)
+    w["per_expert_scale"] = np.ones(E, np.float32)
+    dense = {}
+    for name, ci, co in DENSE:
+        p, s, _ = O.quantize_q4_0(rng.standard_normal(ci * co, dtype=np.float32) * np.float32(0.02))
+        dense[name] = (p, s, ci, co)
+    return w, dense
+
+
+def cpu_step(L, dense, x, x_o, nthreads):
+    import oracle as O
+    O.layer_forward(L, x, post_norm=True, prec=O.F32, nthreads=nthreads)
+    for name, (p, s, ci, co) in dense.items():
+        O.q4_matmul(p, s, x_o if name == "o" else x, ci, co, prec=O.F32, nthreads=nthreads)
+
+
+def cpu_time(w, dense, M, budget_s, max_steps, nthreads, warmup=1):
+    """Times the oracle's fp32 restatement of the reference kernels."""
+    import numpy as np
+    import oracle as O
+    L = O.make_layer(w)
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((M, D)).astype(np.float32)
+    x_o = rng.standard_normal((M, 4096)).astype(np.float32)
+    use_dense = dense if M == 16 else {}
+    for _ in range(warmup):
+        cpu_step(L, use_dense, x, x_o, nthreads)
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_steps and (n == 0 or time.perf_counter() - t0 < budget_s):
+        cpu_step(L, use_dense, x, x_o, nthreads)
+        n += 1
+    dt = time.perf_counter() - t0
+    return M * n / dt, n, dt
+
+
+def run_reference(args, ws, rank):
+    """--impl reference: the reference's CPU algorithm (oracle fp32 port of
+    moe_kernels.mojo; the Mojo toolchain is absent) on the host cores."""
+    if rank != 0:
+        return 0
+    M = WORKLOADS[args.workload]
+    nthreads = os.cpu_count() or 1
+    w, dense = host_layer(seed=0)
+    # bounded sample: at most ~120 s for the K timed steps
+    t_one = cpu_time(w, dense, M, 0.0, 1, nthreads, warmup=0)
+    per_step = M / t_one[0]
+    budget = 120.0 / max(1, args.steps)
+    m = M
+    if per_step > budget and M > 1:
+        m = 5 if M > 5 and per_step * 5 / M <= budget else 1
+    import numpy as np
+    import oracle as O
+    L = O.make_layer(w)
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((m, D)).astype(np.float32)
+    x_o = rng.standard_normal((m, 4096)).astype(np.float32)
+    use_dense = dense if M == 16 else {}
+    for _ in range(max(0, min(args.warmup, 3))):
+        cpu_step(L, use_dense, x, x_o, nthreads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(L, use_dense, x, x_o, nthreads)
+    dt = time.perf_counter() - t0
+    value = m * args.steps / dt
+    sample = f"{m} of {M} tokens per step, {args.steps} steps, 1 layer (+dense q/k/v/o)" if M == 16 \
+        else f"{m} of {M} tokens per step, {args.steps} steps, 1 layer"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(args, M),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args, M):
+    return {"workload": {"decode16": "cfg2: M=16 decode MoE layer + dense q/k/v/o",
+                         "decode1": "cfg1: M=1 decode MoE layer",
+                         "block256": "cfg3: M=256 block through the MoE layer"}[args.workload],
+            "tokens_per_step": M, "embed_dim": D, "expert_mlp_dim": F, "num_experts": E, "top_k": K,
+            "layers_cycled": args.layers,
+            "l2": f"weights of {args.layers} distinct layers cycled per step ({args.layers * 476} MB > 126 MB L2)",
+            "post_norm": True, "parallelism": f"replicas x{dist_setup()[0]}"}
+
+
+# ----------------------------------------------------------------- GPU leg
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode16", choices=sorted(WORKLOADS))
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    ws, rank, local = dist_setup()
+    if args.impl == "reference":
+        return run_reference(args, ws, rank)
+
+    import numpy as np
+    import torch
+    import moe_b200 as MB
+    import synth
+
+    torch.cuda.set_device(local)
+    pg = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    ctx = MB.Context(local)
+    stream = torch.cuda.current_stream()
+    ctx.set_stream(stream.cuda_stream)
+    M = WORKLOADS[args.workload]
+
+    layers, descs = [], []
+    for li in range(args.layers):
+        lw = synth.make_layer(ctx, seed=1000 * rank + li)
+        layers.append(lw)
+        descs.append(MB.make_desc(lw))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(77 + rank)
+    dense = {}
+    if M == 16:
+        for name, ci, co in DENSE:
+            wt = torch.randn(ci * co, generator=gen, device="cuda") * 0.02
+            p, s = synth.quantize(ctx, wt)
+            dense[name] = (p, s, ci, co)
+    xs = [synth.make_x(M, seed=500 + 10 * rank + li) for li in range(args.layers)]
+    x_o = torch.randn((M, 4096), generator=gen, device="cuda")
+    out = torch.empty((M, D), device="cuda")
+    dense_out = {n: torch.empty((M, co), device="cuda") for n, (_, _, _, co) in dense.items()}
+
+    # routing per layer (unique experts -> algorithmic bytes)
+    uniq = []
+    for li in range(args.layers):
+        cnt = np.zeros(M, np.int64)
+        idx = np.zeros((M, K), np.int64)
+        w = np.zeros((M, K), np.float32)
+        ctx.layer_forward(descs[li], M, xs[li], out, MB.F_POST_NORM, cnt, idx, w)
+        uniq.append(len({int(idx[t, k]) for t in range(M) for k in range(cnt[t])}))
+        pairs = int(cnt.sum())
+
+    def step(i):
+        li = i % args.layers
+        ctx.layer_forward(descs[li], M, xs[li], out, MB.F_POST_NORM)
+        for name, (p, s, ci, co) in dense.items():
+            ctx.q4_matmul_batchN(M, p, s, x_o if name == "o" else xs[li], dense_out[name], ci, co)
+
+    ctx.set_async(True)
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    n0 = ctx.kernel_launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = ctx.kernel_launches - n0
+    ms = ev0.elapsed_time(ev1)
+    if pg:
+        t = torch.tensor([ms], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+        pg.barrier()
+    torch.cuda.synchronize()
+    ms_per_step = ms / args.steps
+    value = ws * M * args.steps / (ms / 1e3)
+
+    # profiled pass over the same steps: per-kernel device time
+    ctx.profile_enable(True)
+    for i in range(args.steps):
+        step(i)
+    prof = ctx.profile_read()
+    ctx.profile_enable(False)
+
+    # end-to-end through the public API with pinned host buffers
+    ctx.set_async(False)
+    x_h = [x.cpu().pin_memory() for x in xs]
+    xo_h = x_o.cpu().pin_memory()
+    out_h = torch.empty((M, D)).pin_memory()
+    dout_h = {n: torch.empty((M, co)).pin_memory() for n, (_, _, _, co) in dense.items()}
+    h2d = M * D * 4 + sum((M * (4096 if n == "o" else D) * 4) for n in dense)
+    d2h = M * D * 4 + sum(M * co * 4 for (_, _, _, co) in dense.values())
+
+    def step_e2e(i):
+        li = i % args.layers
+        ctx.layer_forward(descs[li], M, x_h[li], out_h, MB.F_POST_NORM)
+        for name, (p, s, ci, co) in dense.items():
+            ctx.q4_matmul_batchN(M, p, s, xo_h if name == "o" else x_h[li], dout_h[name], ci, co)
+
+    e2e_steps = max(1, min(args.steps, 500))
+    for i in range(3):
+        step_e2e(i)
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(e2e_steps):
+        step_e2e(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if pg:
+        t = torch.tensor([e2e_ms], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = ws * M * e2e_steps / (e2e_ms / 1e3)
+
+    # roofline of the dominant kernel (largest share of profiled time)
+    hbm, _, src = peaks()
+    u_mean = sum(uniq) / len(uniq)
+    dom = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
+    alg = {
+        "gemv_gate_up": u_mean * GU_BYTES + M * D * 4 + M * K * F * 4,
+        "gemv_down": u_mean * DN_BYTES + M * K * F * 4 + M * K * D * 4,
+        "q4_matmul": sum(q4_bytes(ci, co) + M * (ci + co) * 4 for (_, _, ci, co) in dense.values()) / max(1, len(dense)),
+        "route": ROUTER_BYTES + 2 * M * D * 4,
+    }
+    roof = None
+    if dom in alg and prof[dom][1] > 0:
+        avg_ms = prof[dom][0] / prof[dom][1]
+        achieved = alg[dom] / (avg_ms / 1e3) / 1e9
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tp):
+            with open(tp) as f:
+                traffic = json.load(f).get(args.workload, {}).get(dom)
+        roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "traffic": traffic,
+                "alg_bytes_per_launch": alg[dom], "avg_launch_ms": avg_ms,
+                "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({'of measured' if src == 'measured' else 'of fallback'})"}
+    step_bytes = u_mean * (GU_BYTES + DN_BYTES) + ROUTER_BYTES + 2 * M * D * 4 + \
+        sum(q4_bytes(ci, co) for (_, _, ci, co) in dense.values())
+    step_roof = {"alg_bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (ms_per_step / 1e3) / 1e9,
+                 "frac_of_hbm": step_bytes / (ms_per_step / 1e3) / 1e9 / hbm,
+                 "unique_experts_per_step": u_mean, "pairs_per_step": pairs,
+                 "kernel_ms_per_step": {k: v[0] / args.steps for k, v in prof.items()}}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        host = synth.to_host(layers[0])
+        hd = {n: (p.cpu().numpy(), s.cpu().numpy(), ci, co) for n, (p, s, ci, co) in dense.items()}
+        nth = os.cpu_count() or 1
+        v, n, dt = cpu_time(host, hd, M, args.cpu_budget_s, 200, nth)
+        cpu = {"value": v, "unit": "tokens/s", "cores": nth, "kind": "port",
+               "sample": f"{n} full steps of {M} tokens (layer 0{', + dense q/k/v/o' if hd else ''}) in {dt:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args, M), "roofline": roof, "step_roofline": step_roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "gpu_launches": launches, "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

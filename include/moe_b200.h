@@ -1,0 +1,239 @@
+/*
+ * moe_b200.h -- C ABI of libmoe_b200.so, a B200 (sm_100a) implementation of
+ * phildrip/llm-mojo's Q4_0 Mixture-of-Experts FFN hot path.
+ *
+ * Every compute entry point replaces one Mojo routine of the reference; the
+ * comment above it cites that routine (file:line within the reference
+ * project) and states where the arguments differ.  Conventions shared by all
+ * entry points:
+ *
+ *  - Pointers are plain addresses.  A pointer may be (a) a device pointer,
+ *    (b) a host pointer inside a range registered with moe_register_weights
+ *    (it is translated to the HBM mirror of that range), or (c) for
+ *    activations, routing arrays and outputs only, any other host pointer:
+ *    the call copies it to the device and the results back.  Weight
+ *    pointers of kind (c) are rejected with MOE_E_UNREGISTERED so that a
+ *    forgotten registration never streams gigabytes over PCIe per call.
+ *  - Index arrays are int64 (Mojo ``Int``).  Weights are the reference's
+ *    packed Q4_0 layout: per row, K/2 bytes (byte j of block b holds element
+ *    32b+2j in its low nibble and 32b+2j+1 in its high nibble) plus K/32
+ *    fp32 scales; value = (nibble - 8) * scale.  K must be a multiple of 32.
+ *  - Calls are synchronous unless moe_set_async(ctx, 1) was called; then
+ *    they are enqueued on the context's stream and moe_wait() completes them.
+ *  - Every call returns MOE_OK (0) or an MOE_E_* code; moe_last_error()
+ *    gives the message.  There is no CPU fallback: a context can only be
+ *    created on a CUDA device.
+ *  - One context per host thread.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct moe_ctx moe_ctx;
+
+enum moe_status {
+    MOE_OK = 0,
+    MOE_E_ARG = 1,          /* null pointer or bad enum */
+    MOE_E_SHAPE = 2,        /* dimension not supported (e.g. K % 32 != 0) */
+    MOE_E_UNREGISTERED = 3, /* weight pointer is neither device memory nor registered */
+    MOE_E_CUDA = 4,         /* CUDA runtime error */
+    MOE_E_NCCL = 5,         /* collective error (expert parallel) */
+    MOE_E_TIMEOUT = 6,      /* bounded wait expired (moe_wait, EP init, device wait) */
+    MOE_E_NOMEM = 7,        /* device or pinned allocation failed */
+    MOE_E_STATE = 8         /* call not valid in the context's current state */
+};
+
+enum moe_activation {
+    MOE_ACT_SIGMOID1702 = 0, /* g * sigmoid(1.702 g) * u  (moe_kernels.mojo:438-442, the reference's form) */
+    MOE_ACT_GELU_TANH = 1    /* 0.5 g (1 + tanh(0.79788456 (g + 0.044715 g^3))) * u */
+};
+
+/* layout of an activation input row of length K */
+enum moe_x_layout {
+    MOE_X_NATURAL = 0,      /* x[k] */
+    MOE_X_DEINT_HALVES = 1, /* [x[0],x[2],...,x[K-2] | x[1],x[3],...]  per 32-block pairs, as
+                               moe_kernels.mojo:96-101 (even half then odd half) */
+    MOE_X_DEINT_BLOCK32 = 2 /* per 32-block: 16 even then 16 odd (diffusion_kernels.mojo:52-75) */
+};
+
+/* ----------------------------------------------------------- context */
+int moe_ctx_create(int device, moe_ctx** out);
+int moe_ctx_destroy(moe_ctx* ctx);
+const char* moe_last_error(const moe_ctx* ctx);
+/* Number of kernels this context has launched so far (evidence counter). */
+uint64_t moe_kernel_launches(const moe_ctx* ctx);
+/* Use the caller's CUDA stream (cudaStream_t) instead of the context's own. */
+int moe_set_stream(moe_ctx* ctx, void* cuda_stream);
+/* 1: calls return after enqueueing; 0 (default): calls complete before returning. */
+int moe_set_async(moe_ctx* ctx, int async_mode);
+/* Completes enqueued work.  Gives up with MOE_E_TIMEOUT after timeout_ns
+ * (0 = wait without limit).  Modelled on enqueue_matmul/wait_matmul
+ * (kfd_gpu.mojo:1216-1260), which raise after a bounded poll. */
+int moe_wait(moe_ctx* ctx, uint64_t timeout_ns);
+
+/* Per-kernel timing with CUDA events recorded on the launching stream
+ * around each kernel of the path (off by default; the reference's
+ * perf_counter phase accumulators, model_speculative_moe.mojo:732-734, are
+ * its CPU counterpart).  Enabling clears the accumulators. */
+int moe_profile_enable(moe_ctx* ctx, int on);
+/* Completes outstanding work, then reports per kernel name (32-byte
+ * NUL-terminated slots in `names`) the total device milliseconds and launch
+ * count since moe_profile_enable.  *n_out receives the number of names. */
+int moe_profile_read(moe_ctx* ctx, int n_max, char* names, double* total_ms, uint64_t* counts,
+                     int* n_out);
+
+/* Mirror a host weight blob (e.g. the whole gemma4_moe_weights_q4.bin
+ * allocation, model_speculative_moe_batched.mojo:1347-1356) to HBM once.
+ * Later calls may pass any host pointer inside [host_base, host_base+bytes). */
+int moe_register_weights(moe_ctx* ctx, const void* host_base, size_t bytes);
+int moe_unregister_weights(moe_ctx* ctx, const void* host_base);
+
+/* ------------------------------------------------ Q4_0 kernels, one matrix */
+/* quantize_fp32_to_q4_0 (moe_kernels.mojo:7-56; convert_gemma4_moe.py:9-35).
+ * Bit-exact with the reference on every input without an exact .5 tie. */
+int moe_quantize_fp32_to_q4_0(moe_ctx* ctx, const float* src, uint8_t* dst_packed,
+                              float* dst_scales, int64_t num_elements);
+
+/* q4_matmul_vec (moe_kernels.mojo:59-67): out[c_out] = W[c_out x c_in] x[c_in]. */
+int moe_q4_matmul_vec(moe_ctx* ctx, const uint8_t* W_packed, const float* scales,
+                      const float* x, float* out, int64_t c_in, int64_t c_out);
+
+/* q4_matmul_batchN (moe_kernels.mojo:254-264) and q4_matmul_batch5 (:165-174):
+ * out[b*c_out + r] for b < batch_size.  Any batch_size >= 1 (the reference
+ * limits it to 5). */
+int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch_size, const uint8_t* W_packed,
+                         const float* scales, const float* x_batch, float* out_batch,
+                         int64_t c_in, int64_t c_out);
+
+/* ------------------------------------------------------------- routing */
+/* compute_moe_lod_weights (moe_kernels.mojo:445-490) for `batch` tokens laid
+ * out back to back (top_k entries each).  active_count[b] receives the count
+ * the reference returns. */
+int moe_compute_moe_lod_weights(moe_ctx* ctx, int64_t batch, const int64_t* top_idx,
+                                const float* top_val, const float* per_expert_scale,
+                                float moe_top_p, int64_t* active_idx, float* active_weights,
+                                int64_t* active_count, int64_t top_k);
+
+/* apply_moe_lod_and_set_cover (diffusion_kernels.mojo:3607-3664).
+ * eb_mask (uint8, 0/1) and active_canvas_idx may be NULL. */
+int moe_apply_moe_lod_and_set_cover(moe_ctx* ctx, const int64_t* canvas_top_idx,
+                                    const float* canvas_top_val,
+                                    const float* router_per_expert_scale,
+                                    float* canvas_top_weights, int64_t B, int64_t top_k_experts,
+                                    int64_t active_top_k, float moe_top_p,
+                                    const uint8_t* eb_mask, const int64_t* active_canvas_idx,
+                                    int64_t unaccepted_top_k);
+
+/* compute_subbatch_set_cover_moe_weights (moe_kernels.mojo:493-611). */
+int moe_compute_subbatch_set_cover_moe_weights(
+    moe_ctx* ctx, int64_t sub_b, const int64_t* all_top_idx, const float* all_top_val,
+    const float* per_expert_scale, float moe_top_p, int64_t* tok_active_count,
+    int64_t* tok_active_idx, float* tok_active_weights, int64_t num_experts, int64_t top_k,
+    float core_top_p, float singleton_min_prob);
+
+/* ------------------------------------------------------- expert stages */
+/* run_moe_experts_stage1_8core (moe_kernels.mojo:614-627): for each active
+ * slot s, gate_up_out_all[s*2F + r] = W_gu[e_s][r] . moe_in and
+ * act_all[s*F + j] = act(g_j) * u_j.  gate_up_out_all may be NULL (it is
+ * scratch for the reference's callers).  The reference's moe_in_deint
+ * scratch argument is not needed. */
+int moe_run_moe_experts_stage1(moe_ctx* ctx, const uint8_t* experts_gate_up_packed,
+                               const float* experts_gate_up_scales, const float* moe_in,
+                               const int64_t* active_idx, int64_t active_count,
+                               float* gate_up_out_all, float* act_all, int64_t embed_dim,
+                               int64_t expert_mlp_dim, int activation);
+
+/* run_moe_experts_stage2_8core (moe_kernels.mojo:699-712): moe_out[r] =
+ * sum_s active_weights[s] * (W_dn[e_s][r] . act_all[s]), slots in order. */
+int moe_run_moe_experts_stage2(moe_ctx* ctx, const uint8_t* experts_down_packed,
+                               const float* experts_down_scales, const float* act_all,
+                               const int64_t* active_idx, const float* active_weights,
+                               int64_t active_count, float* moe_out, int64_t embed_dim,
+                               int64_t expert_mlp_dim);
+
+/* run_moe_coalesced_core (moe_kernels.mojo:1321-1345): bucket-sorted expert
+ * evaluation of sub_b tokens (any sub_b >= 1; the reference allows <= 5).
+ * batch_in is in `x_layout` (the reference passes MOE_X_DEINT_HALVES).
+ * tok_active_idx / weights have stride top_k (8 in the reference). */
+int moe_run_moe_coalesced_core(moe_ctx* ctx, int64_t sub_b,
+                               const uint8_t* experts_gate_up_packed,
+                               const float* experts_gate_up_scales,
+                               const uint8_t* experts_down_packed,
+                               const float* experts_down_scales, const float* batch_in,
+                               int x_layout, const int64_t* tok_active_count,
+                               const int64_t* tok_active_idx, const float* tok_active_weights,
+                               float* batch_moe_out, int64_t embed_dim, int64_t expert_mlp_dim,
+                               int64_t num_experts, int64_t top_k, int activation);
+
+/* run_diffusion_moe_experts_parallel (diffusion_kernels.mojo:236-253): fp16
+ * canvas in/out (IEEE binary16 bits), a slot is active iff its weight > 0,
+ * per-token fp32 combine then one rounding to fp16.  The reference's three
+ * preallocated scratch buffers are not needed. */
+int moe_run_diffusion_moe_experts_parallel(moe_ctx* ctx, const uint8_t* experts_gate_up_packed,
+                                           const float* experts_gate_up_scales,
+                                           const uint8_t* experts_down_packed,
+                                           const float* experts_down_scales,
+                                           const uint16_t* canvas_moe_in,
+                                           const int64_t* canvas_top_idx,
+                                           const float* canvas_top_weights,
+                                           uint16_t* canvas_moe_out, int64_t B,
+                                           int64_t embed_dim, int64_t expert_mlp_dim,
+                                           int64_t top_k_experts, int activation);
+
+/* --------------------------------------------------------- whole layer */
+enum moe_layer_flags {
+    MOE_F_POST_NORM = 1, /* apply rms_norm(moe_out, post_norm_w) (model_speculative_moe_batched.mojo:1144-1150) */
+    MOE_F_SET_COVER = 4, /* set-cover routing per sub-batch of 5 (:1060-1072) instead of LOD */
+    MOE_F_FP16_OUT = 8   /* write the output as fp16 bits instead of fp32 */
+};
+
+typedef struct moe_layer_desc {
+    int64_t embed_dim;      /* d, 2816 */
+    int64_t expert_mlp_dim; /* F, 704 */
+    int64_t num_experts;    /* E, 128 (<= 1024) */
+    int64_t top_k;          /* 8 (<= 32) */
+    int32_t activation;     /* moe_activation */
+    float r_scale_factor;   /* 1/sqrt(d) (model_speculative_moe_batched.mojo:1868) */
+    float moe_top_p;        /* 1.0 = lossless LOD (:1269) */
+    const uint8_t* router_packed; /* Q4_0 router [E x d] (:155, :179) */
+    const float* router_scales;
+    const float* router_f32;      /* optional fp32 router [E x d], used when router_packed == NULL */
+    const float* router_logit_bias; /* optional [E] added to router scores; NULL in the reference.
+                                       Synthetic skewed-routing workloads only. */
+    const float* router_scale;     /* [d] */
+    const float* per_expert_scale; /* [E] */
+    const float* pre_norm_w;       /* [d] pre_feedforward_layernorm_2 */
+    const float* post_norm_w;      /* [d] post_feedforward_layernorm_2 (MOE_F_POST_NORM) */
+    const uint8_t* gate_up_packed; /* [E][2F x d] */
+    const float* gate_up_scales;
+    const uint8_t* down_packed;    /* [E][d x F] */
+    const float* down_scales;
+} moe_layer_desc;
+
+/* Router half of run_moe_coalesced_subbatch_stage1
+ * (model_speculative_moe_batched.mojo:957-1083; decode block :2102-2118) for
+ * M tokens: rms_norm_noscale(x) * router_scale * r_scale_factor -> Q4 router
+ * -> softmax -> top-k -> LOD (or set-cover), and moe_in = rms_norm(x,
+ * pre_norm_w).  Output pointers other than the three tok_active_* may be NULL. */
+int moe_route(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const float* x, int flags,
+              float* scores, int64_t* top_idx, float* top_val, int64_t* tok_active_count,
+              int64_t* tok_active_idx, float* tok_active_weights, float* moe_in);
+
+/* run_moe_coalesced_subbatch (model_speculative_moe_batched.mojo:1155-1204)
+ * for any M: route, expert evaluation and (flag) the post-norm.  `out` is
+ * fp32 [M x d] (fp16 bits with MOE_F_FP16_OUT).  The routing outputs may be
+ * NULL. */
+int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const float* x,
+                      void* out, int flags, int64_t* tok_active_count, int64_t* tok_active_idx,
+                      float* tok_active_weights);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_B200_H */

@@ -1,0 +1,83 @@
+// common.cuh -- shared device helpers for libmoe_b200 (sm_100a).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+constexpr int kWarp = 32;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide reductions (blockDim.x a multiple of 32, <= 1024). `red` is
+// shared scratch of >= 33 floats.  All threads receive the result.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    if (wid == 0) {
+        float t = lane < nw ? red[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) red[32] = t;
+    }
+    __syncthreads();
+    return red[32];
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    if (wid == 0) {
+        float t = lane < nw ? red[lane] : -INFINITY;
+        t = warp_max(t);
+        if (lane == 0) red[32] = t;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+// Nibble k (0..7) of a 32-bit word of packed Q4_0 bytes, returned as the
+// fp32 value 1 + n/16 (n = raw nibble 0..15).  The nibble is moved into
+// mantissa bits 19..22 and OR-ed with the exponent of 1.0: one shift and one
+// LOP3, no int->float conversion.  Because the bytes hold element 2j in the
+// low and 2j+1 in the high nibble, nibble k of word w of a block is element
+// 8w + k of that block, in natural order.
+template <int k>
+__device__ __forceinline__ float nib_1p(uint32_t w) {
+    uint32_t s = (4 * k <= 19) ? (w << (19 - 4 * k)) : (w >> (4 * k - 19));
+    return __uint_as_float((s & 0x00780000u) | 0x3F800000u);
+}
+
+// fp32 activation of the gated unit (moe_kernels.mojo:438-442 for kind 0).
+__device__ __forceinline__ float act_fn(float g, float u, int kind) {
+    if (kind == 1) {
+        float t = tanhf(0.7978845608f * (g + 0.044715f * g * g * g));
+        return 0.5f * g * (1.0f + t) * u;
+    }
+    float sig = 1.0f / (1.0f + expf(-1.702f * g));
+    return (g * sig) * u;
+}
+
+// Position of natural element j of a K-long row inside each input layout.
+__device__ __forceinline__ int64_t x_src_index(int64_t j, int64_t K, int layout) {
+    if (layout == 0) return j;
+    const int64_t b = j >> 5, w = j & 31, i = w >> 1;
+    if (layout == 1) return (w & 1) ? (K / 2 + b * 16 + i) : (b * 16 + i);
+    return b * 32 + ((w & 1) ? 16 : 0) + i;  // layout 2: block32 deinterleave
+}
+
+}  // namespace moe

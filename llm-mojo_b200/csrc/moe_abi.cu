@@ -1,0 +1,1057 @@
+// moe_abi.cu -- the extern "C" boundary of libmoe_b200.so (declared in
+// include/moe_b200.h): contexts, weight registration, pointer translation,
+// host staging and the entry points that replace the reference's Mojo
+// routines.  No CPU compute path exists here: every result is produced by
+// the kernels in moe_kernels.cu / moe_tc.cu.
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/moe_b200.h"
+#include "moe_internal.h"
+
+namespace {
+
+struct Reg {
+    const char* host;
+    size_t bytes;
+    char* dev;
+};
+
+struct CopyBack {
+    void* host;
+    const void* dev;
+    size_t bytes;
+};
+
+struct Status {
+    int code = MOE_OK;
+    std::string msg;
+};
+
+}  // namespace
+
+struct moe_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = true;
+    int async_mode = 0;
+    std::string err;
+    std::vector<Reg> regs;
+    char* ws = nullptr;
+    size_t ws_cap = 0;
+    size_t ws_off = 0;
+    size_t ws_res = 0;
+    int* err_flag = nullptr;
+    uint64_t launches = 0;
+    int num_sms = 148;
+    std::vector<CopyBack> pending;
+    cudaEvent_t done = nullptr;
+    // profiling (moe_profile_enable)
+    int profile = 0;
+    std::vector<cudaEvent_t> ev_pool;
+    struct ProfRec {
+        int name;
+        cudaEvent_t a, b;
+    };
+    std::vector<ProfRec> prof_pending;
+    std::vector<std::string> prof_names;
+    std::vector<double> prof_ms;
+    std::vector<uint64_t> prof_cnt;
+};
+
+namespace {
+
+cudaEvent_t pool_event(moe_ctx* c) {
+    if (!c->ev_pool.empty()) {
+        cudaEvent_t e = c->ev_pool.back();
+        c->ev_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+int prof_name_id(moe_ctx* c, const char* name) {
+    for (size_t i = 0; i < c->prof_names.size(); ++i)
+        if (c->prof_names[i] == name) return (int)i;
+    c->prof_names.push_back(name);
+    c->prof_ms.push_back(0.0);
+    c->prof_cnt.push_back(0);
+    return (int)c->prof_names.size() - 1;
+}
+
+// Brackets the kernels launched during its lifetime with events on the
+// context's stream when profiling is on.
+struct ProfScope {
+    moe_ctx* c;
+    int id = -1;
+    cudaEvent_t a = nullptr;
+    ProfScope(moe_ctx* ctx, const char* name) : c(ctx) {
+        if (!c->profile) return;
+        id = prof_name_id(c, name);
+        a = pool_event(c);
+        cudaEventRecord(a, c->stream);
+    }
+    ~ProfScope() {
+        if (id < 0) return;
+        cudaEvent_t b = pool_event(c);
+        cudaEventRecord(b, c->stream);
+        c->prof_pending.push_back({id, a, b});
+    }
+};
+
+}  // namespace
+
+namespace {
+
+constexpr size_t kAlign = 256;
+
+int fail(moe_ctx* c, int code, const std::string& m) {
+    if (c) c->err = m;
+    return code;
+}
+
+int cuda_fail(moe_ctx* c, cudaError_t e, const char* where) {
+    std::string m = std::string(where) + ": " + cudaGetErrorString(e);
+    return fail(c, MOE_E_CUDA, m);
+}
+
+#define MOE_CUDA(call)                                        \
+    do {                                                      \
+        cudaError_t _e = (call);                              \
+        if (_e != cudaSuccess) return cuda_fail(ctx, _e, #call); \
+    } while (0)
+
+// Reserve `bytes` of workspace for one call (grows only between calls).
+int ws_reserve(moe_ctx* ctx, size_t bytes) {
+    bytes += 64 * kAlign;
+    ctx->ws_off = 0;
+    ctx->ws_res = bytes;
+    if (bytes <= ctx->ws_cap) return MOE_OK;
+    MOE_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (ctx->ws) cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    size_t cap = std::max(bytes, ctx->ws_cap * 2);
+    cudaError_t e = cudaMalloc(&ctx->ws, cap);
+    if (e != cudaSuccess) {
+        ctx->ws_cap = 0;
+        cudaGetLastError();
+        return fail(ctx, MOE_E_NOMEM, "workspace allocation failed");
+    }
+    ctx->ws_cap = cap;
+    return MOE_OK;
+}
+
+void* ws_take(moe_ctx* ctx, size_t bytes) {
+    size_t off = (ctx->ws_off + kAlign - 1) / kAlign * kAlign;
+    if (off + bytes > ctx->ws_cap) return nullptr;
+    ctx->ws_off = off + bytes;
+    return ctx->ws + off;
+}
+
+size_t al(size_t b) { return (b + kAlign - 1) / kAlign * kAlign; }
+
+enum Kind { K_W, K_IN, K_OUT, K_INOUT };
+
+// Translates p into a device pointer.  Registered host ranges map to their
+// HBM mirror; device/managed memory is used as is; other host memory is
+// staged through the workspace (inputs copied in now, outputs copied back
+// at the end of the call).  Weights must not be staged.
+int dev_ptr(moe_ctx* ctx, const void* p, size_t bytes, Kind k, void** out) {
+    *out = nullptr;
+    if (!p) return MOE_OK;
+    const char* c = static_cast<const char*>(p);
+    for (const Reg& r : ctx->regs)
+        if (c >= r.host && c < r.host + r.bytes) {
+            if (c + bytes > r.host + r.bytes)
+                return fail(ctx, MOE_E_ARG, "buffer runs past the end of its registered range");
+            *out = r.dev + (c - r.host);
+            return MOE_OK;
+        }
+    cudaPointerAttributes at;
+    cudaError_t e = cudaPointerGetAttributes(&at, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        at.type = cudaMemoryTypeUnregistered;
+    }
+    if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) {
+        *out = at.devicePointer ? at.devicePointer : const_cast<void*>(p);
+        return MOE_OK;
+    }
+    if (k == K_W)
+        return fail(ctx, MOE_E_UNREGISTERED,
+                    "weight pointer is neither device memory nor inside a registered range");
+    void* d = ws_take(ctx, bytes);
+    if (!d) return fail(ctx, MOE_E_NOMEM, "workspace exhausted while staging a host buffer");
+    if (k == K_IN || k == K_INOUT)
+        MOE_CUDA(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    if (k == K_OUT || k == K_INOUT) ctx->pending.push_back({const_cast<void*>(p), d, bytes});
+    *out = d;
+    return MOE_OK;
+}
+
+#define TRY(x)                        \
+    do {                              \
+        int _s = (x);                 \
+        if (_s != MOE_OK) return _s;  \
+    } while (0)
+
+int begin(moe_ctx* ctx) {
+    if (!ctx) return MOE_E_ARG;
+    ctx->err.clear();
+    ctx->pending.clear();
+    MOE_CUDA(cudaSetDevice(ctx->device));
+    return MOE_OK;
+}
+
+// Launch-error check, copy-back of staged outputs, optional completion.
+int finish(moe_ctx* ctx) {
+    MOE_CUDA(cudaGetLastError());
+    for (const CopyBack& cb : ctx->pending)
+        MOE_CUDA(cudaMemcpyAsync(cb.host, cb.dev, cb.bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    ctx->pending.clear();
+    MOE_CUDA(cudaEventRecord(ctx->done, ctx->stream));
+    if (!ctx->async_mode) {
+        MOE_CUDA(cudaEventSynchronize(ctx->done));
+        int flag = 0;
+        MOE_CUDA(cudaMemcpy(&flag, ctx->err_flag, sizeof(int), cudaMemcpyDeviceToHost));
+        if (flag) {
+            MOE_CUDA(cudaMemset(ctx->err_flag, 0, sizeof(int)));
+            return fail(ctx, MOE_E_ARG, "expert index out of range in a routing array");
+        }
+    }
+    return MOE_OK;
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int check_q4_shape(moe_ctx* ctx, int64_t K, int64_t rows) {
+    if (K <= 0 || K % 32 != 0) return fail(ctx, MOE_E_SHAPE, "inner dimension must be a positive multiple of 32");
+    if (rows <= 0) return fail(ctx, MOE_E_SHAPE, "row count must be positive");
+    if (K > (1 << 20)) return fail(ctx, MOE_E_SHAPE, "inner dimension too large");
+    return MOE_OK;
+}
+
+// Internal buffers of an expert evaluation for M tokens x K slots.
+struct ExpertBufs {
+    int* slot_expert;
+    float* slot_weight;
+    moe::BucketOut b;
+    float* act;
+    float* y;
+};
+
+size_t expert_bufs_bytes(int64_t M, int64_t K, int64_t d, int64_t F, int64_t E) {
+    const int64_t P = M * K;
+    return al(P * 4) * 2 + al(16) + al(E * 4) * 3 + al(P * 4) * 3 + al(P * F * 4) + al(P * d * 4);
+}
+
+int take_expert_bufs(moe_ctx* ctx, int64_t M, int64_t K, int64_t d, int64_t F, int64_t E,
+                     ExpertBufs* o) {
+    const int64_t P = M * K;
+    o->slot_expert = (int*)ws_take(ctx, P * 4);
+    o->slot_weight = (float*)ws_take(ctx, P * 4);
+    o->b.meta = (int*)ws_take(ctx, 16);
+    o->b.unique_expert = (int*)ws_take(ctx, E * 4);
+    o->b.seg_start = (int*)ws_take(ctx, E * 4);
+    o->b.seg_count = (int*)ws_take(ctx, E * 4);
+    o->b.pair_token = (int*)ws_take(ctx, P * 4);
+    o->b.pair_slot = (int*)ws_take(ctx, P * 4);
+    o->b.slot_pair = (int*)ws_take(ctx, P * 4);
+    o->act = (float*)ws_take(ctx, P * F * 4);
+    o->y = (float*)ws_take(ctx, P * d * 4);
+    if (!o->y) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+    return MOE_OK;
+}
+
+struct ExpertWeights {
+    const uint8_t* gu_p;
+    const float* gu_s;
+    const uint8_t* dn_p;
+    const float* dn_s;
+};
+
+// slot table -> bucket -> gate/up (+act) -> down -> combine
+int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int64_t d, int64_t F,
+                int64_t E, const void* X, int x_layout, int x_f16, int act, ExpertBufs& bb,
+                const moe::CombineArgs* comb_tmpl, void* out) {
+    cudaStream_t s = ctx->stream;
+    const int64_t P = M * K;
+    {
+        ProfScope ps(ctx, "bucket");
+        ctx->launches += moe::launch_bucket(bb.slot_expert, P, (int)K, (int)E, bb.b, s);
+    }
+    const int max_u = (int)std::min<int64_t>(E, P);
+    const int max_t = (int)std::max<int64_t>(1, M);
+
+    moe::GemvArgs g1;
+    g1.Wp = w.gu_p;
+    g1.Ws = w.gu_s;
+    g1.rows_per_expert = 2 * F;
+    g1.K = (int)d;
+    g1.X = X;
+    g1.x_layout = x_layout;
+    g1.x_f16 = x_f16;
+    g1.meta = bb.b.meta;
+    g1.unique_expert = bb.b.unique_expert;
+    g1.seg_start = bb.b.seg_start;
+    g1.seg_count = bb.b.seg_count;
+    g1.pair_row = bb.b.pair_token;
+    g1.out = bb.act;
+    g1.out_stride = F;
+    g1.F = (int)F;
+    g1.act = act;
+    g1.max_tokens = max_t;
+    g1.max_unique = max_u;
+    {
+        ProfScope ps(ctx, "gemv_gate_up");
+        ctx->launches += moe::launch_gemv(moe::GEMV_ACT, g1, ctx->num_sms, s);
+    }
+
+    moe::GemvArgs g2 = g1;
+    g2.Wp = w.dn_p;
+    g2.Ws = w.dn_s;
+    g2.rows_per_expert = d;
+    g2.K = (int)F;
+    g2.X = bb.act;
+    g2.x_layout = 0;
+    g2.x_f16 = 0;
+    g2.pair_row = nullptr;
+    g2.out = bb.y;
+    g2.out_stride = d;
+    {
+        ProfScope ps(ctx, "gemv_down");
+        ctx->launches += moe::launch_gemv(moe::GEMV_PLAIN, g2, ctx->num_sms, s);
+    }
+
+    moe::CombineArgs c = *comb_tmpl;
+    c.y = bb.y;
+    c.d = d;
+    c.K = (int)K;
+    c.slot_pair = bb.b.slot_pair;
+    c.slot_weight = bb.slot_weight;
+    c.out = out;
+    {
+        ProfScope ps(ctx, "combine");
+        ctx->launches += moe::launch_combine(c, M, s);
+    }
+    return MOE_OK;
+}
+
+}  // namespace
+
+// ======================================================================
+extern "C" {
+
+int moe_ctx_create(int device, moe_ctx** out) {
+    if (!out) return MOE_E_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return MOE_E_CUDA;
+    }
+    if (device < 0 || device >= n) return MOE_E_ARG;
+    moe_ctx* ctx = new moe_ctx();
+    ctx->device = device;
+    if (cudaSetDevice(device) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->done, cudaEventDisableTiming) != cudaSuccess ||
+        cudaMalloc(&ctx->err_flag, sizeof(int)) != cudaSuccess ||
+        cudaMemset(ctx->err_flag, 0, sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        delete ctx;
+        return MOE_E_CUDA;
+    }
+    cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+    *out = ctx;
+    return MOE_OK;
+}
+
+int moe_ctx_destroy(moe_ctx* ctx) {
+    if (!ctx) return MOE_E_ARG;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    for (Reg& r : ctx->regs) cudaFree(r.dev);
+    if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->err_flag) cudaFree(ctx->err_flag);
+    if (ctx->done) cudaEventDestroy(ctx->done);
+    for (auto& r : ctx->prof_pending) {
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    for (cudaEvent_t e : ctx->ev_pool) cudaEventDestroy(e);
+    if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return MOE_OK;
+}
+
+const char* moe_last_error(const moe_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+uint64_t moe_kernel_launches(const moe_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+int moe_set_stream(moe_ctx* ctx, void* stream) {
+    if (!ctx) return MOE_E_ARG;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+    if (stream) {
+        ctx->stream = static_cast<cudaStream_t>(stream);
+        ctx->own_stream = false;
+    } else {
+        if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess)
+            return fail(ctx, MOE_E_CUDA, "stream creation failed");
+        ctx->own_stream = true;
+    }
+    return MOE_OK;
+}
+
+int moe_set_async(moe_ctx* ctx, int async_mode) {
+    if (!ctx) return MOE_E_ARG;
+    ctx->async_mode = async_mode ? 1 : 0;
+    return MOE_OK;
+}
+
+int moe_wait(moe_ctx* ctx, uint64_t timeout_ns) {
+    if (!ctx) return MOE_E_ARG;
+    cudaSetDevice(ctx->device);
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t e = cudaEventQuery(ctx->done);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) return cuda_fail(ctx, e, "moe_wait");
+        if (timeout_ns) {
+            const auto dt = std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                std::chrono::steady_clock::now() - t0)
+                                .count();
+            if ((uint64_t)dt > timeout_ns) return fail(ctx, MOE_E_TIMEOUT, "moe_wait: deadline expired");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+    int flag = 0;
+    MOE_CUDA(cudaMemcpy(&flag, ctx->err_flag, sizeof(int), cudaMemcpyDeviceToHost));
+    if (flag) {
+        MOE_CUDA(cudaMemset(ctx->err_flag, 0, sizeof(int)));
+        return fail(ctx, MOE_E_ARG, "expert index out of range in a routing array");
+    }
+    return MOE_OK;
+}
+
+int moe_profile_enable(moe_ctx* ctx, int on) {
+    if (!ctx) return MOE_E_ARG;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    for (auto& r : ctx->prof_pending) {
+        ctx->ev_pool.push_back(r.a);
+        ctx->ev_pool.push_back(r.b);
+    }
+    ctx->prof_pending.clear();
+    ctx->prof_names.clear();
+    ctx->prof_ms.clear();
+    ctx->prof_cnt.clear();
+    ctx->profile = on ? 1 : 0;
+    return MOE_OK;
+}
+
+int moe_profile_read(moe_ctx* ctx, int n_max, char* names, double* total_ms, uint64_t* counts,
+                     int* n_out) {
+    if (!ctx || !n_out) return MOE_E_ARG;
+    cudaSetDevice(ctx->device);
+    MOE_CUDA(cudaStreamSynchronize(ctx->stream));
+    for (auto& r : ctx->prof_pending) {
+        float ms = 0.f;
+        MOE_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+        ctx->prof_ms[r.name] += ms;
+        ctx->prof_cnt[r.name] += 1;
+        ctx->ev_pool.push_back(r.a);
+        ctx->ev_pool.push_back(r.b);
+    }
+    ctx->prof_pending.clear();
+    const int n = (int)ctx->prof_names.size();
+    *n_out = n;
+    for (int i = 0; i < n && i < n_max; ++i) {
+        if (names) {
+            std::strncpy(names + 32 * i, ctx->prof_names[i].c_str(), 31);
+            names[32 * i + 31] = 0;
+        }
+        if (total_ms) total_ms[i] = ctx->prof_ms[i];
+        if (counts) counts[i] = ctx->prof_cnt[i];
+    }
+    return MOE_OK;
+}
+
+int moe_register_weights(moe_ctx* ctx, const void* host_base, size_t bytes) {
+    TRY(begin(ctx));
+    if (!host_base || !bytes) return fail(ctx, MOE_E_ARG, "null or empty range");
+    const char* h = static_cast<const char*>(host_base);
+    for (const Reg& r : ctx->regs)
+        if (h < r.host + r.bytes && r.host < h + bytes)
+            return fail(ctx, MOE_E_ARG, "range overlaps an existing registration");
+    char* d = nullptr;
+    if (cudaMalloc(&d, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, MOE_E_NOMEM, "device allocation for the weight mirror failed");
+    }
+    cudaError_t e = cudaMemcpy(d, host_base, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return cuda_fail(ctx, e, "weight upload");
+    }
+    ctx->regs.push_back({h, bytes, d});
+    return MOE_OK;
+}
+
+int moe_unregister_weights(moe_ctx* ctx, const void* host_base) {
+    TRY(begin(ctx));
+    for (size_t i = 0; i < ctx->regs.size(); ++i)
+        if (ctx->regs[i].host == host_base) {
+            MOE_CUDA(cudaStreamSynchronize(ctx->stream));
+            cudaFree(ctx->regs[i].dev);
+            ctx->regs.erase(ctx->regs.begin() + i);
+            return MOE_OK;
+        }
+    return fail(ctx, MOE_E_ARG, "no registration starts at this address");
+}
+
+// ----------------------------------------------------------------- Q4_0
+int moe_quantize_fp32_to_q4_0(moe_ctx* ctx, const float* src, uint8_t* dst_packed,
+                              float* dst_scales, int64_t n) {
+    TRY(begin(ctx));
+    if (!src || !dst_packed || !dst_scales) return fail(ctx, MOE_E_ARG, "null pointer");
+    if (n < 0 || n % 32) return fail(ctx, MOE_E_SHAPE, "num_elements must be a multiple of 32");
+    if (n == 0) return MOE_OK;
+    TRY(ws_reserve(ctx, al(n * 4) + al(n / 2) + al(n / 8)));
+    void *s, *p, *sc;
+    TRY(dev_ptr(ctx, src, n * 4, K_IN, &s));
+    TRY(dev_ptr(ctx, dst_packed, n / 2, K_OUT, &p));
+    TRY(dev_ptr(ctx, dst_scales, n / 32 * 4, K_OUT, &sc));
+    if (!al16(s) || !al16(p)) return fail(ctx, MOE_E_ARG, "device buffers must be 16-byte aligned");
+    ctx->launches += moe::launch_quantize((const float*)s, (uint8_t*)p, (float*)sc, n / 32, ctx->stream);
+    return finish(ctx);
+}
+
+int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch, const uint8_t* W, const float* S,
+                         const float* x, float* out, int64_t c_in, int64_t c_out) {
+    TRY(begin(ctx));
+    if (!W || !S || !x || !out) return fail(ctx, MOE_E_ARG, "null pointer");
+    TRY(check_q4_shape(ctx, c_in, c_out));
+    if (batch <= 0) return fail(ctx, MOE_E_SHAPE, "batch_size must be >= 1");
+    if (batch > (1 << 20)) return fail(ctx, MOE_E_SHAPE, "batch_size too large");
+    TRY(ws_reserve(ctx, al(batch * c_in * 4) + al(batch * c_out * 4)));
+    void *w, *sc, *xd, *od;
+    TRY(dev_ptr(ctx, W, c_out * c_in / 2, K_W, &w));
+    TRY(dev_ptr(ctx, S, c_out * c_in / 32 * 4, K_W, &sc));
+    TRY(dev_ptr(ctx, x, batch * c_in * 4, K_IN, &xd));
+    TRY(dev_ptr(ctx, out, batch * c_out * 4, K_OUT, &od));
+    if (!al16(w)) return fail(ctx, MOE_E_ARG, "packed weights must be 16-byte aligned");
+    moe::GemvArgs g;
+    g.Wp = (const uint8_t*)w;
+    g.Ws = (const float*)sc;
+    g.rows_per_expert = c_out;
+    g.K = (int)c_in;
+    g.X = xd;
+    g.dense_tokens = (int)batch;
+    g.out = (float*)od;
+    g.out_stride = c_out;
+    g.max_tokens = (int)batch;
+    g.max_unique = 1;
+    {
+        ProfScope ps(ctx, "q4_matmul");
+        ctx->launches += moe::launch_gemv(moe::GEMV_PLAIN, g, ctx->num_sms, ctx->stream);
+    }
+    return finish(ctx);
+}
+
+int moe_q4_matmul_vec(moe_ctx* ctx, const uint8_t* W, const float* S, const float* x, float* out,
+                      int64_t c_in, int64_t c_out) {
+    return moe_q4_matmul_batchN(ctx, 1, W, S, x, out, c_in, c_out);
+}
+
+// -------------------------------------------------------------- routing
+int moe_compute_moe_lod_weights(moe_ctx* ctx, int64_t batch, const int64_t* top_idx,
+                                const float* top_val, const float* pes, float top_p,
+                                int64_t* act_idx, float* act_w, int64_t* act_count,
+                                int64_t top_k) {
+    TRY(begin(ctx));
+    if (!top_idx || !top_val || !pes || !act_idx || !act_w || !act_count)
+        return fail(ctx, MOE_E_ARG, "null pointer");
+    if (batch <= 0 || top_k <= 0) return fail(ctx, MOE_E_SHAPE, "batch and top_k must be >= 1");
+    // per_expert_scale is indexed by expert id; when it has to be staged its
+    // extent is taken from the largest id (host index arrays) or 128.
+    int64_t E = 128;
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, top_idx) != cudaSuccess) cudaGetLastError();
+    else if (at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged) {
+        int64_t mx = -1;
+        for (int64_t i = 0; i < batch * top_k; ++i) mx = std::max(mx, top_idx[i]);
+        for (int64_t i = 0; i < batch * top_k; ++i)
+            if (top_idx[i] < 0) return fail(ctx, MOE_E_ARG, "negative expert index");
+        E = std::max<int64_t>(E, mx + 1);
+    }
+    const int64_t P = batch * top_k;
+    TRY(ws_reserve(ctx, al(P * 8) * 2 + al(P * 4) * 2 + al(E * 4) + al(batch * 8)));
+    void *ti, *tv, *pe, *ai, *aw, *ac;
+    TRY(dev_ptr(ctx, top_idx, P * 8, K_IN, &ti));
+    TRY(dev_ptr(ctx, top_val, P * 4, K_IN, &tv));
+    TRY(dev_ptr(ctx, pes, E * 4, K_IN, &pe));
+    TRY(dev_ptr(ctx, act_idx, P * 8, K_INOUT, &ai));
+    TRY(dev_ptr(ctx, act_w, P * 4, K_INOUT, &aw));
+    TRY(dev_ptr(ctx, act_count, batch * 8, K_OUT, &ac));
+    ctx->launches += moe::launch_lod(batch, (const int64_t*)ti, (const float*)tv, (const float*)pe,
+                                     top_p, (int64_t*)ai, (float*)aw, (int64_t*)ac, (int)top_k,
+                                     E, ctx->err_flag, ctx->stream);
+    return finish(ctx);
+}
+
+int moe_apply_moe_lod_and_set_cover(moe_ctx* ctx, const int64_t* top_idx, const float* top_val,
+                                    const float* pes, float* top_w, int64_t B, int64_t top_k,
+                                    int64_t active_top_k, float top_p, const uint8_t* eb_mask,
+                                    const int64_t* active_canvas_idx, int64_t unaccepted_top_k) {
+    (void)top_p;
+    TRY(begin(ctx));
+    if (!top_idx || !top_val || !pes || !top_w) return fail(ctx, MOE_E_ARG, "null pointer");
+    if (B <= 0 || top_k <= 0) return fail(ctx, MOE_E_SHAPE, "B and top_k must be >= 1");
+    const int64_t P = B * top_k;
+    // eb_mask is indexed by the original canvas position
+    int64_t mask_n = B;
+    if (eb_mask && active_canvas_idx) {
+        cudaPointerAttributes at;
+        if (cudaPointerGetAttributes(&at, active_canvas_idx) != cudaSuccess) cudaGetLastError();
+        else if (at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged)
+            for (int64_t i = 0; i < B; ++i) mask_n = std::max(mask_n, active_canvas_idx[i] + 1);
+    }
+    TRY(ws_reserve(ctx, al(P * 8) + al(P * 4) * 2 + al(128 * 4) + al(mask_n) + al(B * 8)));
+    void *ti, *tv, *pe, *tw, *eb = nullptr, *ac = nullptr;
+    TRY(dev_ptr(ctx, top_idx, P * 8, K_IN, &ti));
+    TRY(dev_ptr(ctx, top_val, P * 4, K_IN, &tv));
+    TRY(dev_ptr(ctx, pes, 128 * 4, K_IN, &pe));
+    TRY(dev_ptr(ctx, top_w, P * 4, K_OUT, &tw));
+    if (eb_mask) TRY(dev_ptr(ctx, eb_mask, mask_n, K_IN, &eb));
+    if (active_canvas_idx) TRY(dev_ptr(ctx, active_canvas_idx, B * 8, K_IN, &ac));
+    ctx->launches += moe::launch_apply_lod((const int64_t*)ti, (const float*)tv, (const float*)pe,
+                                           (float*)tw, B, (int)top_k, active_top_k,
+                                           (const uint8_t*)eb, (const int64_t*)ac,
+                                           unaccepted_top_k, ctx->stream);
+    return finish(ctx);
+}
+
+int moe_compute_subbatch_set_cover_moe_weights(moe_ctx* ctx, int64_t sub_b, const int64_t* ti,
+                                               const float* tv, const float* pes, float top_p,
+                                               int64_t* tc, int64_t* tidx, float* tw,
+                                               int64_t num_experts, int64_t top_k,
+                                               float core_top_p, float smp) {
+    TRY(begin(ctx));
+    if (!ti || !tv || !pes || !tc || !tidx || !tw) return fail(ctx, MOE_E_ARG, "null pointer");
+    if (sub_b <= 0 || sub_b > 64) return fail(ctx, MOE_E_SHAPE, "sub_b must be in [1, 64]");
+    if (top_k <= 0 || top_k > 32) return fail(ctx, MOE_E_SHAPE, "top_k must be in [1, 32]");
+    if (num_experts <= 0 || num_experts > 1024) return fail(ctx, MOE_E_SHAPE, "num_experts must be in [1, 1024]");
+    const int64_t P = sub_b * top_k;
+    TRY(ws_reserve(ctx, al(P * 8) * 3 + al(P * 4) * 4 + al(num_experts * 4) + al(sub_b * 8)));
+    void *dti, *dtv, *dpe, *dtc, *dtidx, *dtw;
+    TRY(dev_ptr(ctx, ti, P * 8, K_IN, &dti));
+    TRY(dev_ptr(ctx, tv, P * 4, K_IN, &dtv));
+    TRY(dev_ptr(ctx, pes, num_experts * 4, K_IN, &dpe));
+    TRY(dev_ptr(ctx, tc, sub_b * 8, K_OUT, &dtc));
+    TRY(dev_ptr(ctx, tidx, P * 8, K_INOUT, &dtidx));
+    TRY(dev_ptr(ctx, tw, P * 4, K_INOUT, &dtw));
+    // the kernel reads int32 ids; narrow them on device
+    int* ti32 = (int*)ws_take(ctx, P * 4);
+    float* dummy_w = (float*)ws_take(ctx, P * 4);
+    ctx->launches += moe::launch_slots_from_lists(sub_b, (int)top_k, nullptr, top_k,
+                                                  (const int64_t*)dti, nullptr, ti32, dummy_w,
+                                                  (int)num_experts, ctx->err_flag, ctx->stream);
+    ctx->launches += moe::launch_set_cover(ti32, (const float*)dtv, sub_b, (int)top_k,
+                                           (int)num_experts, (const float*)dpe, top_p, core_top_p,
+                                           smp, (int)sub_b, nullptr, nullptr, (int64_t*)dtc,
+                                           (int64_t*)dtidx, (float*)dtw, ctx->stream);
+    return finish(ctx);
+}
+
+// -------------------------------------------------------- expert stages
+int moe_run_moe_experts_stage1(moe_ctx* ctx, const uint8_t* gu_p, const float* gu_s,
+                               const float* moe_in, const int64_t* active_idx, int64_t count,
+                               float* gu_out_all, float* act_all, int64_t d, int64_t F,
+                               int activation) {
+    TRY(begin(ctx));
+    if (!gu_p || !gu_s || !moe_in || !act_all || (count > 0 && !active_idx))
+        return fail(ctx, MOE_E_ARG, "null pointer");
+    TRY(check_q4_shape(ctx, d, 2 * F));
+    TRY(check_q4_shape(ctx, F, d));
+    if (count < 0 || count > 32) return fail(ctx, MOE_E_SHAPE, "active_count must be in [0, 32]");
+    if (activation < 0 || activation > 1) return fail(ctx, MOE_E_ARG, "bad activation");
+    if (count == 0) return MOE_OK;
+    const int64_t E = 1024;
+    TRY(ws_reserve(ctx, expert_bufs_bytes(1, count, d, F, E) + al(d * 4) + al(count * 8) +
+                            al(count * 2 * F * 4) + al(count * F * 4)));
+    void *wp, *ws, *xi, *ai, *go = nullptr, *ao;
+    TRY(dev_ptr(ctx, gu_p, 1, K_W, &wp));
+    TRY(dev_ptr(ctx, gu_s, 1, K_W, &ws));
+    TRY(dev_ptr(ctx, moe_in, d * 4, K_IN, &xi));
+    TRY(dev_ptr(ctx, active_idx, count * 8, K_IN, &ai));
+    if (gu_out_all) TRY(dev_ptr(ctx, gu_out_all, count * 2 * F * 4, K_OUT, &go));
+    TRY(dev_ptr(ctx, act_all, count * F * 4, K_OUT, &ao));
+    if (!al16(wp)) return fail(ctx, MOE_E_ARG, "packed weights must be 16-byte aligned");
+    ExpertBufs bb;
+    TRY(take_expert_bufs(ctx, 1, count, d, F, E, &bb));
+    cudaStream_t s = ctx->stream;
+    ctx->launches += moe::launch_slots_from_lists(1, (int)count, nullptr, count,
+                                                  (const int64_t*)ai, nullptr, bb.slot_expert,
+                                                  bb.slot_weight, (int)E, ctx->err_flag, s);
+    ctx->launches += moe::launch_bucket(bb.slot_expert, count, (int)count, (int)E, bb.b, s);
+    moe::GemvArgs g;
+    g.Wp = (const uint8_t*)wp;
+    g.Ws = (const float*)ws;
+    g.rows_per_expert = 2 * F;
+    g.K = (int)d;
+    g.X = xi;
+    g.meta = bb.b.meta;
+    g.unique_expert = bb.b.unique_expert;
+    g.seg_start = bb.b.seg_start;
+    g.seg_count = bb.b.seg_count;
+    g.pair_row = bb.b.pair_token;
+    g.out_row = bb.b.pair_slot;
+    g.out = (float*)ao;
+    g.out_stride = F;
+    g.gu_out = (float*)go;
+    g.gu_stride = 2 * F;
+    g.F = (int)F;
+    g.act = activation;
+    g.max_tokens = 1;
+    g.max_unique = (int)count;
+    ctx->launches += moe::launch_gemv(moe::GEMV_ACT, g, ctx->num_sms, s);
+    return finish(ctx);
+}
+
+int moe_run_moe_experts_stage2(moe_ctx* ctx, const uint8_t* dn_p, const float* dn_s,
+                               const float* act_all, const int64_t* active_idx,
+                               const float* active_w, int64_t count, float* moe_out, int64_t d,
+                               int64_t F) {
+    TRY(begin(ctx));
+    if (!dn_p || !dn_s || !moe_out || (count > 0 && (!act_all || !active_idx || !active_w)))
+        return fail(ctx, MOE_E_ARG, "null pointer");
+    TRY(check_q4_shape(ctx, F, d));
+    if (count < 0 || count > 32) return fail(ctx, MOE_E_SHAPE, "active_count must be in [0, 32]");
+    const int64_t E = 1024, Kc = std::max<int64_t>(count, 1);
+    TRY(ws_reserve(ctx, expert_bufs_bytes(1, Kc, d, F, E) + al(Kc * F * 4) + al(Kc * 8) +
+                            al(Kc * 4) + al(d * 4)));
+    void *wp, *ws, *aa = nullptr, *ai = nullptr, *aw = nullptr, *mo;
+    TRY(dev_ptr(ctx, dn_p, 1, K_W, &wp));
+    TRY(dev_ptr(ctx, dn_s, 1, K_W, &ws));
+    if (count > 0) {
+        TRY(dev_ptr(ctx, act_all, count * F * 4, K_IN, &aa));
+        TRY(dev_ptr(ctx, active_idx, count * 8, K_IN, &ai));
+        TRY(dev_ptr(ctx, active_w, count * 4, K_IN, &aw));
+    }
+    TRY(dev_ptr(ctx, moe_out, d * 4, K_OUT, &mo));
+    if (!al16(wp)) return fail(ctx, MOE_E_ARG, "packed weights must be 16-byte aligned");
+    cudaStream_t s = ctx->stream;
+    if (count == 0) {  // moe_kernels.mojo:742-743 zeroes moe_out
+        MOE_CUDA(cudaMemsetAsync(mo, 0, d * 4, s));
+        return finish(ctx);
+    }
+    ExpertBufs bb;
+    TRY(take_expert_bufs(ctx, 1, count, d, F, E, &bb));
+    ctx->launches += moe::launch_slots_from_lists(1, (int)count, nullptr, count,
+                                                  (const int64_t*)ai, (const float*)aw,
+                                                  bb.slot_expert, bb.slot_weight, (int)E,
+                                                  ctx->err_flag, s);
+    ctx->launches += moe::launch_bucket(bb.slot_expert, count, (int)count, (int)E, bb.b, s);
+    moe::GemvArgs g;
+    g.Wp = (const uint8_t*)wp;
+    g.Ws = (const float*)ws;
+    g.rows_per_expert = d;
+    g.K = (int)F;
+    g.X = aa;
+    g.meta = bb.b.meta;
+    g.unique_expert = bb.b.unique_expert;
+    g.seg_start = bb.b.seg_start;
+    g.seg_count = bb.b.seg_count;
+    g.pair_row = bb.b.pair_slot;  // act_all rows are in slot order
+    g.out = bb.y;
+    g.out_stride = d;
+    g.max_tokens = 1;
+    g.max_unique = (int)count;
+    ctx->launches += moe::launch_gemv(moe::GEMV_PLAIN, g, ctx->num_sms, s);
+    moe::CombineArgs c;
+    c.y = bb.y;
+    c.d = d;
+    c.K = (int)count;
+    c.slot_pair = bb.b.slot_pair;
+    c.slot_weight = bb.slot_weight;
+    c.out = mo;
+    ctx->launches += moe::launch_combine(c, 1, s);
+    return finish(ctx);
+}
+
+int moe_run_moe_coalesced_core(moe_ctx* ctx, int64_t sub_b, const uint8_t* gu_p, const float* gu_s,
+                               const uint8_t* dn_p, const float* dn_s, const float* batch_in,
+                               int x_layout, const int64_t* tok_count, const int64_t* tok_idx,
+                               const float* tok_w, float* batch_out, int64_t d, int64_t F,
+                               int64_t E, int64_t top_k, int activation) {
+    TRY(begin(ctx));
+    if (!gu_p || !gu_s || !dn_p || !dn_s || !batch_in || !tok_count || !tok_idx || !tok_w || !batch_out)
+        return fail(ctx, MOE_E_ARG, "null pointer");
+    TRY(check_q4_shape(ctx, d, 2 * F));
+    TRY(check_q4_shape(ctx, F, d));
+    if (sub_b <= 0) return fail(ctx, MOE_E_SHAPE, "sub_b must be >= 1");
+    if (top_k <= 0 || top_k > 32) return fail(ctx, MOE_E_SHAPE, "top_k must be in [1, 32]");
+    if (E <= 0 || E > 1024) return fail(ctx, MOE_E_SHAPE, "num_experts must be in [1, 1024]");
+    if (x_layout < 0 || x_layout > 2 || activation < 0 || activation > 1)
+        return fail(ctx, MOE_E_ARG, "bad layout or activation");
+    const int64_t P = sub_b * top_k;
+    TRY(ws_reserve(ctx, expert_bufs_bytes(sub_b, top_k, d, F, E) + al(sub_b * d * 4) * 2 +
+                            al(sub_b * 8) + al(P * 8) + al(P * 4)));
+    void *gp, *gs, *dp, *ds, *xi, *tc, *ti, *tw, *out;
+    TRY(dev_ptr(ctx, gu_p, 1, K_W, &gp));
+    TRY(dev_ptr(ctx, gu_s, 1, K_W, &gs));
+    TRY(dev_ptr(ctx, dn_p, 1, K_W, &dp));
+    TRY(dev_ptr(ctx, dn_s, 1, K_W, &ds));
+    TRY(dev_ptr(ctx, batch_in, sub_b * d * 4, K_IN, &xi));
+    TRY(dev_ptr(ctx, tok_count, sub_b * 8, K_IN, &tc));
+    TRY(dev_ptr(ctx, tok_idx, P * 8, K_IN, &ti));
+    TRY(dev_ptr(ctx, tok_w, P * 4, K_IN, &tw));
+    TRY(dev_ptr(ctx, batch_out, sub_b * d * 4, K_OUT, &out));
+    if (!al16(gp) || !al16(dp)) return fail(ctx, MOE_E_ARG, "packed weights must be 16-byte aligned");
+    ExpertBufs bb;
+    TRY(take_expert_bufs(ctx, sub_b, top_k, d, F, E, &bb));
+    ctx->launches += moe::launch_slots_from_lists(sub_b, (int)top_k, (const int64_t*)tc, 0,
+                                                  (const int64_t*)ti, (const float*)tw,
+                                                  bb.slot_expert, bb.slot_weight, (int)E,
+                                                  ctx->err_flag, ctx->stream);
+    ExpertWeights w{(const uint8_t*)gp, (const float*)gs, (const uint8_t*)dp, (const float*)ds};
+    moe::CombineArgs c;
+    TRY(run_experts(ctx, w, sub_b, top_k, d, F, E, xi, x_layout, 0, activation, bb, &c, out));
+    return finish(ctx);
+}
+
+int moe_run_diffusion_moe_experts_parallel(moe_ctx* ctx, const uint8_t* gu_p, const float* gu_s,
+                                           const uint8_t* dn_p, const float* dn_s,
+                                           const uint16_t* in_f16, const int64_t* top_idx,
+                                           const float* top_w, uint16_t* out_f16, int64_t B,
+                                           int64_t d, int64_t F, int64_t top_k, int activation) {
+    TRY(begin(ctx));
+    if (!gu_p || !gu_s || !dn_p || !dn_s || !in_f16 || !top_idx || !top_w || !out_f16)
+        return fail(ctx, MOE_E_ARG, "null pointer");
+    TRY(check_q4_shape(ctx, d, 2 * F));
+    TRY(check_q4_shape(ctx, F, d));
+    if (B <= 0) return fail(ctx, MOE_E_SHAPE, "B must be >= 1");
+    if (top_k <= 0 || top_k > 32) return fail(ctx, MOE_E_SHAPE, "top_k must be in [1, 32]");
+    if (activation < 0 || activation > 1) return fail(ctx, MOE_E_ARG, "bad activation");
+    const int64_t E = 128;  // diffusion_kernels.mojo:255 fixes 128 expert buckets
+    const int64_t P = B * top_k;
+    TRY(ws_reserve(ctx, expert_bufs_bytes(B, top_k, d, F, E) + al(B * d * 2) * 2 + al(P * 8) +
+                            al(P * 4)));
+    void *gp, *gs, *dp, *ds, *xi, *ti, *tw, *out;
+    TRY(dev_ptr(ctx, gu_p, 1, K_W, &gp));
+    TRY(dev_ptr(ctx, gu_s, 1, K_W, &gs));
+    TRY(dev_ptr(ctx, dn_p, 1, K_W, &dp));
+    TRY(dev_ptr(ctx, dn_s, 1, K_W, &ds));
+    TRY(dev_ptr(ctx, in_f16, B * d * 2, K_IN, &xi));
+    TRY(dev_ptr(ctx, top_idx, P * 8, K_IN, &ti));
+    TRY(dev_ptr(ctx, top_w, P * 4, K_IN, &tw));
+    TRY(dev_ptr(ctx, out_f16, B * d * 2, K_OUT, &out));
+    if (!al16(gp) || !al16(dp)) return fail(ctx, MOE_E_ARG, "packed weights must be 16-byte aligned");
+    ExpertBufs bb;
+    TRY(take_expert_bufs(ctx, B, top_k, d, F, E, &bb));
+    ctx->launches += moe::launch_slots_from_topw(B, (int)top_k, (const int64_t*)ti, (const float*)tw,
+                                                 bb.slot_expert, bb.slot_weight, (int)E,
+                                                 ctx->err_flag, ctx->stream);
+    ExpertWeights w{(const uint8_t*)gp, (const float*)gs, (const uint8_t*)dp, (const float*)ds};
+    moe::CombineArgs c;
+    c.fma_mode = 1;
+    c.out_f16 = 1;
+    TRY(run_experts(ctx, w, B, top_k, d, F, E, xi, MOE_X_NATURAL, 1, activation, bb, &c, out));
+    return finish(ctx);
+}
+
+// ------------------------------------------------------------ layer level
+namespace {
+
+struct LayerDev {
+    const uint8_t* rp = nullptr;
+    const float* rs = nullptr;
+    const float* rf32 = nullptr;
+    const float* bias = nullptr;
+    const float* router_scale = nullptr;
+    const float* pes = nullptr;
+    const float* pre_w = nullptr;
+    const float* post_w = nullptr;
+    ExpertWeights w{};
+};
+
+int check_desc(moe_ctx* ctx, const moe_layer_desc* L) {
+    if (!L) return fail(ctx, MOE_E_ARG, "null layer descriptor");
+    TRY(check_q4_shape(ctx, L->embed_dim, 2 * L->expert_mlp_dim));
+    TRY(check_q4_shape(ctx, L->expert_mlp_dim, L->embed_dim));
+    if (L->embed_dim > 12288) return fail(ctx, MOE_E_SHAPE, "embed_dim must be <= 12288");
+    if (L->num_experts <= 0 || L->num_experts > 1024) return fail(ctx, MOE_E_SHAPE, "num_experts must be in [1, 1024]");
+    if (L->top_k <= 0 || L->top_k > 32 || L->top_k > L->num_experts)
+        return fail(ctx, MOE_E_SHAPE, "top_k must be in [1, min(32, num_experts)]");
+    if (L->activation < 0 || L->activation > 1) return fail(ctx, MOE_E_ARG, "bad activation");
+    if (!(L->router_packed && L->router_scales) && !L->router_f32)
+        return fail(ctx, MOE_E_ARG, "no router weights");
+    if (!L->router_scale || !L->per_expert_scale || !L->pre_norm_w || !L->gate_up_packed ||
+        !L->gate_up_scales || !L->down_packed || !L->down_scales)
+        return fail(ctx, MOE_E_ARG, "null weight pointer in layer descriptor");
+    return MOE_OK;
+}
+
+size_t layer_small_bytes(const moe_layer_desc* L) {
+    const int64_t d = L->embed_dim, E = L->num_experts;
+    return al(d * 4) * 3 + al(E * 4) * 2 + (L->router_f32 ? al(E * d * 4) : 0);
+}
+
+int layer_dev(moe_ctx* ctx, const moe_layer_desc* L, int flags, LayerDev* o) {
+    const int64_t d = L->embed_dim, E = L->num_experts, F = L->expert_mlp_dim;
+    void* p;
+    if (L->router_packed) {
+        TRY(dev_ptr(ctx, L->router_packed, E * d / 2, K_W, &p));
+        o->rp = (const uint8_t*)p;
+        TRY(dev_ptr(ctx, L->router_scales, E * d / 32 * 4, K_W, &p));
+        o->rs = (const float*)p;
+        if (!al16(o->rp)) return fail(ctx, MOE_E_ARG, "router weights must be 16-byte aligned");
+    } else {
+        TRY(dev_ptr(ctx, L->router_f32, E * d * 4, K_IN, &p));
+        o->rf32 = (const float*)p;
+    }
+    if (L->router_logit_bias) {
+        TRY(dev_ptr(ctx, L->router_logit_bias, E * 4, K_IN, &p));
+        o->bias = (const float*)p;
+    }
+    TRY(dev_ptr(ctx, L->router_scale, d * 4, K_IN, &p));
+    o->router_scale = (const float*)p;
+    TRY(dev_ptr(ctx, L->per_expert_scale, E * 4, K_IN, &p));
+    o->pes = (const float*)p;
+    TRY(dev_ptr(ctx, L->pre_norm_w, d * 4, K_IN, &p));
+    o->pre_w = (const float*)p;
+    if (flags & MOE_F_POST_NORM) {
+        if (!L->post_norm_w) return fail(ctx, MOE_E_ARG, "MOE_F_POST_NORM needs post_norm_w");
+        TRY(dev_ptr(ctx, L->post_norm_w, d * 4, K_IN, &p));
+        o->post_w = (const float*)p;
+    }
+    TRY(dev_ptr(ctx, L->gate_up_packed, E * 2 * F * d / 2, K_W, &p));
+    o->w.gu_p = (const uint8_t*)p;
+    TRY(dev_ptr(ctx, L->gate_up_scales, E * 2 * F * d / 32 * 4, K_W, &p));
+    o->w.gu_s = (const float*)p;
+    TRY(dev_ptr(ctx, L->down_packed, E * d * F / 2, K_W, &p));
+    o->w.dn_p = (const uint8_t*)p;
+    TRY(dev_ptr(ctx, L->down_scales, E * d * F / 32 * 4, K_W, &p));
+    o->w.dn_s = (const float*)p;
+    if (!al16(o->w.gu_p) || !al16(o->w.dn_p)) return fail(ctx, MOE_E_ARG, "packed weights must be 16-byte aligned");
+    return MOE_OK;
+}
+
+int route_dev(moe_ctx* ctx, const moe_layer_desc* L, const LayerDev& ld, int64_t M,
+              const float* xd, int flags, float* moe_in, int* slot_expert, float* slot_weight,
+              float* probs, int64_t* top_idx, float* top_val, int64_t* tc, int64_t* ti,
+              float* tw) {
+    const int64_t K = L->top_k;
+    int* ti32 = (int*)ws_take(ctx, M * K * 4);
+    float* tv = (float*)ws_take(ctx, M * K * 4);
+    if (!tv) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+    moe::RouteArgs a;
+    a.x = xd;
+    a.d = L->embed_dim;
+    a.E = (int)L->num_experts;
+    a.K = (int)K;
+    a.rp = ld.rp;
+    a.rs = ld.rs;
+    a.rf32 = ld.rf32;
+    a.bias = ld.bias;
+    a.router_scale = ld.router_scale;
+    a.rsf = L->r_scale_factor;
+    a.pes = ld.pes;
+    a.top_p = L->moe_top_p;
+    a.pre_w = ld.pre_w;
+    a.lod = (flags & MOE_F_SET_COVER) ? 0 : 1;
+    a.moe_in = moe_in;
+    a.probs_out = probs;
+    a.top_idx = top_idx;
+    a.top_val = top_val;
+    a.ti32 = ti32;
+    a.tv = tv;
+    a.slot_expert = slot_expert;
+    a.slot_weight = slot_weight;
+    a.tok_count = tc;
+    a.tok_idx = ti;
+    a.tok_w = tw;
+    {
+        ProfScope ps(ctx, "route");
+        ctx->launches += moe::launch_route(a, M, ctx->stream);
+    }
+    if (flags & MOE_F_SET_COVER)
+        ctx->launches += moe::launch_set_cover(ti32, tv, M, (int)K, (int)L->num_experts, ld.pes,
+                                               L->moe_top_p, 0.85f, 0.068f, 5, slot_expert,
+                                               slot_weight, tc, ti, tw, ctx->stream);
+    return MOE_OK;
+}
+
+}  // namespace
+
+int moe_route(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const float* x, int flags,
+              float* scores, int64_t* top_idx, float* top_val, int64_t* tc, int64_t* ti,
+              float* tw, float* moe_in) {
+    TRY(begin(ctx));
+    TRY(check_desc(ctx, L));
+    if (!x || !tc || !ti || !tw) return fail(ctx, MOE_E_ARG, "null pointer");
+    if (M <= 0) return fail(ctx, MOE_E_SHAPE, "M must be >= 1");
+    const int64_t d = L->embed_dim, E = L->num_experts, K = L->top_k, P = M * K;
+    TRY(ws_reserve(ctx, layer_small_bytes(L) + al(M * d * 4) * 2 + al(M * E * 4) + al(P * 8) * 2 +
+                            al(P * 4) * 6 + al(M * 8)));
+    LayerDev ld;
+    TRY(layer_dev(ctx, L, flags & ~MOE_F_POST_NORM, &ld));
+    void *xd, *sc = nullptr, *dti = nullptr, *dtv = nullptr, *dtc, *dtidx, *dtw, *mi = nullptr;
+    TRY(dev_ptr(ctx, x, M * d * 4, K_IN, &xd));
+    if (scores) TRY(dev_ptr(ctx, scores, M * E * 4, K_OUT, &sc));
+    if (top_idx) TRY(dev_ptr(ctx, top_idx, P * 8, K_OUT, &dti));
+    if (top_val) TRY(dev_ptr(ctx, top_val, P * 4, K_OUT, &dtv));
+    TRY(dev_ptr(ctx, tc, M * 8, K_OUT, &dtc));
+    TRY(dev_ptr(ctx, ti, P * 8, K_OUT, &dtidx));
+    TRY(dev_ptr(ctx, tw, P * 4, K_OUT, &dtw));
+    if (moe_in) TRY(dev_ptr(ctx, moe_in, M * d * 4, K_OUT, &mi));
+    int* se = (int*)ws_take(ctx, P * 4);
+    float* sw = (float*)ws_take(ctx, P * 4);
+    TRY(route_dev(ctx, L, ld, M, (const float*)xd, flags, (float*)mi, se, sw, (float*)sc,
+                  (int64_t*)dti, (float*)dtv, (int64_t*)dtc, (int64_t*)dtidx, (float*)dtw));
+    return finish(ctx);
+}
+
+int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const float* x, void* out,
+                      int flags, int64_t* tc, int64_t* ti, float* tw) {
+    TRY(begin(ctx));
+    TRY(check_desc(ctx, L));
+    if (!x || !out) return fail(ctx, MOE_E_ARG, "null pointer");
+    if (M <= 0) return fail(ctx, MOE_E_SHAPE, "M must be >= 1");
+    const int64_t d = L->embed_dim, E = L->num_experts, K = L->top_k, F = L->expert_mlp_dim;
+    const int64_t P = M * K;
+    const size_t out_bytes = M * d * ((flags & MOE_F_FP16_OUT) ? 2 : 4);
+    TRY(ws_reserve(ctx, layer_small_bytes(L) + expert_bufs_bytes(M, K, d, F, E) + al(M * d * 4) * 2 +
+                            al(out_bytes) + al(P * 4) * 2 + al(M * 8) + al(P * 8) + al(P * 4)));
+    LayerDev ld;
+    TRY(layer_dev(ctx, L, flags, &ld));
+    void *xd, *od, *dtc = nullptr, *dti = nullptr, *dtw = nullptr;
+    TRY(dev_ptr(ctx, x, M * d * 4, K_IN, &xd));
+    TRY(dev_ptr(ctx, out, out_bytes, K_OUT, &od));
+    if (tc) TRY(dev_ptr(ctx, tc, M * 8, K_OUT, &dtc));
+    if (ti) TRY(dev_ptr(ctx, ti, P * 8, K_OUT, &dti));
+    if (tw) TRY(dev_ptr(ctx, tw, P * 4, K_OUT, &dtw));
+    float* moe_in = (float*)ws_take(ctx, M * d * 4);
+    ExpertBufs bb;
+    TRY(take_expert_bufs(ctx, M, K, d, F, E, &bb));
+    TRY(route_dev(ctx, L, ld, M, (const float*)xd, flags, moe_in, bb.slot_expert, bb.slot_weight,
+                  nullptr, nullptr, nullptr, (int64_t*)dtc, (int64_t*)dti, (float*)dtw));
+    moe::CombineArgs c;
+    c.post_norm = (flags & MOE_F_POST_NORM) ? 1 : 0;
+    c.post_w = ld.post_w;
+    c.out_f16 = (flags & MOE_F_FP16_OUT) ? 1 : 0;
+    TRY(run_experts(ctx, ld.w, M, K, d, F, E, moe_in, MOE_X_NATURAL, 0, L->activation, bb, &c, od));
+    return finish(ctx);
+}
+
+}  // extern "C"

@@ -1,0 +1,115 @@
+// moe_internal.h -- launch interface between the C ABI (moe_abi.cu) and the
+// kernels (moe_kernels.cu).  Internal to libmoe_b200.so.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+// Grouped Q4_0 GEMV over a device-side work list (see k_q4_gemv).
+struct GemvArgs {
+    const uint8_t* Wp = nullptr;  // expert 0's packed rows
+    const float* Ws = nullptr;    // expert 0's scales
+    int64_t rows_per_expert = 0;  // R
+    int K = 0;                    // inner dimension (multiple of 32)
+    const void* X = nullptr;      // input rows [*, K]
+    int x_layout = 0;             // moe_x_layout
+    int x_f16 = 0;                // input rows are fp16
+    const int* meta = nullptr;    // meta[0] = number of unique experts U
+    const int* unique_expert = nullptr;
+    const int* seg_start = nullptr;
+    const int* seg_count = nullptr;
+    const int* pair_row = nullptr;  // input row of sorted pair p (nullptr: p)
+    const int* out_row = nullptr;   // output row of sorted pair p (nullptr: p)
+    int dense_tokens = 0;           // > 0: one matrix (expert 0), tokens 0..n-1
+    float* out = nullptr;
+    int64_t out_stride = 0;
+    float* gu_out = nullptr;        // optional raw gate/up values (ACT mode)
+    int64_t gu_stride = 0;
+    int F = 0;                      // ACT mode: act rows; gate = rows [0,F), up = [F,2F)
+    int act = 0;
+    int max_tokens = 1;             // upper bound on tokens per expert (host side)
+    int max_unique = 1;             // upper bound on U (host side)
+};
+
+enum GemvMode { GEMV_PLAIN = 0, GEMV_ACT = 1 };
+
+struct RouteArgs {
+    const float* x = nullptr;  // [M][d] fp32 natural
+    int64_t d = 0;
+    int E = 0, K = 0;
+    const uint8_t* rp = nullptr;
+    const float* rs = nullptr;
+    const float* rf32 = nullptr;
+    const float* bias = nullptr;
+    const float* router_scale = nullptr;
+    float rsf = 0.f;
+    const float* pes = nullptr;
+    float top_p = 1.f;
+    const float* pre_w = nullptr;
+    int lod = 1;
+    float* moe_in = nullptr;
+    float* probs_out = nullptr;
+    int64_t* top_idx = nullptr;
+    float* top_val = nullptr;
+    int* ti32 = nullptr;
+    float* tv = nullptr;
+    int* slot_expert = nullptr;
+    float* slot_weight = nullptr;
+    int64_t* tok_count = nullptr;
+    int64_t* tok_idx = nullptr;
+    float* tok_w = nullptr;
+};
+
+struct BucketOut {
+    int* meta = nullptr;  // [0] U, [1] total pairs
+    int* unique_expert = nullptr;
+    int* seg_start = nullptr;
+    int* seg_count = nullptr;
+    int* pair_token = nullptr;
+    int* pair_slot = nullptr;
+    int* slot_pair = nullptr;
+};
+
+struct CombineArgs {
+    const float* y = nullptr;  // [pairs][d]
+    int64_t d = 0;
+    int K = 0;
+    const int* slot_pair = nullptr;
+    const float* slot_weight = nullptr;
+    const float* post_w = nullptr;
+    int post_norm = 0;
+    int fma_mode = 0;  // 1: s = fma(y, w, s) (diffusion_kernels.mojo:396); 0: s += y*w
+    void* out = nullptr;
+    int out_f16 = 0;
+};
+
+// Every launcher returns the number of kernels it launched.
+int launch_route(const RouteArgs& a, int64_t M, cudaStream_t s);
+int launch_set_cover(const int* ti32, const float* tv, int64_t M, int K, int E, const float* pes,
+                     float top_p, float core_top_p, float singleton_min_prob, int sub_batch,
+                     int* slot_expert, float* slot_weight, int64_t* tok_count, int64_t* tok_idx,
+                     float* tok_w, cudaStream_t s);
+int launch_slots_from_lists(int64_t M, int K, const int64_t* count, int64_t count_scalar,
+                            const int64_t* idx, const float* w, int* slot_expert,
+                            float* slot_weight, int E, int* err_flag, cudaStream_t s);
+int launch_slots_from_topw(int64_t M, int K, const int64_t* idx, const float* w,
+                           int* slot_expert, float* slot_weight, int E, int* err_flag,
+                           cudaStream_t s);
+int launch_bucket(const int* slot_expert, int64_t P, int K, int E, const BucketOut& o,
+                  cudaStream_t s);
+int launch_gemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);
+int launch_combine(const CombineArgs& a, int64_t M, cudaStream_t s);
+int launch_quantize(const float* src, uint8_t* packed, float* scales, int64_t nblocks,
+                    cudaStream_t s);
+int launch_lod(int64_t B, const int64_t* top_idx, const float* top_val, const float* pes,
+               float top_p, int64_t* act_idx, float* act_w, int64_t* act_count, int K,
+               int64_t E, int* err_flag, cudaStream_t s);
+int launch_apply_lod(const int64_t* top_idx, const float* top_val, const float* pes, float* top_w,
+                     int64_t B, int K, int64_t active_top_k, const uint8_t* eb_mask,
+                     const int64_t* active_canvas_idx, int64_t unaccepted_top_k, cudaStream_t s);
+
+size_t gemv_smem_bytes(int K, int maxt);
+int gemv_pick_maxt(int K, int max_tokens);
+
+}  // namespace moe

@@ -1,0 +1,927 @@
+// moe_kernels.cu -- CUDA-core kernels of the Q4_0 MoE-FFN path (sm_100a):
+// router, expert bucketing, grouped Q4_0 GEMV with fused activation,
+// weighted combine (+ post-norm), quantizer and routing helpers.
+//
+// The grouped GEMV (k_q4_gemv) is the memory-bound decode kernel: weights are
+// streamed once with 128-bit non-allocating loads, nibbles are dequantised in
+// registers (one shift + one LOP3 per weight, see nib_1p), activations sit in
+// shared memory in a bank-conflict-free swizzle and partial sums are reduced
+// with warp shuffles.
+#include <float.h>
+
+#include "common.cuh"
+#include "moe_internal.h"
+
+namespace moe {
+
+// ------------------------------------------------------------------ loads
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ float ldg_stream_f(const float* p) {
+    float r;
+    asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(r) : "l"(p));
+    return r;
+}
+
+// Dot product of one Q4_0 block (16 bytes, 32 weights) with 32 activations
+// held in the swizzled shared layout, using the 1 + n/16 representation:
+//   sum_k (n_k - 8) x_k = 16 * (sum_k (1 + n_k/16) x_k - 1.5 * sum_k x_k).
+// Returns sum_k (1 + n_k/16) x_k; the caller subtracts 1.5*sum(x).
+struct Deq32 {
+    float f[32];
+    __device__ __forceinline__ void load(uint4 q) {
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            f[8 * i + 0] = nib_1p<0>(w[i]);
+            f[8 * i + 1] = nib_1p<1>(w[i]);
+            f[8 * i + 2] = nib_1p<2>(w[i]);
+            f[8 * i + 3] = nib_1p<3>(w[i]);
+            f[8 * i + 4] = nib_1p<4>(w[i]);
+            f[8 * i + 5] = nib_1p<5>(w[i]);
+            f[8 * i + 6] = nib_1p<6>(w[i]);
+            f[8 * i + 7] = nib_1p<7>(w[i]);
+        }
+    }
+    // xb points at the 32 swizzled floats of block b
+    __device__ __forceinline__ float dot(const float* xb, int b) const {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; q += 2) {
+            const float4 v0 = *reinterpret_cast<const float4*>(xb + (((q + b) & 7) << 2));
+            const float4 v1 = *reinterpret_cast<const float4*>(xb + (((q + 1 + b) & 7) << 2));
+            a0 = fmaf(f[4 * q + 0], v0.x, a0);
+            a1 = fmaf(f[4 * q + 1], v0.y, a1);
+            a2 = fmaf(f[4 * q + 2], v0.z, a2);
+            a3 = fmaf(f[4 * q + 3], v0.w, a3);
+            a0 = fmaf(f[4 * q + 4], v1.x, a0);
+            a1 = fmaf(f[4 * q + 5], v1.y, a1);
+            a2 = fmaf(f[4 * q + 6], v1.z, a2);
+            a3 = fmaf(f[4 * q + 7], v1.w, a3);
+        }
+        return (a0 + a1) + (a2 + a3);
+    }
+};
+
+__device__ __forceinline__ int swz(int j) {  // natural index -> swizzled smem index
+    const int b = j >> 5, q = (j >> 2) & 7;
+    return (b << 5) + (((q + b) & 7) << 2) + (j & 3);
+}
+
+// ------------------------------------------------------------ grouped GEMV
+// Work item = (unique expert u, tile of rows).  Each warp owns 4 rows per
+// pass (8 lanes per row, lane l8 takes blocks l8, l8+8, ...), RPW passes;
+// all loads of a chunk of NBL blocks per lane are issued before any math.
+// ACT mode: the warp's 4 rows are gate a, gate a+1, up a, up a+1, and the
+// activation is applied after the lane reduction.
+template <int MODE, int NBL, int RPW, int MAXT>
+__global__ void __launch_bounds__(256, 2) k_q4_gemv(GemvArgs a) {
+    extern __shared__ float4 smem4[];
+    float* xs = reinterpret_cast<float*>(smem4);  // [MAXT][K] swizzled
+    const int K = a.K, nb = K >> 5;
+    float* xsum = xs + (size_t)MAXT * K;  // [MAXT][nb]  (1.5 * sum of block)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 3, l8 = lane & 7;
+    const int nbl = (nb + 7) >> 3;
+    const int rows_per_tile = (MODE == GEMV_ACT) ? 16 * RPW : 32 * RPW;
+    const int64_t tile_rows = (MODE == GEMV_ACT) ? a.F : a.rows_per_expert;
+    const int n_tiles = (int)((tile_rows + rows_per_tile - 1) / rows_per_tile);
+    const int U = a.dense_tokens > 0 ? 1 : a.meta[0];
+    const int n_items = U * n_tiles;
+    int staged_u = -1;
+
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const int u = item / n_tiles, tile = item - u * n_tiles;
+        const int e = a.dense_tokens > 0 ? 0 : a.unique_expert[u];
+        const int n = a.dense_tokens > 0 ? a.dense_tokens : a.seg_count[u];
+        const int s0 = a.dense_tokens > 0 ? 0 : a.seg_start[u];
+        const uint8_t* Wp = a.Wp + (size_t)e * a.rows_per_expert * (K >> 1);
+        const float* Ws = a.Ws + (size_t)e * a.rows_per_expert * nb;
+
+        // rows of this lane group for every pass
+        int64_t row[RPW];
+        bool rv[RPW];
+        int arow[RPW];
+#pragma unroll
+        for (int ip = 0; ip < RPW; ++ip) {
+            if (MODE == GEMV_ACT) {
+                const int ar = tile * rows_per_tile + warp * 2 * RPW + ip * 2 + (g & 1);
+                arow[ip] = ar;
+                rv[ip] = ar < a.F;
+                row[ip] = (g < 2) ? ar : (int64_t)a.F + ar;
+            } else {
+                const int64_t r = (int64_t)tile * rows_per_tile + warp * 4 * RPW + ip * 4 + g;
+                arow[ip] = 0;
+                rv[ip] = r < a.rows_per_expert;
+                row[ip] = r;
+            }
+        }
+
+        for (int c0 = 0; c0 < n; c0 += MAXT) {
+            const int nt = min(MAXT, n - c0);
+            if (!(n <= MAXT && staged_u == u)) {
+                __syncthreads();
+                const int64_t tot = (int64_t)nt * K;
+                for (int64_t j = threadIdx.x; j < tot; j += blockDim.x) {
+                    const int t = (int)(j / K), jj = (int)(j - (int64_t)t * K);
+                    const int p = s0 + c0 + t;
+                    const int64_t src_row = a.pair_row ? a.pair_row[p] : p;
+                    const int64_t si = src_row * K + x_src_index(jj, K, a.x_layout);
+                    float v;
+                    if (a.x_f16)
+                        v = __half2float(reinterpret_cast<const __half*>(a.X)[si]);
+                    else
+                        v = reinterpret_cast<const float*>(a.X)[si];
+                    xs[(size_t)t * K + swz(jj)] = v;
+                }
+                __syncthreads();
+                for (int j = threadIdx.x; j < nt * nb; j += blockDim.x) {
+                    const float* xb = xs + (size_t)j * 32;  // (t, b) -> t*K + b*32 == j*32
+                    float s = 0.f;
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) s += xb[k];
+                    xsum[j] = 1.5f * s;
+                }
+                __syncthreads();
+                staged_u = (n <= MAXT) ? u : -1;
+            }
+
+            float acc[RPW][MAXT];
+#pragma unroll
+            for (int ip = 0; ip < RPW; ++ip)
+#pragma unroll
+                for (int t = 0; t < MAXT; ++t) acc[ip][t] = 0.f;
+
+            for (int cb = 0; cb < nbl; cb += NBL) {
+                uint4 wq[RPW][NBL];
+                float sc[RPW][NBL];
+#pragma unroll
+                for (int ip = 0; ip < RPW; ++ip)
+#pragma unroll
+                    for (int ib = 0; ib < NBL; ++ib) {
+                        const int b = l8 + 8 * (cb + ib);
+                        if (rv[ip] && b < nb) {
+                            wq[ip][ib] = ldg_stream(Wp + row[ip] * (K >> 1) + b * 16);
+                            sc[ip][ib] = ldg_stream_f(Ws + row[ip] * nb + b);
+                        } else {
+                            wq[ip][ib] = make_uint4(0, 0, 0, 0);
+                            sc[ip][ib] = 0.f;
+                        }
+                    }
+#pragma unroll
+                for (int ip = 0; ip < RPW; ++ip)
+#pragma unroll
+                    for (int ib = 0; ib < NBL; ++ib) {
+                        const int b = l8 + 8 * (cb + ib);
+                        if (rv[ip] && b < nb) {
+                            Deq32 dq;
+                            dq.load(wq[ip][ib]);
+                            const float s16 = 16.0f * sc[ip][ib];
+#pragma unroll
+                            for (int t = 0; t < MAXT; ++t)
+                                if (t < nt) {
+                                    const float d = dq.dot(xs + (size_t)t * K + b * 32, b);
+                                    acc[ip][t] = fmaf(s16, d - xsum[t * nb + b], acc[ip][t]);
+                                }
+                        }
+                    }
+            }
+
+            // reduce the 8 lanes of each row, then write
+#pragma unroll
+            for (int ip = 0; ip < RPW; ++ip)
+#pragma unroll
+                for (int t = 0; t < MAXT; ++t) {
+                    float v = acc[ip][t];
+                    v += __shfl_xor_sync(0xffffffffu, v, 1);
+                    v += __shfl_xor_sync(0xffffffffu, v, 2);
+                    v += __shfl_xor_sync(0xffffffffu, v, 4);
+                    const int p = s0 + c0 + t;
+                    if (MODE == GEMV_ACT) {
+                        const float up = __shfl_down_sync(0xffffffffu, v, 16);
+                        if (t < nt && rv[ip]) {
+                            const int64_t orow = a.out_row ? a.out_row[p] : p;
+                            if (l8 == 0 && a.gu_out) a.gu_out[orow * a.gu_stride + row[ip]] = v;
+                            if (lane == 0 || lane == 8)
+                                a.out[orow * a.out_stride + arow[ip]] = act_fn(v, up, a.act);
+                        }
+                    } else {
+                        if (t < nt && rv[ip] && l8 == 0) {
+                            const int64_t orow = a.out_row ? a.out_row[p] : p;
+                            a.out[orow * a.out_stride + row[ip]] = v;
+                        }
+                    }
+                }
+        }
+    }
+}
+
+size_t gemv_smem_bytes(int K, int maxt) {
+    return (size_t)maxt * ((size_t)K + (size_t)(K / 32)) * sizeof(float);
+}
+
+int gemv_pick_maxt(int K, int max_tokens) {
+    int m = 8;
+    while (m > 1 && (m / 2 >= max_tokens || gemv_smem_bytes(K, m) > 100 * 1024)) m /= 2;
+    return m;
+}
+
+template <int MODE, int NBL, int RPW, int MAXT>
+static void gemv_launch_t(const GemvArgs& a, int num_sms, cudaStream_t s) {
+    const size_t smem = gemv_smem_bytes(a.K, MAXT);
+    auto kern = k_q4_gemv<MODE, NBL, RPW, MAXT>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int rows_per_tile = (MODE == GEMV_ACT) ? 16 * RPW : 32 * RPW;
+    const int64_t tile_rows = (MODE == GEMV_ACT) ? a.F : a.rows_per_expert;
+    const int64_t n_tiles = (tile_rows + rows_per_tile - 1) / rows_per_tile;
+    const int64_t items = n_tiles * (a.dense_tokens > 0 ? 1 : a.max_unique);
+    const int64_t cap = (int64_t)num_sms * 4;
+    const int grid = (int)(items < cap ? items : cap);
+    if (grid <= 0) return;
+    kern<<<grid, 256, smem, s>>>(a);
+}
+
+template <int MODE, int NBL, int RPW>
+static void gemv_dispatch_t(const GemvArgs& a, int num_sms, cudaStream_t s) {
+    const int maxt = gemv_pick_maxt(a.K, a.max_tokens);
+    switch (maxt) {
+        case 1: gemv_launch_t<MODE, NBL, RPW, 1>(a, num_sms, s); break;
+        case 2: gemv_launch_t<MODE, NBL, RPW, 2>(a, num_sms, s); break;
+        case 4: gemv_launch_t<MODE, NBL, RPW, 4>(a, num_sms, s); break;
+        default: gemv_launch_t<MODE, NBL, RPW, 8>(a, num_sms, s); break;
+    }
+}
+
+template <int MODE>
+static void gemv_dispatch_mode(const GemvArgs& a, int num_sms, cudaStream_t s) {
+    const int nb = a.K / 32, nbl = (nb + 7) / 8;
+    if (nbl == 11)
+        gemv_dispatch_t<MODE, 11, 1>(a, num_sms, s);  // K = 2816 (and 2560..2816)
+    else if (nbl <= 3)
+        gemv_dispatch_t<MODE, 3, 4>(a, num_sms, s);   // K <= 768 (704: down projection)
+    else if (nbl <= 8)
+        gemv_dispatch_t<MODE, 8, 1>(a, num_sms, s);   // K <= 2048
+    else
+        gemv_dispatch_t<MODE, 6, 1>(a, num_sms, s);   // other K, chunked
+}
+
+int launch_gemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s) {
+    if (mode == GEMV_ACT)
+        gemv_dispatch_mode<GEMV_ACT>(a, num_sms, s);
+    else
+        gemv_dispatch_mode<GEMV_PLAIN>(a, num_sms, s);
+    return 1;
+}
+
+// ------------------------------------------------------------------ router
+// One CTA per token: model_speculative_moe_batched.mojo:2102-2118 (decode)
+// and :1001-1083 (sub-batch): norms, Q4 router GEMV, softmax (:921-933),
+// top-k by insertion semantics (:936-953; equal values keep the lower index
+// first) and, when a.lod, compute_moe_lod_weights (moe_kernels.mojo:445-490).
+__global__ void __launch_bounds__(256) k_route(RouteArgs a) {
+    extern __shared__ float4 smem4[];
+    const int64_t d = a.d;
+    const int nb = (int)(d >> 5), E = a.E, K = a.K;
+    float* xs = reinterpret_cast<float*>(smem4);  // [d] natural (x, then scaled x)
+    float* xw = xs + d;                            // [d] swizzled scaled x
+    float* xsum = xw + d;                          // [nb]
+    float* pr = xsum + nb;                         // [E]
+    float* red = pr + E;                           // [33]
+    float* tval = red + 33;                        // [K]
+    int* tidx = reinterpret_cast<int*>(tval + K);  // [K]
+    const int t = blockIdx.x;
+    const float* x = a.x + (size_t)t * d;
+
+    float ss = 0.f;
+    for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
+        const float v = x[j];
+        xs[j] = v;
+        ss += v * v;
+    }
+    ss = block_sum(ss, red);
+    const float inv = 1.0f / sqrtf(ss / (float)d + 1e-6f);
+    for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
+        const float nx = xs[j] * inv;
+        if (a.moe_in) a.moe_in[(size_t)t * d + j] = nx * a.pre_w[j];
+        const float sx = nx * a.router_scale[j] * a.rsf;
+        xs[j] = sx;
+        xw[swz((int)j)] = sx;
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+        float s = 0.f;
+        for (int k = 0; k < 32; ++k) s += xs[b * 32 + k];
+        xsum[b] = 1.5f * s;
+    }
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    if (a.rp) {
+        const int g = lane >> 3, l8 = lane & 7;
+        for (int r0 = warp * 4; r0 < E; r0 += nwarp * 4) {
+            const int r = r0 + g;
+            float acc = 0.f;
+            if (r < E) {
+                for (int b = l8; b < nb; b += 8) {
+                    const uint4 q = *reinterpret_cast<const uint4*>(a.rp + (size_t)r * (d >> 1) + b * 16);
+                    Deq32 dq;
+                    dq.load(q);
+                    const float dd = dq.dot(xw + b * 32, b);
+                    acc = fmaf(16.0f * a.rs[(size_t)r * nb + b], dd - xsum[b], acc);
+                }
+            }
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+            if (r < E && l8 == 0) pr[r] = acc + (a.bias ? a.bias[r] : 0.f);
+        }
+    } else {
+        for (int r = warp; r < E; r += nwarp) {
+            float acc = 0.f;
+            for (int64_t j = lane; j < d; j += 32) acc = fmaf(a.rf32[(size_t)r * d + j], xs[j], acc);
+            acc = warp_sum(acc);
+            if (lane == 0) pr[r] = acc + (a.bias ? a.bias[r] : 0.f);
+        }
+    }
+    __syncthreads();
+
+    // softmax
+    float m = -INFINITY;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) m = fmaxf(m, pr[e]);
+    m = block_max(m, red);
+    float se = 0.f;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const float v = expf(pr[e] - m);
+        pr[e] = v;
+        se += v;
+    }
+    se = block_sum(se, red);
+    const float den = se + 1e-10f;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        pr[e] = pr[e] / den;
+        if (a.probs_out) a.probs_out[(size_t)t * E + e] = pr[e];
+    }
+    if (threadIdx.x < K) {
+        tval[threadIdx.x] = -999999.0f;
+        tidx[threadIdx.x] = -1;
+    }
+    __syncthreads();
+
+    // top-k by rank: rank(i) = #{j: p_j > p_i} + #{j < i: p_j == p_i}
+    for (int i = threadIdx.x; i < E; i += blockDim.x) {
+        const float pi = pr[i];
+        if (pi == pi) {
+            int rank = 0;
+            for (int j = 0; j < E; ++j) {
+                const float pj = pr[j];
+                rank += (pj > pi) || (pj == pi && j < i);
+            }
+            if (rank < K) {
+                tval[rank] = pi;
+                tidx[rank] = i;
+            }
+        }
+    }
+    __syncthreads();
+
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < K; ++k) {
+            if (a.top_idx) a.top_idx[(size_t)t * K + k] = tidx[k];
+            if (a.top_val) a.top_val[(size_t)t * K + k] = tval[k];
+            a.ti32[(size_t)t * K + k] = tidx[k];
+            a.tv[(size_t)t * K + k] = tval[k];
+        }
+        if (a.lod) {
+            float sum = 0.f;
+            for (int k = 0; k < K; ++k) sum += tval[k];
+            const float inv_sum = 1.0f / (sum + 1e-10f);
+            const float tp = (a.top_p == a.top_p) ? a.top_p : 1.0f;
+            int cnt = 0;
+            int oi[32];
+            float ow[32];
+            if (tp >= 1.0f) {
+                for (int k = 0; k < K; ++k) {
+                    const float np_ = tval[k] * inv_sum;
+                    if ((np_ >= 0.05f || k == 0) && tidx[k] >= 0) {
+                        const int e = tidx[k];
+                        oi[cnt] = e;
+                        ow[cnt] = np_ * a.pes[e];
+                        ++cnt;
+                    }
+                }
+            } else {
+                float cum = 0.f;
+                for (int k = 0; k < K; ++k) {
+                    const float np_ = tval[k] * inv_sum;
+                    if (k > 0 && (np_ < 0.05f || cum >= tp)) break;
+                    if (tidx[k] < 0) break;
+                    oi[cnt] = tidx[k];
+                    ow[cnt] = np_;
+                    cum += np_;
+                    ++cnt;
+                }
+                const float rn = 1.0f / (cum + 1e-10f);
+                for (int k = 0; k < cnt; ++k) ow[k] = (ow[k] * rn) * a.pes[oi[k]];
+            }
+            for (int k = 0; k < K; ++k) {
+                const bool on = k < cnt;
+                a.slot_expert[(size_t)t * K + k] = on ? oi[k] : -1;
+                a.slot_weight[(size_t)t * K + k] = on ? ow[k] : 0.f;
+                if (a.tok_idx) a.tok_idx[(size_t)t * K + k] = on ? oi[k] : 0;
+                if (a.tok_w) a.tok_w[(size_t)t * K + k] = on ? ow[k] : 0.f;
+            }
+            if (a.tok_count) a.tok_count[t] = cnt;
+        }
+    }
+}
+
+int launch_route(const RouteArgs& a, int64_t M, cudaStream_t s) {
+    if (M <= 0) return 0;
+    const size_t smem = (size_t)(2 * a.d + a.d / 32 + a.E + 33 + 2 * a.K) * sizeof(float);
+    cudaFuncSetAttribute(k_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_route<<<(unsigned)M, 256, smem, s>>>(a);
+    return 1;
+}
+
+// ---------------------------------------------------------------- set cover
+// compute_subbatch_set_cover_moe_weights (moe_kernels.mojo:493-611), one
+// thread per sub-batch of `sub_batch` tokens (5 in the engine).
+__global__ void k_set_cover(const int* ti, const float* tv, int64_t M, int K, int E,
+                            const float* pes, float top_p, float core_top_p, float smp,
+                            int sub_batch, int* slot_expert, float* slot_weight,
+                            int64_t* tok_count, int64_t* tok_idx, float* tok_w) {
+    const int64_t t0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * sub_batch;
+    if (t0 >= M) return;
+    const int sb = (int)min((int64_t)sub_batch, M - t0);
+    const float safe = (top_p == top_p) ? top_p : 1.0f;
+    int cnt_out[64];
+    int oi[64][32];
+    float ow[64][32];
+    // anchor token: compute_moe_lod_weights
+    {
+        const int* i0 = ti + t0 * K;
+        const float* v0 = tv + t0 * K;
+        float sum = 0.f;
+        for (int k = 0; k < K; ++k) sum += v0[k];
+        const float inv = 1.0f / (sum + 1e-10f);
+        int c = 0;
+        if (safe >= 1.0f) {
+            for (int k = 0; k < K; ++k) {
+                const float np_ = v0[k] * inv;
+                if ((np_ >= 0.05f || k == 0) && i0[k] >= 0 && i0[k] < E) {
+                    oi[0][c] = i0[k];
+                    ow[0][c] = np_ * pes[i0[k]];
+                    ++c;
+                }
+            }
+        } else {
+            float cum = 0.f;
+            for (int k = 0; k < K; ++k) {
+                const float np_ = v0[k] * inv;
+                if (k > 0 && (np_ < 0.05f || cum >= safe)) break;
+                if (i0[k] < 0 || i0[k] >= E) break;
+                oi[0][c] = i0[k];
+                ow[0][c] = np_;
+                cum += np_;
+                ++c;
+            }
+            const float rn = 1.0f / (cum + 1e-10f);
+            for (int k = 0; k < c; ++k) ow[0][k] = (ow[0][k] * rn) * pes[oi[0][k]];
+        }
+        cnt_out[0] = c;
+    }
+    uint8_t in_pool[256], freq[256];
+    for (int i = 0; i < 256; ++i) in_pool[i] = freq[i] = 0;
+    for (int k = 0; k < cnt_out[0]; ++k) {
+        const int e0 = oi[0][k];
+        if (e0 >= 0 && e0 < 256) {
+            in_pool[e0] = 1;
+            freq[e0] = 1;
+        }
+    }
+    float inv_s[64], elig[64];
+    for (int b = 1; b < sb; ++b) {
+        const int* ib = ti + (t0 + b) * K;
+        const float* vb = tv + (t0 + b) * K;
+        float s = 0.f;
+        for (int k = 0; k < K; ++k) s += vb[k];
+        const float is = 1.0f / (s + 1e-10f);
+        inv_s[b] = is;
+        float cum = 0.f;
+        for (int k = 0; k < K; ++k) {
+            const float np_ = vb[k] * is;
+            if (safe >= 1.0f) {
+                if (np_ < 0.05f && k > 0) continue;
+            } else if (k > 0 && (np_ < 0.05f || cum >= safe)) {
+                break;
+            }
+            const int e = ib[k];
+            if (e >= 0 && e < 256) {
+                freq[e] = (uint8_t)(freq[e] + 1);
+                if (k < 2 || np_ >= smp || cum < core_top_p) in_pool[e] = 1;
+            }
+            cum += np_;
+        }
+        elig[b] = cum;
+    }
+    for (int b = 1; b < sb; ++b) {
+        const int* ib = ti + (t0 + b) * K;
+        const float* vb = tv + (t0 + b) * K;
+        float cum = 0.f, kept = 0.f;
+        int c = 0;
+        bool pruned = false;
+        for (int k = 0; k < K; ++k) {
+            const float np_ = vb[k] * inv_s[b];
+            if (safe >= 1.0f) {
+                if (np_ < 0.05f && k > 0) continue;
+            } else if (k > 0 && (np_ < 0.05f || cum >= safe)) {
+                break;
+            }
+            const int e = ib[k];
+            const bool core = (k < 2) || (np_ >= smp) || (cum < core_top_p);
+            const bool shared = (e >= 0 && e < 256) && (in_pool[e] != 0 || freq[e] >= 2);
+            cum += np_;
+            if ((core || shared) && e >= 0 && e < E) {
+                oi[b][c] = e;
+                ow[b][c] = np_;
+                kept += np_;
+                ++c;
+            } else {
+                pruned = true;
+            }
+        }
+        const float target = (safe < 1.0f) ? 1.0f : elig[b];
+        const float rn = (pruned || safe < 1.0f) ? (target / (kept + 1e-10f)) : 1.0f;
+        for (int k = 0; k < c; ++k) ow[b][k] = (ow[b][k] * rn) * pes[oi[b][k]];
+        cnt_out[b] = c;
+    }
+    for (int b = 0; b < sb; ++b) {
+        const int64_t t = t0 + b;
+        for (int k = 0; k < K; ++k) {
+            const bool on = k < cnt_out[b];
+            if (slot_expert) slot_expert[t * K + k] = on ? oi[b][k] : -1;
+            if (slot_weight) slot_weight[t * K + k] = on ? ow[b][k] : 0.f;
+            if (tok_idx) tok_idx[t * K + k] = on ? oi[b][k] : 0;
+            if (tok_w) tok_w[t * K + k] = on ? ow[b][k] : 0.f;
+        }
+        if (tok_count) tok_count[t] = cnt_out[b];
+    }
+}
+
+int launch_set_cover(const int* ti32, const float* tv, int64_t M, int K, int E, const float* pes,
+                     float top_p, float core_top_p, float smp, int sub_batch, int* slot_expert,
+                     float* slot_weight, int64_t* tok_count, int64_t* tok_idx, float* tok_w,
+                     cudaStream_t s) {
+    if (M <= 0) return 0;
+    const int64_t groups = (M + sub_batch - 1) / sub_batch;
+    const int threads = 32;
+    const int blocks = (int)((groups + threads - 1) / threads);
+    k_set_cover<<<blocks, threads, 0, s>>>(ti32, tv, M, K, E, pes, top_p, core_top_p, smp,
+                                           sub_batch, slot_expert, slot_weight, tok_count,
+                                           tok_idx, tok_w);
+    return 1;
+}
+
+// -------------------------------------------------------- slot conversions
+// Compact per-token lists (count + int64 ids, as compute_moe_lod_weights
+// returns them) -> internal [M][K] slot table.  Out-of-range ids raise
+// err_flag and are dropped.
+__global__ void k_slots_from_lists(int64_t M, int K, const int64_t* count, int64_t count_scalar,
+                                   const int64_t* idx, const float* w, int* slot_expert,
+                                   float* slot_weight, int E, int* err_flag) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= M * K) return;
+    const int64_t t = i / K;
+    const int k = (int)(i - t * K);
+    const int64_t c = count ? count[t] : count_scalar;
+    int e = -1;
+    float wt = 0.f;
+    if (k < c) {
+        const int64_t v = idx[i];
+        if (v >= 0 && v < E) {
+            e = (int)v;
+            wt = w ? w[i] : 0.f;
+        } else {
+            atomicExch(err_flag, 1);
+        }
+    }
+    slot_expert[i] = e;
+    slot_weight[i] = wt;
+}
+
+int launch_slots_from_lists(int64_t M, int K, const int64_t* count, int64_t count_scalar,
+                            const int64_t* idx, const float* w, int* slot_expert,
+                            float* slot_weight, int E, int* err_flag, cudaStream_t s) {
+    const int64_t n = M * K;
+    if (n <= 0) return 0;
+    k_slots_from_lists<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        M, K, count, count_scalar, idx, w, slot_expert, slot_weight, E, err_flag);
+    return 1;
+}
+
+// Diffusion convention (diffusion_kernels.mojo:263-266): slot active iff w > 0.
+__global__ void k_slots_from_topw(int64_t n, const int64_t* idx, const float* w, int* slot_expert,
+                                  float* slot_weight, int E, int* err_flag) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int e = -1;
+    float wt = 0.f;
+    if (w[i] > 0.0f) {
+        const int64_t v = idx[i];
+        if (v >= 0 && v < E) {
+            e = (int)v;
+            wt = w[i];
+        } else {
+            atomicExch(err_flag, 1);
+        }
+    }
+    slot_expert[i] = e;
+    slot_weight[i] = wt;
+}
+
+int launch_slots_from_topw(int64_t M, int K, const int64_t* idx, const float* w, int* slot_expert,
+                           float* slot_weight, int E, int* err_flag, cudaStream_t s) {
+    const int64_t n = M * K;
+    if (n <= 0) return 0;
+    k_slots_from_topw<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(n, idx, w, slot_expert,
+                                                                  slot_weight, E, err_flag);
+    return 1;
+}
+
+// ------------------------------------------------------------------ bucket
+// Groups the (token, slot) pairs by expert, ascending expert id, like the
+// Hoare bucket sort of moe_kernels.mojo:815-835.  Order inside a bucket is
+// not fixed (atomics): every pair's result is computed independently, so
+// outputs do not depend on it.  One CTA of 1024 threads; E <= 1024.
+__device__ __forceinline__ int block_excl_scan(int v, int* wsum, int* total) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+        int w = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < nw) wsum[lane] = w;
+    }
+    __syncthreads();
+    const int base = wid > 0 ? wsum[wid - 1] : 0;
+    const int tot = wsum[nw - 1];
+    __syncthreads();
+    *total = tot;
+    return base + x - v;
+}
+
+__global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t P, int K, int E,
+                                                 BucketOut o) {
+    __shared__ int cnt[1024];
+    __shared__ int cur[1024];
+    __shared__ int wsum[32];
+    const int tid = threadIdx.x;
+    cnt[tid] = 0;
+    __syncthreads();
+    for (int64_t p = tid; p < P; p += blockDim.x) {
+        const int e = slot_expert[p];
+        if (e >= 0) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    const int c = tid < E ? cnt[tid] : 0;
+    int total_pairs = 0, total_u = 0;
+    const int off = block_excl_scan(c, wsum, &total_pairs);
+    const int ui = block_excl_scan(c > 0 ? 1 : 0, wsum, &total_u);
+    if (c > 0) {
+        o.unique_expert[ui] = tid;
+        o.seg_start[ui] = off;
+        o.seg_count[ui] = c;
+    }
+    cur[tid] = off;
+    if (tid == 0) {
+        o.meta[0] = total_u;
+        o.meta[1] = total_pairs;
+    }
+    __syncthreads();
+    for (int64_t p = tid; p < P; p += blockDim.x) {
+        const int e = slot_expert[p];
+        if (e >= 0) {
+            const int pos = atomicAdd(&cur[e], 1);
+            o.pair_token[pos] = (int)(p / K);
+            o.pair_slot[pos] = (int)p;
+            o.slot_pair[p] = pos;
+        } else {
+            o.slot_pair[p] = -1;
+        }
+    }
+}
+
+int launch_bucket(const int* slot_expert, int64_t P, int K, int E, const BucketOut& o,
+                  cudaStream_t s) {
+    k_bucket<<<1, 1024, 0, s>>>(slot_expert, P, K, E, o);
+    return 1;
+}
+
+// ----------------------------------------------------------------- combine
+// moe_out[t][r] = sum over slots k (in slot order) of w_k * y[pair(t,k)][r]
+// (moe_kernels.mojo:775-779, diffusion_kernels.mojo:386-399), then optionally
+// rms_norm with post_feedforward_layernorm_2 (model_speculative_moe_batched
+// .mojo:1144-1150) and fp16 rounding.
+__global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
+    extern __shared__ float4 smem4[];
+    float* row = reinterpret_cast<float*>(smem4);
+    __shared__ float red[33];
+    __shared__ int sp[32];
+    __shared__ float sw[32];
+    const int t = blockIdx.x;
+    const int K = a.K;
+    if (threadIdx.x < K) {
+        sp[threadIdx.x] = a.slot_pair[(size_t)t * K + threadIdx.x];
+        sw[threadIdx.x] = a.slot_weight[(size_t)t * K + threadIdx.x];
+    }
+    __syncthreads();
+    float ss = 0.f;
+    for (int64_t j = threadIdx.x; j < a.d; j += blockDim.x) {
+        float s = 0.f;
+        for (int k = 0; k < K; ++k) {
+            const int p = sp[k];
+            if (p >= 0) {
+                const float y = a.y[(size_t)p * a.d + j];
+                s = a.fma_mode ? fmaf(y, sw[k], s) : __fadd_rn(s, __fmul_rn(y, sw[k]));
+            }
+        }
+        row[j] = s;
+        ss += s * s;
+    }
+    float inv = 1.f;
+    if (a.post_norm) {
+        ss = block_sum(ss, red);
+        inv = 1.0f / sqrtf(ss / (float)a.d + 1e-6f);
+    }
+    for (int64_t j = threadIdx.x; j < a.d; j += blockDim.x) {
+        float v = row[j];
+        if (a.post_norm) v = v * inv * a.post_w[j];
+        if (a.out_f16)
+            reinterpret_cast<__half*>(a.out)[(size_t)t * a.d + j] = __float2half_rn(v);
+        else
+            reinterpret_cast<float*>(a.out)[(size_t)t * a.d + j] = v;
+    }
+}
+
+int launch_combine(const CombineArgs& a, int64_t M, cudaStream_t s) {
+    if (M <= 0) return 0;
+    const size_t smem = (size_t)a.d * sizeof(float);
+    cudaFuncSetAttribute(k_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_combine<<<(unsigned)M, 256, smem, s>>>(a);
+    return 1;
+}
+
+// ---------------------------------------------------------------- quantize
+// quantize_fp32_to_q4_0 (moe_kernels.mojo:7-56): one thread per 32-block;
+// IEEE division (no fast-math) so scale and 1/scale match the reference bit
+// for bit; rint rounds exact ties to even like numpy.
+__global__ void k_quantize(const float* src, uint8_t* packed, float* scales, int64_t nblocks) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    const float4* s4 = reinterpret_cast<const float4*>(src + b * 32);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 q = s4[i];
+        v[4 * i] = q.x;
+        v[4 * i + 1] = q.y;
+        v[4 * i + 2] = q.z;
+        v[4 * i + 3] = q.w;
+    }
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
+    float scale = __fdiv_rn(mx, 7.0f);
+    if (scale < 1e-5f) scale = 1e-5f;
+    scales[b] = scale;
+    const float inv = __fdiv_rn(1.0f, scale);
+    uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        float q0 = rintf(__fmul_rn(v[2 * j], inv));
+        float q1 = rintf(__fmul_rn(v[2 * j + 1], inv));
+        q0 = fminf(fmaxf(q0, -8.0f), 7.0f);
+        q1 = fminf(fmaxf(q1, -8.0f), 7.0f);
+        const uint32_t byte = (uint32_t)((int)q0 + 8) | ((uint32_t)((int)q1 + 8) << 4);
+        w[j >> 2] |= byte << (8 * (j & 3));
+    }
+    *reinterpret_cast<uint4*>(packed + b * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+int launch_quantize(const float* src, uint8_t* packed, float* scales, int64_t nblocks,
+                    cudaStream_t s) {
+    if (nblocks <= 0) return 0;
+    k_quantize<<<(unsigned)((nblocks + 255) / 256), 256, 0, s>>>(src, packed, scales, nblocks);
+    return 1;
+}
+
+// ---------------------------------------------------------------- LOD APIs
+__global__ void k_lod(int64_t B, const int64_t* top_idx, const float* top_val, const float* pes,
+                      float top_p, int64_t* act_idx, float* act_w, int64_t* act_count, int K,
+                      int64_t E, int* err_flag) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= B) return;
+    const int64_t* ti = top_idx + t * K;
+    const float* tv = top_val + t * K;
+    int64_t* ai = act_idx + t * K;
+    float* aw = act_w + t * K;
+    float sum = 0.f;
+    for (int k = 0; k < K; ++k) sum += tv[k];
+    const float inv = 1.0f / (sum + 1e-10f);
+    const float safe = (top_p == top_p) ? top_p : 1.0f;
+    int64_t c = 0;
+    if (safe >= 1.0f) {
+        for (int k = 0; k < K; ++k) {
+            const float np_ = tv[k] * inv;
+            if (np_ >= 0.05f || k == 0) {
+                if (ti[k] < 0 || ti[k] >= E) {
+                    atomicExch(err_flag, 1);
+                    continue;
+                }
+                ai[c] = ti[k];
+                aw[c] = np_ * pes[ti[k]];
+                ++c;
+            }
+        }
+    } else {
+        float cum = 0.f;
+        for (int k = 0; k < K; ++k) {
+            const float np_ = tv[k] * inv;
+            if (k > 0 && (np_ < 0.05f || cum >= safe)) break;
+            if (ti[k] < 0 || ti[k] >= E) {
+                atomicExch(err_flag, 1);
+                break;
+            }
+            ai[c] = ti[k];
+            aw[c] = np_;
+            cum += np_;
+            ++c;
+        }
+        const float rn = 1.0f / (cum + 1e-10f);
+        for (int64_t k = 0; k < c; ++k) aw[k] = (aw[k] * rn) * pes[ai[k]];
+    }
+    act_count[t] = c;
+}
+
+int launch_lod(int64_t B, const int64_t* top_idx, const float* top_val, const float* pes,
+               float top_p, int64_t* act_idx, float* act_w, int64_t* act_count, int K,
+               int64_t E, int* err_flag, cudaStream_t s) {
+    if (B <= 0) return 0;
+    k_lod<<<(unsigned)((B + 127) / 128), 128, 0, s>>>(B, top_idx, top_val, pes, top_p, act_idx,
+                                                       act_w, act_count, K, E, err_flag);
+    return 1;
+}
+
+// apply_moe_lod_and_set_cover (diffusion_kernels.mojo:3607-3664)
+__global__ void k_apply_lod(const int64_t* top_idx, const float* top_val, const float* pes,
+                            float* top_w, int64_t B, int K, int64_t eff_k, int64_t unacc_k,
+                            const uint8_t* eb_mask, const int64_t* active_canvas_idx) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const int64_t orig = active_canvas_idx ? active_canvas_idx[b] : b;
+    const bool accepted = eb_mask ? (eb_mask[orig] != 0) : true;
+    const int64_t tok_k = accepted ? eff_k : unacc_k;
+    const int64_t* ti = top_idx + b * K;
+    const float* tv = top_val + b * K;
+    float* tw = top_w + b * K;
+    float sd = 0.f;
+    for (int64_t s = 0; s < tok_k; ++s)
+        if (ti[s] >= 0) sd += tv[s];
+    const float inv = 1.0f / (sd + 1e-10f);
+    for (int s = 0; s < K; ++s) {
+        const int64_t e = ti[s];
+        const float np_ = tv[s] * inv;
+        tw[s] = (s < tok_k && e >= 0 && e < 128 && np_ >= 0.05f) ? np_ * pes[e] : 0.0f;
+    }
+}
+
+int launch_apply_lod(const int64_t* top_idx, const float* top_val, const float* pes, float* top_w,
+                     int64_t B, int K, int64_t active_top_k, const uint8_t* eb_mask,
+                     const int64_t* active_canvas_idx, int64_t unaccepted_top_k, cudaStream_t s) {
+    if (B <= 0) return 0;
+    int64_t eff_k = active_top_k <= K ? active_top_k : K;
+    if (eff_k < 1) eff_k = 1;
+    int64_t unacc = unaccepted_top_k <= eff_k ? unaccepted_top_k : eff_k;
+    if (unacc < 1) unacc = 1;
+    k_apply_lod<<<(unsigned)((B + 127) / 128), 128, 0, s>>>(top_idx, top_val, pes, top_w, B, K,
+                                                             eff_k, unacc, eb_mask,
+                                                             active_canvas_idx);
+    return 1;
+}
+
+}  // namespace moe

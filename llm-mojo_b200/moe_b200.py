@@ -1,0 +1,330 @@
+"""Python host mirror of the reference's Mojo entry points over libmoe_b200.so.
+
+Function names, argument order and meaning follow phildrip/llm-mojo's
+``moe_kernels.mojo`` / ``diffusion_kernels.mojo`` / the layer glue in
+``model_speculative_moe_batched.mojo`` (file:line in each docstring); the
+``num_tasks`` thread-count arguments of the CPU originals are accepted and
+ignored.  Arrays may be numpy (host; staged by the library) or torch CUDA
+tensors (used in place).  Every call goes through the C ABI of
+include/moe_b200.h; there is no CPU fallback: without a CUDA device
+``Context()`` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmoe_b200.so")
+
+ACT_SIGMOID1702, ACT_GELU_TANH = 0, 1
+X_NATURAL, X_DEINT_HALVES, X_DEINT_BLOCK32 = 0, 1, 2
+F_POST_NORM, F_SET_COVER, F_FP16_OUT = 1, 4, 8
+
+STATUS = {0: "MOE_OK", 1: "MOE_E_ARG", 2: "MOE_E_SHAPE", 3: "MOE_E_UNREGISTERED",
+          4: "MOE_E_CUDA", 5: "MOE_E_NCCL", 6: "MOE_E_TIMEOUT", 7: "MOE_E_NOMEM",
+          8: "MOE_E_STATE"}
+
+# every symbol declared in include/moe_b200.h
+EXPORTS = [
+    "moe_ctx_create", "moe_ctx_destroy", "moe_last_error", "moe_kernel_launches",
+    "moe_set_stream", "moe_set_async", "moe_wait", "moe_profile_enable", "moe_profile_read",
+    "moe_register_weights",
+    "moe_unregister_weights", "moe_quantize_fp32_to_q4_0", "moe_q4_matmul_vec",
+    "moe_q4_matmul_batchN", "moe_compute_moe_lod_weights", "moe_apply_moe_lod_and_set_cover",
+    "moe_compute_subbatch_set_cover_moe_weights", "moe_run_moe_experts_stage1",
+    "moe_run_moe_experts_stage2", "moe_run_moe_coalesced_core",
+    "moe_run_diffusion_moe_experts_parallel", "moe_route", "moe_layer_forward",
+]
+
+
+class MoeError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS.get(code, code)}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH):
+    """Loads the shared library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(path):
+            raise OSError(f"{path} not built: run python llm-mojo_b200/build.py")
+        _lib = C.CDLL(path)
+        _declare(_lib)
+    return _lib
+
+
+_p, _i64, _int, _f, _u64 = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_uint64
+
+
+class LayerDesc(C.Structure):
+    """moe_layer_desc of include/moe_b200.h."""
+    _fields_ = [
+        ("embed_dim", _i64), ("expert_mlp_dim", _i64), ("num_experts", _i64), ("top_k", _i64),
+        ("activation", C.c_int32), ("r_scale_factor", _f), ("moe_top_p", _f),
+        ("router_packed", _p), ("router_scales", _p), ("router_f32", _p),
+        ("router_logit_bias", _p), ("router_scale", _p), ("per_expert_scale", _p),
+        ("pre_norm_w", _p), ("post_norm_w", _p), ("gate_up_packed", _p),
+        ("gate_up_scales", _p), ("down_packed", _p), ("down_scales", _p),
+    ]
+
+
+def _declare(L):
+    L.moe_ctx_create.argtypes = [_int, C.POINTER(_p)]
+    L.moe_ctx_destroy.argtypes = [_p]
+    L.moe_last_error.argtypes = [_p]
+    L.moe_last_error.restype = C.c_char_p
+    L.moe_kernel_launches.argtypes = [_p]
+    L.moe_kernel_launches.restype = _u64
+    L.moe_set_stream.argtypes = [_p, _p]
+    L.moe_set_async.argtypes = [_p, _int]
+    L.moe_wait.argtypes = [_p, _u64]
+    L.moe_profile_enable.argtypes = [_p, _int]
+    L.moe_profile_read.argtypes = [_p, _int, _p, _p, _p, C.POINTER(_int)]
+    L.moe_register_weights.argtypes = [_p, _p, C.c_size_t]
+    L.moe_unregister_weights.argtypes = [_p, _p]
+    L.moe_quantize_fp32_to_q4_0.argtypes = [_p, _p, _p, _p, _i64]
+    L.moe_q4_matmul_vec.argtypes = [_p, _p, _p, _p, _p, _i64, _i64]
+    L.moe_q4_matmul_batchN.argtypes = [_p, _i64, _p, _p, _p, _p, _i64, _i64]
+    L.moe_compute_moe_lod_weights.argtypes = [_p, _i64, _p, _p, _p, _f, _p, _p, _p, _i64]
+    L.moe_apply_moe_lod_and_set_cover.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64, _f, _p,
+                                                  _p, _i64]
+    L.moe_compute_subbatch_set_cover_moe_weights.argtypes = [_p, _i64, _p, _p, _p, _f, _p, _p,
+                                                             _p, _i64, _i64, _f, _f]
+    L.moe_run_moe_experts_stage1.argtypes = [_p, _p, _p, _p, _p, _i64, _p, _p, _i64, _i64, _int]
+    L.moe_run_moe_experts_stage2.argtypes = [_p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64]
+    L.moe_run_moe_coalesced_core.argtypes = [_p, _i64, _p, _p, _p, _p, _p, _int, _p, _p, _p, _p,
+                                             _i64, _i64, _i64, _i64, _int]
+    L.moe_run_diffusion_moe_experts_parallel.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
+                                                         _i64, _i64, _i64, _int]
+    L.moe_route.argtypes = [_p, C.POINTER(LayerDesc), _i64, _p, _int, _p, _p, _p, _p, _p, _p, _p]
+    L.moe_layer_forward.argtypes = [_p, C.POINTER(LayerDesc), _i64, _p, _p, _int, _p, _p, _p]
+    for name in EXPORTS:
+        if name not in ("moe_last_error", "moe_kernel_launches"):
+            getattr(L, name).restype = _int
+
+
+def _addr(a):
+    """Address of a numpy array or torch tensor (None -> NULL)."""
+    if a is None:
+        return None
+    if isinstance(a, np.ndarray):
+        assert a.flags["C_CONTIGUOUS"], "arrays must be C-contiguous"
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):
+        assert a.is_contiguous(), "tensors must be contiguous"
+        return a.data_ptr()
+    if isinstance(a, int):
+        return a
+    raise TypeError(f"unsupported buffer type {type(a)}")
+
+
+class Context:
+    """One device context (moe_ctx_create); use one per host thread."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load_library()
+        h = _p()
+        rc = self.lib.moe_ctx_create(device, C.byref(h))
+        if rc != 0:
+            raise MoeError(rc, f"moe_ctx_create(device={device}) failed (no CUDA device?)")
+        self.h = h
+        self.device = device
+        self._keep = []
+
+    def close(self):
+        if self.h:
+            self.lib.moe_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, rc: int):
+        if rc != 0:
+            raise MoeError(rc, self.lib.moe_last_error(self.h).decode())
+
+    @property
+    def kernel_launches(self) -> int:
+        return int(self.lib.moe_kernel_launches(self.h))
+
+    def set_stream(self, stream_ptr: int | None):
+        self.check(self.lib.moe_set_stream(self.h, stream_ptr))
+
+    def set_async(self, on: bool):
+        self.check(self.lib.moe_set_async(self.h, int(on)))
+
+    def wait(self, timeout_ns: int = 0):
+        self.check(self.lib.moe_wait(self.h, timeout_ns))
+
+    def profile_enable(self, on: bool = True):
+        self.check(self.lib.moe_profile_enable(self.h, int(on)))
+
+    def profile_read(self) -> dict:
+        """{kernel name: (total device ms, launches)} since profile_enable."""
+        n_max = 64
+        names = C.create_string_buffer(32 * n_max)
+        ms = (C.c_double * n_max)()
+        cnt = (C.c_uint64 * n_max)()
+        n = _int(0)
+        self.check(self.lib.moe_profile_read(self.h, n_max, names, ms, cnt, C.byref(n)))
+        out = {}
+        for i in range(min(n.value, n_max)):
+            nm = names.raw[32 * i:32 * i + 32].split(b"\0", 1)[0].decode()
+            out[nm] = (ms[i], int(cnt[i]))
+        return out
+
+    def register_weights(self, arr: np.ndarray):
+        self.check(self.lib.moe_register_weights(self.h, _addr(arr), arr.nbytes))
+        self._keep.append(arr)
+
+    def unregister_weights(self, arr: np.ndarray):
+        self.check(self.lib.moe_unregister_weights(self.h, _addr(arr)))
+
+    # ------------------------------------------------- moe_kernels.mojo API
+    def quantize_fp32_to_q4_0(self, src, dst_packed, dst_scales, num_elements, num_tasks=None):
+        """moe_kernels.mojo:7-56."""
+        self.check(self.lib.moe_quantize_fp32_to_q4_0(self.h, _addr(src), _addr(dst_packed),
+                                                      _addr(dst_scales), num_elements))
+
+    def q4_matmul_vec(self, W_packed, scales, x, out_ptr, c_in, c_out, num_tasks=None):
+        """moe_kernels.mojo:59-67."""
+        self.check(self.lib.moe_q4_matmul_vec(self.h, _addr(W_packed), _addr(scales), _addr(x),
+                                              _addr(out_ptr), c_in, c_out))
+
+    def q4_matmul_batchN(self, batch_size, W_packed, scales, x_batch, out_batch, c_in, c_out,
+                         num_tasks=None):
+        """moe_kernels.mojo:254-264 (and q4_matmul_batch5 :165)."""
+        self.check(self.lib.moe_q4_matmul_batchN(self.h, batch_size, _addr(W_packed),
+                                                 _addr(scales), _addr(x_batch), _addr(out_batch),
+                                                 c_in, c_out))
+
+    def compute_moe_lod_weights(self, top_idx, top_val, per_expert_scale, moe_top_p,
+                                active_idx, active_weights, top_k=8, batch=1, active_count=None):
+        """moe_kernels.mojo:445-490; returns the count (batch == 1) or fills active_count."""
+        cnt = np.zeros(batch, np.int64) if active_count is None else active_count
+        self.check(self.lib.moe_compute_moe_lod_weights(self.h, batch, _addr(top_idx),
+                                                        _addr(top_val), _addr(per_expert_scale),
+                                                        moe_top_p, _addr(active_idx),
+                                                        _addr(active_weights), _addr(cnt), top_k))
+        if active_count is None and batch == 1:
+            return int(cnt[0])
+        return cnt
+
+    def compute_subbatch_set_cover_moe_weights(self, sub_b, all_top_idx, all_top_val,
+                                               per_expert_scale, moe_top_p, tok_active_count,
+                                               tok_active_idx, tok_active_weights,
+                                               num_experts=128, top_k=8, core_top_p=0.85,
+                                               singleton_min_prob=0.068):
+        """moe_kernels.mojo:493-611."""
+        self.check(self.lib.moe_compute_subbatch_set_cover_moe_weights(
+            self.h, sub_b, _addr(all_top_idx), _addr(all_top_val), _addr(per_expert_scale),
+            moe_top_p, _addr(tok_active_count), _addr(tok_active_idx),
+            _addr(tok_active_weights), num_experts, top_k, core_top_p, singleton_min_prob))
+
+    def run_moe_experts_stage1_8core(self, experts_gate_up_packed, experts_gate_up_scales, moe_in,
+                                     moe_in_deint, active_idx, active_count, gate_up_out_all,
+                                     act_all, embed_dim=2816, expert_mlp_dim=704, num_tasks=8,
+                                     activation=ACT_SIGMOID1702):
+        """moe_kernels.mojo:614-627 (moe_in_deint scratch unused)."""
+        self.check(self.lib.moe_run_moe_experts_stage1(
+            self.h, _addr(experts_gate_up_packed), _addr(experts_gate_up_scales), _addr(moe_in),
+            _addr(active_idx), active_count, _addr(gate_up_out_all), _addr(act_all), embed_dim,
+            expert_mlp_dim, activation))
+
+    def run_moe_experts_stage2_8core(self, experts_down_packed, experts_down_scales, act_all,
+                                     act_deint, active_idx, active_weights, active_count, moe_out,
+                                     embed_dim=2816, expert_mlp_dim=704, num_tasks=8):
+        """moe_kernels.mojo:699-712 (act_deint scratch unused)."""
+        self.check(self.lib.moe_run_moe_experts_stage2(
+            self.h, _addr(experts_down_packed), _addr(experts_down_scales), _addr(act_all),
+            _addr(active_idx), _addr(active_weights), active_count, _addr(moe_out), embed_dim,
+            expert_mlp_dim))
+
+    def run_moe_coalesced_core(self, sub_b, experts_gate_up_packed, experts_gate_up_scales,
+                               experts_down_packed, experts_down_scales, batch_in_deint,
+                               tok_active_count, tok_active_idx, tok_active_weights,
+                               batch_moe_out, embed_dim=2816, expert_mlp_dim=704, num_experts=128,
+                               num_tasks=8, x_layout=X_DEINT_HALVES, top_k=8,
+                               activation=ACT_SIGMOID1702):
+        """moe_kernels.mojo:1321-1345 (bucket/scratch arguments are internal here)."""
+        self.check(self.lib.moe_run_moe_coalesced_core(
+            self.h, sub_b, _addr(experts_gate_up_packed), _addr(experts_gate_up_scales),
+            _addr(experts_down_packed), _addr(experts_down_scales), _addr(batch_in_deint),
+            x_layout, _addr(tok_active_count), _addr(tok_active_idx), _addr(tok_active_weights),
+            _addr(batch_moe_out), embed_dim, expert_mlp_dim, num_experts, top_k, activation))
+
+    # ------------------------------------------- diffusion_kernels.mojo API
+    def run_diffusion_moe_experts_parallel(self, experts_gate_up_packed, experts_gate_up_scales,
+                                           experts_down_packed, experts_down_scales,
+                                           canvas_moe_in, canvas_top_idx, canvas_top_weights,
+                                           canvas_moe_out, B, embed_dim, expert_mlp_dim,
+                                           top_k_experts, num_tasks=8,
+                                           activation=ACT_SIGMOID1702):
+        """diffusion_kernels.mojo:236-253 (fp16 canvas in/out)."""
+        self.check(self.lib.moe_run_diffusion_moe_experts_parallel(
+            self.h, _addr(experts_gate_up_packed), _addr(experts_gate_up_scales),
+            _addr(experts_down_packed), _addr(experts_down_scales), _addr(canvas_moe_in),
+            _addr(canvas_top_idx), _addr(canvas_top_weights), _addr(canvas_moe_out), B,
+            embed_dim, expert_mlp_dim, top_k_experts, activation))
+
+    def apply_moe_lod_and_set_cover(self, canvas_top_idx, canvas_top_val, router_per_expert_scale,
+                                    canvas_top_weights, B, top_k_experts, active_top_k,
+                                    moe_top_p, eb_mask=None, active_canvas_idx=None,
+                                    unaccepted_top_k=8):
+        """diffusion_kernels.mojo:3607-3664."""
+        self.check(self.lib.moe_apply_moe_lod_and_set_cover(
+            self.h, _addr(canvas_top_idx), _addr(canvas_top_val), _addr(router_per_expert_scale),
+            _addr(canvas_top_weights), B, top_k_experts, active_top_k, moe_top_p,
+            _addr(eb_mask), _addr(active_canvas_idx), unaccepted_top_k))
+
+    # ------------------------------------------------------- layer glue
+    def route(self, desc: LayerDesc, M, x, tok_active_count, tok_active_idx, tok_active_weights,
+              flags=0, scores=None, top_idx=None, top_val=None, moe_in=None):
+        """Router half of model_speculative_moe_batched.mojo:957-1083 / :2102-2118."""
+        self.check(self.lib.moe_route(self.h, C.byref(desc), M, _addr(x), flags, _addr(scores),
+                                      _addr(top_idx), _addr(top_val), _addr(tok_active_count),
+                                      _addr(tok_active_idx), _addr(tok_active_weights),
+                                      _addr(moe_in)))
+
+    def layer_forward(self, desc: LayerDesc, M, x, out, flags=F_POST_NORM, tok_active_count=None,
+                      tok_active_idx=None, tok_active_weights=None):
+        """run_moe_coalesced_subbatch, model_speculative_moe_batched.mojo:1155-1204, any M."""
+        self.check(self.lib.moe_layer_forward(self.h, C.byref(desc), M, _addr(x), _addr(out),
+                                              flags, _addr(tok_active_count),
+                                              _addr(tok_active_idx), _addr(tok_active_weights)))
+
+
+def make_desc(w: dict, act=ACT_SIGMOID1702, top_p=1.0, r_scale_factor=None, bias=None,
+              router_fp32=False) -> LayerDesc:
+    """Builds a LayerDesc from a dict of arrays/tensors (keys as in synth.make_layer)."""
+    d = LayerDesc()
+    d.embed_dim, d.expert_mlp_dim, d.num_experts, d.top_k = w["d"], w["F"], w["E"], w["top_k"]
+    d.activation = act
+    d.r_scale_factor = float(1.0 / np.sqrt(np.float32(w["d"]))) if r_scale_factor is None else r_scale_factor
+    d.moe_top_p = top_p
+    if router_fp32:
+        d.router_f32 = _addr(w["router_f32"])
+    else:
+        d.router_packed = _addr(w["router_p"])
+        d.router_scales = _addr(w["router_s"])
+    d.router_logit_bias = _addr(bias)
+    d.router_scale = _addr(w["router_scale"])
+    d.per_expert_scale = _addr(w["per_expert_scale"])
+    d.pre_norm_w = _addr(w["pre_norm_w"])
+    d.post_norm_w = _addr(w["post_norm_w"])
+    d.gate_up_packed = _addr(w["gu_p"])
+    d.gate_up_scales = _addr(w["gu_s"])
+    d.down_packed = _addr(w["dn_p"])
+    d.down_scales = _addr(w["dn_s"])
+    d._keep = (w, bias)
+    return d
