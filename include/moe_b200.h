@@ -20,6 +20,9 @@
  *    fp32 scales; value = (nibble - 8) * scale.  K must be a multiple of 32.
  *  - Calls are synchronous unless moe_set_async(ctx, 1) was called; then
  *    they are enqueued on the context's stream and moe_wait() completes them.
+ *    The context's own stream is a blocking stream, so its kernels run after
+ *    earlier work on the legacy default stream; device buffers produced on
+ *    any other stream need moe_set_stream() (or a caller-side sync) first.
  *  - Every call returns MOE_OK (0) or an MOE_E_* code; moe_last_error()
  *    gives the message.  There is no CPU fallback: a context can only be
  *    created on a CUDA device.

@@ -361,7 +361,7 @@ int moe_ctx_create(int device, moe_ctx** out) {
     moe_ctx* ctx = new moe_ctx();
     ctx->device = device;
     if (cudaSetDevice(device) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&ctx->stream, cudaStreamDefault) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->done, cudaEventDisableTiming) != cudaSuccess ||
         cudaMalloc(&ctx->err_flag, sizeof(int)) != cudaSuccess ||
         cudaMemset(ctx->err_flag, 0, sizeof(int)) != cudaSuccess) {
@@ -405,7 +405,7 @@ int moe_set_stream(moe_ctx* ctx, void* stream) {
         ctx->stream = static_cast<cudaStream_t>(stream);
         ctx->own_stream = false;
     } else {
-        if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess)
+        if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamDefault) != cudaSuccess)
             return fail(ctx, MOE_E_CUDA, "stream creation failed");
         ctx->own_stream = true;
     }

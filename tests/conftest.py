@@ -31,7 +31,19 @@ def full_layer(ctx):
     import synth
     dev = synth.make_layer(ctx, seed=0)
     host = synth.to_host(dev)
+    check_layer_stats(host)
     return dev, host, O.make_layer(host)
+
+
+def check_layer_stats(host):
+    """The dequantised weights must look like N(0, 0.02): catches a layer
+    built from memory the generator had not written yet."""
+    import numpy as np
+    p = host["gu_p"][: 1408 * 1408].astype(np.int32)
+    s = host["gu_s"][: 1408 * 88]
+    v = (np.stack([(p & 15) - 8, (p >> 4) - 8], 1).reshape(-1, 32) * s[:, None])
+    assert 0.018 < float(v.std()) < 0.022, float(v.std())
+    assert 0.005 < float(host["dn_s"].mean()) < 0.009
 
 
 @pytest.fixture(scope="session")
