@@ -366,12 +366,14 @@ def main():
     # roofline of the dominant kernel (largest share of profiled time)
     hbm, _, src = peaks()
     u_mean = sum(uniq) / len(uniq)
-    dom = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
+    dom = max((kv for kv in prof.items() if kv[0] in ("gemv_gate_up", "gemv_down", "q4_matmul")),
+              key=lambda kv: kv[1][0])[0] if prof else None
     alg = {
         "gemv_gate_up": u_mean * GU_BYTES + M * D * 4 + M * K * F * 4,
         "gemv_down": u_mean * DN_BYTES + M * K * F * 4 + M * K * D * 4,
         "q4_matmul": sum(q4_bytes(ci, co) + M * (ci + co) * 4 for (_, _, ci, co) in dense.values()) / max(1, len(dense)),
-        "route": ROUTER_BYTES + 2 * M * D * 4,
+        "router": ROUTER_BYTES + M * D * 4 + M * E * 4,
+        "prep": 4 * M * D * 4,
     }
     roof = None
     if dom in alg and prof[dom][1] > 0:

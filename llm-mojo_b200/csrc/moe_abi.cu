@@ -243,13 +243,16 @@ struct ExpertBufs {
     int* slot_expert;
     float* slot_weight;
     moe::BucketOut b;
-    float* act;
-    float* y;
+    float* x32;   // [M][d] gate/up input, fp32 natural
+    float* xsum;  // [M][d/32] 1.5 * block sums of x32
+    float* act;   // [P][F]
+    float* y;     // [P][d]
 };
 
 size_t expert_bufs_bytes(int64_t M, int64_t K, int64_t d, int64_t F, int64_t E) {
     const int64_t P = M * K;
-    return al(P * 4) * 2 + al(16) + al(E * 4) * 3 + al(P * 4) * 3 + al(P * F * 4) + al(P * d * 4);
+    return al(P * 4) * 2 + al(16) + al(E * 4) * 3 + al(P * 4) * 3 + al(M * d * 4) +
+           al(M * d / 32 * 4) + al(P * F * 4) + al(P * d * 4);
 }
 
 int take_expert_bufs(moe_ctx* ctx, int64_t M, int64_t K, int64_t d, int64_t F, int64_t E,
@@ -264,6 +267,8 @@ int take_expert_bufs(moe_ctx* ctx, int64_t M, int64_t K, int64_t d, int64_t F, i
     o->b.pair_token = (int*)ws_take(ctx, P * 4);
     o->b.pair_slot = (int*)ws_take(ctx, P * 4);
     o->b.slot_pair = (int*)ws_take(ctx, P * 4);
+    o->x32 = (float*)ws_take(ctx, M * d * 4);
+    o->xsum = (float*)ws_take(ctx, M * d / 32 * 4);
     o->act = (float*)ws_take(ctx, P * F * 4);
     o->y = (float*)ws_take(ctx, P * d * 4);
     if (!o->y) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
@@ -277,10 +282,25 @@ struct ExpertWeights {
     const float* dn_s;
 };
 
-// slot table -> bucket -> gate/up (+act) -> down -> combine
+// Rows of an input (any layout, fp32 or fp16) -> fp32 natural + block sums.
+int prep_rows(moe_ctx* ctx, const void* X, int x_layout, int x_f16, int64_t M, int64_t K,
+              float* out, float* out_sum) {
+    moe::PrepArgs pa;
+    pa.x = X;
+    pa.x_f16 = x_f16;
+    pa.x_layout = x_layout;
+    pa.K = K;
+    pa.out = out;
+    pa.out_sum = out_sum;
+    ProfScope ps(ctx, "prep");
+    ctx->launches += moe::launch_prep(pa, M, ctx->stream);
+    return MOE_OK;
+}
+
+// slot table -> bucket -> gate/up (+act) -> down -> combine.  bb.x32 and
+// bb.xsum must hold the gate/up input (prep_rows or the router's prep).
 int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int64_t d, int64_t F,
-                int64_t E, const void* X, int x_layout, int x_f16, int act, ExpertBufs& bb,
-                const moe::CombineArgs* comb_tmpl, void* out) {
+                int64_t E, int act, ExpertBufs& bb, const moe::CombineArgs* comb_tmpl, void* out) {
     cudaStream_t s = ctx->stream;
     const int64_t P = M * K;
     {
@@ -295,9 +315,8 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     g1.Ws = w.gu_s;
     g1.rows_per_expert = 2 * F;
     g1.K = (int)d;
-    g1.X = X;
-    g1.x_layout = x_layout;
-    g1.x_f16 = x_f16;
+    g1.X = bb.x32;
+    g1.xsum = bb.xsum;
     g1.meta = bb.b.meta;
     g1.unique_expert = bb.b.unique_expert;
     g1.seg_start = bb.b.seg_start;
@@ -320,8 +339,7 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     g2.rows_per_expert = d;
     g2.K = (int)F;
     g2.X = bb.act;
-    g2.x_layout = 0;
-    g2.x_f16 = 0;
+    g2.xsum = nullptr;
     g2.pair_row = nullptr;
     g2.out = bb.y;
     g2.out_stride = d;
@@ -543,19 +561,24 @@ int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch, const uint8_t* W, const fl
     TRY(check_q4_shape(ctx, c_in, c_out));
     if (batch <= 0) return fail(ctx, MOE_E_SHAPE, "batch_size must be >= 1");
     if (batch > (1 << 20)) return fail(ctx, MOE_E_SHAPE, "batch_size too large");
-    TRY(ws_reserve(ctx, al(batch * c_in * 4) + al(batch * c_out * 4)));
+    TRY(ws_reserve(ctx, al(batch * c_in * 4) * 2 + al(batch * c_out * 4)));
     void *w, *sc, *xd, *od;
     TRY(dev_ptr(ctx, W, c_out * c_in / 2, K_W, &w));
     TRY(dev_ptr(ctx, S, c_out * c_in / 32 * 4, K_W, &sc));
     TRY(dev_ptr(ctx, x, batch * c_in * 4, K_IN, &xd));
     TRY(dev_ptr(ctx, out, batch * c_out * 4, K_OUT, &od));
     if (!al16(w)) return fail(ctx, MOE_E_ARG, "packed weights must be 16-byte aligned");
+    if (!al16(xd)) {  // the GEMV reads activations as float4
+        float* xc = (float*)ws_take(ctx, batch * c_in * 4);
+        TRY(prep_rows(ctx, xd, MOE_X_NATURAL, 0, batch, c_in, xc, nullptr));
+        xd = xc;
+    }
     moe::GemvArgs g;
     g.Wp = (const uint8_t*)w;
     g.Ws = (const float*)sc;
     g.rows_per_expert = c_out;
     g.K = (int)c_in;
-    g.X = xd;
+    g.X = (const float*)xd;
     g.dense_tokens = (int)batch;
     g.out = (float*)od;
     g.out_stride = c_out;
@@ -704,12 +727,14 @@ int moe_run_moe_experts_stage1(moe_ctx* ctx, const uint8_t* gu_p, const float* g
                                                   (const int64_t*)ai, nullptr, bb.slot_expert,
                                                   bb.slot_weight, (int)E, ctx->err_flag, s);
     ctx->launches += moe::launch_bucket(bb.slot_expert, count, (int)count, (int)E, bb.b, s);
+    TRY(prep_rows(ctx, xi, MOE_X_NATURAL, 0, 1, d, bb.x32, bb.xsum));
     moe::GemvArgs g;
     g.Wp = (const uint8_t*)wp;
     g.Ws = (const float*)ws;
     g.rows_per_expert = 2 * F;
     g.K = (int)d;
-    g.X = xi;
+    g.X = bb.x32;
+    g.xsum = bb.xsum;
     g.meta = bb.b.meta;
     g.unique_expert = bb.b.unique_expert;
     g.seg_start = bb.b.seg_start;
@@ -738,7 +763,7 @@ int moe_run_moe_experts_stage2(moe_ctx* ctx, const uint8_t* dn_p, const float* d
     TRY(check_q4_shape(ctx, F, d));
     if (count < 0 || count > 32) return fail(ctx, MOE_E_SHAPE, "active_count must be in [0, 32]");
     const int64_t E = 1024, Kc = std::max<int64_t>(count, 1);
-    TRY(ws_reserve(ctx, expert_bufs_bytes(1, Kc, d, F, E) + al(Kc * F * 4) + al(Kc * 8) +
+    TRY(ws_reserve(ctx, expert_bufs_bytes(1, Kc, d, F, E) + al(Kc * F * 4) * 2 + al(Kc * 8) +
                             al(Kc * 4) + al(d * 4)));
     void *wp, *ws, *aa = nullptr, *ai = nullptr, *aw = nullptr, *mo;
     TRY(dev_ptr(ctx, dn_p, 1, K_W, &wp));
@@ -762,12 +787,17 @@ int moe_run_moe_experts_stage2(moe_ctx* ctx, const uint8_t* dn_p, const float* d
                                                   bb.slot_expert, bb.slot_weight, (int)E,
                                                   ctx->err_flag, s);
     ctx->launches += moe::launch_bucket(bb.slot_expert, count, (int)count, (int)E, bb.b, s);
+    if (!al16(aa)) {
+        float* ac = (float*)ws_take(ctx, count * F * 4);
+        TRY(prep_rows(ctx, aa, MOE_X_NATURAL, 0, count, F, ac, nullptr));
+        aa = ac;
+    }
     moe::GemvArgs g;
     g.Wp = (const uint8_t*)wp;
     g.Ws = (const float*)ws;
     g.rows_per_expert = d;
     g.K = (int)F;
-    g.X = aa;
+    g.X = (const float*)aa;
     g.meta = bb.b.meta;
     g.unique_expert = bb.b.unique_expert;
     g.seg_start = bb.b.seg_start;
@@ -826,7 +856,8 @@ int moe_run_moe_coalesced_core(moe_ctx* ctx, int64_t sub_b, const uint8_t* gu_p,
                                                   ctx->err_flag, ctx->stream);
     ExpertWeights w{(const uint8_t*)gp, (const float*)gs, (const uint8_t*)dp, (const float*)ds};
     moe::CombineArgs c;
-    TRY(run_experts(ctx, w, sub_b, top_k, d, F, E, xi, x_layout, 0, activation, bb, &c, out));
+    TRY(prep_rows(ctx, xi, x_layout, 0, sub_b, d, bb.x32, bb.xsum));
+    TRY(run_experts(ctx, w, sub_b, top_k, d, F, E, activation, bb, &c, out));
     return finish(ctx);
 }
 
@@ -866,7 +897,8 @@ int moe_run_diffusion_moe_experts_parallel(moe_ctx* ctx, const uint8_t* gu_p, co
     moe::CombineArgs c;
     c.fma_mode = 1;
     c.out_f16 = 1;
-    TRY(run_experts(ctx, w, B, top_k, d, F, E, xi, MOE_X_NATURAL, 1, activation, bb, &c, out));
+    TRY(prep_rows(ctx, xi, MOE_X_NATURAL, 1, B, d, bb.x32, bb.xsum));
+    TRY(run_experts(ctx, w, B, top_k, d, F, E, activation, bb, &c, out));
     return finish(ctx);
 }
 
@@ -947,30 +979,67 @@ int layer_dev(moe_ctx* ctx, const moe_layer_desc* L, int flags, LayerDev* o) {
     return MOE_OK;
 }
 
+// Bytes route_dev takes from the workspace.
+size_t route_bytes(int64_t M, int64_t d, int64_t E, int64_t K) {
+    return al(M * K * 4) * 2 + al(M * d * 4) * 2 + al(M * d / 32 * 4) + al(M * E * 4);
+}
+
+// Router: prep (norms, router input, block sums) -> router GEMV -> softmax /
+// top-k / LOD (or set-cover).  moe_in / moe_in_sum receive the expert input.
 int route_dev(moe_ctx* ctx, const moe_layer_desc* L, const LayerDev& ld, int64_t M,
-              const float* xd, int flags, float* moe_in, int* slot_expert, float* slot_weight,
-              float* probs, int64_t* top_idx, float* top_val, int64_t* tc, int64_t* ti,
-              float* tw) {
-    const int64_t K = L->top_k;
+              const float* xd, int flags, float* moe_in, float* moe_in_sum, int* slot_expert,
+              float* slot_weight, float* probs, int64_t* top_idx, float* top_val, int64_t* tc,
+              int64_t* ti, float* tw) {
+    const int64_t K = L->top_k, d = L->embed_dim, E = L->num_experts;
     int* ti32 = (int*)ws_take(ctx, M * K * 4);
     float* tv = (float*)ws_take(ctx, M * K * 4);
-    if (!tv) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
-    moe::RouteArgs a;
-    a.x = xd;
-    a.d = L->embed_dim;
-    a.E = (int)L->num_experts;
-    a.K = (int)K;
-    a.rp = ld.rp;
-    a.rs = ld.rs;
-    a.rf32 = ld.rf32;
+    float* scaled = (float*)ws_take(ctx, M * d * 4);
+    float* scores = (float*)ws_take(ctx, M * E * 4);
+    if (!moe_in) moe_in = (float*)ws_take(ctx, M * d * 4);
+    if (!moe_in_sum) moe_in_sum = (float*)ws_take(ctx, M * d / 32 * 4);
+    if (!tv || !scaled || !scores || !moe_in || !moe_in_sum)
+        return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+    cudaStream_t s = ctx->stream;
+    moe::PrepArgs pa;
+    pa.x = xd;
+    pa.K = d;
+    pa.norm = 1;
+    pa.pre_w = ld.pre_w;
+    pa.router_scale = ld.router_scale;
+    pa.rsf = L->r_scale_factor;
+    pa.out = moe_in;
+    pa.out_sum = moe_in_sum;
+    pa.scaled = scaled;
+    {
+        ProfScope ps(ctx, "prep");
+        ctx->launches += moe::launch_prep(pa, M, s);
+    }
+    {
+        ProfScope ps(ctx, "router");
+        if (ld.rp) {
+            moe::GemvArgs g;
+            g.Wp = ld.rp;
+            g.Ws = ld.rs;
+            g.rows_per_expert = E;
+            g.K = (int)d;
+            g.X = scaled;
+            g.dense_tokens = (int)M;
+            g.out = scores;
+            g.out_stride = E;
+            g.max_tokens = (int)M;
+            ctx->launches += moe::launch_gemv(moe::GEMV_PLAIN, g, ctx->num_sms, s);
+        } else {
+            ctx->launches += moe::launch_gemv_f32(ld.rf32, scaled, scores, M, E, d, s);
+        }
+    }
+    moe::TopkArgs a;
+    a.scores = scores;
     a.bias = ld.bias;
-    a.router_scale = ld.router_scale;
-    a.rsf = L->r_scale_factor;
+    a.E = (int)E;
+    a.K = (int)K;
     a.pes = ld.pes;
     a.top_p = L->moe_top_p;
-    a.pre_w = ld.pre_w;
     a.lod = (flags & MOE_F_SET_COVER) ? 0 : 1;
-    a.moe_in = moe_in;
     a.probs_out = probs;
     a.top_idx = top_idx;
     a.top_val = top_val;
@@ -982,13 +1051,13 @@ int route_dev(moe_ctx* ctx, const moe_layer_desc* L, const LayerDev& ld, int64_t
     a.tok_idx = ti;
     a.tok_w = tw;
     {
-        ProfScope ps(ctx, "route");
-        ctx->launches += moe::launch_route(a, M, ctx->stream);
+        ProfScope ps(ctx, "topk");
+        ctx->launches += moe::launch_topk(a, M, s);
     }
     if (flags & MOE_F_SET_COVER)
-        ctx->launches += moe::launch_set_cover(ti32, tv, M, (int)K, (int)L->num_experts, ld.pes,
-                                               L->moe_top_p, 0.85f, 0.068f, 5, slot_expert,
-                                               slot_weight, tc, ti, tw, ctx->stream);
+        ctx->launches += moe::launch_set_cover(ti32, tv, M, (int)K, (int)E, ld.pes, L->moe_top_p,
+                                               0.85f, 0.068f, 5, slot_expert, slot_weight, tc, ti,
+                                               tw, s);
     return MOE_OK;
 }
 
@@ -1002,8 +1071,8 @@ int moe_route(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const float* x, 
     if (!x || !tc || !ti || !tw) return fail(ctx, MOE_E_ARG, "null pointer");
     if (M <= 0) return fail(ctx, MOE_E_SHAPE, "M must be >= 1");
     const int64_t d = L->embed_dim, E = L->num_experts, K = L->top_k, P = M * K;
-    TRY(ws_reserve(ctx, layer_small_bytes(L) + al(M * d * 4) * 2 + al(M * E * 4) + al(P * 8) * 2 +
-                            al(P * 4) * 6 + al(M * 8)));
+    TRY(ws_reserve(ctx, layer_small_bytes(L) + route_bytes(M, d, E, K) + al(M * d * 4) * 2 +
+                            al(M * E * 4) + al(P * 8) * 2 + al(P * 4) * 6 + al(M * 8)));
     LayerDev ld;
     TRY(layer_dev(ctx, L, flags & ~MOE_F_POST_NORM, &ld));
     void *xd, *sc = nullptr, *dti = nullptr, *dtv = nullptr, *dtc, *dtidx, *dtw, *mi = nullptr;
@@ -1017,8 +1086,9 @@ int moe_route(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const float* x, 
     if (moe_in) TRY(dev_ptr(ctx, moe_in, M * d * 4, K_OUT, &mi));
     int* se = (int*)ws_take(ctx, P * 4);
     float* sw = (float*)ws_take(ctx, P * 4);
-    TRY(route_dev(ctx, L, ld, M, (const float*)xd, flags, (float*)mi, se, sw, (float*)sc,
-                  (int64_t*)dti, (float*)dtv, (int64_t*)dtc, (int64_t*)dtidx, (float*)dtw));
+    TRY(route_dev(ctx, L, ld, M, (const float*)xd, flags, (float*)mi, nullptr, se, sw,
+                  (float*)sc, (int64_t*)dti, (float*)dtv, (int64_t*)dtc, (int64_t*)dtidx,
+                  (float*)dtw));
     return finish(ctx);
 }
 
@@ -1031,8 +1101,9 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
     const int64_t d = L->embed_dim, E = L->num_experts, K = L->top_k, F = L->expert_mlp_dim;
     const int64_t P = M * K;
     const size_t out_bytes = M * d * ((flags & MOE_F_FP16_OUT) ? 2 : 4);
-    TRY(ws_reserve(ctx, layer_small_bytes(L) + expert_bufs_bytes(M, K, d, F, E) + al(M * d * 4) * 2 +
-                            al(out_bytes) + al(P * 4) * 2 + al(M * 8) + al(P * 8) + al(P * 4)));
+    TRY(ws_reserve(ctx, layer_small_bytes(L) + expert_bufs_bytes(M, K, d, F, E) +
+                            route_bytes(M, d, E, K) + al(M * d * 4) + al(out_bytes) +
+                            al(P * 4) * 2 + al(M * 8) + al(P * 8) + al(P * 4)));
     LayerDev ld;
     TRY(layer_dev(ctx, L, flags, &ld));
     void *xd, *od, *dtc = nullptr, *dti = nullptr, *dtw = nullptr;
@@ -1041,16 +1112,16 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
     if (tc) TRY(dev_ptr(ctx, tc, M * 8, K_OUT, &dtc));
     if (ti) TRY(dev_ptr(ctx, ti, P * 8, K_OUT, &dti));
     if (tw) TRY(dev_ptr(ctx, tw, P * 4, K_OUT, &dtw));
-    float* moe_in = (float*)ws_take(ctx, M * d * 4);
     ExpertBufs bb;
     TRY(take_expert_bufs(ctx, M, K, d, F, E, &bb));
-    TRY(route_dev(ctx, L, ld, M, (const float*)xd, flags, moe_in, bb.slot_expert, bb.slot_weight,
-                  nullptr, nullptr, nullptr, (int64_t*)dtc, (int64_t*)dti, (float*)dtw));
+    TRY(route_dev(ctx, L, ld, M, (const float*)xd, flags, bb.x32, bb.xsum, bb.slot_expert,
+                  bb.slot_weight, nullptr, nullptr, nullptr, (int64_t*)dtc, (int64_t*)dti,
+                  (float*)dtw));
     moe::CombineArgs c;
     c.post_norm = (flags & MOE_F_POST_NORM) ? 1 : 0;
     c.post_w = ld.post_w;
     c.out_f16 = (flags & MOE_F_FP16_OUT) ? 1 : 0;
-    TRY(run_experts(ctx, ld.w, M, K, d, F, E, moe_in, MOE_X_NATURAL, 0, L->activation, bb, &c, od));
+    TRY(run_experts(ctx, ld.w, M, K, d, F, E, L->activation, bb, &c, od));
     return finish(ctx);
 }
 

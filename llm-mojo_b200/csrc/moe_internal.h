@@ -12,9 +12,8 @@ struct GemvArgs {
     const float* Ws = nullptr;    // expert 0's scales
     int64_t rows_per_expert = 0;  // R
     int K = 0;                    // inner dimension (multiple of 32)
-    const void* X = nullptr;      // input rows [*, K]
-    int x_layout = 0;             // moe_x_layout
-    int x_f16 = 0;                // input rows are fp16
+    const float* X = nullptr;     // input rows [*, K], fp32 natural order, 16-byte aligned
+    const float* xsum = nullptr;  // [*, K/32] 1.5 * block sums of X, or null (exact dequant)
     const int* meta = nullptr;    // meta[0] = number of unique experts U
     const int* unique_expert = nullptr;
     const int* seg_start = nullptr;
@@ -34,21 +33,28 @@ struct GemvArgs {
 
 enum GemvMode { GEMV_PLAIN = 0, GEMV_ACT = 1 };
 
-struct RouteArgs {
-    const float* x = nullptr;  // [M][d] fp32 natural
-    int64_t d = 0;
-    int E = 0, K = 0;
-    const uint8_t* rp = nullptr;
-    const float* rs = nullptr;
-    const float* rf32 = nullptr;
-    const float* bias = nullptr;
+// Per-row preparation: layout/fp16 conversion, optional norms, block sums.
+struct PrepArgs {
+    const void* x = nullptr;
+    int x_f16 = 0;
+    int x_layout = 0;
+    int64_t K = 0;
+    int norm = 0;                   // rms-normalise (then out = x*inv*pre_w)
+    const float* pre_w = nullptr;
     const float* router_scale = nullptr;
     float rsf = 0.f;
+    float* out = nullptr;           // [M][K] fp32
+    float* out_sum = nullptr;       // [M][K/32] 1.5 * block sums of out (nullable)
+    float* scaled = nullptr;        // [M][K] x*inv*router_scale*rsf (nullable)
+};
+
+struct TopkArgs {
+    const float* scores = nullptr;  // [M][E] router logits
+    const float* bias = nullptr;
+    int E = 0, K = 0;
     const float* pes = nullptr;
     float top_p = 1.f;
-    const float* pre_w = nullptr;
     int lod = 1;
-    float* moe_in = nullptr;
     float* probs_out = nullptr;
     int64_t* top_idx = nullptr;
     float* top_val = nullptr;
@@ -85,7 +91,10 @@ struct CombineArgs {
 };
 
 // Every launcher returns the number of kernels it launched.
-int launch_route(const RouteArgs& a, int64_t M, cudaStream_t s);
+int launch_prep(const PrepArgs& a, int64_t M, cudaStream_t s);
+int launch_topk(const TopkArgs& a, int64_t M, cudaStream_t s);
+int launch_gemv_f32(const float* W, const float* X, float* out, int64_t M, int64_t E, int64_t d,
+                    cudaStream_t s);
 int launch_set_cover(const int* ti32, const float* tv, int64_t M, int K, int E, const float* pes,
                      float top_p, float core_top_p, float singleton_min_prob, int sub_batch,
                      int* slot_expert, float* slot_weight, int64_t* tok_count, int64_t* tok_idx,
@@ -109,7 +118,5 @@ int launch_apply_lod(const int64_t* top_idx, const float* top_val, const float* 
                      int64_t B, int K, int64_t active_top_k, const uint8_t* eb_mask,
                      const int64_t* active_canvas_idx, int64_t unaccepted_top_k, cudaStream_t s);
 
-size_t gemv_smem_bytes(int K, int maxt);
-int gemv_pick_maxt(int K, int max_tokens);
 
 }  // namespace moe

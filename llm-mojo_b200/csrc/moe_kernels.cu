@@ -28,331 +28,371 @@ __device__ __forceinline__ float ldg_stream_f(const float* p) {
     return r;
 }
 
-// Dot product of one Q4_0 block (16 bytes, 32 weights) with 32 activations
-// held in the swizzled shared layout, using the 1 + n/16 representation:
-//   sum_k (n_k - 8) x_k = 16 * (sum_k (1 + n_k/16) x_k - 1.5 * sum_k x_k).
-// Returns sum_k (1 + n_k/16) x_k; the caller subtracts 1.5*sum(x).
-struct Deq32 {
-    float f[32];
-    __device__ __forceinline__ void load(uint4 q) {
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+// Dot products of one Q4_0 block (16 bytes = 32 weights) with the
+// matching 32 activations of T rows, one 32-bit word (8 weights) at a time.
+// XS = true: weights as 1 + n/16 (shift + LOP3 per weight, see nib_1p); the
+//   caller then uses sum (n-8) x = 16 * (dot - 1.5 * sum x).
+// XS = false: exact n - 8 (shift + LOP3 + FADD per weight).
+template <bool XS, int T>
+__device__ __forceinline__ void block_dot(uint4 q, const float* const (&xp)[T], float (&d)[T]) {
+    const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            f[8 * i + 0] = nib_1p<0>(w[i]);
-            f[8 * i + 1] = nib_1p<1>(w[i]);
-            f[8 * i + 2] = nib_1p<2>(w[i]);
-            f[8 * i + 3] = nib_1p<3>(w[i]);
-            f[8 * i + 4] = nib_1p<4>(w[i]);
-            f[8 * i + 5] = nib_1p<5>(w[i]);
-            f[8 * i + 6] = nib_1p<6>(w[i]);
-            f[8 * i + 7] = nib_1p<7>(w[i]);
+    for (int t = 0; t < T; ++t) d[t] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float f[8];
+        if (XS) {
+            f[0] = nib_1p<0>(wv[i]);
+            f[1] = nib_1p<1>(wv[i]);
+            f[2] = nib_1p<2>(wv[i]);
+            f[3] = nib_1p<3>(wv[i]);
+            f[4] = nib_1p<4>(wv[i]);
+            f[5] = nib_1p<5>(wv[i]);
+            f[6] = nib_1p<6>(wv[i]);
+            f[7] = nib_1p<7>(wv[i]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                f[k] = __uint_as_float(0x4B000000u | ((wv[i] >> (4 * k)) & 0xFu)) - 8388616.0f;
+        }
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+            const float4* x4 = reinterpret_cast<const float4*>(xp[t]) + 2 * i;
+            const float4 v0 = __ldg(x4), v1 = __ldg(x4 + 1);
+            float p0 = f[0] * v0.x;
+            float p1 = f[1] * v0.y;
+            p0 = fmaf(f[2], v0.z, p0);
+            p1 = fmaf(f[3], v0.w, p1);
+            p0 = fmaf(f[4], v1.x, p0);
+            p1 = fmaf(f[5], v1.y, p1);
+            p0 = fmaf(f[6], v1.z, p0);
+            p1 = fmaf(f[7], v1.w, p1);
+            d[t] += p0 + p1;
         }
     }
-    // xb points at the 32 swizzled floats of block b
-    __device__ __forceinline__ float dot(const float* xb, int b) const {
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; q += 2) {
-            const float4 v0 = *reinterpret_cast<const float4*>(xb + (((q + b) & 7) << 2));
-            const float4 v1 = *reinterpret_cast<const float4*>(xb + (((q + 1 + b) & 7) << 2));
-            a0 = fmaf(f[4 * q + 0], v0.x, a0);
-            a1 = fmaf(f[4 * q + 1], v0.y, a1);
-            a2 = fmaf(f[4 * q + 2], v0.z, a2);
-            a3 = fmaf(f[4 * q + 3], v0.w, a3);
-            a0 = fmaf(f[4 * q + 4], v1.x, a0);
-            a1 = fmaf(f[4 * q + 5], v1.y, a1);
-            a2 = fmaf(f[4 * q + 6], v1.z, a2);
-            a3 = fmaf(f[4 * q + 7], v1.w, a3);
-        }
-        return (a0 + a1) + (a2 + a3);
-    }
-};
-
-__device__ __forceinline__ int swz(int j) {  // natural index -> swizzled smem index
-    const int b = j >> 5, q = (j >> 2) & 7;
-    return (b << 5) + (((q + b) & 7) << 2) + (j & 3);
 }
 
 // ------------------------------------------------------------ grouped GEMV
-// Work item = (unique expert u, tile of rows).  Each warp owns 4 rows per
-// pass (8 lanes per row, lane l8 takes blocks l8, l8+8, ...), RPW passes;
-// all loads of a chunk of NBL blocks per lane are issued before any math.
-// ACT mode: the warp's 4 rows are gate a, gate a+1, up a, up a+1, and the
-// activation is applied after the lane reduction.
-template <int MODE, int NBL, int RPW, int MAXT>
-__global__ void __launch_bounds__(256, 2) k_q4_gemv(GemvArgs a) {
-    extern __shared__ float4 smem4[];
-    float* xs = reinterpret_cast<float*>(smem4);  // [MAXT][K] swizzled
-    const int K = a.K, nb = K >> 5;
-    float* xsum = xs + (size_t)MAXT * K;  // [MAXT][nb]  (1.5 * sum of block)
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 3, l8 = lane & 7;
-    const int nbl = (nb + 7) >> 3;
-    const int rows_per_tile = (MODE == GEMV_ACT) ? 16 * RPW : 32 * RPW;
-    const int64_t tile_rows = (MODE == GEMV_ACT) ? a.F : a.rows_per_expert;
-    const int n_tiles = (int)((tile_rows + rows_per_tile - 1) / rows_per_tile);
-    const int U = a.dense_tokens > 0 ? 1 : a.meta[0];
-    const int n_items = U * n_tiles;
-    int staged_u = -1;
+// Warp-level work item = (unique expert u, row group).  A warp owns 4 rows
+// per pass (8 lanes per row; lane l8 takes blocks l8, l8+8, ...) and RPW
+// passes.  All weight loads of the item are issued before any math; the
+// activations are read through L1 (every lane group of the warp reads the
+// same 128-byte block, so each load is a broadcast).  In ACT mode the 4
+// rows of a pass are gate a, gate a+1, up a, up a+1 and the activation is
+// applied after the 8-lane shuffle reduction.
+struct GemvWarp {
+    int lane, g, l8;
+};
 
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int u = item / n_tiles, tile = item - u * n_tiles;
+template <int MODE, bool XS, int NBL, int RPW, int T>
+__device__ __forceinline__ void gemv_tokens(const GemvArgs& a, const GemvWarp& W, int cb, int nb,
+                                            const uint4 (&wq)[RPW][NBL], const float (&sc)[RPW][NBL],
+                                            const int64_t (&row)[RPW], const bool (&rv)[RPW],
+                                            const int (&arow)[RPW], int p0) {
+    const int K = a.K;
+    int64_t xr[T];
+    int po[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const int p = p0 + t;
+        xr[t] = a.pair_row ? a.pair_row[p] : p;
+        po[t] = a.out_row ? a.out_row[p] : p;
+    }
+    float acc[RPW][T];
+#pragma unroll
+    for (int ip = 0; ip < RPW; ++ip)
+#pragma unroll
+        for (int t = 0; t < T; ++t) acc[ip][t] = 0.f;
+#pragma unroll
+    for (int ip = 0; ip < RPW; ++ip)
+#pragma unroll
+        for (int ib = 0; ib < NBL; ++ib) {
+            const int b = W.l8 + 8 * (cb + ib);
+            if (rv[ip] && b < nb) {
+                const float* xp[T];
+#pragma unroll
+                for (int t = 0; t < T; ++t) xp[t] = a.X + xr[t] * K + b * 32;
+                float dd[T];
+                block_dot<XS, T>(wq[ip][ib], xp, dd);
+                const float s = XS ? 16.0f * sc[ip][ib] : sc[ip][ib];
+#pragma unroll
+                for (int t = 0; t < T; ++t)
+                    acc[ip][t] = XS ? fmaf(s, dd[t] - __ldg(a.xsum + xr[t] * nb + b), acc[ip][t])
+                                    : fmaf(s, dd[t], acc[ip][t]);
+            }
+        }
+#pragma unroll
+    for (int ip = 0; ip < RPW; ++ip)
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+            float v = acc[ip][t];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            if (MODE == GEMV_ACT) {
+                const float up = __shfl_down_sync(0xffffffffu, v, 16);
+                if (rv[ip]) {
+                    if (W.l8 == 0 && a.gu_out) a.gu_out[(int64_t)po[t] * a.gu_stride + row[ip]] = v;
+                    if (W.lane == 0 || W.lane == 8)
+                        a.out[(int64_t)po[t] * a.out_stride + arow[ip]] = act_fn(v, up, a.act);
+                }
+            } else if (rv[ip] && W.l8 == 0) {
+                a.out[(int64_t)po[t] * a.out_stride + row[ip]] = v;
+            }
+        }
+}
+
+template <int MODE, bool XS, int NBL, int RPW>
+__global__ void __launch_bounds__(128, 4) k_q4_gemv(GemvArgs a) {
+    GemvWarp W;
+    W.lane = threadIdx.x & 31;
+    W.g = W.lane >> 3;
+    W.l8 = W.lane & 7;
+    const int warp = threadIdx.x >> 5;
+    const int K = a.K, nb = K >> 5, nbl = (nb + 7) >> 3;
+    const int rows_per_item = (MODE == GEMV_ACT) ? 2 * RPW : 4 * RPW;
+    const int64_t tile_rows = (MODE == GEMV_ACT) ? a.F : a.rows_per_expert;
+    const int n_groups = (int)((tile_rows + rows_per_item - 1) / rows_per_item);
+    const int U = a.dense_tokens > 0 ? 1 : a.meta[0];
+    const int64_t n_items = (int64_t)U * n_groups;
+
+    for (int64_t item = (int64_t)blockIdx.x * 4 + warp; item < n_items; item += (int64_t)gridDim.x * 4) {
+        const int u = (int)(item / n_groups), grp = (int)(item - (int64_t)u * n_groups);
         const int e = a.dense_tokens > 0 ? 0 : a.unique_expert[u];
         const int n = a.dense_tokens > 0 ? a.dense_tokens : a.seg_count[u];
         const int s0 = a.dense_tokens > 0 ? 0 : a.seg_start[u];
         const uint8_t* Wp = a.Wp + (size_t)e * a.rows_per_expert * (K >> 1);
         const float* Ws = a.Ws + (size_t)e * a.rows_per_expert * nb;
-
-        // rows of this lane group for every pass
         int64_t row[RPW];
         bool rv[RPW];
         int arow[RPW];
 #pragma unroll
         for (int ip = 0; ip < RPW; ++ip) {
             if (MODE == GEMV_ACT) {
-                const int ar = tile * rows_per_tile + warp * 2 * RPW + ip * 2 + (g & 1);
+                const int ar = grp * rows_per_item + ip * 2 + (W.g & 1);
                 arow[ip] = ar;
                 rv[ip] = ar < a.F;
-                row[ip] = (g < 2) ? ar : (int64_t)a.F + ar;
+                row[ip] = (W.g < 2) ? ar : (int64_t)a.F + ar;
             } else {
-                const int64_t r = (int64_t)tile * rows_per_tile + warp * 4 * RPW + ip * 4 + g;
+                const int64_t r = (int64_t)grp * rows_per_item + ip * 4 + W.g;
                 arow[ip] = 0;
                 rv[ip] = r < a.rows_per_expert;
                 row[ip] = r;
             }
         }
-
-        for (int c0 = 0; c0 < n; c0 += MAXT) {
-            const int nt = min(MAXT, n - c0);
-            if (!(n <= MAXT && staged_u == u)) {
-                __syncthreads();
-                const int64_t tot = (int64_t)nt * K;
-                for (int64_t j = threadIdx.x; j < tot; j += blockDim.x) {
-                    const int t = (int)(j / K), jj = (int)(j - (int64_t)t * K);
-                    const int p = s0 + c0 + t;
-                    const int64_t src_row = a.pair_row ? a.pair_row[p] : p;
-                    const int64_t si = src_row * K + x_src_index(jj, K, a.x_layout);
-                    float v;
-                    if (a.x_f16)
-                        v = __half2float(reinterpret_cast<const __half*>(a.X)[si]);
-                    else
-                        v = reinterpret_cast<const float*>(a.X)[si];
-                    xs[(size_t)t * K + swz(jj)] = v;
-                }
-                __syncthreads();
-                for (int j = threadIdx.x; j < nt * nb; j += blockDim.x) {
-                    const float* xb = xs + (size_t)j * 32;  // (t, b) -> t*K + b*32 == j*32
-                    float s = 0.f;
-#pragma unroll
-                    for (int k = 0; k < 32; ++k) s += xb[k];
-                    xsum[j] = 1.5f * s;
-                }
-                __syncthreads();
-                staged_u = (n <= MAXT) ? u : -1;
-            }
-
-            float acc[RPW][MAXT];
+        // token chunks outermost; within a chunk, K chunks of NBL blocks per lane
+        // (a single K chunk for the layer shapes, so weights are loaded once)
+        const bool one_chunk = nbl <= NBL;
+        uint4 wq[RPW][NBL];
+        float sc[RPW][NBL];
+        auto load = [&](int cb) {
 #pragma unroll
             for (int ip = 0; ip < RPW; ++ip)
 #pragma unroll
-                for (int t = 0; t < MAXT; ++t) acc[ip][t] = 0.f;
-
-            for (int cb = 0; cb < nbl; cb += NBL) {
-                uint4 wq[RPW][NBL];
-                float sc[RPW][NBL];
-#pragma unroll
-                for (int ip = 0; ip < RPW; ++ip)
-#pragma unroll
-                    for (int ib = 0; ib < NBL; ++ib) {
-                        const int b = l8 + 8 * (cb + ib);
-                        if (rv[ip] && b < nb) {
-                            wq[ip][ib] = ldg_stream(Wp + row[ip] * (K >> 1) + b * 16);
-                            sc[ip][ib] = ldg_stream_f(Ws + row[ip] * nb + b);
-                        } else {
-                            wq[ip][ib] = make_uint4(0, 0, 0, 0);
-                            sc[ip][ib] = 0.f;
-                        }
+                for (int ib = 0; ib < NBL; ++ib) {
+                    const int b = W.l8 + 8 * (cb + ib);
+                    if (rv[ip] && b < nb) {
+                        wq[ip][ib] = ldg_stream(Wp + row[ip] * (K >> 1) + b * 16);
+                        sc[ip][ib] = ldg_stream_f(Ws + row[ip] * nb + b);
+                    } else {
+                        wq[ip][ib] = make_uint4(0, 0, 0, 0);
+                        sc[ip][ib] = 0.f;
                     }
-#pragma unroll
-                for (int ip = 0; ip < RPW; ++ip)
-#pragma unroll
-                    for (int ib = 0; ib < NBL; ++ib) {
-                        const int b = l8 + 8 * (cb + ib);
-                        if (rv[ip] && b < nb) {
-                            Deq32 dq;
-                            dq.load(wq[ip][ib]);
-                            const float s16 = 16.0f * sc[ip][ib];
-#pragma unroll
-                            for (int t = 0; t < MAXT; ++t)
-                                if (t < nt) {
-                                    const float d = dq.dot(xs + (size_t)t * K + b * 32, b);
-                                    acc[ip][t] = fmaf(s16, d - xsum[t * nb + b], acc[ip][t]);
-                                }
-                        }
-                    }
+                }
+        };
+        if (one_chunk) {
+            load(0);
+            int t = 0;
+            while (n - t >= 4) {
+                gemv_tokens<MODE, XS, NBL, RPW, 4>(a, W, 0, nb, wq, sc, row, rv, arow, s0 + t);
+                t += 4;
             }
-
-            // reduce the 8 lanes of each row, then write
+            if (n - t >= 2) {
+                gemv_tokens<MODE, XS, NBL, RPW, 2>(a, W, 0, nb, wq, sc, row, rv, arow, s0 + t);
+                t += 2;
+            }
+            if (n - t >= 1) gemv_tokens<MODE, XS, NBL, RPW, 1>(a, W, 0, nb, wq, sc, row, rv, arow, s0 + t);
+        } else {
+            // long rows: one token at a time, K chunk by K chunk, partials kept
+            // in the output row (first chunk stores, later chunks add)
+            for (int t = 0; t < n; ++t) {
+                const int p = s0 + t;
+                const int64_t xr = a.pair_row ? a.pair_row[p] : p;
+                const int64_t po = a.out_row ? a.out_row[p] : p;
+                float acc[RPW];
 #pragma unroll
-            for (int ip = 0; ip < RPW; ++ip)
+                for (int ip = 0; ip < RPW; ++ip) acc[ip] = 0.f;
+                for (int cb = 0; cb < nbl; cb += NBL) {
+                    load(cb);
 #pragma unroll
-                for (int t = 0; t < MAXT; ++t) {
-                    float v = acc[ip][t];
+                    for (int ip = 0; ip < RPW; ++ip)
+#pragma unroll
+                        for (int ib = 0; ib < NBL; ++ib) {
+                            const int b = W.l8 + 8 * (cb + ib);
+                            if (rv[ip] && b < nb) {
+                                const float* xp[1] = {a.X + xr * K + b * 32};
+                                float dd[1];
+                                block_dot<XS, 1>(wq[ip][ib], xp, dd);
+                                const float s = XS ? 16.0f * sc[ip][ib] : sc[ip][ib];
+                                acc[ip] = XS ? fmaf(s, dd[0] - __ldg(a.xsum + xr * nb + b), acc[ip])
+                                             : fmaf(s, dd[0], acc[ip]);
+                            }
+                        }
+                }
+#pragma unroll
+                for (int ip = 0; ip < RPW; ++ip) {
+                    float v = acc[ip];
                     v += __shfl_xor_sync(0xffffffffu, v, 1);
                     v += __shfl_xor_sync(0xffffffffu, v, 2);
                     v += __shfl_xor_sync(0xffffffffu, v, 4);
-                    const int p = s0 + c0 + t;
                     if (MODE == GEMV_ACT) {
                         const float up = __shfl_down_sync(0xffffffffu, v, 16);
-                        if (t < nt && rv[ip]) {
-                            const int64_t orow = a.out_row ? a.out_row[p] : p;
-                            if (l8 == 0 && a.gu_out) a.gu_out[orow * a.gu_stride + row[ip]] = v;
-                            if (lane == 0 || lane == 8)
-                                a.out[orow * a.out_stride + arow[ip]] = act_fn(v, up, a.act);
+                        if (rv[ip]) {
+                            if (W.l8 == 0 && a.gu_out) a.gu_out[po * a.gu_stride + row[ip]] = v;
+                            if (W.lane == 0 || W.lane == 8)
+                                a.out[po * a.out_stride + arow[ip]] = act_fn(v, up, a.act);
                         }
-                    } else {
-                        if (t < nt && rv[ip] && l8 == 0) {
-                            const int64_t orow = a.out_row ? a.out_row[p] : p;
-                            a.out[orow * a.out_stride + row[ip]] = v;
-                        }
+                    } else if (rv[ip] && W.l8 == 0) {
+                        a.out[po * a.out_stride + row[ip]] = v;
                     }
                 }
+            }
         }
     }
 }
 
-size_t gemv_smem_bytes(int K, int maxt) {
-    return (size_t)maxt * ((size_t)K + (size_t)(K / 32)) * sizeof(float);
-}
-
-int gemv_pick_maxt(int K, int max_tokens) {
-    int m = 8;
-    while (m > 1 && (m / 2 >= max_tokens || gemv_smem_bytes(K, m) > 100 * 1024)) m /= 2;
-    return m;
-}
-
-template <int MODE, int NBL, int RPW, int MAXT>
+template <int MODE, bool XS, int NBL, int RPW>
 static void gemv_launch_t(const GemvArgs& a, int num_sms, cudaStream_t s) {
-    const size_t smem = gemv_smem_bytes(a.K, MAXT);
-    auto kern = k_q4_gemv<MODE, NBL, RPW, MAXT>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    const int rows_per_tile = (MODE == GEMV_ACT) ? 16 * RPW : 32 * RPW;
+    const int rows_per_item = (MODE == GEMV_ACT) ? 2 * RPW : 4 * RPW;
     const int64_t tile_rows = (MODE == GEMV_ACT) ? a.F : a.rows_per_expert;
-    const int64_t n_tiles = (tile_rows + rows_per_tile - 1) / rows_per_tile;
-    const int64_t items = n_tiles * (a.dense_tokens > 0 ? 1 : a.max_unique);
-    const int64_t cap = (int64_t)num_sms * 4;
-    const int grid = (int)(items < cap ? items : cap);
+    const int64_t n_groups = (tile_rows + rows_per_item - 1) / rows_per_item;
+    const int64_t items = n_groups * (a.dense_tokens > 0 ? 1 : a.max_unique);
+    const int64_t blocks = (items + 3) / 4;
+    const int64_t cap = (int64_t)num_sms * 16;
+    const int grid = (int)(blocks < cap ? blocks : cap);
     if (grid <= 0) return;
-    kern<<<grid, 256, smem, s>>>(a);
+    k_q4_gemv<MODE, XS, NBL, RPW><<<grid, 128, 0, s>>>(a);
 }
 
-template <int MODE, int NBL, int RPW>
-static void gemv_dispatch_t(const GemvArgs& a, int num_sms, cudaStream_t s) {
-    const int maxt = gemv_pick_maxt(a.K, a.max_tokens);
-    switch (maxt) {
-        case 1: gemv_launch_t<MODE, NBL, RPW, 1>(a, num_sms, s); break;
-        case 2: gemv_launch_t<MODE, NBL, RPW, 2>(a, num_sms, s); break;
-        case 4: gemv_launch_t<MODE, NBL, RPW, 4>(a, num_sms, s); break;
-        default: gemv_launch_t<MODE, NBL, RPW, 8>(a, num_sms, s); break;
-    }
-}
-
-template <int MODE>
-static void gemv_dispatch_mode(const GemvArgs& a, int num_sms, cudaStream_t s) {
+template <int MODE, bool XS>
+static void gemv_dispatch(const GemvArgs& a, int num_sms, cudaStream_t s) {
     const int nb = a.K / 32, nbl = (nb + 7) / 8;
     if (nbl == 11)
-        gemv_dispatch_t<MODE, 11, 1>(a, num_sms, s);  // K = 2816 (and 2560..2816)
+        gemv_launch_t<MODE, XS, 11, 1>(a, num_sms, s);  // K in (2560, 2816]
     else if (nbl <= 3)
-        gemv_dispatch_t<MODE, 3, 4>(a, num_sms, s);   // K <= 768 (704: down projection)
-    else if (nbl <= 8)
-        gemv_dispatch_t<MODE, 8, 1>(a, num_sms, s);   // K <= 2048
+        gemv_launch_t<MODE, XS, 3, 2>(a, num_sms, s);   // K <= 768 (704: down projection)
     else
-        gemv_dispatch_t<MODE, 6, 1>(a, num_sms, s);   // other K, chunked
+        gemv_launch_t<MODE, XS, 8, 1>(a, num_sms, s);   // other K, chunked beyond 2048
 }
 
 int launch_gemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s) {
-    if (mode == GEMV_ACT)
-        gemv_dispatch_mode<GEMV_ACT>(a, num_sms, s);
-    else
-        gemv_dispatch_mode<GEMV_PLAIN>(a, num_sms, s);
+    const bool xs = a.xsum != nullptr;
+    if (mode == GEMV_ACT) {
+        if (xs) gemv_dispatch<GEMV_ACT, true>(a, num_sms, s);
+        else gemv_dispatch<GEMV_ACT, false>(a, num_sms, s);
+    } else {
+        if (xs) gemv_dispatch<GEMV_PLAIN, true>(a, num_sms, s);
+        else gemv_dispatch<GEMV_PLAIN, false>(a, num_sms, s);
+    }
     return 1;
 }
 
-// ------------------------------------------------------------------ router
-// One CTA per token: model_speculative_moe_batched.mojo:2102-2118 (decode)
-// and :1001-1083 (sub-batch): norms, Q4 router GEMV, softmax (:921-933),
-// top-k by insertion semantics (:936-953; equal values keep the lower index
-// first) and, when a.lod, compute_moe_lod_weights (moe_kernels.mojo:445-490).
-__global__ void __launch_bounds__(256) k_route(RouteArgs a) {
-    extern __shared__ float4 smem4[];
-    const int64_t d = a.d;
-    const int nb = (int)(d >> 5), E = a.E, K = a.K;
-    float* xs = reinterpret_cast<float*>(smem4);  // [d] natural (x, then scaled x)
-    float* xw = xs + d;                            // [d] swizzled scaled x
-    float* xsum = xw + d;                          // [nb]
-    float* pr = xsum + nb;                         // [E]
-    float* red = pr + E;                           // [33]
-    float* tval = red + 33;                        // [K]
-    int* tidx = reinterpret_cast<int*>(tval + K);  // [K]
-    const int t = blockIdx.x;
-    const float* x = a.x + (size_t)t * d;
+// fp32 router (the literal reading of the configs' "router weight fp32"):
+// out[t][e] = W[e] . X[t]; one warp per (token, expert), float4 loads.
+__global__ void __launch_bounds__(128) k_gemv_f32(const float* W, const float* X, float* out,
+                                                  int64_t M, int64_t E, int64_t d) {
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (gw >= M * E) return;
+    const int64_t t = gw / E, e = gw - t * E;
+    const float4* w4 = reinterpret_cast<const float4*>(W + e * d);
+    const float4* x4 = reinterpret_cast<const float4*>(X + t * d);
+    float acc = 0.f;
+    for (int64_t j = lane; j < d / 4; j += 32) {
+        const float4 a = __ldg(w4 + j), b = __ldg(x4 + j);
+        acc = fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, fmaf(a.w, b.w, acc))));
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) out[t * E + e] = acc;
+}
 
+int launch_gemv_f32(const float* W, const float* X, float* out, int64_t M, int64_t E, int64_t d,
+                    cudaStream_t s) {
+    const int64_t warps = M * E;
+    if (warps <= 0) return 0;
+    k_gemv_f32<<<(unsigned)((warps + 3) / 4), 128, 0, s>>>(W, X, out, M, E, d);
+    return 1;
+}
+
+// ------------------------------------------------------------ row prep
+// One CTA per row: layout conversion (moe_x_layout), fp16 -> fp32, optional
+// rms norms (model_speculative_moe_batched.mojo:857-879): out = x * inv *
+// pre_w and scaled = x * inv * router_scale * r_scale_factor; and the
+// per-32-block sums (x1.5) the XS GEMV needs.
+__global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
+    extern __shared__ float4 smem4[];
+    float* xs = reinterpret_cast<float*>(smem4);
+    __shared__ float red[33];
+    const int64_t K = a.K, t = blockIdx.x;
     float ss = 0.f;
-    for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
-        const float v = x[j];
+    for (int64_t j = threadIdx.x; j < K; j += blockDim.x) {
+        const int64_t si = t * K + x_src_index(j, K, a.x_layout);
+        const float v = a.x_f16 ? __half2float(reinterpret_cast<const __half*>(a.x)[si])
+                                : reinterpret_cast<const float*>(a.x)[si];
         xs[j] = v;
         ss += v * v;
     }
-    ss = block_sum(ss, red);
-    const float inv = 1.0f / sqrtf(ss / (float)d + 1e-6f);
-    for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
-        const float nx = xs[j] * inv;
-        if (a.moe_in) a.moe_in[(size_t)t * d + j] = nx * a.pre_w[j];
-        const float sx = nx * a.router_scale[j] * a.rsf;
-        xs[j] = sx;
-        xw[swz((int)j)] = sx;
-    }
-    __syncthreads();
-    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
-        float s = 0.f;
-        for (int k = 0; k < 32; ++k) s += xs[b * 32 + k];
-        xsum[b] = 1.5f * s;
-    }
-    __syncthreads();
-
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
-    if (a.rp) {
-        const int g = lane >> 3, l8 = lane & 7;
-        for (int r0 = warp * 4; r0 < E; r0 += nwarp * 4) {
-            const int r = r0 + g;
-            float acc = 0.f;
-            if (r < E) {
-                for (int b = l8; b < nb; b += 8) {
-                    const uint4 q = *reinterpret_cast<const uint4*>(a.rp + (size_t)r * (d >> 1) + b * 16);
-                    Deq32 dq;
-                    dq.load(q);
-                    const float dd = dq.dot(xw + b * 32, b);
-                    acc = fmaf(16.0f * a.rs[(size_t)r * nb + b], dd - xsum[b], acc);
-                }
-            }
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-            if (r < E && l8 == 0) pr[r] = acc + (a.bias ? a.bias[r] : 0.f);
-        }
+    float inv = 1.f;
+    if (a.norm) {
+        ss = block_sum(ss, red);
+        inv = 1.0f / sqrtf(ss / (float)K + 1e-6f);
     } else {
-        for (int r = warp; r < E; r += nwarp) {
-            float acc = 0.f;
-            for (int64_t j = lane; j < d; j += 32) acc = fmaf(a.rf32[(size_t)r * d + j], xs[j], acc);
-            acc = warp_sum(acc);
-            if (lane == 0) pr[r] = acc + (a.bias ? a.bias[r] : 0.f);
+        __syncthreads();
+    }
+    for (int64_t j = threadIdx.x; j < K; j += blockDim.x) {
+        const float v = xs[j];
+        if (a.scaled) a.scaled[t * K + j] = v * inv * a.router_scale[j] * a.rsf;
+        const float o = a.norm ? v * inv * a.pre_w[j] : v;
+        xs[j] = o;
+        a.out[t * K + j] = o;
+    }
+    if (a.out_sum) {
+        __syncthreads();
+        const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+        for (int64_t b = w; b < K / 32; b += nw) {
+            const float s = warp_sum(xs[b * 32 + lane]);
+            if (lane == 0) a.out_sum[t * (K / 32) + b] = 1.5f * s;
         }
     }
-    __syncthreads();
+}
 
-    // softmax
+int launch_prep(const PrepArgs& a, int64_t M, cudaStream_t s) {
+    if (M <= 0) return 0;
+    const size_t smem = (size_t)a.K * sizeof(float);
+    cudaFuncSetAttribute(k_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_prep<<<(unsigned)M, 256, smem, s>>>(a);
+    return 1;
+}
+
+// ------------------------------------------------------ softmax + top-k + LOD
+// One CTA per token on the router scores: softmax (model_speculative_moe_
+// batched.mojo:921-933), top-k with insertion semantics (:936-953; equal
+// values keep the lower index first) and, when a.lod,
+// compute_moe_lod_weights (moe_kernels.mojo:445-490).
+__global__ void __launch_bounds__(128) k_topk(TopkArgs a) {
+    extern __shared__ float4 smem4[];
+    float* pr = reinterpret_cast<float*>(smem4);  // [E]
+    __shared__ float red[33];
+    __shared__ float tval[32];
+    __shared__ int tidx[32];
+    const int E = a.E, K = a.K;
+    const int64_t t = blockIdx.x;
     float m = -INFINITY;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) m = fmaxf(m, pr[e]);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const float v = a.scores[t * E + e] + (a.bias ? a.bias[e] : 0.f);
+        pr[e] = v;
+        m = fmaxf(m, v);
+    }
     m = block_max(m, red);
     float se = 0.f;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -364,15 +404,13 @@ __global__ void __launch_bounds__(256) k_route(RouteArgs a) {
     const float den = se + 1e-10f;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         pr[e] = pr[e] / den;
-        if (a.probs_out) a.probs_out[(size_t)t * E + e] = pr[e];
+        if (a.probs_out) a.probs_out[t * E + e] = pr[e];
     }
     if (threadIdx.x < K) {
         tval[threadIdx.x] = -999999.0f;
         tidx[threadIdx.x] = -1;
     }
     __syncthreads();
-
-    // top-k by rank: rank(i) = #{j: p_j > p_i} + #{j < i: p_j == p_i}
     for (int i = threadIdx.x; i < E; i += blockDim.x) {
         const float pi = pr[i];
         if (pi == pi) {
@@ -388,63 +426,59 @@ __global__ void __launch_bounds__(256) k_route(RouteArgs a) {
         }
     }
     __syncthreads();
-
-    if (threadIdx.x == 0) {
-        for (int k = 0; k < K; ++k) {
-            if (a.top_idx) a.top_idx[(size_t)t * K + k] = tidx[k];
-            if (a.top_val) a.top_val[(size_t)t * K + k] = tval[k];
-            a.ti32[(size_t)t * K + k] = tidx[k];
-            a.tv[(size_t)t * K + k] = tval[k];
-        }
-        if (a.lod) {
-            float sum = 0.f;
-            for (int k = 0; k < K; ++k) sum += tval[k];
-            const float inv_sum = 1.0f / (sum + 1e-10f);
-            const float tp = (a.top_p == a.top_p) ? a.top_p : 1.0f;
-            int cnt = 0;
-            int oi[32];
-            float ow[32];
-            if (tp >= 1.0f) {
-                for (int k = 0; k < K; ++k) {
-                    const float np_ = tval[k] * inv_sum;
-                    if ((np_ >= 0.05f || k == 0) && tidx[k] >= 0) {
-                        const int e = tidx[k];
-                        oi[cnt] = e;
-                        ow[cnt] = np_ * a.pes[e];
-                        ++cnt;
-                    }
-                }
-            } else {
-                float cum = 0.f;
-                for (int k = 0; k < K; ++k) {
-                    const float np_ = tval[k] * inv_sum;
-                    if (k > 0 && (np_ < 0.05f || cum >= tp)) break;
-                    if (tidx[k] < 0) break;
-                    oi[cnt] = tidx[k];
-                    ow[cnt] = np_;
-                    cum += np_;
-                    ++cnt;
-                }
-                const float rn = 1.0f / (cum + 1e-10f);
-                for (int k = 0; k < cnt; ++k) ow[k] = (ow[k] * rn) * a.pes[oi[k]];
-            }
-            for (int k = 0; k < K; ++k) {
-                const bool on = k < cnt;
-                a.slot_expert[(size_t)t * K + k] = on ? oi[k] : -1;
-                a.slot_weight[(size_t)t * K + k] = on ? ow[k] : 0.f;
-                if (a.tok_idx) a.tok_idx[(size_t)t * K + k] = on ? oi[k] : 0;
-                if (a.tok_w) a.tok_w[(size_t)t * K + k] = on ? ow[k] : 0.f;
-            }
-            if (a.tok_count) a.tok_count[t] = cnt;
-        }
+    if (threadIdx.x != 0) return;
+    for (int k = 0; k < K; ++k) {
+        if (a.top_idx) a.top_idx[t * K + k] = tidx[k];
+        if (a.top_val) a.top_val[t * K + k] = tval[k];
+        a.ti32[t * K + k] = tidx[k];
+        a.tv[t * K + k] = tval[k];
     }
+    if (!a.lod) return;
+    float sum = 0.f;
+    for (int k = 0; k < K; ++k) sum += tval[k];
+    const float inv_sum = 1.0f / (sum + 1e-10f);
+    const float tp = (a.top_p == a.top_p) ? a.top_p : 1.0f;
+    int cnt = 0;
+    int oi[32];
+    float ow[32];
+    if (tp >= 1.0f) {
+        for (int k = 0; k < K; ++k) {
+            const float np_ = tval[k] * inv_sum;
+            if ((np_ >= 0.05f || k == 0) && tidx[k] >= 0) {
+                const int e = tidx[k];
+                oi[cnt] = e;
+                ow[cnt] = np_ * a.pes[e];
+                ++cnt;
+            }
+        }
+    } else {
+        float cum = 0.f;
+        for (int k = 0; k < K; ++k) {
+            const float np_ = tval[k] * inv_sum;
+            if (k > 0 && (np_ < 0.05f || cum >= tp)) break;
+            if (tidx[k] < 0) break;
+            oi[cnt] = tidx[k];
+            ow[cnt] = np_;
+            cum += np_;
+            ++cnt;
+        }
+        const float rn = 1.0f / (cum + 1e-10f);
+        for (int k = 0; k < cnt; ++k) ow[k] = (ow[k] * rn) * a.pes[oi[k]];
+    }
+    for (int k = 0; k < K; ++k) {
+        const bool on = k < cnt;
+        a.slot_expert[t * K + k] = on ? oi[k] : -1;
+        a.slot_weight[t * K + k] = on ? ow[k] : 0.f;
+        if (a.tok_idx) a.tok_idx[t * K + k] = on ? oi[k] : 0;
+        if (a.tok_w) a.tok_w[t * K + k] = on ? ow[k] : 0.f;
+    }
+    if (a.tok_count) a.tok_count[t] = cnt;
 }
 
-int launch_route(const RouteArgs& a, int64_t M, cudaStream_t s) {
+int launch_topk(const TopkArgs& a, int64_t M, cudaStream_t s) {
     if (M <= 0) return 0;
-    const size_t smem = (size_t)(2 * a.d + a.d / 32 + a.E + 33 + 2 * a.K) * sizeof(float);
-    cudaFuncSetAttribute(k_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_route<<<(unsigned)M, 256, smem, s>>>(a);
+    const size_t smem = (size_t)a.E * sizeof(float);
+    k_topk<<<(unsigned)M, 128, smem, s>>>(a);
     return 1;
 }
 
@@ -736,53 +770,71 @@ int launch_bucket(const int* slot_expert, int64_t P, int K, int E, const BucketO
 // moe_out[t][r] = sum over slots k (in slot order) of w_k * y[pair(t,k)][r]
 // (moe_kernels.mojo:775-779, diffusion_kernels.mojo:386-399), then optionally
 // rms_norm with post_feedforward_layernorm_2 (model_speculative_moe_batched
-// .mojo:1144-1150) and fp16 rounding.
+// .mojo:1144-1150) and fp16 rounding.  float4 per thread, d % 4 == 0.
 __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
-    extern __shared__ float4 smem4[];
-    float* row = reinterpret_cast<float*>(smem4);
     __shared__ float red[33];
     __shared__ int sp[32];
     __shared__ float sw[32];
-    const int t = blockIdx.x;
+    const int64_t t = blockIdx.x;
     const int K = a.K;
     if (threadIdx.x < K) {
-        sp[threadIdx.x] = a.slot_pair[(size_t)t * K + threadIdx.x];
-        sw[threadIdx.x] = a.slot_weight[(size_t)t * K + threadIdx.x];
+        sp[threadIdx.x] = a.slot_pair[t * K + threadIdx.x];
+        sw[threadIdx.x] = a.slot_weight[t * K + threadIdx.x];
     }
     __syncthreads();
+    const int64_t d4 = a.d / 4;
+    constexpr int MAXV = 12;  // d <= 12288 keeps the row in registers
+    float4 acc[MAXV];
     float ss = 0.f;
-    for (int64_t j = threadIdx.x; j < a.d; j += blockDim.x) {
-        float s = 0.f;
-        for (int k = 0; k < K; ++k) {
-            const int p = sp[k];
-            if (p >= 0) {
-                const float y = a.y[(size_t)p * a.d + j];
-                s = a.fma_mode ? fmaf(y, sw[k], s) : __fadd_rn(s, __fmul_rn(y, sw[k]));
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int64_t j = threadIdx.x + (int64_t)i * blockDim.x;
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < d4) {
+            for (int k = 0; k < K; ++k) {
+                const int p = sp[k];
+                if (p < 0) continue;
+                const float4 y = __ldg(reinterpret_cast<const float4*>(a.y + (size_t)p * a.d) + j);
+                const float w = sw[k];
+                if (a.fma_mode) {
+                    s.x = fmaf(y.x, w, s.x); s.y = fmaf(y.y, w, s.y);
+                    s.z = fmaf(y.z, w, s.z); s.w = fmaf(y.w, w, s.w);
+                } else {
+                    s.x = __fadd_rn(s.x, __fmul_rn(y.x, w)); s.y = __fadd_rn(s.y, __fmul_rn(y.y, w));
+                    s.z = __fadd_rn(s.z, __fmul_rn(y.z, w)); s.w = __fadd_rn(s.w, __fmul_rn(y.w, w));
+                }
             }
+            ss += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
         }
-        row[j] = s;
-        ss += s * s;
+        acc[i] = s;
     }
     float inv = 1.f;
     if (a.post_norm) {
         ss = block_sum(ss, red);
         inv = 1.0f / sqrtf(ss / (float)a.d + 1e-6f);
     }
-    for (int64_t j = threadIdx.x; j < a.d; j += blockDim.x) {
-        float v = row[j];
-        if (a.post_norm) v = v * inv * a.post_w[j];
-        if (a.out_f16)
-            reinterpret_cast<__half*>(a.out)[(size_t)t * a.d + j] = __float2half_rn(v);
-        else
-            reinterpret_cast<float*>(a.out)[(size_t)t * a.d + j] = v;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int64_t j = threadIdx.x + (int64_t)i * blockDim.x;
+        if (j >= d4) continue;
+        float4 v = acc[i];
+        if (a.post_norm) {
+            const float4 w = __ldg(reinterpret_cast<const float4*>(a.post_w) + j);
+            v.x = v.x * inv * w.x; v.y = v.y * inv * w.y; v.z = v.z * inv * w.z; v.w = v.w * inv * w.w;
+        }
+        if (a.out_f16) {
+            __half2* o = reinterpret_cast<__half2*>(a.out) + (t * a.d) / 2 + 2 * j;
+            o[0] = __floats2half2_rn(v.x, v.y);
+            o[1] = __floats2half2_rn(v.z, v.w);
+        } else {
+            reinterpret_cast<float4*>(a.out)[(t * a.d) / 4 + j] = v;
+        }
     }
 }
 
 int launch_combine(const CombineArgs& a, int64_t M, cudaStream_t s) {
     if (M <= 0) return 0;
-    const size_t smem = (size_t)a.d * sizeof(float);
-    cudaFuncSetAttribute(k_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_combine<<<(unsigned)M, 256, smem, s>>>(a);
+    k_combine<<<(unsigned)M, 256, 0, s>>>(a);
     return 1;
 }
 
