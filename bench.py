@@ -224,7 +224,8 @@ def workload_config(args, M):
             "tokens_per_step": M, "embed_dim": D, "expert_mlp_dim": F, "num_experts": E, "top_k": K,
             "layers_cycled": args.layers,
             "l2": f"weights of {args.layers} distinct layers cycled per step ({args.layers * 476} MB > 126 MB L2)",
-            "post_norm": True, "parallelism": f"replicas x{dist_setup()[0]}"}
+            "post_norm": True, "parallelism": f"replicas x{dist_setup()[0]}",
+            "gemm_path": getattr(args, "path", "auto")}
 
 
 # ----------------------------------------------------------------- GPU leg
@@ -238,6 +239,8 @@ def main():
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"],
+                    help="expert/dense GEMM path: CUDA-core GEMV, tcgen05, or automatic")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = dist_setup()
@@ -260,6 +263,7 @@ def main():
     ctx = MB.Context(local)
     stream = torch.cuda.current_stream()
     ctx.set_stream(stream.cuda_stream)
+    ctx.set_gemm_path({"auto": MB.PATH_AUTO, "gemv": MB.PATH_GEMV, "tc": MB.PATH_TC}[args.path])
     M = WORKLOADS[args.workload]
 
     layers, descs = [], []
@@ -366,11 +370,14 @@ def main():
     # roofline of the dominant kernel (largest share of profiled time)
     hbm, _, src = peaks()
     u_mean = sum(uniq) / len(uniq)
-    dom = max((kv for kv in prof.items() if kv[0] in ("gemv_gate_up", "gemv_down", "q4_matmul")),
+    dom = max((kv for kv in prof.items() if kv[0] in ("gemv_gate_up", "gemv_down", "q4_matmul",
+                                                       "tc_gate_up", "tc_down")),
               key=lambda kv: kv[1][0])[0] if prof else None
     alg = {
         "gemv_gate_up": u_mean * GU_BYTES + M * D * 4 + M * K * F * 4,
         "gemv_down": u_mean * DN_BYTES + M * K * F * 4 + M * K * D * 4,
+        "tc_gate_up": u_mean * GU_BYTES + M * K * D * 2 + M * K * F * 2,
+        "tc_down": u_mean * DN_BYTES + M * K * F * 2 + M * K * D * 4,
         "q4_matmul": sum(q4_bytes(ci, co) + M * (ci + co) * 4 for (_, _, ci, co) in dense.values()) / max(1, len(dense)),
         "router": ROUTER_BYTES + M * D * 4 + M * E * 4,
         "prep": 4 * M * D * 4,

@@ -80,6 +80,19 @@ int moe_set_async(moe_ctx* ctx, int async_mode);
  * (kfd_gpu.mojo:1216-1260), which raise after a bounded poll. */
 int moe_wait(moe_ctx* ctx, uint64_t timeout_ns);
 
+/* Context options (moe_set_option). */
+enum moe_option {
+    MOE_OPT_GEMM_PATH = 1,        /* value: moe_gemm_path */
+    MOE_OPT_TC_MIN_TOKENS = 2,    /* auto path: tensor cores from this many tokens (default 8) */
+    MOE_OPT_DEVICE_TIMEOUT_NS = 3 /* deadline of every device-side wait (default 4 s) */
+};
+enum moe_gemm_path {
+    MOE_PATH_AUTO = 0, /* CUDA-core GEMV for few tokens, tensor cores above the threshold */
+    MOE_PATH_GEMV = 1, /* always the CUDA-core grouped GEMV (fp32 arithmetic) */
+    MOE_PATH_TC = 2    /* always the tcgen05 grouped GEMM (fp16 operands, fp32 accumulate) */
+};
+int moe_set_option(moe_ctx* ctx, int option, int64_t value);
+
 /* Per-kernel timing with CUDA events recorded on the launching stream
  * around each kernel of the path (off by default; the reference's
  * perf_counter phase accumulators, model_speculative_moe.mojo:732-734, are

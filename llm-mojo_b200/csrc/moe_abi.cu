@@ -13,6 +13,7 @@
 
 #include "../../include/moe_b200.h"
 #include "moe_internal.h"
+#include "moe_tc.h"
 
 namespace {
 
@@ -51,6 +52,9 @@ struct moe_ctx {
     int num_sms = 148;
     std::vector<CopyBack> pending;
     cudaEvent_t done = nullptr;
+    int gemm_path = MOE_PATH_AUTO;       // moe_set_option(MOE_OPT_GEMM_PATH)
+    int tc_min_tokens = 8;               // auto: tensor cores from this many tokens
+    uint64_t device_timeout_ns = 4000000000ull;
     // profiling (moe_profile_enable)
     int profile = 0;
     std::vector<cudaEvent_t> ev_pool;
@@ -210,6 +214,17 @@ int begin(moe_ctx* ctx) {
     return MOE_OK;
 }
 
+// Device error word: 1 = bad expert index in a routing array, 2 = a bounded
+// device-side wait expired.
+int check_flag(moe_ctx* ctx) {
+    int flag = 0;
+    MOE_CUDA(cudaMemcpy(&flag, ctx->err_flag, sizeof(int), cudaMemcpyDeviceToHost));
+    if (!flag) return MOE_OK;
+    MOE_CUDA(cudaMemset(ctx->err_flag, 0, sizeof(int)));
+    if (flag == 2) return fail(ctx, MOE_E_TIMEOUT, "a device-side wait exceeded its deadline");
+    return fail(ctx, MOE_E_ARG, "expert index out of range in a routing array");
+}
+
 // Launch-error check, copy-back of staged outputs, optional completion.
 int finish(moe_ctx* ctx) {
     MOE_CUDA(cudaGetLastError());
@@ -219,17 +234,13 @@ int finish(moe_ctx* ctx) {
     MOE_CUDA(cudaEventRecord(ctx->done, ctx->stream));
     if (!ctx->async_mode) {
         MOE_CUDA(cudaEventSynchronize(ctx->done));
-        int flag = 0;
-        MOE_CUDA(cudaMemcpy(&flag, ctx->err_flag, sizeof(int), cudaMemcpyDeviceToHost));
-        if (flag) {
-            MOE_CUDA(cudaMemset(ctx->err_flag, 0, sizeof(int)));
-            return fail(ctx, MOE_E_ARG, "expert index out of range in a routing array");
-        }
+        return check_flag(ctx);
     }
     return MOE_OK;
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+bool al8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
 
 int check_q4_shape(moe_ctx* ctx, int64_t K, int64_t rows) {
     if (K <= 0 || K % 32 != 0) return fail(ctx, MOE_E_SHAPE, "inner dimension must be a positive multiple of 32");
@@ -247,12 +258,16 @@ struct ExpertBufs {
     float* xsum;  // [M][d/32] 1.5 * block sums of x32
     float* act;   // [P][F]
     float* y;     // [P][d]
+    __half* x16;  // [P][d]   tensor-core path: gathered gate/up input
+    __half* a16;  // [P][F]   tensor-core path: activations (down input)
+    int* tt_prefix;  // [E+1]
 };
 
 size_t expert_bufs_bytes(int64_t M, int64_t K, int64_t d, int64_t F, int64_t E) {
     const int64_t P = M * K;
     return al(P * 4) * 2 + al(16) + al(E * 4) * 3 + al(P * 4) * 3 + al(M * d * 4) +
-           al(M * d / 32 * 4) + al(P * F * 4) + al(P * d * 4);
+           al(M * d / 32 * 4) + al(P * F * 4) + al(P * d * 4) + al(P * d * 2) + al(P * F * 2) +
+           al((E + 1) * 4);
 }
 
 int take_expert_bufs(moe_ctx* ctx, int64_t M, int64_t K, int64_t d, int64_t F, int64_t E,
@@ -271,7 +286,10 @@ int take_expert_bufs(moe_ctx* ctx, int64_t M, int64_t K, int64_t d, int64_t F, i
     o->xsum = (float*)ws_take(ctx, M * d / 32 * 4);
     o->act = (float*)ws_take(ctx, P * F * 4);
     o->y = (float*)ws_take(ctx, P * d * 4);
-    if (!o->y) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+    o->x16 = (__half*)ws_take(ctx, P * d * 2);
+    o->a16 = (__half*)ws_take(ctx, P * F * 2);
+    o->tt_prefix = (int*)ws_take(ctx, (E + 1) * 4);
+    if (!o->tt_prefix) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
     return MOE_OK;
 }
 
@@ -297,6 +315,16 @@ int prep_rows(moe_ctx* ctx, const void* X, int x_layout, int x_f16, int64_t M, i
     return MOE_OK;
 }
 
+// Tensor cores for the expert GEMMs: forced by the option, or (auto) from
+// tc_min_tokens tokens on, when shapes and alignments allow.
+bool use_tc(moe_ctx* ctx, int64_t M, int64_t d, int64_t F, const ExpertWeights& w) {
+    if (ctx->gemm_path == MOE_PATH_GEMV) return false;
+    if (!moe::tc_supported(d, 2 * F, 1, F) || !moe::tc_supported(F, d, 0, F)) return false;
+    if (!al16(w.gu_p) || !al16(w.dn_p) || !al8(w.gu_s) || !al8(w.dn_s)) return false;
+    if (ctx->gemm_path == MOE_PATH_TC) return true;
+    return M >= ctx->tc_min_tokens;
+}
+
 // slot table -> bucket -> gate/up (+act) -> down -> combine.  bb.x32 and
 // bb.xsum must hold the gate/up input (prep_rows or the router's prep).
 int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int64_t d, int64_t F,
@@ -310,6 +338,61 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     const int max_u = (int)std::min<int64_t>(E, P);
     const int max_t = (int)std::max<int64_t>(1, M);
 
+    if (use_tc(ctx, M, d, F, w)) {
+        // token tile from the mean load of an active expert
+        const int64_t mean = (P + max_u - 1) / max_u;
+        int BN = 16;
+        while (BN < 256 && BN < mean) BN *= 2;
+        ctx->launches += moe::launch_tt_prefix(bb.b.meta, bb.b.seg_count, BN, bb.tt_prefix, s);
+        {
+            ProfScope ps(ctx, "gather");
+            ctx->launches += moe::launch_gather_f16(bb.x32, d, bb.b.pair_token, bb.b.meta, P, 0, bb.x16, s);
+        }
+        moe::TcLaunch t1;
+        t1.a.Ws = w.gu_s;
+        t1.a.K = (int)d;
+        t1.a.R = 2 * F;
+        t1.a.F = (int)F;
+        t1.a.act = act;
+        t1.a.meta = bb.b.meta;
+        t1.a.unique_expert = bb.b.unique_expert;
+        t1.a.seg_start = bb.b.seg_start;
+        t1.a.seg_count = bb.b.seg_count;
+        t1.a.tt_prefix = bb.tt_prefix;
+        t1.a.act_out = bb.a16;
+        t1.a.err_flag = ctx->err_flag;
+        t1.a.timeout_ns = ctx->device_timeout_ns;
+        t1.Wp = w.gu_p;
+        t1.total_rows = E * 2 * F;
+        t1.B = bb.x16;
+        t1.b_rows = P;
+        t1.BN = BN;
+        t1.max_items = (int64_t)(F / 64) * (max_u + (P + BN - 1) / BN);
+        int r;
+        {
+            ProfScope ps(ctx, "tc_gate_up");
+            r = moe::launch_tc_gemm(moe::TC_ACT, t1, ctx->num_sms, s);
+        }
+        if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core GEMM setup failed (gate/up)");
+        ctx->launches += r;
+        moe::TcLaunch t2 = t1;
+        t2.a.Ws = w.dn_s;
+        t2.a.K = (int)F;
+        t2.a.R = d;
+        t2.a.act_out = nullptr;
+        t2.a.y_out = bb.y;
+        t2.a.y_stride = d;
+        t2.Wp = w.dn_p;
+        t2.total_rows = E * d;
+        t2.B = bb.a16;
+        t2.max_items = ((d + 127) / 128) * (max_u + (P + BN - 1) / BN);
+        {
+            ProfScope ps(ctx, "tc_down");
+            r = moe::launch_tc_gemm(moe::TC_PLAIN, t2, ctx->num_sms, s);
+        }
+        if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core GEMM setup failed (down)");
+        ctx->launches += r;
+    } else {
     moe::GemvArgs g1;
     g1.Wp = w.gu_p;
     g1.Ws = w.gu_s;
@@ -346,6 +429,7 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     {
         ProfScope ps(ctx, "gemv_down");
         ctx->launches += moe::launch_gemv(moe::GEMV_PLAIN, g2, ctx->num_sms, s);
+    }
     }
 
     moe::CombineArgs c = *comb_tmpl;
@@ -452,13 +536,27 @@ int moe_wait(moe_ctx* ctx, uint64_t timeout_ns) {
         }
         std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
-    int flag = 0;
-    MOE_CUDA(cudaMemcpy(&flag, ctx->err_flag, sizeof(int), cudaMemcpyDeviceToHost));
-    if (flag) {
-        MOE_CUDA(cudaMemset(ctx->err_flag, 0, sizeof(int)));
-        return fail(ctx, MOE_E_ARG, "expert index out of range in a routing array");
+    return check_flag(ctx);
+}
+
+int moe_set_option(moe_ctx* ctx, int option, int64_t value) {
+    if (!ctx) return MOE_E_ARG;
+    switch (option) {
+        case MOE_OPT_GEMM_PATH:
+            if (value < MOE_PATH_AUTO || value > MOE_PATH_TC) return fail(ctx, MOE_E_ARG, "bad path");
+            ctx->gemm_path = (int)value;
+            return MOE_OK;
+        case MOE_OPT_TC_MIN_TOKENS:
+            if (value < 1) return fail(ctx, MOE_E_ARG, "bad token threshold");
+            ctx->tc_min_tokens = (int)value;
+            return MOE_OK;
+        case MOE_OPT_DEVICE_TIMEOUT_NS:
+            if (value <= 0) return fail(ctx, MOE_E_ARG, "bad timeout");
+            ctx->device_timeout_ns = (uint64_t)value;
+            return MOE_OK;
+        default:
+            return fail(ctx, MOE_E_ARG, "unknown option");
     }
-    return MOE_OK;
 }
 
 int moe_profile_enable(moe_ctx* ctx, int on) {
@@ -561,7 +659,7 @@ int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch, const uint8_t* W, const fl
     TRY(check_q4_shape(ctx, c_in, c_out));
     if (batch <= 0) return fail(ctx, MOE_E_SHAPE, "batch_size must be >= 1");
     if (batch > (1 << 20)) return fail(ctx, MOE_E_SHAPE, "batch_size too large");
-    TRY(ws_reserve(ctx, al(batch * c_in * 4) * 2 + al(batch * c_out * 4)));
+    TRY(ws_reserve(ctx, al(batch * c_in * 4) * 2 + al(batch * c_out * 4) + al(batch * c_in * 2)));
     void *w, *sc, *xd, *od;
     TRY(dev_ptr(ctx, W, c_out * c_in / 2, K_W, &w));
     TRY(dev_ptr(ctx, S, c_out * c_in / 32 * 4, K_W, &sc));
@@ -572,6 +670,38 @@ int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch, const uint8_t* W, const fl
         float* xc = (float*)ws_take(ctx, batch * c_in * 4);
         TRY(prep_rows(ctx, xd, MOE_X_NATURAL, 0, batch, c_in, xc, nullptr));
         xd = xc;
+    }
+    const bool tc = ctx->gemm_path != MOE_PATH_GEMV && moe::tc_supported(c_in, c_out, 0, 0) &&
+                    al8(sc) && (ctx->gemm_path == MOE_PATH_TC || batch >= ctx->tc_min_tokens);
+    if (tc) {
+        __half* x16 = (__half*)ws_take(ctx, batch * c_in * 2);
+        ctx->launches += moe::launch_gather_f16((const float*)xd, c_in, nullptr, nullptr, batch, (int)batch,
+                                                x16, ctx->stream);
+        moe::TcLaunch t;
+        t.a.Ws = (const float*)sc;
+        t.a.K = (int)c_in;
+        t.a.R = c_out;
+        t.a.dense_tokens = (int)batch;
+        t.a.y_out = (float*)od;
+        t.a.y_stride = c_out;
+        t.a.err_flag = ctx->err_flag;
+        t.a.timeout_ns = ctx->device_timeout_ns;
+        t.Wp = (const uint8_t*)w;
+        t.total_rows = c_out;
+        t.B = x16;
+        t.b_rows = batch;
+        int BN = 16;
+        while (BN < 256 && BN < batch) BN *= 2;
+        t.BN = BN;
+        t.max_items = ((c_out + 127) / 128) * ((batch + BN - 1) / BN);
+        int r;
+        {
+            ProfScope ps(ctx, "q4_matmul");
+            r = moe::launch_tc_gemm(moe::TC_PLAIN, t, ctx->num_sms, ctx->stream);
+        }
+        if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core GEMM setup failed");
+        ctx->launches += r;
+        return finish(ctx);
     }
     moe::GemvArgs g;
     g.Wp = (const uint8_t*)w;

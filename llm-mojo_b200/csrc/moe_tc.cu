@@ -1,0 +1,650 @@
+// moe_tc.cu -- tensor-core grouped Q4_0 GEMM for sm_100a (tcgen05 + TMA).
+//
+// D[rows][tokens] = W_e[rows][K] . X[tokens][K]^T for every (expert, row
+// tile, token tile) work item of a device-side list, "swap-AB": the weight
+// rows are the MMA's M = 128, the tokens its N = BN.
+//
+// Warp roles (320 threads):
+//   warp 0     TMA producer: packed Q4 tiles (SWIZZLE_32B) and fp16
+//              activation tiles (SWIZZLE_128B) into smem rings.
+//   warp 1     TMEM owner and single-thread tcgen05.mma issuer; fp32
+//              accumulators live in TMEM, double-buffered across items.
+//   warps 2-5  dequant: thread t turns row t's 64 nibbles of a k-tile into
+//              fp16 ((n-8)*scale computed in fp32, one rounding) and stores
+//              them in the UMMA K-major SWIZZLE_128B layout.
+//   warps 6-9  epilogue: tcgen05.ld of the accumulator; ACT mode pairs gate
+//              and up rows with a warp shuffle and writes the activated
+//              result as fp16, PLAIN mode writes fp32 rows.
+//
+// ACT tiles cover 64 act rows: TMA brings the 64 gate rows and the 64 up
+// rows as two boxes; A-tile row t = 32q + l holds gate row 16q + l (l < 16)
+// or up row 16q + l - 16 (l >= 16), so each TMEM lane quarter q (the lanes
+// one epilogue warp may read) has a gate row and its up row 16 lanes apart.
+//
+// Inside every 8-element group of K, both operands are stored in the order
+// [0,4,1,5,2,6,3,7]: the dequantiser produces nibble pairs (k, k+4) of a
+// 32-bit word with one mask, and the activations are written in the same
+// order (k_gather_f16 and the ACT epilogue), so the contraction is unchanged.
+//
+// Every mbarrier wait is bounded (globaltimer deadline); on expiry the kernel
+// raises err_flag = 2, every role drains what it issued and the CTA frees
+// its TMEM and returns.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "moe_tc.h"
+
+namespace moe {
+namespace tc {
+
+// ------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t a, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t a) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+struct Guard {
+    volatile int* abort;  // shared flag
+    int* err;
+    uint64_t deadline;
+};
+
+// Waits for the phase of `parity`; false when the deadline passed or another
+// role aborted (then the caller stops issuing work).
+__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, const Guard& g) {
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try(a, parity)) return true;
+        if ((it & 255u) == 255u) {
+            if (*g.abort) return false;
+            if (globaltimer() > g.deadline) {
+                *g.abort = 1;
+                atomicExch(g.err, 2);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t mbar,
+                                            int32_t x, int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(mbar), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// tcgen05.ld 32 lanes x 32 bit, N consecutive columns per thread
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// UMMA shared-memory descriptor: K-major, SWIZZLE_128B, 8-row groups of
+// 1024 bytes (SBO = 1024), version 1 (sm_100), LBO unused (1).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;                 // LBO (ignored for swizzled K-major)
+    d |= (uint64_t)(1024u >> 4) << 32;       // SBO
+    d |= (uint64_t)1u << 46;                 // version
+    d |= (uint64_t)2u << 61;                 // SWIZZLE_128B
+    return d;
+}
+// Instruction descriptor, kind::f16: D f32, A f16, B f16, both K-major.
+__host__ __device__ constexpr uint32_t f16_idesc(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// position of K element m (0..7) inside its group of 8
+__device__ __forceinline__ int kpos(int m) { return m < 4 ? 2 * m : 2 * (m - 4) + 1; }
+
+// ---------------------------------------------------------------- layout
+constexpr int SQ = 8;             // Q4 ring stages (4 KB each)
+constexpr int SA = 3;             // fp16 A ring stages (16 KB each)
+constexpr int SB = 4;             // activation ring stages (BN * 128 B each)
+constexpr int KT = 64;            // K per k-tile
+constexpr int THREADS = 320;
+
+template <int BN>
+struct Smem {
+    static constexpr int A_BYTES = 128 * KT * 2;          // 16384
+    static constexpr int B_BYTES = BN * KT * 2;
+    static constexpr int Q_BYTES = 128 * KT / 2;          // 4096
+    static constexpr int OFF_A = 0;
+    static constexpr int OFF_B = OFF_A + SA * A_BYTES;
+    static constexpr int OFF_Q = OFF_B + SB * B_BYTES;
+    static constexpr int OFF_BAR = OFF_Q + SQ * Q_BYTES;
+    static constexpr int N_BAR = 2 * SQ + 2 * SA + 2 * SB + 4 + 1;
+    static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
+    static constexpr int TOTAL = OFF_MISC + 16 + 1024;    // + alignment slack
+};
+
+__host__ __device__ constexpr uint32_t tmem_cols(int BN) {
+    return (2 * BN) <= 32 ? 32u : (2 * BN) <= 64 ? 64u : (2 * BN) <= 128 ? 128u : (2 * BN) <= 256 ? 256u : 512u;
+}
+
+// ------------------------------------------------------------ work list
+struct Item {
+    int u, e, rt, tt, n, s0;
+};
+
+__device__ __forceinline__ bool decode_item(const TcArgs& a, int64_t item, int row_tiles, int BN,
+                                            Item& it) {
+    if (a.dense_tokens > 0) {
+        const int ntt = (a.dense_tokens + BN - 1) / BN;
+        if (item >= (int64_t)row_tiles * ntt) return false;
+        it.u = 0;
+        it.e = 0;
+        it.rt = (int)(item / ntt);
+        it.tt = (int)(item - (int64_t)it.rt * ntt);
+        it.n = a.dense_tokens;
+        it.s0 = 0;
+        return true;
+    }
+    const int U = a.meta[0];
+    const int64_t total = (int64_t)row_tiles * a.tt_prefix[U];
+    if (item >= total) return false;
+    int lo = 0, hi = U - 1;  // last u with row_tiles * tt_prefix[u] <= item
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if ((int64_t)row_tiles * a.tt_prefix[mid] <= item) lo = mid;
+        else hi = mid - 1;
+    }
+    const int u = lo;
+    const int ntt = a.tt_prefix[u + 1] - a.tt_prefix[u];
+    const int64_t rem = item - (int64_t)row_tiles * a.tt_prefix[u];
+    it.u = u;
+    it.e = a.unique_expert[u];
+    it.rt = (int)(rem / ntt);
+    it.tt = (int)(rem - (int64_t)it.rt * ntt);
+    it.n = a.seg_count[u];
+    it.s0 = a.seg_start[u];
+    return true;
+}
+
+// -------------------------------------------------------------- kernel
+template <int MODE, int BN>
+__global__ void __launch_bounds__(THREADS, 1)
+    k_tc_gemm(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap bmap, TcArgs a) {
+    using L = Smem<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+    const uint32_t bar0 = smem_u32(bars);
+    auto q_full = [&](int s) { return bar0 + 8u * s; };
+    auto q_empty = [&](int s) { return bar0 + 8u * (SQ + s); };
+    auto a_full = [&](int s) { return bar0 + 8u * (2 * SQ + s); };
+    auto a_empty = [&](int s) { return bar0 + 8u * (2 * SQ + SA + s); };
+    auto b_full = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + s); };
+    auto b_empty = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + SB + s); };
+    auto acc_full = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + 2 * SB + s); };
+    auto acc_empty = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + 2 * SB + 2 + s); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * SQ + 2 * SA + 2 * SB + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int K = a.K, nk = K / KT, nb = K / 32;
+    const int row_tiles = (MODE == TC_ACT) ? (a.F / 64) : (int)((a.R + 127) / 128);
+    constexpr uint32_t NCOL = tmem_cols(BN);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SQ; ++s) {
+            mbar_init(q_full(s), 1);
+            mbar_init(q_empty(s), 4);
+        }
+        for (int s = 0; s < SA; ++s) {
+            mbar_init(a_full(s), 4);
+            mbar_init(a_empty(s), 1);
+        }
+        for (int s = 0; s < SB; ++s) {
+            mbar_init(b_full(s), 1);
+            mbar_init(b_empty(s), 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(acc_full(s), 1);
+            mbar_init(acc_empty(s), 4);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        prefetch_tmap(&qmap);
+        prefetch_tmap(&bmap);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(NCOL)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    Guard G{abort_flag, a.err_flag, globaltimer() + a.timeout_ns};
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int qs = 0, bs = 0;
+            uint32_t qp = 0, bp = 0;
+            uint32_t q_armed = 0, b_armed = 0;  // stages armed in their current phase
+            uint32_t q_par[SQ], b_par[SB];
+            Item it;
+            bool ok = true;
+            for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
+                int row_a, row_b;  // first weight rows of the two 64-row halves
+                if (MODE == TC_ACT) {
+                    row_a = (int)((int64_t)it.e * a.R + it.rt * 64);
+                    row_b = (int)((int64_t)it.e * a.R + a.F + it.rt * 64);
+                } else {
+                    row_a = (int)((int64_t)it.e * a.R + it.rt * 128);
+                    row_b = row_a + 64;
+                }
+                const int tok_row = it.s0 + it.tt * BN;
+                for (int kt = 0; kt < nk; ++kt) {
+                    if (!(ok = mbar_wait(q_empty(qs), qp ^ 1, G))) break;
+                    uint8_t* qd = smem + L::OFF_Q + qs * L::Q_BYTES;
+                    mbar_expect_tx(q_full(qs), L::Q_BYTES);
+                    tma_load_2d(smem_u32(qd), &qmap, q_full(qs), kt * (KT / 2), row_a);
+                    tma_load_2d(smem_u32(qd + L::Q_BYTES / 2), &qmap, q_full(qs), kt * (KT / 2), row_b);
+                    q_armed |= 1u << qs;
+                    q_par[qs] = qp;
+                    if (++qs == SQ) { qs = 0; qp ^= 1; }
+                    if (!(ok = mbar_wait(b_empty(bs), bp ^ 1, G))) break;
+                    uint8_t* bd = smem + L::OFF_B + bs * L::B_BYTES;
+                    mbar_expect_tx(b_full(bs), L::B_BYTES);
+                    tma_load_2d(smem_u32(bd), &bmap, b_full(bs), kt * KT, tok_row);
+                    b_armed |= 1u << bs;
+                    b_par[bs] = bp;
+                    if (++bs == SB) { bs = 0; bp ^= 1; }
+                }
+            }
+            // drain: every armed stage's bytes must have landed before exit
+            Guard Gd{abort_flag, a.err_flag, globaltimer() + a.timeout_ns};
+            volatile int no_abort = 0;
+            Gd.abort = &no_abort;
+            for (int s = 0; s < SQ; ++s)
+                if (q_armed & (1u << s)) mbar_wait(q_full(s), q_par[s], Gd);
+            for (int s = 0; s < SB; ++s)
+                if (b_armed & (1u << s)) mbar_wait(b_full(s), b_par[s], Gd);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int as = 0, bs = 0, ab = 0;
+            uint32_t ap = 0, bp = 0, accp = 0;
+            constexpr uint32_t IDESC = f16_idesc(128, BN);
+            Item it;
+            bool ok = true, issued = false;
+            for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
+                if (!(ok = mbar_wait(acc_empty(ab), accp ^ 1, G))) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(ab * BN);
+                for (int kt = 0; kt < nk; ++kt) {
+                    if (!(ok = mbar_wait(a_full(as), ap, G))) break;
+                    if (!(ok = mbar_wait(b_full(bs), bp, G))) break;
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + L::OFF_A + as * L::A_BYTES);
+                    const uint32_t sb = smem_u32(smem + L::OFF_B + bs * L::B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < KT / 16; ++k)
+                        tc_mma(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), IDESC,
+                               (kt | k) != 0);
+                    issued = true;
+                    tc_commit(a_empty(as));
+                    tc_commit(b_empty(bs));
+                    if (++as == SA) { as = 0; ap ^= 1; }
+                    if (++bs == SB) { bs = 0; bp ^= 1; }
+                }
+                if (!ok) break;
+                tc_commit(acc_full(ab));
+                if (++ab == 2) { ab = 0; accp ^= 1; }
+            }
+            if (issued) {  // all MMAs complete before TMEM is released
+                tc_commit(drain_bar);
+                Guard Gd{abort_flag, a.err_flag, globaltimer() + a.timeout_ns};
+                volatile int no_abort = 0;
+                Gd.abort = &no_abort;
+                mbar_wait(drain_bar, 0, Gd);
+            }
+        }
+    } else if (warp < 6) {
+        // ------------------------------------------------ dequant
+        const int t = threadIdx.x - 64;  // row of the A tile
+        int qs = 0, as = 0;
+        uint32_t qp = 0, ap = 0;
+        Item it;
+        bool ok = true;
+        for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
+            int64_t grow;  // global weight row of this thread
+            int sr;        // its row in the Q4 stage (gate box rows 0-63, up box 64-127)
+            if (MODE == TC_ACT) {
+                const int qq = t >> 5, l = t & 31;
+                const int g = 16 * qq + (l & 15);
+                sr = (l < 16) ? g : 64 + g;
+                grow = (int64_t)it.e * a.R + (l < 16 ? it.rt * 64 + g : a.F + it.rt * 64 + g);
+            } else {
+                sr = t;
+                grow = (int64_t)it.e * a.R + it.rt * 128 + t;
+            }
+            const bool row_ok = (MODE == TC_ACT) || (it.rt * 128 + t < a.R);
+            const float* srow = a.Ws + grow * nb;
+            float2 sreg[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                sreg[j] = (row_ok && j < nk) ? __ldg(reinterpret_cast<const float2*>(srow) + j) : make_float2(0.f, 0.f);
+            for (int kt0 = 0; kt0 < nk && ok; kt0 += 4) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int kt = kt0 + j;
+                    if (kt >= nk) break;
+                    const float2 s = sreg[j];
+                    if (row_ok && kt + 4 < nk) sreg[j] = __ldg(reinterpret_cast<const float2*>(srow) + kt + 4);
+                    if (!(ok = mbar_wait(q_full(qs), qp, G))) break;
+                    if (!(ok = mbar_wait(a_empty(as), ap ^ 1, G))) break;
+                    const uint8_t* qrow = smem + L::OFF_Q + qs * L::Q_BYTES + sr * 32;
+                    const int sw = ((sr >> 2) & 1) << 4;  // SWIZZLE_32B: chunk ^= row bit 2
+                    const uint4 c0 = *reinterpret_cast<const uint4*>(qrow + (0 ^ sw));
+                    const uint4 c1 = *reinterpret_cast<const uint4*>(qrow + (16 ^ sw));
+                    const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                    uint8_t* arow = smem + L::OFF_A + as * L::A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
+#pragma unroll
+                    for (int w = 0; w < 8; ++w) {
+                        const float sc = (w < 4) ? s.x : s.y;
+                        uint32_t h[4];
+#pragma unroll
+                        for (int p = 0; p < 4; ++p) {
+                            const uint32_t v = (wv[w] >> (4 * p)) & 0x000F000Fu;
+                            const float lo = (__uint_as_float(0x4B000000u | (v & 0xFFFFu)) - 8388616.0f) * sc;
+                            const float hi = (__uint_as_float(0x4B000000u | (v >> 16)) - 8388616.0f) * sc;
+                            const __half2 hh = __floats2half2_rn(lo, hi);
+                            h[p] = *reinterpret_cast<const uint32_t*>(&hh);
+                        }
+                        *reinterpret_cast<uint4*>(arow + ((w ^ (t & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+                    }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(a_full(as));
+                        mbar_arrive(q_empty(qs));
+                    }
+                    if (++qs == SQ) { qs = 0; qp ^= 1; }
+                    if (++as == SA) { as = 0; ap ^= 1; }
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------ epilogue
+        const int q = warp & 3;       // TMEM lane quarter this warp may access
+        const int i = q * 32 + lane;  // accumulator row (A-tile row)
+        constexpr int CW = BN < 32 ? BN : 32;
+        int ab = 0;
+        uint32_t accp = 0;
+        Item it;
+        bool ok = true;
+        for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
+            ok = mbar_wait(acc_full(ab), accp, G);
+            tc_fence_after();
+            const int nv = min(BN, it.n - it.tt * BN);
+            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+            for (int c0 = 0; ok && c0 < nv; c0 += CW) {
+                float v[CW];
+                tmem_ld<CW>(tbase + c0, v);
+                if (MODE == TC_ACT) {
+                    const int j = it.rt * 64 + 16 * q + (lane & 15);  // act row
+                    const int jp = (j & ~7) | kpos(j & 7);
+#pragma unroll
+                    for (int cc = 0; cc < CW; ++cc) {
+                        const float up = __shfl_down_sync(0xffffffffu, v[cc], 16);
+                        if (lane < 16 && c0 + cc < nv) {
+                            const int p = it.s0 + it.tt * BN + c0 + cc;
+                            a.act_out[(int64_t)p * a.F + jp] = __float2half_rn(act_fn(v[cc], up, a.act));
+                        }
+                    }
+                } else {
+                    const int64_t r = (int64_t)it.rt * 128 + i;
+                    if (r < a.R) {
+#pragma unroll
+                        for (int cc = 0; cc < CW; ++cc) {
+                            if (c0 + cc < nv) {
+                                const int p = it.s0 + it.tt * BN + c0 + cc;
+                                const int64_t orow = a.out_row ? a.out_row[p] : p;
+                                a.y_out[orow * a.y_stride + r] = v[cc];
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty(ab));
+            if (++ab == 2) { ab = 0; accp ^= 1; }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(NCOL) : "memory");
+}
+
+// ---------------------------------------------------------- helpers
+// Token tiles per unique expert -> exclusive prefix (one CTA, U <= 1024).
+__global__ void __launch_bounds__(1024) k_tt_prefix(const int* meta, const int* seg_count, int BN,
+                                                    int* tt_prefix) {
+    __shared__ int wsum[32];
+    const int U = meta[0];
+    const int tid = threadIdx.x;
+    const int v = tid < U ? (seg_count[tid] + BN - 1) / BN : 0;
+    const int lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+        int w = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < nw) wsum[lane] = w;
+    }
+    __syncthreads();
+    const int excl = (wid > 0 ? wsum[wid - 1] : 0) + x - v;
+    if (tid < U) tt_prefix[tid] = excl;
+    if (tid == 0) tt_prefix[U] = wsum[nw - 1];
+}
+
+// out[p][.] = fp16(X[row(p)][.]) with every 8-group of K in [0,4,1,5,2,6,3,7]
+// order; rows p >= meta[1] (no pair) are skipped.
+__global__ void __launch_bounds__(256) k_gather_f16(const float* X, int64_t K, const int* pair_row,
+                                                    const int* meta, int dense_rows, __half* out) {
+    const int64_t p = blockIdx.x;
+    const int64_t P = dense_rows > 0 ? dense_rows : meta[1];
+    if (p >= P) return;
+    const int64_t src = pair_row ? pair_row[p] : p;
+    const float4* x4 = reinterpret_cast<const float4*>(X + src * K);
+    uint4* o = reinterpret_cast<uint4*>(out + p * K);
+    for (int64_t g = threadIdx.x; g < K / 8; g += blockDim.x) {
+        const float4 a = __ldg(x4 + 2 * g), b = __ldg(x4 + 2 * g + 1);
+        const __half2 h0 = __floats2half2_rn(a.x, b.x);  // elements 0,4
+        const __half2 h1 = __floats2half2_rn(a.y, b.y);  // 1,5
+        const __half2 h2 = __floats2half2_rn(a.z, b.z);  // 2,6
+        const __half2 h3 = __floats2half2_rn(a.w, b.w);  // 3,7
+        o[g] = make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                          *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+    }
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------ host
+namespace {
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+    static EncodeFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeFn>(p);
+    }
+    return fn;
+}
+
+bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
+    EncodeFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int MODE, int BN>
+int launch_t(const TcLaunch& L, int num_sms, cudaStream_t s) {
+    CUtensorMap qmap, bmap;
+    if (!make_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.Wp, (uint64_t)L.a.K / 2, (uint64_t)L.total_rows,
+                  (uint64_t)L.a.K / 2, 32, 64, CU_TENSOR_MAP_SWIZZLE_32B))
+        return -1;
+    if (!make_map(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.B, (uint64_t)L.a.K, (uint64_t)L.b_rows,
+                  (uint64_t)L.a.K * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+        return -1;
+    const int smem = tc::Smem<BN>::TOTAL;
+    auto kern = tc::k_tc_gemm<MODE, BN>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -1;
+    const int per_sm = smem <= 110 * 1024 ? 2 : 1;
+    int grid = num_sms * per_sm;
+    if (L.max_items > 0 && L.max_items < grid) grid = (int)L.max_items;
+    if (grid <= 0) return 0;
+    kern<<<grid, tc::THREADS, smem, s>>>(qmap, bmap, L.a);
+    return 1;
+}
+
+template <int MODE>
+int launch_mode(const TcLaunch& L, int num_sms, cudaStream_t s) {
+    switch (L.BN) {
+        case 16: return launch_t<MODE, 16>(L, num_sms, s);
+        case 32: return launch_t<MODE, 32>(L, num_sms, s);
+        case 64: return launch_t<MODE, 64>(L, num_sms, s);
+        case 128: return launch_t<MODE, 128>(L, num_sms, s);
+        case 256: return launch_t<MODE, 256>(L, num_sms, s);
+        default: return -1;
+    }
+}
+
+}  // namespace
+
+int launch_tc_gemm(int mode, const TcLaunch& L, int num_sms, cudaStream_t s) {
+    return mode == TC_ACT ? launch_mode<TC_ACT>(L, num_sms, s) : launch_mode<TC_PLAIN>(L, num_sms, s);
+}
+
+int launch_tt_prefix(const int* meta, const int* seg_count, int BN, int* tt_prefix, cudaStream_t s) {
+    tc::k_tt_prefix<<<1, 1024, 0, s>>>(meta, seg_count, BN, tt_prefix);
+    return 1;
+}
+
+int launch_gather_f16(const float* X, int64_t K, const int* pair_row, const int* meta, int64_t rows,
+                      int dense_rows, __half* out, cudaStream_t s) {
+    if (rows <= 0) return 0;
+    tc::k_gather_f16<<<(unsigned)rows, 256, 0, s>>>(X, K, pair_row, meta, dense_rows, out);
+    return 1;
+}
+
+bool tc_supported(int64_t K, int64_t R, int act_mode, int64_t F) {
+    if (K % 64 != 0 || K > 65536) return false;
+    if (act_mode) return F % 64 == 0;
+    return R > 0;
+}
+
+}  // namespace moe

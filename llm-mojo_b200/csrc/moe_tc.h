@@ -1,0 +1,49 @@
+// moe_tc.h -- launch interface of the tcgen05 grouped Q4_0 GEMM (moe_tc.cu).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+enum TcMode { TC_PLAIN = 0, TC_ACT = 1 };
+
+struct TcArgs {
+    const float* Ws = nullptr;      // expert 0's scales [E*R][K/32] (8-byte aligned)
+    int K = 0;                      // multiple of 64
+    int64_t R = 0;                  // rows per expert (2F in ACT mode)
+    int F = 0;                      // ACT: act rows per expert (multiple of 64)
+    int act = 0;                    // activation kind
+    const int* meta = nullptr;      // meta[0] = U
+    const int* unique_expert = nullptr;
+    const int* seg_start = nullptr;
+    const int* seg_count = nullptr;
+    const int* tt_prefix = nullptr; // [U+1] exclusive prefix of token tiles
+    int dense_tokens = 0;           // > 0: one matrix, tokens 0..n-1
+    __half* act_out = nullptr;      // ACT: [P][F] fp16, K-group order [0,4,1,5,2,6,3,7]
+    float* y_out = nullptr;         // PLAIN: rows of y_stride floats
+    int64_t y_stride = 0;
+    const int* out_row = nullptr;   // PLAIN: output row of pair p (nullptr: p)
+    int* err_flag = nullptr;        // set to 2 when a bounded wait expires
+    uint64_t timeout_ns = 4000000000ull;
+};
+
+struct TcLaunch {
+    TcArgs a;
+    const uint8_t* Wp = nullptr;  // expert 0's packed rows (16-byte aligned)
+    int64_t total_rows = 0;       // rows covered by the Q4 tensor map (E * R)
+    const __half* B = nullptr;    // activation rows [b_rows][K] fp16 (16-byte aligned)
+    int64_t b_rows = 0;
+    int BN = 16;                  // token tile: 16, 32, 64, 128 or 256
+    int64_t max_items = 0;        // upper bound on work items (limits the grid), 0 = none
+};
+
+// Returns the number of kernels launched, or -1 when the shape or the tensor
+// map is not supported (the caller then uses the CUDA-core GEMV).
+int launch_tc_gemm(int mode, const TcLaunch& L, int num_sms, cudaStream_t s);
+int launch_tt_prefix(const int* meta, const int* seg_count, int BN, int* tt_prefix, cudaStream_t s);
+int launch_gather_f16(const float* X, int64_t K, const int* pair_row, const int* meta, int64_t rows,
+                      int dense_rows, __half* out, cudaStream_t s);
+bool tc_supported(int64_t K, int64_t R, int act_mode, int64_t F);
+
+}  // namespace moe

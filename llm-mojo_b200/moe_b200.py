@@ -22,6 +22,8 @@ LIB_PATH = os.path.join(HERE, "libmoe_b200.so")
 ACT_SIGMOID1702, ACT_GELU_TANH = 0, 1
 X_NATURAL, X_DEINT_HALVES, X_DEINT_BLOCK32 = 0, 1, 2
 F_POST_NORM, F_SET_COVER, F_FP16_OUT = 1, 4, 8
+OPT_GEMM_PATH, OPT_TC_MIN_TOKENS, OPT_DEVICE_TIMEOUT_NS = 1, 2, 3
+PATH_AUTO, PATH_GEMV, PATH_TC = 0, 1, 2
 
 STATUS = {0: "MOE_OK", 1: "MOE_E_ARG", 2: "MOE_E_SHAPE", 3: "MOE_E_UNREGISTERED",
           4: "MOE_E_CUDA", 5: "MOE_E_NCCL", 6: "MOE_E_TIMEOUT", 7: "MOE_E_NOMEM",
@@ -30,7 +32,8 @@ STATUS = {0: "MOE_OK", 1: "MOE_E_ARG", 2: "MOE_E_SHAPE", 3: "MOE_E_UNREGISTERED"
 # every symbol declared in include/moe_b200.h
 EXPORTS = [
     "moe_ctx_create", "moe_ctx_destroy", "moe_last_error", "moe_kernel_launches",
-    "moe_set_stream", "moe_set_async", "moe_wait", "moe_profile_enable", "moe_profile_read",
+    "moe_set_stream", "moe_set_async", "moe_wait", "moe_set_option", "moe_profile_enable",
+    "moe_profile_read",
     "moe_register_weights",
     "moe_unregister_weights", "moe_quantize_fp32_to_q4_0", "moe_q4_matmul_vec",
     "moe_q4_matmul_batchN", "moe_compute_moe_lod_weights", "moe_apply_moe_lod_and_set_cover",
@@ -85,6 +88,7 @@ def _declare(L):
     L.moe_set_stream.argtypes = [_p, _p]
     L.moe_set_async.argtypes = [_p, _int]
     L.moe_wait.argtypes = [_p, _u64]
+    L.moe_set_option.argtypes = [_p, _int, _i64]
     L.moe_profile_enable.argtypes = [_p, _int]
     L.moe_profile_read.argtypes = [_p, _int, _p, _p, _p, C.POINTER(_int)]
     L.moe_register_weights.argtypes = [_p, _p, C.c_size_t]
@@ -165,6 +169,13 @@ class Context:
 
     def wait(self, timeout_ns: int = 0):
         self.check(self.lib.moe_wait(self.h, timeout_ns))
+
+    def set_option(self, option: int, value: int):
+        self.check(self.lib.moe_set_option(self.h, option, value))
+
+    def set_gemm_path(self, path: int):
+        """PATH_AUTO, PATH_GEMV (CUDA cores, fp32) or PATH_TC (tcgen05, fp16 operands)."""
+        self.set_option(OPT_GEMM_PATH, path)
 
     def profile_enable(self, on: bool = True):
         self.check(self.lib.moe_profile_enable(self.h, int(on)))

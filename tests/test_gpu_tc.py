@@ -1,0 +1,93 @@
+"""GPU parity of the tcgen05 grouped-GEMM path (fp16 operands, fp32
+accumulation in TMEM) against the CPU oracle, through the C ABI.
+
+The bar for the MoE path output is the north-star one (max-abs 2e-3, rel-L2
+1e-3 vs the fp32 reference).  Dense projections are not the MoE path's
+output; their outputs are ~N(0, 1) rather than ~0.15, so the absolute bar is
+scaled by the output rms there (rel-L2 bar unchanged).
+"""
+import numpy as np
+import pytest
+
+import moe_b200 as MB
+import oracle as O
+import synth
+from tolerances import assert_close, near_tie_tokens
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture()
+def tc(ctx):
+    ctx.set_gemm_path(MB.PATH_TC)
+    yield ctx
+    ctx.set_gemm_path(MB.PATH_AUTO)
+
+
+def _softmax_rows(s):
+    return np.stack([O.softmax(r) for r in s])
+
+
+@pytest.mark.parametrize("c_in,c_out,batch", [(2816, 4096, 16), (2816, 1024, 16), (4096, 2816, 16),
+                                              (704, 2816, 40), (2816, 128, 300)])
+def test_tc_dense_q4_matmul(tc, c_in, c_out, batch):
+    import torch
+    rng = np.random.default_rng(c_in * 7 + batch)
+    W, S, _ = O.quantize_q4_0(rng.normal(0, 0.02, c_out * c_in).astype(np.float32))
+    x = rng.standard_normal((batch, c_in)).astype(np.float32)
+    out = np.zeros((batch, c_out), np.float32)
+    tc.q4_matmul_batchN(batch, torch.from_numpy(W).cuda(), torch.from_numpy(S).cuda(), x, out, c_in, c_out)
+    ref = O.q4_matmul(W, S, x, c_in, c_out, prec=O.F64)
+    rms = float(np.sqrt((ref.astype(np.float64) ** 2).mean()))
+    assert_close(out, ref, max_abs=2e-3 * max(1.0, rms), what=f"tc dense {c_in}x{c_out}x{batch}")
+
+
+@pytest.mark.parametrize("M", [16, 64])
+def test_tc_layer_forward_vs_oracle(tc, full_layer, M):
+    dev, host, L = full_layer
+    desc = MB.make_desc(dev)
+    x = synth.make_x(M, seed=300 + M).cpu().numpy()
+    out = np.zeros((M, 2816), np.float32)
+    cnt = np.zeros(M, np.int64)
+    idx = np.zeros((M, 8), np.int64)
+    w = np.zeros((M, 8), np.float32)
+    tc.layer_forward(desc, M, x, out, flags=0, tok_active_count=cnt, tok_active_idx=idx,
+                     tok_active_weights=w)
+    ref = O.route(L, x)
+    ties = set(near_tie_tokens(_softmax_rows(ref["scores"]), 8).tolist())
+    keep = [t for t in range(M) if t not in ties and cnt[t] == ref["count"][t]
+            and np.array_equal(idx[t, :cnt[t]], ref["idx"][t, :cnt[t]])]
+    assert len(keep) >= M - len(ties)
+    moe_ref = O.experts_forward(L, ref["moe_in"], ref["count"], ref["idx"], ref["w"], prec=O.F64)
+    assert_close(out[keep], moe_ref[keep], what=f"tc layer M={M}")
+
+
+def test_tc_diffusion_block_vs_oracle(tc, full_layer):
+    dev, host, L = full_layer
+    B = 256
+    x = synth.make_x(B, seed=41, bf16_representable=True).cpu().numpy()
+    ref = O.route(L, x)
+    w = O.apply_moe_lod_and_set_cover(ref["top_idx"], ref["top_val"], host["per_expert_scale"], B, 8, 8, 1.0)
+    x16 = ref["moe_in"].astype(np.float16)
+    out = np.zeros((B, 2816), np.float16)
+    tc.run_diffusion_moe_experts_parallel(dev["gu_p"], dev["gu_s"], dev["dn_p"], dev["dn_s"], x16,
+                                          ref["top_idx"], w, out, B, 2816, 704, 8)
+    o64 = O.diffusion_experts(host["gu_p"], host["gu_s"], host["dn_p"], host["dn_s"], x16,
+                              ref["top_idx"], w, 2816, 704, 8, prec=O.F64)
+    assert_close(out.astype(np.float32), o64.astype(np.float32), what="tc diffusion block")
+
+
+def test_tc_matches_gemv_path(ctx, full_layer):
+    """Both paths through the same call; the gap is the fp16 operand rounding."""
+    dev, host, L = full_layer
+    desc = MB.make_desc(dev)
+    M = 32
+    x = synth.make_x(M, seed=77)
+    outs = []
+    for path in (MB.PATH_GEMV, MB.PATH_TC):
+        ctx.set_gemm_path(path)
+        o = np.zeros((M, 2816), np.float32)
+        ctx.layer_forward(desc, M, x.cpu().numpy(), o, flags=0)
+        outs.append(o)
+    ctx.set_gemm_path(MB.PATH_AUTO)
+    assert_close(outs[1], outs[0], what="tc vs gemv")
