@@ -54,6 +54,8 @@ struct moe_ctx {
     cudaEvent_t done = nullptr;
     int gemm_path = MOE_PATH_AUTO;       // moe_set_option(MOE_OPT_GEMM_PATH)
     int tc_min_tokens = 8;               // auto: tensor cores from this many tokens
+    int dense_tc_min_tokens = 64;        // auto, dense projections
+    bool tc_a_in_smem = false;           // MOE_OPT_TC_A_IN_SMEM
     uint64_t device_timeout_ns = 4000000000ull;
     // profiling (moe_profile_enable)
     int profile = 0;
@@ -368,6 +370,7 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
         t1.b_rows = P;
         t1.BN = BN;
         t1.max_items = (int64_t)(F / 64) * (max_u + (P + BN - 1) / BN);
+        t1.a_in_smem = ctx->tc_a_in_smem;
         int r;
         {
             ProfScope ps(ctx, "tc_gate_up");
@@ -554,6 +557,13 @@ int moe_set_option(moe_ctx* ctx, int option, int64_t value) {
             if (value <= 0) return fail(ctx, MOE_E_ARG, "bad timeout");
             ctx->device_timeout_ns = (uint64_t)value;
             return MOE_OK;
+        case MOE_OPT_DENSE_TC_MIN_TOKENS:
+            if (value < 1) return fail(ctx, MOE_E_ARG, "bad token threshold");
+            ctx->dense_tc_min_tokens = (int)value;
+            return MOE_OK;
+        case MOE_OPT_TC_A_IN_SMEM:
+            ctx->tc_a_in_smem = value != 0;
+            return MOE_OK;
         default:
             return fail(ctx, MOE_E_ARG, "unknown option");
     }
@@ -671,8 +681,10 @@ int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch, const uint8_t* W, const fl
         TRY(prep_rows(ctx, xd, MOE_X_NATURAL, 0, batch, c_in, xc, nullptr));
         xd = xc;
     }
+    // dense projections: tensor cores only from dense_tc_min_tokens tokens on
+    // (below that the token-chunked GEMV keeps every SM busy in fp32)
     const bool tc = ctx->gemm_path != MOE_PATH_GEMV && moe::tc_supported(c_in, c_out, 0, 0) &&
-                    al8(sc) && (ctx->gemm_path == MOE_PATH_TC || batch >= ctx->tc_min_tokens);
+                    al8(sc) && (ctx->gemm_path == MOE_PATH_TC || batch >= ctx->dense_tc_min_tokens);
     if (tc) {
         __half* x16 = (__half*)ws_take(ctx, batch * c_in * 2);
         ctx->launches += moe::launch_gather_f16((const float*)xd, c_in, nullptr, nullptr, batch, (int)batch,
@@ -694,6 +706,7 @@ int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch, const uint8_t* W, const fl
         while (BN < 256 && BN < batch) BN *= 2;
         t.BN = BN;
         t.max_items = ((c_out + 127) / 128) * ((batch + BN - 1) / BN);
+        t.a_in_smem = ctx->tc_a_in_smem;
         int r;
         {
             ProfScope ps(ctx, "q4_matmul");

@@ -142,6 +142,8 @@ __device__ __forceinline__ void gemv_tokens(const GemvArgs& a, const GemvWarp& W
         }
 }
 
+constexpr int DENSE_CHUNK = 4;
+
 template <int MODE, bool XS, int NBL, int RPW>
 __global__ void __launch_bounds__(128, 4) k_q4_gemv(GemvArgs a) {
     GemvWarp W;
@@ -153,14 +155,17 @@ __global__ void __launch_bounds__(128, 4) k_q4_gemv(GemvArgs a) {
     const int rows_per_item = (MODE == GEMV_ACT) ? 2 * RPW : 4 * RPW;
     const int64_t tile_rows = (MODE == GEMV_ACT) ? a.F : a.rows_per_expert;
     const int n_groups = (int)((tile_rows + rows_per_item - 1) / rows_per_item);
-    const int U = a.dense_tokens > 0 ? 1 : a.meta[0];
+    // dense mode splits the tokens into chunks of DENSE_CHUNK per item, so a
+    // small matrix with many tokens (the router) still spreads over the GPU
+    const int n_chunks = a.dense_tokens > 0 ? (a.dense_tokens + DENSE_CHUNK - 1) / DENSE_CHUNK : 1;
+    const int U = a.dense_tokens > 0 ? n_chunks : a.meta[0];
     const int64_t n_items = (int64_t)U * n_groups;
 
     for (int64_t item = (int64_t)blockIdx.x * 4 + warp; item < n_items; item += (int64_t)gridDim.x * 4) {
         const int u = (int)(item / n_groups), grp = (int)(item - (int64_t)u * n_groups);
         const int e = a.dense_tokens > 0 ? 0 : a.unique_expert[u];
-        const int n = a.dense_tokens > 0 ? a.dense_tokens : a.seg_count[u];
-        const int s0 = a.dense_tokens > 0 ? 0 : a.seg_start[u];
+        const int n = a.dense_tokens > 0 ? min(DENSE_CHUNK, a.dense_tokens - u * DENSE_CHUNK) : a.seg_count[u];
+        const int s0 = a.dense_tokens > 0 ? u * DENSE_CHUNK : a.seg_start[u];
         const uint8_t* Wp = a.Wp + (size_t)e * a.rows_per_expert * (K >> 1);
         const float* Ws = a.Ws + (size_t)e * a.rows_per_expert * nb;
         int64_t row[RPW];
@@ -266,7 +271,8 @@ static void gemv_launch_t(const GemvArgs& a, int num_sms, cudaStream_t s) {
     const int rows_per_item = (MODE == GEMV_ACT) ? 2 * RPW : 4 * RPW;
     const int64_t tile_rows = (MODE == GEMV_ACT) ? a.F : a.rows_per_expert;
     const int64_t n_groups = (tile_rows + rows_per_item - 1) / rows_per_item;
-    const int64_t items = n_groups * (a.dense_tokens > 0 ? 1 : a.max_unique);
+    const int64_t items =
+        n_groups * (a.dense_tokens > 0 ? (a.dense_tokens + DENSE_CHUNK - 1) / DENSE_CHUNK : a.max_unique);
     const int64_t blocks = (items + 3) / 4;
     const int64_t cap = (int64_t)num_sms * 16;
     const int grid = (int)(blocks < cap ? blocks : cap);

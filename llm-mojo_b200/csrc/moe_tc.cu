@@ -9,9 +9,16 @@
 //              activation tiles (SWIZZLE_128B) into smem rings.
 //   warp 1     TMEM owner and single-thread tcgen05.mma issuer; fp32
 //              accumulators live in TMEM, double-buffered across items.
-//   warps 2-5  dequant: thread t turns row t's 64 nibbles of a k-tile into
-//              fp16 ((n-8)*scale computed in fp32, one rounding) and stores
-//              them in the UMMA K-major SWIZZLE_128B layout.
+//   warps 2-5  dequant: the thread owning A-tile row t turns the row's 64
+//              nibbles of a k-tile into fp16.  Two variants of the A operand:
+//              A_TMEM (token tiles <= 64, memory-bound): (n-8) exact in fp16
+//                via one LOP3 per nibble pair, times the fp16 scale (HMUL2),
+//                stored with tcgen05.st straight into TMEM; the MMA reads A
+//                from TMEM, so shared memory carries only the Q4 and
+//                activation tiles.
+//              A in shared memory (large token tiles, compute-bound):
+//                (n-8)*scale in fp32, one rounding to fp16, stored in the UMMA
+//                K-major SWIZZLE_128B layout.
 //   warps 6-9  epilogue: tcgen05.ld of the accumulator; ACT mode pairs gate
 //              and up rows with a warp shuffle and writes the activated
 //              result as fp16, PLAIN mode writes fp32 rows.
@@ -123,6 +130,30 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t
         : "memory");
 }
 
+// A from tensor memory (lanes = the 128 rows, 32-bit columns = K pairs)
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// tcgen05.st 32 lanes x 32 bit x 32 columns (this thread's lane, 32 values)
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // tcgen05.ld 32 lanes x 32 bit, N consecutive columns per thread
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]);
@@ -180,13 +211,13 @@ constexpr int SB = 4;             // activation ring stages (BN * 128 B each)
 constexpr int KT = 64;            // K per k-tile
 constexpr int THREADS = 320;
 
-template <int BN>
+template <int BN, bool A_TMEM>
 struct Smem {
     static constexpr int A_BYTES = 128 * KT * 2;          // 16384
     static constexpr int B_BYTES = BN * KT * 2;
     static constexpr int Q_BYTES = 128 * KT / 2;          // 4096
     static constexpr int OFF_A = 0;
-    static constexpr int OFF_B = OFF_A + SA * A_BYTES;
+    static constexpr int OFF_B = OFF_A + (A_TMEM ? 0 : SA * A_BYTES);
     static constexpr int OFF_Q = OFF_B + SB * B_BYTES;
     static constexpr int OFF_BAR = OFF_Q + SQ * Q_BYTES;
     static constexpr int N_BAR = 2 * SQ + 2 * SA + 2 * SB + 4 + 1;
@@ -194,8 +225,14 @@ struct Smem {
     static constexpr int TOTAL = OFF_MISC + 16 + 1024;    // + alignment slack
 };
 
-__host__ __device__ constexpr uint32_t tmem_cols(int BN) {
-    return (2 * BN) <= 32 ? 32u : (2 * BN) <= 64 ? 64u : (2 * BN) <= 128 ? 128u : (2 * BN) <= 256 ? 256u : 512u;
+__host__ __device__ constexpr uint32_t pow2_cols(int n) {
+    return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u;
+}
+// TMEM columns: two fp32 accumulator buffers of BN columns, then (A_TMEM)
+// SA stages of the fp16 A tile, 32 columns (64 fp16 per lane) each.
+__host__ __device__ constexpr int a_col0(int BN) { return ((2 * BN + 31) / 32) * 32; }
+__host__ __device__ constexpr uint32_t tmem_cols(int BN, bool A_TMEM) {
+    return pow2_cols(A_TMEM ? a_col0(BN) + SA * 32 : 2 * BN);
 }
 
 // ------------------------------------------------------------ work list
@@ -238,10 +275,10 @@ __device__ __forceinline__ bool decode_item(const TcArgs& a, int64_t item, int r
 }
 
 // -------------------------------------------------------------- kernel
-template <int MODE, int BN>
+template <int MODE, int BN, bool A_TMEM>
 __global__ void __launch_bounds__(THREADS, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap bmap, TcArgs a) {
-    using L = Smem<BN>;
+    using L = Smem<BN, A_TMEM>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
@@ -261,7 +298,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = a.K, nk = K / KT, nb = K / 32;
     const int row_tiles = (MODE == TC_ACT) ? (a.F / 64) : (int)((a.R + 127) / 128);
-    constexpr uint32_t NCOL = tmem_cols(BN);
+    constexpr uint32_t NCOL = tmem_cols(BN, A_TMEM);
+    constexpr uint32_t ACOL = (uint32_t)a_col0(BN);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SQ; ++s) {
@@ -360,12 +398,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (!(ok = mbar_wait(a_full(as), ap, G))) break;
                     if (!(ok = mbar_wait(b_full(bs), bp, G))) break;
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(smem + L::OFF_A + as * L::A_BYTES);
                     const uint32_t sb = smem_u32(smem + L::OFF_B + bs * L::B_BYTES);
+                    if (A_TMEM) {
+                        const uint32_t ta = tmem_base + ACOL + (uint32_t)(as * 32);
 #pragma unroll
-                    for (int k = 0; k < KT / 16; ++k)
-                        tc_mma(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), IDESC,
-                               (kt | k) != 0);
+                        for (int k = 0; k < KT / 16; ++k)
+                            tc_mma_ts(d_tmem, ta + 8u * k, sw128_desc(sb + 32u * k), IDESC, (kt | k) != 0);
+                    } else {
+                        const uint32_t sa = smem_u32(smem + L::OFF_A + as * L::A_BYTES);
+#pragma unroll
+                        for (int k = 0; k < KT / 16; ++k)
+                            tc_mma(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), IDESC,
+                                   (kt | k) != 0);
+                    }
                     issued = true;
                     tc_commit(a_empty(as));
                     tc_commit(b_empty(bs));
@@ -386,7 +431,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else if (warp < 6) {
         // ------------------------------------------------ dequant
-        const int t = threadIdx.x - 64;  // row of the A tile
+        // row of the A tile; with A in TMEM a warp may only write its own lane
+        // quarter (warp % 4), so the row follows the quarter
+        const int t = A_TMEM ? ((warp & 3) * 32 + lane) : (threadIdx.x - 64);
         int qs = 0, as = 0;
         uint32_t qp = 0, ap = 0;
         Item it;
@@ -423,6 +470,25 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint4 c0 = *reinterpret_cast<const uint4*>(qrow + (0 ^ sw));
                     const uint4 c1 = *reinterpret_cast<const uint4*>(qrow + (16 ^ sw));
                     const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                    if (A_TMEM) {
+                        tc_fence_after();
+                        // (n-8) exact in fp16: (0x6400 | n) is 1024 + n; times the fp16 scale
+                        const __half2 s0 = __float2half2_rn(s.x), s1 = __float2half2_rn(s.y);
+                        const __half2 off = __float2half2_rn(1032.0f);
+                        uint32_t h[32];
+#pragma unroll
+                        for (int w = 0; w < 8; ++w) {
+                            const __half2 sc = (w < 4) ? s0 : s1;
+#pragma unroll
+                            for (int p = 0; p < 4; ++p) {
+                                const uint32_t v = ((wv[w] >> (4 * p)) & 0x000F000Fu) | 0x64006400u;
+                                const __half2 hv = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&v), off), sc);
+                                h[4 * w + p] = *reinterpret_cast<const uint32_t*>(&hv);
+                            }
+                        }
+                        tmem_st32(tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + ACOL + (uint32_t)(as * 32), h);
+                        tc_fence_before();
+                    } else {
                     uint8_t* arow = smem + L::OFF_A + as * L::A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
 #pragma unroll
                     for (int w = 0; w < 8; ++w) {
@@ -439,6 +505,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         *reinterpret_cast<uint4*>(arow + ((w ^ (t & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
                     }
                     fence_async_smem();
+                    }
                     __syncwarp();
                     if (lane == 0) {
                         mbar_arrive(a_full(as));
@@ -591,7 +658,7 @@ bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int MODE, int BN>
+template <int MODE, int BN, bool A_TMEM>
 int launch_t(const TcLaunch& L, int num_sms, cudaStream_t s) {
     CUtensorMap qmap, bmap;
     if (!make_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.Wp, (uint64_t)L.a.K / 2, (uint64_t)L.total_rows,
@@ -600,10 +667,14 @@ int launch_t(const TcLaunch& L, int num_sms, cudaStream_t s) {
     if (!make_map(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.B, (uint64_t)L.a.K, (uint64_t)L.b_rows,
                   (uint64_t)L.a.K * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B))
         return -1;
-    const int smem = tc::Smem<BN>::TOTAL;
-    auto kern = tc::k_tc_gemm<MODE, BN>;
+    const int smem = tc::Smem<BN, A_TMEM>::TOTAL;
+    auto kern = tc::k_tc_gemm<MODE, BN, A_TMEM>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -1;
-    const int per_sm = smem <= 110 * 1024 ? 2 : 1;
+    int per_sm = (227 * 1024) / smem;
+    const int by_tmem = 512 / (int)tc::tmem_cols(BN, A_TMEM);
+    if (per_sm > by_tmem) per_sm = by_tmem;
+    if (per_sm > 2) per_sm = 2;  // 320 threads x 2 = 20 warps; registers allow no more
+    if (per_sm < 1) per_sm = 1;
     int grid = num_sms * per_sm;
     if (L.max_items > 0 && L.max_items < grid) grid = (int)L.max_items;
     if (grid <= 0) return 0;
@@ -613,12 +684,22 @@ int launch_t(const TcLaunch& L, int num_sms, cudaStream_t s) {
 
 template <int MODE>
 int launch_mode(const TcLaunch& L, int num_sms, cudaStream_t s) {
-    switch (L.BN) {
-        case 16: return launch_t<MODE, 16>(L, num_sms, s);
-        case 32: return launch_t<MODE, 32>(L, num_sms, s);
-        case 64: return launch_t<MODE, 64>(L, num_sms, s);
-        case 128: return launch_t<MODE, 128>(L, num_sms, s);
-        case 256: return launch_t<MODE, 256>(L, num_sms, s);
+    if (L.a_in_smem) {
+        switch (L.BN) {
+            case 16: return launch_t<MODE, 16, false>(L, num_sms, s);
+            case 32: return launch_t<MODE, 32, false>(L, num_sms, s);
+            case 64: return launch_t<MODE, 64, false>(L, num_sms, s);
+            case 128: return launch_t<MODE, 128, false>(L, num_sms, s);
+            case 256: return launch_t<MODE, 256, false>(L, num_sms, s);
+            default: return -1;
+        }
+    }
+    switch (L.BN) {  // A in TMEM: token tiles up to 64 (accumulators + A stages fit 256 columns)
+        case 16: return launch_t<MODE, 16, true>(L, num_sms, s);
+        case 32: return launch_t<MODE, 32, true>(L, num_sms, s);
+        case 64: return launch_t<MODE, 64, true>(L, num_sms, s);
+        case 128: return launch_t<MODE, 128, false>(L, num_sms, s);
+        case 256: return launch_t<MODE, 256, false>(L, num_sms, s);
         default: return -1;
     }
 }

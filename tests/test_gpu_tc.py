@@ -17,10 +17,14 @@ from tolerances import assert_close, near_tie_tokens
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture()
-def tc(ctx):
+@pytest.fixture(params=["a_tmem", "a_smem"])
+def tc(ctx, request):
+    """Tensor-core path with the dequantised weights in TMEM (default for
+    token tiles <= 64) or staged in shared memory."""
     ctx.set_gemm_path(MB.PATH_TC)
+    ctx.set_option(MB.OPT_TC_A_IN_SMEM, int(request.param == "a_smem"))
     yield ctx
+    ctx.set_option(MB.OPT_TC_A_IN_SMEM, 0)
     ctx.set_gemm_path(MB.PATH_AUTO)
 
 
