@@ -53,8 +53,8 @@ struct moe_ctx {
     std::vector<CopyBack> pending;
     cudaEvent_t done = nullptr;
     int gemm_path = MOE_PATH_AUTO;       // moe_set_option(MOE_OPT_GEMM_PATH)
-    int tc_min_tokens = 8;               // auto: tensor cores from this many tokens
-    int dense_tc_min_tokens = 64;        // auto, dense projections
+    int tc_min_tokens = 1;               // auto: tensor cores from this many tokens
+    int dense_tc_min_tokens = 2;         // auto, dense projections and router
     bool tc_a_in_smem = false;           // MOE_OPT_TC_A_IN_SMEM
     uint64_t device_timeout_ns = 4000000000ull;
     // profiling (moe_profile_enable)
@@ -252,6 +252,7 @@ int check_q4_shape(moe_ctx* ctx, int64_t K, int64_t rows) {
 }
 
 // Internal buffers of an expert evaluation for M tokens x K slots.
+constexpr int64_t kMaxSplitY = 4;  // split-K partials of the down projection kept in y
 struct ExpertBufs {
     int* slot_expert;
     float* slot_weight;
@@ -268,8 +269,8 @@ struct ExpertBufs {
 size_t expert_bufs_bytes(int64_t M, int64_t K, int64_t d, int64_t F, int64_t E) {
     const int64_t P = M * K;
     return al(P * 4) * 2 + al(16) + al(E * 4) * 3 + al(P * 4) * 3 + al(M * d * 4) +
-           al(M * d / 32 * 4) + al(P * F * 4) + al(P * d * 4) + al(P * d * 2) + al(P * F * 2) +
-           al((E + 1) * 4);
+           al(M * d / 32 * 4) + al(P * F * 4) + al(P * d * 4 * kMaxSplitY) + al(P * d * 2) +
+           al(P * F * 2) + al((E + 1) * 4);
 }
 
 int take_expert_bufs(moe_ctx* ctx, int64_t M, int64_t K, int64_t d, int64_t F, int64_t E,
@@ -287,7 +288,7 @@ int take_expert_bufs(moe_ctx* ctx, int64_t M, int64_t K, int64_t d, int64_t F, i
     o->x32 = (float*)ws_take(ctx, M * d * 4);
     o->xsum = (float*)ws_take(ctx, M * d / 32 * 4);
     o->act = (float*)ws_take(ctx, P * F * 4);
-    o->y = (float*)ws_take(ctx, P * d * 4);
+    o->y = (float*)ws_take(ctx, P * d * 4 * kMaxSplitY);
     o->x16 = (__half*)ws_take(ctx, P * d * 2);
     o->a16 = (__half*)ws_take(ctx, P * F * 2);
     o->tt_prefix = (int*)ws_take(ctx, (E + 1) * 4);
@@ -317,6 +318,16 @@ int prep_rows(moe_ctx* ctx, const void* X, int x_layout, int x_f16, int64_t M, i
     return MOE_OK;
 }
 
+// Split-K factor for a PLAIN tensor-core GEMM with `items` work items: enough
+// items to give every SM two, at least 4 k-tiles per split.
+int choose_ksplit(moe_ctx* ctx, int64_t items, int64_t K) {
+    const int64_t nk = K / 64, target = 2LL * ctx->num_sms;
+    if (items <= 0 || items >= target) return 1;
+    int64_t ks = (target + items - 1) / items;
+    const int64_t cap = std::max<int64_t>(1, nk / 4);
+    return (int)std::min(ks, cap);
+}
+
 // Tensor cores for the expert GEMMs: forced by the option, or (auto) from
 // tc_min_tokens tokens on, when shapes and alignments allow.
 bool use_tc(moe_ctx* ctx, int64_t M, int64_t d, int64_t F, const ExpertWeights& w) {
@@ -340,6 +351,7 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     const int max_u = (int)std::min<int64_t>(E, P);
     const int max_t = (int)std::max<int64_t>(1, M);
 
+    int ksplit = 1;
     if (use_tc(ctx, M, d, F, w)) {
         // token tile from the mean load of an active expert
         const int64_t mean = (P + max_u - 1) / max_u;
@@ -389,6 +401,10 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
         t2.total_rows = E * d;
         t2.B = bb.a16;
         t2.max_items = ((d + 127) / 128) * (max_u + (P + BN - 1) / BN);
+        t2.a.ksplit = (int)std::min<int64_t>(choose_ksplit(ctx, ((d + 127) / 128) * max_u, F), kMaxSplitY);
+        t2.a.split_stride = P * d;
+        t2.max_items *= t2.a.ksplit;
+        ksplit = t2.a.ksplit;
         {
             ProfScope ps(ctx, "tc_down");
             r = moe::launch_tc_gemm(moe::TC_PLAIN, t2, ctx->num_sms, s);
@@ -436,6 +452,8 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     }
 
     moe::CombineArgs c = *comb_tmpl;
+    c.ksplit = ksplit;
+    c.split_stride = P * d;
     c.y = bb.y;
     c.d = d;
     c.K = (int)K;
@@ -446,6 +464,74 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
         ProfScope ps(ctx, "combine");
         ctx->launches += moe::launch_combine(c, M, s);
     }
+    return MOE_OK;
+}
+
+// Workspace dense_q4 may take (fp16 copy of x and split-K partials).
+size_t dense_bytes(int64_t batch, int64_t c_in, int64_t c_out) {
+    return al(batch * c_in * 2) + al(batch * c_out * 4 * (c_in / 256 + 1));
+}
+
+// out[batch][c_out] = W[c_out][c_in] . x[batch][c_in]^T on device buffers
+// (x fp32, 16-byte aligned).  Tensor cores (split-K, deterministic reduce)
+// from dense_tc_min_tokens tokens on, else the token-chunked fp32 GEMV.
+int dense_q4(moe_ctx* ctx, const uint8_t* w, const float* sc, const float* xd, float* od, int64_t c_in,
+             int64_t c_out, int64_t batch, const char* prof_name) {
+    const bool tc = ctx->gemm_path != MOE_PATH_GEMV && moe::tc_supported(c_in, c_out, 0, 0) &&
+                    al8(sc) && (ctx->gemm_path == MOE_PATH_TC || batch >= ctx->dense_tc_min_tokens);
+    if (tc) {
+        __half* x16 = (__half*)ws_take(ctx, batch * c_in * 2);
+        if (!x16) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+        moe::TcLaunch t;
+        t.a.Ws = sc;
+        t.a.K = (int)c_in;
+        t.a.R = c_out;
+        t.a.dense_tokens = (int)batch;
+        t.a.y_out = od;
+        t.a.y_stride = c_out;
+        t.a.err_flag = ctx->err_flag;
+        t.a.timeout_ns = ctx->device_timeout_ns;
+        t.Wp = w;
+        t.total_rows = c_out;
+        t.B = x16;
+        t.b_rows = batch;
+        int BN = 16;
+        while (BN < 256 && BN < batch) BN *= 2;
+        t.BN = BN;
+        t.max_items = ((c_out + 127) / 128) * ((batch + BN - 1) / BN);
+        t.a_in_smem = ctx->tc_a_in_smem;
+        const int ks = choose_ksplit(ctx, t.max_items, c_in);
+        float* part = nullptr;
+        if (ks > 1) {
+            part = (float*)ws_take(ctx, (size_t)ks * batch * c_out * 4);
+            if (!part) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+            t.a.y_out = part;
+            t.a.ksplit = ks;
+            t.a.split_stride = batch * c_out;
+            t.max_items *= ks;
+        }
+        ProfScope ps(ctx, prof_name);
+        ctx->launches += moe::launch_gather_f16(xd, c_in, nullptr, nullptr, batch, (int)batch, x16, ctx->stream);
+        const int r = moe::launch_tc_gemm(moe::TC_PLAIN, t, ctx->num_sms, ctx->stream);
+        if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core GEMM setup failed");
+        ctx->launches += r;
+        if (ks > 1)
+            ctx->launches += moe::launch_reduce_splits(part, batch * c_out, ks, od, batch * c_out, ctx->stream);
+        return MOE_OK;
+    }
+    moe::GemvArgs g;
+    g.Wp = w;
+    g.Ws = sc;
+    g.rows_per_expert = c_out;
+    g.K = (int)c_in;
+    g.X = xd;
+    g.dense_tokens = (int)batch;
+    g.out = od;
+    g.out_stride = c_out;
+    g.max_tokens = (int)batch;
+    g.max_unique = 1;
+    ProfScope ps(ctx, prof_name);
+    ctx->launches += moe::launch_gemv(moe::GEMV_PLAIN, g, ctx->num_sms, ctx->stream);
     return MOE_OK;
 }
 
@@ -669,7 +755,8 @@ int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch, const uint8_t* W, const fl
     TRY(check_q4_shape(ctx, c_in, c_out));
     if (batch <= 0) return fail(ctx, MOE_E_SHAPE, "batch_size must be >= 1");
     if (batch > (1 << 20)) return fail(ctx, MOE_E_SHAPE, "batch_size too large");
-    TRY(ws_reserve(ctx, al(batch * c_in * 4) * 2 + al(batch * c_out * 4) + al(batch * c_in * 2)));
+    TRY(ws_reserve(ctx, al(batch * c_in * 4) * 2 + al(batch * c_out * 4) + al(batch * c_in * 2) +
+                            al(batch * c_out * 4 * (c_in / 256 + 1))));
     void *w, *sc, *xd, *od;
     TRY(dev_ptr(ctx, W, c_out * c_in / 2, K_W, &w));
     TRY(dev_ptr(ctx, S, c_out * c_in / 32 * 4, K_W, &sc));
@@ -681,56 +768,8 @@ int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch, const uint8_t* W, const fl
         TRY(prep_rows(ctx, xd, MOE_X_NATURAL, 0, batch, c_in, xc, nullptr));
         xd = xc;
     }
-    // dense projections: tensor cores only from dense_tc_min_tokens tokens on
-    // (below that the token-chunked GEMV keeps every SM busy in fp32)
-    const bool tc = ctx->gemm_path != MOE_PATH_GEMV && moe::tc_supported(c_in, c_out, 0, 0) &&
-                    al8(sc) && (ctx->gemm_path == MOE_PATH_TC || batch >= ctx->dense_tc_min_tokens);
-    if (tc) {
-        __half* x16 = (__half*)ws_take(ctx, batch * c_in * 2);
-        ctx->launches += moe::launch_gather_f16((const float*)xd, c_in, nullptr, nullptr, batch, (int)batch,
-                                                x16, ctx->stream);
-        moe::TcLaunch t;
-        t.a.Ws = (const float*)sc;
-        t.a.K = (int)c_in;
-        t.a.R = c_out;
-        t.a.dense_tokens = (int)batch;
-        t.a.y_out = (float*)od;
-        t.a.y_stride = c_out;
-        t.a.err_flag = ctx->err_flag;
-        t.a.timeout_ns = ctx->device_timeout_ns;
-        t.Wp = (const uint8_t*)w;
-        t.total_rows = c_out;
-        t.B = x16;
-        t.b_rows = batch;
-        int BN = 16;
-        while (BN < 256 && BN < batch) BN *= 2;
-        t.BN = BN;
-        t.max_items = ((c_out + 127) / 128) * ((batch + BN - 1) / BN);
-        t.a_in_smem = ctx->tc_a_in_smem;
-        int r;
-        {
-            ProfScope ps(ctx, "q4_matmul");
-            r = moe::launch_tc_gemm(moe::TC_PLAIN, t, ctx->num_sms, ctx->stream);
-        }
-        if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core GEMM setup failed");
-        ctx->launches += r;
-        return finish(ctx);
-    }
-    moe::GemvArgs g;
-    g.Wp = (const uint8_t*)w;
-    g.Ws = (const float*)sc;
-    g.rows_per_expert = c_out;
-    g.K = (int)c_in;
-    g.X = (const float*)xd;
-    g.dense_tokens = (int)batch;
-    g.out = (float*)od;
-    g.out_stride = c_out;
-    g.max_tokens = (int)batch;
-    g.max_unique = 1;
-    {
-        ProfScope ps(ctx, "q4_matmul");
-        ctx->launches += moe::launch_gemv(moe::GEMV_PLAIN, g, ctx->num_sms, ctx->stream);
-    }
+    TRY(dense_q4(ctx, (const uint8_t*)w, (const float*)sc, (const float*)xd, (float*)od, c_in, c_out,
+                 batch, "q4_matmul"));
     return finish(ctx);
 }
 
@@ -1124,7 +1163,7 @@ int layer_dev(moe_ctx* ctx, const moe_layer_desc* L, int flags, LayerDev* o) {
 
 // Bytes route_dev takes from the workspace.
 size_t route_bytes(int64_t M, int64_t d, int64_t E, int64_t K) {
-    return al(M * K * 4) * 2 + al(M * d * 4) * 2 + al(M * d / 32 * 4) + al(M * E * 4);
+    return al(M * K * 4) * 2 + al(M * d * 4) * 2 + al(M * d / 32 * 4) + al(M * E * 4) + dense_bytes(M, d, E);
 }
 
 // Router: prep (norms, router input, block sums) -> router GEMV -> softmax /
@@ -1157,23 +1196,11 @@ int route_dev(moe_ctx* ctx, const moe_layer_desc* L, const LayerDev& ld, int64_t
         ProfScope ps(ctx, "prep");
         ctx->launches += moe::launch_prep(pa, M, s);
     }
-    {
+    if (ld.rp) {
+        TRY(dense_q4(ctx, ld.rp, ld.rs, scaled, scores, d, E, M, "router"));
+    } else {
         ProfScope ps(ctx, "router");
-        if (ld.rp) {
-            moe::GemvArgs g;
-            g.Wp = ld.rp;
-            g.Ws = ld.rs;
-            g.rows_per_expert = E;
-            g.K = (int)d;
-            g.X = scaled;
-            g.dense_tokens = (int)M;
-            g.out = scores;
-            g.out_stride = E;
-            g.max_tokens = (int)M;
-            ctx->launches += moe::launch_gemv(moe::GEMV_PLAIN, g, ctx->num_sms, s);
-        } else {
-            ctx->launches += moe::launch_gemv_f32(ld.rf32, scaled, scores, M, E, d, s);
-        }
+        ctx->launches += moe::launch_gemv_f32(ld.rf32, scaled, scores, M, E, d, s);
     }
     moe::TopkArgs a;
     a.scores = scores;

@@ -86,6 +86,8 @@ struct CombineArgs {
     const float* post_w = nullptr;
     int post_norm = 0;
     int fma_mode = 0;  // 1: s = fma(y, w, s) (diffusion_kernels.mojo:396); 0: s += y*w
+    int ksplit = 1;             // y holds this many partial sums ...
+    int64_t split_stride = 0;   // ... this many floats apart
     void* out = nullptr;
     int out_f16 = 0;
 };

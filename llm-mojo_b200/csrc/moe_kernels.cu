@@ -800,7 +800,12 @@ __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
             for (int k = 0; k < K; ++k) {
                 const int p = sp[k];
                 if (p < 0) continue;
-                const float4 y = __ldg(reinterpret_cast<const float4*>(a.y + (size_t)p * a.d) + j);
+                float4 y = __ldg(reinterpret_cast<const float4*>(a.y + (size_t)p * a.d) + j);
+                for (int ks = 1; ks < a.ksplit; ++ks) {  // split-K partials, fixed order
+                    const float4 z = __ldg(reinterpret_cast<const float4*>(a.y + ks * a.split_stride +
+                                                                           (size_t)p * a.d) + j);
+                    y.x += z.x; y.y += z.y; y.z += z.z; y.w += z.w;
+                }
                 const float w = sw[k];
                 if (a.fma_mode) {
                     s.x = fmaf(y.x, w, s.x); s.y = fmaf(y.y, w, s.y);

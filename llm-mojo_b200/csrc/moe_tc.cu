@@ -205,14 +205,18 @@ __host__ __device__ constexpr uint32_t f16_idesc(int M, int N) {
 __device__ __forceinline__ int kpos(int m) { return m < 4 ? 2 * m : 2 * (m - 4) + 1; }
 
 // ---------------------------------------------------------------- layout
-constexpr int SQ = 8;             // Q4 ring stages (4 KB each)
-constexpr int SA = 3;             // fp16 A ring stages (16 KB each)
-constexpr int SB = 4;             // activation ring stages (BN * 128 B each)
+constexpr int SA = 3;             // fp16 A ring stages (16 KB in smem, or 32 TMEM columns)
 constexpr int KT = 64;            // K per k-tile
 constexpr int THREADS = 320;
 
+// Ring depths.  The producer issues a Q4 tile and an activation tile per
+// k-tile and waits for a free slot in each ring, so the activation ring is at
+// least as deep as the Q4 ring; small token tiles (memory-bound) keep 12 Q4
+// tiles (48 KB) per CTA in flight.
 template <int BN, bool A_TMEM>
 struct Smem {
+    static constexpr int SQ = A_TMEM ? (BN <= 32 ? 12 : 8) : 8;
+    static constexpr int SB = A_TMEM ? (BN <= 32 ? 14 : 9) : 4;
     static constexpr int A_BYTES = 128 * KT * 2;          // 16384
     static constexpr int B_BYTES = BN * KT * 2;
     static constexpr int Q_BYTES = 128 * KT / 2;          // 4096
@@ -237,11 +241,13 @@ __host__ __device__ constexpr uint32_t tmem_cols(int BN, bool A_TMEM) {
 
 // ------------------------------------------------------------ work list
 struct Item {
-    int u, e, rt, tt, n, s0;
+    int u, e, rt, tt, n, s0, ks;
 };
 
 __device__ __forceinline__ bool decode_item(const TcArgs& a, int64_t item, int row_tiles, int BN,
                                             Item& it) {
+    it.ks = (int)(item % a.ksplit);  // split-K index (PLAIN mode), fastest varying
+    item /= a.ksplit;
     if (a.dense_tokens > 0) {
         const int ntt = (a.dense_tokens + BN - 1) / BN;
         if (item >= (int64_t)row_tiles * ntt) return false;
@@ -279,6 +285,8 @@ template <int MODE, int BN, bool A_TMEM>
 __global__ void __launch_bounds__(THREADS, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap bmap, TcArgs a) {
     using L = Smem<BN, A_TMEM>;
+    constexpr int SQ = L::SQ;
+    constexpr int SB = L::SB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
@@ -297,6 +305,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = a.K, nk = K / KT, nb = K / 32;
+    auto k_begin = [&](const Item& it) { return (int)((int64_t)it.ks * nk / a.ksplit); };
+    auto k_end = [&](const Item& it) { return (int)((int64_t)(it.ks + 1) * nk / a.ksplit); };
     const int row_tiles = (MODE == TC_ACT) ? (a.F / 64) : (int)((a.R + 127) / 128);
     constexpr uint32_t NCOL = tmem_cols(BN, A_TMEM);
     constexpr uint32_t ACOL = (uint32_t)a_col0(BN);
@@ -355,7 +365,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     row_b = row_a + 64;
                 }
                 const int tok_row = it.s0 + it.tt * BN;
-                for (int kt = 0; kt < nk; ++kt) {
+                for (int kt = k_begin(it); kt < k_end(it); ++kt) {
                     if (!(ok = mbar_wait(q_empty(qs), qp ^ 1, G))) break;
                     uint8_t* qd = smem + L::OFF_Q + qs * L::Q_BYTES;
                     mbar_expect_tx(q_full(qs), L::Q_BYTES);
@@ -394,7 +404,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (!(ok = mbar_wait(acc_empty(ab), accp ^ 1, G))) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(ab * BN);
-                for (int kt = 0; kt < nk; ++kt) {
+                const int kb = k_begin(it);
+                for (int kt = kb; kt < k_end(it); ++kt) {
                     if (!(ok = mbar_wait(a_full(as), ap, G))) break;
                     if (!(ok = mbar_wait(b_full(bs), bp, G))) break;
                     tc_fence_after();
@@ -403,13 +414,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint32_t ta = tmem_base + ACOL + (uint32_t)(as * 32);
 #pragma unroll
                         for (int k = 0; k < KT / 16; ++k)
-                            tc_mma_ts(d_tmem, ta + 8u * k, sw128_desc(sb + 32u * k), IDESC, (kt | k) != 0);
+                            tc_mma_ts(d_tmem, ta + 8u * k, sw128_desc(sb + 32u * k), IDESC, (kt != kb) || k);
                     } else {
                         const uint32_t sa = smem_u32(smem + L::OFF_A + as * L::A_BYTES);
 #pragma unroll
                         for (int k = 0; k < KT / 16; ++k)
                             tc_mma(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), IDESC,
-                                   (kt | k) != 0);
+                                   (kt != kb) || k);
                     }
                     issued = true;
                     tc_commit(a_empty(as));
@@ -452,17 +463,19 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             const bool row_ok = (MODE == TC_ACT) || (it.rt * 128 + t < a.R);
             const float* srow = a.Ws + grow * nb;
+            const int kb = k_begin(it), ke = k_end(it);
             float2 sreg[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-                sreg[j] = (row_ok && j < nk) ? __ldg(reinterpret_cast<const float2*>(srow) + j) : make_float2(0.f, 0.f);
-            for (int kt0 = 0; kt0 < nk && ok; kt0 += 4) {
+                sreg[j] = (row_ok && kb + j < ke) ? __ldg(reinterpret_cast<const float2*>(srow) + kb + j)
+                                                  : make_float2(0.f, 0.f);
+            for (int kt0 = kb; kt0 < ke && ok; kt0 += 4) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int kt = kt0 + j;
-                    if (kt >= nk) break;
+                    if (kt >= ke) break;
                     const float2 s = sreg[j];
-                    if (row_ok && kt + 4 < nk) sreg[j] = __ldg(reinterpret_cast<const float2*>(srow) + kt + 4);
+                    if (row_ok && kt + 4 < ke) sreg[j] = __ldg(reinterpret_cast<const float2*>(srow) + kt + 4);
                     if (!(ok = mbar_wait(q_full(qs), qp, G))) break;
                     if (!(ok = mbar_wait(a_empty(as), ap ^ 1, G))) break;
                     const uint8_t* qrow = smem + L::OFF_Q + qs * L::Q_BYTES + sr * 32;
@@ -552,7 +565,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             if (c0 + cc < nv) {
                                 const int p = it.s0 + it.tt * BN + c0 + cc;
                                 const int64_t orow = a.out_row ? a.out_row[p] : p;
-                                a.y_out[orow * a.y_stride + r] = v[cc];
+                                a.y_out[it.ks * a.split_stride + orow * a.y_stride + r] = v[cc];
                             }
                         }
                     }
@@ -708,6 +721,22 @@ int launch_mode(const TcLaunch& L, int num_sms, cudaStream_t s) {
 
 int launch_tc_gemm(int mode, const TcLaunch& L, int num_sms, cudaStream_t s) {
     return mode == TC_ACT ? launch_mode<TC_ACT>(L, num_sms, s) : launch_mode<TC_PLAIN>(L, num_sms, s);
+}
+
+// out[i] = sum over s < splits of part[s * stride + i] (fixed order)
+__global__ void k_reduce_splits(const float* part, int64_t stride, int splits, float* out, int64_t n) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float v = part[i];
+    for (int s = 1; s < splits; ++s) v += part[s * stride + i];
+    out[i] = v;
+}
+
+int launch_reduce_splits(const float* part, int64_t stride, int splits, float* out, int64_t n,
+                         cudaStream_t s) {
+    if (n <= 0) return 0;
+    k_reduce_splits<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, stride, splits, out, n);
+    return 1;
 }
 
 int launch_tt_prefix(const int* meta, const int* seg_count, int BN, int* tt_prefix, cudaStream_t s) {

@@ -24,6 +24,8 @@ struct TcArgs {
     float* y_out = nullptr;         // PLAIN: rows of y_stride floats
     int64_t y_stride = 0;
     const int* out_row = nullptr;   // PLAIN: output row of pair p (nullptr: p)
+    int ksplit = 1;                 // PLAIN: K split into this many partial sums
+    int64_t split_stride = 0;       // PLAIN: floats between the partial-sum buffers
     int* err_flag = nullptr;        // set to 2 when a bounded wait expires
     uint64_t timeout_ns = 4000000000ull;
 };
@@ -46,5 +48,7 @@ int launch_tt_prefix(const int* meta, const int* seg_count, int BN, int* tt_pref
 int launch_gather_f16(const float* X, int64_t K, const int* pair_row, const int* meta, int64_t rows,
                       int dense_rows, __half* out, cudaStream_t s);
 bool tc_supported(int64_t K, int64_t R, int act_mode, int64_t F);
+int launch_reduce_splits(const float* part, int64_t stride, int splits, float* out, int64_t n,
+                         cudaStream_t s);
 
 }  // namespace moe
