@@ -87,8 +87,10 @@ enum moe_option {
     MOE_OPT_DEVICE_TIMEOUT_NS = 3, /* deadline of every device-side wait (default 4 s) */
     MOE_OPT_DENSE_TC_MIN_TOKENS = 4, /* auto path, dense projections and router: tensor cores from this
                                         many tokens (default 2) */
-    MOE_OPT_TC_A_IN_SMEM = 5       /* 1: stage the dequantised weights in shared memory even for token
+    MOE_OPT_TC_A_IN_SMEM = 5,      /* 1: stage the dequantised weights in shared memory even for token
                                       tiles <= 64 (default 0: tensor memory) */
+    MOE_OPT_ROUTER_TC_MIN_TOKENS = 6 /* router on tensor cores from this many tokens (default 2048;
+                                        below it the router runs in fp32 like the reference) */
 };
 enum moe_gemm_path {
     MOE_PATH_AUTO = 0, /* CUDA-core GEMV for few tokens, tensor cores above the threshold */

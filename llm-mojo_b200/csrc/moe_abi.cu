@@ -54,7 +54,8 @@ struct moe_ctx {
     cudaEvent_t done = nullptr;
     int gemm_path = MOE_PATH_AUTO;       // moe_set_option(MOE_OPT_GEMM_PATH)
     int tc_min_tokens = 1;               // auto: tensor cores from this many tokens
-    int dense_tc_min_tokens = 2;         // auto, dense projections and router
+    int dense_tc_min_tokens = 2;         // auto, dense projections
+    int router_tc_min_tokens = 2048;     // router on tensor cores from this many tokens
     bool tc_a_in_smem = false;           // MOE_OPT_TC_A_IN_SMEM
     uint64_t device_timeout_ns = 4000000000ull;
     // profiling (moe_profile_enable)
@@ -519,19 +520,8 @@ int dense_q4(moe_ctx* ctx, const uint8_t* w, const float* sc, const float* xd, f
             ctx->launches += moe::launch_reduce_splits(part, batch * c_out, ks, od, batch * c_out, ctx->stream);
         return MOE_OK;
     }
-    moe::GemvArgs g;
-    g.Wp = w;
-    g.Ws = sc;
-    g.rows_per_expert = c_out;
-    g.K = (int)c_in;
-    g.X = xd;
-    g.dense_tokens = (int)batch;
-    g.out = od;
-    g.out_stride = c_out;
-    g.max_tokens = (int)batch;
-    g.max_unique = 1;
     ProfScope ps(ctx, prof_name);
-    ctx->launches += moe::launch_gemv(moe::GEMV_PLAIN, g, ctx->num_sms, ctx->stream);
+    ctx->launches += moe::launch_gemv_wide(w, sc, xd, od, c_out, (int)c_in, (int)batch, c_out, ctx->stream);
     return MOE_OK;
 }
 
@@ -649,6 +639,10 @@ int moe_set_option(moe_ctx* ctx, int option, int64_t value) {
             return MOE_OK;
         case MOE_OPT_TC_A_IN_SMEM:
             ctx->tc_a_in_smem = value != 0;
+            return MOE_OK;
+        case MOE_OPT_ROUTER_TC_MIN_TOKENS:
+            if (value < 1) return fail(ctx, MOE_E_ARG, "bad token threshold");
+            ctx->router_tc_min_tokens = (int)value;
             return MOE_OK;
         default:
             return fail(ctx, MOE_E_ARG, "unknown option");
@@ -1196,8 +1190,11 @@ int route_dev(moe_ctx* ctx, const moe_layer_desc* L, const LayerDev& ld, int64_t
         ProfScope ps(ctx, "prep");
         ctx->launches += moe::launch_prep(pa, M, s);
     }
-    if (ld.rp) {
+    if (ld.rp && M >= ctx->router_tc_min_tokens && ctx->gemm_path != MOE_PATH_GEMV) {
         TRY(dense_q4(ctx, ld.rp, ld.rs, scaled, scores, d, E, M, "router"));
+    } else if (ld.rp) {  // fp32 router: routing follows the reference's arithmetic
+        ProfScope ps(ctx, "router");
+        ctx->launches += moe::launch_gemv_wide(ld.rp, ld.rs, scaled, scores, E, (int)d, (int)M, E, s);
     } else {
         ProfScope ps(ctx, "router");
         ctx->launches += moe::launch_gemv_f32(ld.rf32, scaled, scores, M, E, d, s);

@@ -110,6 +110,8 @@ int launch_slots_from_topw(int64_t M, int K, const int64_t* idx, const float* w,
 int launch_bucket(const int* slot_expert, int64_t P, int K, int E, const BucketOut& o,
                   cudaStream_t s);
 int launch_gemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);
+int launch_gemv_wide(const uint8_t* W, const float* S, const float* X, float* out, int64_t rows, int K,
+                     int ntok, int64_t out_stride, cudaStream_t s);
 int launch_combine(const CombineArgs& a, int64_t M, cudaStream_t s);
 int launch_quantize(const float* src, uint8_t* packed, float* scales, int64_t nblocks,
                     cudaStream_t s);

@@ -330,6 +330,59 @@ int launch_gemv_f32(const float* W, const float* X, float* out, int64_t M, int64
     return 1;
 }
 
+// ------------------------------------------------------------ wide GEMV
+// Dense Q4_0 GEMV for few rows and few tokens (the router: 128 rows): one
+// warp per (row, chunk of up to 4 tokens), lanes across K (lane takes blocks
+// lane, lane+32, ...), exact (n-8) dequant, fp32 FMA, full-warp reduction.
+// Token chunks vary slowest so the warps of an SM share the activation rows
+// in L1.
+template <int T>
+__global__ void __launch_bounds__(256) k_gemv_wide(const uint8_t* __restrict__ W, const float* __restrict__ S,
+                                                   const float* __restrict__ X, float* __restrict__ out,
+                                                   int64_t rows, int K, int ntok, int64_t out_stride) {
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nb = K >> 5;
+    const int64_t chunks = (ntok + T - 1) / T;
+    if (gw >= rows * chunks) return;
+    const int64_t r = gw % rows;
+    const int t0 = (int)(gw / rows) * T;
+    const int nt = min(T, ntok - t0);
+    float acc[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) acc[t] = 0.f;
+    const uint8_t* wr = W + r * (K >> 1);
+    const float* sr = S + r * nb;
+    for (int b = lane; b < nb; b += 32) {
+        const uint4 q = ldg_stream(wr + b * 16);
+        const float s = __ldg(sr + b);
+        const float* xp[T];
+#pragma unroll
+        for (int t = 0; t < T; ++t) xp[t] = X + (int64_t)(t0 + (t < nt ? t : 0)) * K + b * 32;
+        float d[T];
+        block_dot<false, T>(q, xp, d);
+#pragma unroll
+        for (int t = 0; t < T; ++t) acc[t] = fmaf(s, d[t], acc[t]);
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const float v = warp_sum(acc[t]);
+        if (lane == 0 && t < nt) out[(int64_t)(t0 + t) * out_stride + r] = v;
+    }
+}
+
+int launch_gemv_wide(const uint8_t* W, const float* S, const float* X, float* out, int64_t rows, int K,
+                     int ntok, int64_t out_stride, cudaStream_t s) {
+    if (rows <= 0 || ntok <= 0) return 0;
+    const int T = ntok >= 4 ? 4 : (ntok >= 2 ? 2 : 1);
+    const int64_t warps = rows * ((ntok + T - 1) / T);
+    const unsigned blocks = (unsigned)((warps + 7) / 8);
+    if (T == 4) k_gemv_wide<4><<<blocks, 256, 0, s>>>(W, S, X, out, rows, K, ntok, out_stride);
+    else if (T == 2) k_gemv_wide<2><<<blocks, 256, 0, s>>>(W, S, X, out, rows, K, ntok, out_stride);
+    else k_gemv_wide<1><<<blocks, 256, 0, s>>>(W, S, X, out, rows, K, ntok, out_stride);
+    return 1;
+}
+
 // ------------------------------------------------------------ row prep
 // One CTA per row: layout conversion (moe_x_layout), fp16 -> fp32, optional
 // rms norms (model_speculative_moe_batched.mojo:857-879): out = x * inv *

@@ -23,7 +23,7 @@ ACT_SIGMOID1702, ACT_GELU_TANH = 0, 1
 X_NATURAL, X_DEINT_HALVES, X_DEINT_BLOCK32 = 0, 1, 2
 F_POST_NORM, F_SET_COVER, F_FP16_OUT = 1, 4, 8
 OPT_GEMM_PATH, OPT_TC_MIN_TOKENS, OPT_DEVICE_TIMEOUT_NS = 1, 2, 3
-OPT_DENSE_TC_MIN_TOKENS, OPT_TC_A_IN_SMEM = 4, 5
+OPT_DENSE_TC_MIN_TOKENS, OPT_TC_A_IN_SMEM, OPT_ROUTER_TC_MIN_TOKENS = 4, 5, 6
 PATH_AUTO, PATH_GEMV, PATH_TC = 0, 1, 2
 
 STATUS = {0: "MOE_OK", 1: "MOE_E_ARG", 2: "MOE_E_SHAPE", 3: "MOE_E_UNREGISTERED",
