@@ -225,7 +225,8 @@ def workload_config(args, M):
             "layers_cycled": args.layers,
             "l2": f"weights of {args.layers} distinct layers cycled per step ({args.layers * 476} MB > 126 MB L2)",
             "post_norm": True, "parallelism": f"replicas x{dist_setup()[0]}",
-            "gemm_path": getattr(args, "path", "auto")}
+            "gemm_path": getattr(args, "path", "auto"),
+            "cuda_graph": not getattr(args, "no_graph", False)}
 
 
 # ----------------------------------------------------------------- GPU leg
@@ -239,6 +240,7 @@ def main():
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"],
                     help="expert/dense GEMM path: CUDA-core GEMV, tcgen05, or automatic")
     args = ap.parse_args()
@@ -304,6 +306,31 @@ def main():
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+
+    # One CUDA graph per layer holding a whole step (the library's calls are
+    # asynchronous and allocation-free once warm), replayed step by step.
+    graphs, launches_per_step = [], None
+    if not args.no_graph:
+        cap = torch.cuda.Stream()
+        ctx.set_stream(cap.cuda_stream)
+        n_cap = ctx.kernel_launches
+        for li in range(args.layers):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                step(li)
+            graphs.append(g)
+        launches_per_step = (ctx.kernel_launches - n_cap) / args.layers
+        ctx.set_stream(stream.cuda_stream)
+        for i in range(args.warmup):
+            graphs[i % args.layers].replay()
+        torch.cuda.synchronize()
+
+    def run_step(i):
+        if graphs:
+            graphs[i % args.layers].replay()
+        else:
+            step(i)
+
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
@@ -312,10 +339,10 @@ def main():
     with ClockSampler(local) as clk:
         ev0.record(stream)
         for i in range(args.steps):
-            step(i)
+            run_step(i)
         ev1.record(stream)
         torch.cuda.synchronize()
-    launches = ctx.kernel_launches - n0
+    launches = ctx.kernel_launches - n0 if not graphs else int(round(launches_per_step * args.steps))
     ms = ev0.elapsed_time(ev1)
     if pg:
         t = torch.tensor([ms], device="cuda")
