@@ -394,12 +394,24 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
     __shared__ float red[33];
     const int64_t K = a.K, t = blockIdx.x;
     float ss = 0.f;
-    for (int64_t j = threadIdx.x; j < K; j += blockDim.x) {
-        const int64_t si = t * K + x_src_index(j, K, a.x_layout);
-        const float v = a.x_f16 ? __half2float(reinterpret_cast<const __half*>(a.x)[si])
-                                : reinterpret_cast<const float*>(a.x)[si];
-        xs[j] = v;
-        ss += v * v;
+    if (a.x_layout == 0 && !a.x_f16 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0) {
+        // natural fp32 rows: float4 loads, several in flight per thread
+        const float4* x4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.x) + t * K);
+#pragma unroll 4
+        for (int64_t j = threadIdx.x; j < K / 4; j += blockDim.x) {
+            const float4 v = __ldg(x4 + j);
+            reinterpret_cast<float4*>(xs)[j] = v;
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+    } else {
+#pragma unroll 4
+        for (int64_t j = threadIdx.x; j < K; j += blockDim.x) {
+            const int64_t si = t * K + x_src_index(j, K, a.x_layout);
+            const float v = a.x_f16 ? __half2float(reinterpret_cast<const __half*>(a.x)[si])
+                                    : reinterpret_cast<const float*>(a.x)[si];
+            xs[j] = v;
+            ss += v * v;
+        }
     }
     float inv = 1.f;
     if (a.norm) {
@@ -408,10 +420,11 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
     } else {
         __syncthreads();
     }
+#pragma unroll 4
     for (int64_t j = threadIdx.x; j < K; j += blockDim.x) {
         const float v = xs[j];
-        if (a.scaled) a.scaled[t * K + j] = v * inv * a.router_scale[j] * a.rsf;
-        const float o = a.norm ? v * inv * a.pre_w[j] : v;
+        if (a.scaled) a.scaled[t * K + j] = v * inv * __ldg(a.router_scale + j) * a.rsf;
+        const float o = a.norm ? v * inv * __ldg(a.pre_w + j) : v;
         xs[j] = o;
         a.out[t * K + j] = o;
     }
@@ -428,8 +441,8 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
 int launch_prep(const PrepArgs& a, int64_t M, cudaStream_t s) {
     if (M <= 0) return 0;
     const size_t smem = (size_t)a.K * sizeof(float);
-    cudaFuncSetAttribute(k_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_prep<<<(unsigned)M, 256, smem, s>>>(a);
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_prep<<<(unsigned)M, 512, smem, s>>>(a);
     return 1;
 }
 
@@ -830,7 +843,7 @@ int launch_bucket(const int* slot_expert, int64_t P, int K, int E, const BucketO
 // (moe_kernels.mojo:775-779, diffusion_kernels.mojo:386-399), then optionally
 // rms_norm with post_feedforward_layernorm_2 (model_speculative_moe_batched
 // .mojo:1144-1150) and fp16 rounding.  float4 per thread, d % 4 == 0.
-__global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
+__global__ void __launch_bounds__(512) k_combine(CombineArgs a) {
     __shared__ float red[33];
     __shared__ int sp[32];
     __shared__ float sw[32];
@@ -842,7 +855,7 @@ __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
     }
     __syncthreads();
     const int64_t d4 = a.d / 4;
-    constexpr int MAXV = 12;  // d <= 12288 keeps the row in registers
+    constexpr int MAXV = 6;  // 512 threads x 6 float4: d <= 12288 kept in registers
     float4 acc[MAXV];
     float ss = 0.f;
 #pragma unroll
@@ -850,6 +863,7 @@ __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
         const int64_t j = threadIdx.x + (int64_t)i * blockDim.x;
         float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
         if (j < d4) {
+#pragma unroll 8
             for (int k = 0; k < K; ++k) {
                 const int p = sp[k];
                 if (p < 0) continue;
@@ -898,7 +912,7 @@ __global__ void __launch_bounds__(256) k_combine(CombineArgs a) {
 
 int launch_combine(const CombineArgs& a, int64_t M, cudaStream_t s) {
     if (M <= 0) return 0;
-    k_combine<<<(unsigned)M, 256, 0, s>>>(a);
+    k_combine<<<(unsigned)M, 512, 0, s>>>(a);
     return 1;
 }
 

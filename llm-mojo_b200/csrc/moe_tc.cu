@@ -62,14 +62,17 @@ __device__ __forceinline__ void mbar_arrive(uint32_t a) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
 }
+// try_wait with a suspend-time hint: a waiting warp sleeps until the phase
+// completes (or ~50 us pass) instead of polling, leaving the issue slots to
+// the dequant warps.
 __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(a), "r"(parity)
+        : "r"(a), "r"(parity), "r"(50000u)
         : "memory");
     return ok != 0;
 }
@@ -85,7 +88,7 @@ struct Guard {
 __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, const Guard& g) {
     for (uint32_t it = 0;; ++it) {
         if (mbar_try(a, parity)) return true;
-        if ((it & 255u) == 255u) {
+        if ((it & 15u) == 15u) {
             if (*g.abort) return false;
             if (globaltimer() > g.deadline) {
                 *g.abort = 1;
@@ -464,18 +467,19 @@ __global__ void __launch_bounds__(THREADS, 1)
             const bool row_ok = (MODE == TC_ACT) || (it.rt * 128 + t < a.R);
             const float* srow = a.Ws + grow * nb;
             const int kb = k_begin(it), ke = k_end(it);
-            float2 sreg[4];
+            constexpr int PF = 8;  // scale prefetch distance in k-tiles
+            float2 sreg[PF];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int j = 0; j < PF; ++j)
                 sreg[j] = (row_ok && kb + j < ke) ? __ldg(reinterpret_cast<const float2*>(srow) + kb + j)
                                                   : make_float2(0.f, 0.f);
-            for (int kt0 = kb; kt0 < ke && ok; kt0 += 4) {
+            for (int kt0 = kb; kt0 < ke && ok; kt0 += PF) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
+                for (int j = 0; j < PF; ++j) {
                     const int kt = kt0 + j;
                     if (kt >= ke) break;
                     const float2 s = sreg[j];
-                    if (row_ok && kt + 4 < ke) sreg[j] = __ldg(reinterpret_cast<const float2*>(srow) + kt + 4);
+                    if (row_ok && kt + PF < ke) sreg[j] = __ldg(reinterpret_cast<const float2*>(srow) + kt + PF);
                     if (!(ok = mbar_wait(q_full(qs), qp, G))) break;
                     if (!(ok = mbar_wait(a_empty(as), ap ^ 1, G))) break;
                     const uint8_t* qrow = smem + L::OFF_Q + qs * L::Q_BYTES + sr * 32;
