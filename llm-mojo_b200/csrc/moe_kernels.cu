@@ -388,7 +388,7 @@ int launch_gemv_wide(const uint8_t* W, const float* S, const float* X, float* ou
 // rms norms (model_speculative_moe_batched.mojo:857-879): out = x * inv *
 // pre_w and scaled = x * inv * router_scale * r_scale_factor; and the
 // per-32-block sums (x1.5) the XS GEMV needs.
-__global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
+__global__ void __launch_bounds__(512) k_prep(PrepArgs a) {
     extern __shared__ float4 smem4[];
     float* xs = reinterpret_cast<float*>(smem4);
     __shared__ float red[33];
