@@ -4,13 +4,14 @@
 // tile, token tile) work item of a device-side list, "swap-AB": the weight
 // rows are the MMA's M = 128, the tokens its N = BN.
 //
-// Warp roles (320 threads):
+// Warp roles (448 threads):
 //   warp 0     TMA producer: packed Q4 tiles (SWIZZLE_32B) and fp16
 //              activation tiles (SWIZZLE_128B) into smem rings.
 //   warp 1     TMEM owner and single-thread tcgen05.mma issuer; fp32
 //              accumulators live in TMEM, double-buffered across items.
-//   warps 2-5  dequant: the thread owning A-tile row t turns the row's 64
-//              nibbles of a k-tile into fp16.  Two variants of the A operand:
+//   warps 2-9  dequant: two warps per TMEM lane quarter; the thread owning
+//              A-tile row t and K half h turns the row's 32 nibbles of that
+//              half of a k-tile into fp16.  Two variants of the A operand:
 //              A_TMEM (token tiles <= 64, memory-bound): (n-8) exact in fp16
 //                via one LOP3 per nibble pair, times the fp16 scale (HMUL2),
 //                stored with tcgen05.st straight into TMEM; the MMA reads A
@@ -19,7 +20,7 @@
 //              A in shared memory (large token tiles, compute-bound):
 //                (n-8)*scale in fp32, one rounding to fp16, stored in the UMMA
 //                K-major SWIZZLE_128B layout.
-//   warps 6-9  epilogue: tcgen05.ld of the accumulator; ACT mode pairs gate
+//   warps 10-13 epilogue: tcgen05.ld of the accumulator; ACT mode pairs gate
 //              and up rows with a warp shuffle and writes the activated
 //              result as fp16, PLAIN mode writes fp32 rows.
 //
@@ -62,17 +63,14 @@ __device__ __forceinline__ void mbar_arrive(uint32_t a) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
 }
-// try_wait with a suspend-time hint: a waiting warp sleeps until the phase
-// completes (or ~50 us pass) instead of polling, leaving the issue slots to
-// the dequant warps.
 __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(a), "r"(parity), "r"(50000u)
+        : "r"(a), "r"(parity)
         : "memory");
     return ok != 0;
 }
@@ -88,7 +86,7 @@ struct Guard {
 __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, const Guard& g) {
     for (uint32_t it = 0;; ++it) {
         if (mbar_try(a, parity)) return true;
-        if ((it & 15u) == 15u) {
+        if ((it & 255u) == 255u) {
             if (*g.abort) return false;
             if (globaltimer() > g.deadline) {
                 *g.abort = 1;
@@ -142,6 +140,16 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+
+// tcgen05.st 32 lanes x 32 bit x 16 columns (this thread's lane, 16 values)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // tcgen05.st 32 lanes x 32 bit x 32 columns (this thread's lane, 32 values)
@@ -210,7 +218,9 @@ __device__ __forceinline__ int kpos(int m) { return m < 4 ? 2 * m : 2 * (m - 4) 
 // ---------------------------------------------------------------- layout
 constexpr int SA = 3;             // fp16 A ring stages (16 KB in smem, or 32 TMEM columns)
 constexpr int KT = 64;            // K per k-tile
-constexpr int THREADS = 320;
+constexpr int THREADS = 448;
+constexpr int DQ_WARPS = 8;        // warps 2-9: two per TMEM lane quarter, one K half each
+constexpr int EPI_WARP0 = 2 + DQ_WARPS;
 
 // Ring depths.  The producer issues a Q4 tile and an activation tile per
 // k-tile and waits for a free slot in each ring, so the activation ring is at
@@ -285,7 +295,7 @@ __device__ __forceinline__ bool decode_item(const TcArgs& a, int64_t item, int r
 
 // -------------------------------------------------------------- kernel
 template <int MODE, int BN, bool A_TMEM>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap bmap, TcArgs a) {
     using L = Smem<BN, A_TMEM>;
     constexpr int SQ = L::SQ;
@@ -317,10 +327,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < SQ; ++s) {
             mbar_init(q_full(s), 1);
-            mbar_init(q_empty(s), 4);
+            mbar_init(q_empty(s), DQ_WARPS);
         }
         for (int s = 0; s < SA; ++s) {
-            mbar_init(a_full(s), 4);
+            mbar_init(a_full(s), DQ_WARPS);
             mbar_init(a_empty(s), 1);
         }
         for (int s = 0; s < SB; ++s) {
@@ -443,11 +453,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mbar_wait(drain_bar, 0, Gd);
             }
         }
-    } else if (warp < 6) {
+    } else if (warp < EPI_WARP0) {
         // ------------------------------------------------ dequant
-        // row of the A tile; with A in TMEM a warp may only write its own lane
-        // quarter (warp % 4), so the row follows the quarter
-        const int t = A_TMEM ? ((warp & 3) * 32 + lane) : (threadIdx.x - 64);
+        // A-tile row t follows the warp's TMEM lane quarter (warp % 4); the two
+        // warps of a quarter take K half h = 0 / 1 of every k-tile (one 16-byte
+        // Q4 chunk = one 32-weight block with its own scale).
+        const int h = (warp - 2) >> 2;
+        const int t = (warp & 3) * 32 + lane;
         int qs = 0, as = 0;
         uint32_t qp = 0, ap = 0;
         Item it;
@@ -465,63 +477,59 @@ __global__ void __launch_bounds__(THREADS, 1)
                 grow = (int64_t)it.e * a.R + it.rt * 128 + t;
             }
             const bool row_ok = (MODE == TC_ACT) || (it.rt * 128 + t < a.R);
-            const float* srow = a.Ws + grow * nb;
+            const float* srow = a.Ws + grow * nb + h;  // scale of block 2*kt + h
             const int kb = k_begin(it), ke = k_end(it);
             constexpr int PF = 8;  // scale prefetch distance in k-tiles
-            float2 sreg[PF];
+            float sreg[PF];
 #pragma unroll
-            for (int j = 0; j < PF; ++j)
-                sreg[j] = (row_ok && kb + j < ke) ? __ldg(reinterpret_cast<const float2*>(srow) + kb + j)
-                                                  : make_float2(0.f, 0.f);
+            for (int j = 0; j < PF; ++j) sreg[j] = (row_ok && kb + j < ke) ? __ldg(srow + 2 * (kb + j)) : 0.f;
             for (int kt0 = kb; kt0 < ke && ok; kt0 += PF) {
 #pragma unroll
                 for (int j = 0; j < PF; ++j) {
                     const int kt = kt0 + j;
                     if (kt >= ke) break;
-                    const float2 s = sreg[j];
-                    if (row_ok && kt + PF < ke) sreg[j] = __ldg(reinterpret_cast<const float2*>(srow) + kt + PF);
+                    const float s = sreg[j];
+                    if (row_ok && kt + PF < ke) sreg[j] = __ldg(srow + 2 * (kt + PF));
                     if (!(ok = mbar_wait(q_full(qs), qp, G))) break;
                     if (!(ok = mbar_wait(a_empty(as), ap ^ 1, G))) break;
-                    const uint8_t* qrow = smem + L::OFF_Q + qs * L::Q_BYTES + sr * 32;
                     const int sw = ((sr >> 2) & 1) << 4;  // SWIZZLE_32B: chunk ^= row bit 2
-                    const uint4 c0 = *reinterpret_cast<const uint4*>(qrow + (0 ^ sw));
-                    const uint4 c1 = *reinterpret_cast<const uint4*>(qrow + (16 ^ sw));
-                    const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                    const uint4 c = *reinterpret_cast<const uint4*>(smem + L::OFF_Q + qs * L::Q_BYTES + sr * 32 +
+                                                                     ((h << 4) ^ sw));
+                    const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
                     if (A_TMEM) {
                         tc_fence_after();
                         // (n-8) exact in fp16: (0x6400 | n) is 1024 + n; times the fp16 scale
-                        const __half2 s0 = __float2half2_rn(s.x), s1 = __float2half2_rn(s.y);
+                        const __half2 sc = __float2half2_rn(s);
                         const __half2 off = __float2half2_rn(1032.0f);
-                        uint32_t h[32];
+                        uint32_t hv[16];
 #pragma unroll
-                        for (int w = 0; w < 8; ++w) {
-                            const __half2 sc = (w < 4) ? s0 : s1;
+                        for (int w = 0; w < 4; ++w)
 #pragma unroll
                             for (int p = 0; p < 4; ++p) {
                                 const uint32_t v = ((wv[w] >> (4 * p)) & 0x000F000Fu) | 0x64006400u;
-                                const __half2 hv = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&v), off), sc);
-                                h[4 * w + p] = *reinterpret_cast<const uint32_t*>(&hv);
+                                const __half2 x = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&v), off), sc);
+                                hv[4 * w + p] = *reinterpret_cast<const uint32_t*>(&x);
                             }
-                        }
-                        tmem_st32(tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + ACOL + (uint32_t)(as * 32), h);
+                        tmem_st16(tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + ACOL + (uint32_t)(as * 32 + 16 * h),
+                                  hv);
                         tc_fence_before();
                     } else {
-                    uint8_t* arow = smem + L::OFF_A + as * L::A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
+                        uint8_t* arow = smem + L::OFF_A + as * L::A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
 #pragma unroll
-                    for (int w = 0; w < 8; ++w) {
-                        const float sc = (w < 4) ? s.x : s.y;
-                        uint32_t h[4];
+                        for (int w = 0; w < 4; ++w) {
+                            uint32_t hh[4];
 #pragma unroll
-                        for (int p = 0; p < 4; ++p) {
-                            const uint32_t v = (wv[w] >> (4 * p)) & 0x000F000Fu;
-                            const float lo = (__uint_as_float(0x4B000000u | (v & 0xFFFFu)) - 8388616.0f) * sc;
-                            const float hi = (__uint_as_float(0x4B000000u | (v >> 16)) - 8388616.0f) * sc;
-                            const __half2 hh = __floats2half2_rn(lo, hi);
-                            h[p] = *reinterpret_cast<const uint32_t*>(&hh);
+                            for (int p = 0; p < 4; ++p) {
+                                const uint32_t v = (wv[w] >> (4 * p)) & 0x000F000Fu;
+                                const float lo = (__uint_as_float(0x4B000000u | (v & 0xFFFFu)) - 8388616.0f) * s;
+                                const float hi = (__uint_as_float(0x4B000000u | (v >> 16)) - 8388616.0f) * s;
+                                const __half2 x = __floats2half2_rn(lo, hi);
+                                hh[p] = *reinterpret_cast<const uint32_t*>(&x);
+                            }
+                            const int cw = 4 * h + w;  // 16-byte chunk of the 128-byte row
+                            *reinterpret_cast<uint4*>(arow + ((cw ^ (t & 7)) << 4)) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
                         }
-                        *reinterpret_cast<uint4*>(arow + ((w ^ (t & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
-                    }
-                    fence_async_smem();
+                        fence_async_smem();
                     }
                     __syncwarp();
                     if (lane == 0) {
@@ -690,7 +698,12 @@ int launch_t(const TcLaunch& L, int num_sms, cudaStream_t s) {
     int per_sm = (227 * 1024) / smem;
     const int by_tmem = 512 / (int)tc::tmem_cols(BN, A_TMEM);
     if (per_sm > by_tmem) per_sm = by_tmem;
-    if (per_sm > 2) per_sm = 2;  // 320 threads x 2 = 20 warps; registers allow no more
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess && fa.numRegs > 0) {
+        const int by_regs = 65536 / (fa.numRegs * tc::THREADS);
+        if (per_sm > by_regs) per_sm = by_regs;
+    }
+    if (per_sm > 2) per_sm = 2;
     if (per_sm < 1) per_sm = 1;
     int grid = num_sms * per_sm;
     if (L.max_items > 0 && L.max_items < grid) grid = (int)L.max_items;
