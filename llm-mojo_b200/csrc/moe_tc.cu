@@ -216,7 +216,7 @@ __host__ __device__ constexpr uint32_t f16_idesc(int M, int N) {
 __device__ __forceinline__ int kpos(int m) { return m < 4 ? 2 * m : 2 * (m - 4) + 1; }
 
 // ---------------------------------------------------------------- layout
-constexpr int SA = 3;             // fp16 A ring stages (16 KB in smem, or 32 TMEM columns)
+constexpr int SA_SMEM = 3;        // fp16 A ring stages in shared memory (16 KB each)
 constexpr int KT = 64;            // K per k-tile
 constexpr int THREADS = 448;
 constexpr int DQ_WARPS = 8;        // warps 2-9: two per TMEM lane quarter, one K half each
@@ -228,6 +228,7 @@ constexpr int EPI_WARP0 = 2 + DQ_WARPS;
 // tiles (48 KB) per CTA in flight.
 template <int BN, bool A_TMEM>
 struct Smem {
+    static constexpr int SA = A_TMEM ? sa_tmem(BN) : SA_SMEM;
     static constexpr int SQ = A_TMEM ? (BN <= 32 ? 12 : 8) : 8;
     static constexpr int SB = A_TMEM ? (BN <= 32 ? 14 : 9) : 4;
     static constexpr int A_BYTES = 128 * KT * 2;          // 16384
@@ -242,6 +243,10 @@ struct Smem {
     static constexpr int TOTAL = OFF_MISC + 16 + 1024;    // + alignment slack
 };
 
+// A stages in TMEM (32 columns each): as many as fit next to the two
+// accumulator buffers in 256 columns, so two CTAs share an SM's 512.
+__host__ __device__ constexpr int a_col0(int BN);
+__host__ __device__ constexpr int sa_tmem(int BN) { return (256 - a_col0(BN)) / 32; }
 __host__ __device__ constexpr uint32_t pow2_cols(int n) {
     return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u;
 }
@@ -249,7 +254,7 @@ __host__ __device__ constexpr uint32_t pow2_cols(int n) {
 // SA stages of the fp16 A tile, 32 columns (64 fp16 per lane) each.
 __host__ __device__ constexpr int a_col0(int BN) { return ((2 * BN + 31) / 32) * 32; }
 __host__ __device__ constexpr uint32_t tmem_cols(int BN, bool A_TMEM) {
-    return pow2_cols(A_TMEM ? a_col0(BN) + SA * 32 : 2 * BN);
+    return pow2_cols(A_TMEM ? a_col0(BN) + sa_tmem(BN) * 32 : 2 * BN);
 }
 
 // ------------------------------------------------------------ work list
@@ -300,6 +305,7 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
     using L = Smem<BN, A_TMEM>;
     constexpr int SQ = L::SQ;
     constexpr int SB = L::SB;
+    constexpr int SA = L::SA;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
