@@ -222,6 +222,12 @@ constexpr int THREADS = 448;
 constexpr int DQ_WARPS = 8;        // warps 2-9: two per TMEM lane quarter, one K half each
 constexpr int EPI_WARP0 = 2 + DQ_WARPS;
 
+// TMEM columns: two fp32 accumulator buffers of BN columns from column 0;
+// with A in TMEM, A stages (32 columns = 64 fp16 per lane) start at a_col0
+// and fill the rest of 256 columns, so two CTAs share an SM's 512.
+__host__ __device__ constexpr int a_col0(int BN) { return ((2 * BN + 31) / 32) * 32; }
+__host__ __device__ constexpr int sa_tmem(int BN) { return (256 - a_col0(BN)) / 32; }
+
 // Ring depths.  The producer issues a Q4 tile and an activation tile per
 // k-tile and waits for a free slot in each ring, so the activation ring is at
 // least as deep as the Q4 ring; small token tiles (memory-bound) keep 12 Q4
@@ -243,16 +249,11 @@ struct Smem {
     static constexpr int TOTAL = OFF_MISC + 16 + 1024;    // + alignment slack
 };
 
-// A stages in TMEM (32 columns each): as many as fit next to the two
-// accumulator buffers in 256 columns, so two CTAs share an SM's 512.
-__host__ __device__ constexpr int a_col0(int BN);
-__host__ __device__ constexpr int sa_tmem(int BN) { return (256 - a_col0(BN)) / 32; }
 __host__ __device__ constexpr uint32_t pow2_cols(int n) {
     return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u;
 }
 // TMEM columns: two fp32 accumulator buffers of BN columns, then (A_TMEM)
 // SA stages of the fp16 A tile, 32 columns (64 fp16 per lane) each.
-__host__ __device__ constexpr int a_col0(int BN) { return ((2 * BN + 31) / 32) * 32; }
 __host__ __device__ constexpr uint32_t tmem_cols(int BN, bool A_TMEM) {
     return pow2_cols(A_TMEM ? a_col0(BN) + sa_tmem(BN) * 32 : 2 * BN);
 }
