@@ -4,14 +4,14 @@
 // tile, token tile) work item of a device-side list, "swap-AB": the weight
 // rows are the MMA's M = 128, the tokens its N = BN.
 //
-// Warp roles (704 threads, one CTA per SM):
+// Warp roles (448 threads):
 //   warp 0     TMA producer: packed Q4 tiles (SWIZZLE_32B) and fp16
 //              activation tiles (SWIZZLE_128B) into smem rings.
 //   warp 1     TMEM owner and single-thread tcgen05.mma issuer; fp32
 //              accumulators live in TMEM, double-buffered across items.
-//   warps 2-17 dequant: four warps per TMEM lane quarter; the thread owning
-//              A-tile row t and K quarter h turns the row's 16 nibbles of
-//              that part of a k-tile into fp16.  Two variants of the A operand:
+//   warps 2-9  dequant: two warps per TMEM lane quarter; the thread owning
+//              A-tile row t and K half h turns the row's 32 nibbles of that
+//              half of a k-tile into fp16.  Two variants of the A operand:
 //              A_TMEM (token tiles <= 64, memory-bound): (n-8) exact in fp16
 //                via one LOP3 per nibble pair, times the fp16 scale (HMUL2),
 //                stored with tcgen05.st straight into TMEM; the MMA reads A
@@ -20,7 +20,7 @@
 //              A in shared memory (large token tiles, compute-bound):
 //                (n-8)*scale in fp32, one rounding to fp16, stored in the UMMA
 //                K-major SWIZZLE_128B layout.
-//   warps 18-21 epilogue: tcgen05.ld of the accumulator; ACT mode pairs gate
+//   warps 10-13 epilogue: tcgen05.ld of the accumulator; ACT mode pairs gate
 //              and up rows with a warp shuffle and writes the activated
 //              result as fp16, PLAIN mode writes fp32 rows.
 //
@@ -142,14 +142,6 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
         : "memory");
 }
 
-// tcgen05.st 32 lanes x 32 bit x 8 columns (this thread's lane, 8 values)
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
-                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-                 : "memory");
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
 // tcgen05.st 32 lanes x 32 bit x 16 columns (this thread's lane, 16 values)
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
@@ -224,30 +216,20 @@ __host__ __device__ constexpr uint32_t f16_idesc(int M, int N) {
 __device__ __forceinline__ int kpos(int m) { return m < 4 ? 2 * m : 2 * (m - 4) + 1; }
 
 // ---------------------------------------------------------------- layout
-constexpr int SA_SMEM = 3;        // fp16 A ring stages in shared memory (16 KB each)
+constexpr int SA = 3;             // fp16 A ring stages (16 KB in smem, or 32 TMEM columns)
 constexpr int KT = 64;            // K per k-tile
-constexpr int DQ_PER_Q = 4;        // dequant warps per TMEM lane quarter
-constexpr int DQ_WARPS = 4 * DQ_PER_Q;  // warps 2..17
-constexpr int KSUB = 64 / DQ_PER_Q;     // K values of a k-tile per dequant thread (16)
+constexpr int THREADS = 448;
+constexpr int DQ_WARPS = 8;        // warps 2-9: two per TMEM lane quarter, one K half each
 constexpr int EPI_WARP0 = 2 + DQ_WARPS;
-constexpr int THREADS = 32 * (EPI_WARP0 + 4);  // 704
-
-// TMEM columns: two fp32 accumulator buffers of BN columns from column 0;
-// with A in TMEM, A stages (32 columns = 64 fp16 per lane) start at a_col0
-// and fill the rest of the SM's 512 columns (one CTA per SM).
-__host__ __device__ constexpr int a_col0(int BN) { return ((2 * BN + 31) / 32) * 32; }
-__host__ __device__ constexpr int sa_tmem(int BN) { return (512 - a_col0(BN)) / 32 > 15 ? 15 : (512 - a_col0(BN)) / 32; }
 
 // Ring depths.  The producer issues a Q4 tile and an activation tile per
-// k-tile and waits for a free slot in each ring, so the activation ring is as
-// deep as the Q4 ring.
+// k-tile and waits for a free slot in each ring, so the activation ring is at
+// least as deep as the Q4 ring; small token tiles (memory-bound) keep 12 Q4
+// tiles (48 KB) per CTA in flight.
 template <int BN, bool A_TMEM>
 struct Smem {
-    static constexpr int SA = A_TMEM ? sa_tmem(BN) : SA_SMEM;
-    // A in TMEM (memory-bound tiles): one CTA per SM keeps 32 Q4 tiles
-    // (128 KB) in flight, about what HBM needs per SM at its ~3 us loaded latency
-    static constexpr int SQ = A_TMEM ? (BN <= 16 ? 32 : BN <= 32 ? 24 : 14) : 8;
-    static constexpr int SB = A_TMEM ? SQ : 4;
+    static constexpr int SQ = A_TMEM ? (BN <= 32 ? 12 : 8) : 8;
+    static constexpr int SB = A_TMEM ? (BN <= 32 ? 14 : 9) : 4;
     static constexpr int A_BYTES = 128 * KT * 2;          // 16384
     static constexpr int B_BYTES = BN * KT * 2;
     static constexpr int Q_BYTES = 128 * KT / 2;          // 4096
@@ -265,8 +247,9 @@ __host__ __device__ constexpr uint32_t pow2_cols(int n) {
 }
 // TMEM columns: two fp32 accumulator buffers of BN columns, then (A_TMEM)
 // SA stages of the fp16 A tile, 32 columns (64 fp16 per lane) each.
+__host__ __device__ constexpr int a_col0(int BN) { return ((2 * BN + 31) / 32) * 32; }
 __host__ __device__ constexpr uint32_t tmem_cols(int BN, bool A_TMEM) {
-    return pow2_cols(A_TMEM ? a_col0(BN) + sa_tmem(BN) * 32 : 2 * BN);
+    return pow2_cols(A_TMEM ? a_col0(BN) + SA * 32 : 2 * BN);
 }
 
 // ------------------------------------------------------------ work list
@@ -312,12 +295,11 @@ __device__ __forceinline__ bool decode_item(const TcArgs& a, int64_t item, int r
 
 // -------------------------------------------------------------- kernel
 template <int MODE, int BN, bool A_TMEM>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap bmap, TcArgs a) {
     using L = Smem<BN, A_TMEM>;
     constexpr int SQ = L::SQ;
     constexpr int SB = L::SB;
-    constexpr int SA = L::SA;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
@@ -382,7 +364,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             int qs = 0, bs = 0;
             uint32_t qp = 0, bp = 0;
-            uint64_t q_armed = 0, b_armed = 0;  // stages armed in their current phase
+            uint32_t q_armed = 0, b_armed = 0;  // stages armed in their current phase
             uint32_t q_par[SQ], b_par[SB];
             Item it;
             bool ok = true;
@@ -402,14 +384,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mbar_expect_tx(q_full(qs), L::Q_BYTES);
                     tma_load_2d(smem_u32(qd), &qmap, q_full(qs), kt * (KT / 2), row_a);
                     tma_load_2d(smem_u32(qd + L::Q_BYTES / 2), &qmap, q_full(qs), kt * (KT / 2), row_b);
-                    q_armed |= 1ull << qs;
+                    q_armed |= 1u << qs;
                     q_par[qs] = qp;
                     if (++qs == SQ) { qs = 0; qp ^= 1; }
                     if (!(ok = mbar_wait(b_empty(bs), bp ^ 1, G))) break;
                     uint8_t* bd = smem + L::OFF_B + bs * L::B_BYTES;
                     mbar_expect_tx(b_full(bs), L::B_BYTES);
                     tma_load_2d(smem_u32(bd), &bmap, b_full(bs), kt * KT, tok_row);
-                    b_armed |= 1ull << bs;
+                    b_armed |= 1u << bs;
                     b_par[bs] = bp;
                     if (++bs == SB) { bs = 0; bp ^= 1; }
                 }
@@ -419,9 +401,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             volatile int no_abort = 0;
             Gd.abort = &no_abort;
             for (int s = 0; s < SQ; ++s)
-                if (q_armed & (1ull << s)) mbar_wait(q_full(s), q_par[s], Gd);
+                if (q_armed & (1u << s)) mbar_wait(q_full(s), q_par[s], Gd);
             for (int s = 0; s < SB; ++s)
-                if (b_armed & (1ull << s)) mbar_wait(b_full(s), b_par[s], Gd);
+                if (b_armed & (1u << s)) mbar_wait(b_full(s), b_par[s], Gd);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
@@ -473,10 +455,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else if (warp < EPI_WARP0) {
         // ------------------------------------------------ dequant
-        // A-tile row t follows the warp's TMEM lane quarter (warp % 4); the
-        // DQ_PER_Q warps of a quarter split every k-tile's 64 K values into
-        // sub-ranges of KSUB (h = 0..DQ_PER_Q-1); block 2*kt + h*KSUB/32 has
-        // the scale.
+        // A-tile row t follows the warp's TMEM lane quarter (warp % 4); the two
+        // warps of a quarter take K half h = 0 / 1 of every k-tile (one 16-byte
+        // Q4 chunk = one 32-weight block with its own scale).
         const int h = (warp - 2) >> 2;
         const int t = (warp & 3) * 32 + lane;
         int qs = 0, as = 0;
@@ -496,14 +477,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 grow = (int64_t)it.e * a.R + it.rt * 128 + t;
             }
             const bool row_ok = (MODE == TC_ACT) || (it.rt * 128 + t < a.R);
-            const float* srow = a.Ws + grow * nb + (h * KSUB) / 32;  // scale of block 2*kt + h*KSUB/32
+            const float* srow = a.Ws + grow * nb + h;  // scale of block 2*kt + h
             const int kb = k_begin(it), ke = k_end(it);
             constexpr int PF = 8;  // scale prefetch distance in k-tiles
             float sreg[PF];
 #pragma unroll
             for (int j = 0; j < PF; ++j) sreg[j] = (row_ok && kb + j < ke) ? __ldg(srow + 2 * (kb + j)) : 0.f;
-            const int sw = ((sr >> 2) & 1) << 4;  // SWIZZLE_32B: 16-byte chunk ^= row bit 2
-            const int qoff = sr * 32 + (((h * KSUB / 2) & ~15) ^ sw) + ((h * KSUB / 2) & 15);
             for (int kt0 = kb; kt0 < ke && ok; kt0 += PF) {
 #pragma unroll
                 for (int j = 0; j < PF; ++j) {
@@ -513,30 +492,31 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (row_ok && kt + PF < ke) sreg[j] = __ldg(srow + 2 * (kt + PF));
                     if (!(ok = mbar_wait(q_full(qs), qp, G))) break;
                     if (!(ok = mbar_wait(a_empty(as), ap ^ 1, G))) break;
-                    const uint2 c = *reinterpret_cast<const uint2*>(smem + L::OFF_Q + qs * L::Q_BYTES + qoff);
-                    const uint32_t wv[2] = {c.x, c.y};
+                    const int sw = ((sr >> 2) & 1) << 4;  // SWIZZLE_32B: chunk ^= row bit 2
+                    const uint4 c = *reinterpret_cast<const uint4*>(smem + L::OFF_Q + qs * L::Q_BYTES + sr * 32 +
+                                                                     ((h << 4) ^ sw));
+                    const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
                     if (A_TMEM) {
                         tc_fence_after();
                         // (n-8) exact in fp16: (0x6400 | n) is 1024 + n; times the fp16 scale
                         const __half2 sc = __float2half2_rn(s);
                         const __half2 off = __float2half2_rn(1032.0f);
-                        uint32_t hv[8];
+                        uint32_t hv[16];
 #pragma unroll
-                        for (int w = 0; w < 2; ++w)
+                        for (int w = 0; w < 4; ++w)
 #pragma unroll
                             for (int p = 0; p < 4; ++p) {
                                 const uint32_t v = ((wv[w] >> (4 * p)) & 0x000F000Fu) | 0x64006400u;
                                 const __half2 x = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&v), off), sc);
                                 hv[4 * w + p] = *reinterpret_cast<const uint32_t*>(&x);
                             }
-                        tmem_st8(tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + ACOL +
-                                     (uint32_t)(as * 32 + h * (KSUB / 2)),
-                                 hv);
+                        tmem_st16(tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + ACOL + (uint32_t)(as * 32 + 16 * h),
+                                  hv);
                         tc_fence_before();
                     } else {
                         uint8_t* arow = smem + L::OFF_A + as * L::A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
 #pragma unroll
-                        for (int w = 0; w < 2; ++w) {
+                        for (int w = 0; w < 4; ++w) {
                             uint32_t hh[4];
 #pragma unroll
                             for (int p = 0; p < 4; ++p) {
@@ -546,7 +526,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 const __half2 x = __floats2half2_rn(lo, hi);
                                 hh[p] = *reinterpret_cast<const uint32_t*>(&x);
                             }
-                            const int cw = (h * KSUB) / 8 + w;  // 16-byte chunk of the 128-byte row
+                            const int cw = 4 * h + w;  // 16-byte chunk of the 128-byte row
                             *reinterpret_cast<uint4*>(arow + ((cw ^ (t & 7)) << 4)) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
                         }
                         fence_async_smem();
@@ -723,7 +703,7 @@ int launch_t(const TcLaunch& L, int num_sms, cudaStream_t s) {
         const int by_regs = 65536 / (fa.numRegs * tc::THREADS);
         if (per_sm > by_regs) per_sm = by_regs;
     }
-    if (per_sm > 1) per_sm = 1;  // persistent: one CTA per SM
+    if (per_sm > 2) per_sm = 2;
     if (per_sm < 1) per_sm = 1;
     int grid = num_sms * per_sm;
     if (L.max_items > 0 && L.max_items < grid) grid = (int)L.max_items;
