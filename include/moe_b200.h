@@ -133,6 +133,31 @@ int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch_size, const uint8_t* W_pack
                          const float* scales, const float* x_batch, float* out_batch,
                          int64_t c_in, int64_t c_out);
 
+/* moe_q4_matmul_batchN without any allocation during the call.  No
+ * counterpart in the reference (its Mojo routines allocate nothing on a
+ * device); this is for callers that must not allocate while they run: a
+ * server that hands all of HBM to its own arenas at start-up, where a later
+ * cudaMalloc fails, and latency-bound loops, where cudaMalloc/cudaFree would
+ * synchronise the device.  Same arguments and results as
+ * moe_q4_matmul_batchN, except:
+ *  - scratch (the fp16 copy of x_batch and split-K partial sums) lives in
+ *    one static device array of 8 MiB per device, loaded with the library;
+ *    batch_size * c_in * 2 must be <= 8 MiB (8388608 bytes), else the call
+ *    returns MOE_E_SHAPE and does nothing.  The scratch needs no initial
+ *    value: every byte a call reads was written earlier in that call;
+ *  - every pointer must be device memory or inside a registered range
+ *    (MOE_E_ARG otherwise: host buffers are not staged), and x_batch and
+ *    W_packed 16-byte aligned;
+ *  - the first call on a device looks up the scratch's address (once per
+ *    device, with that device current); make that first call before any
+ *    stream capture begins on the calling thread;
+ *  - the scratch is shared by every context and stream on the device: two
+ *    calls in flight at the same time on one device (different streams,
+ *    contexts or threads) race on it.  Calls ordered on one stream do not. */
+int moe_q4_matmul_batchN_noalloc(moe_ctx* ctx, int64_t batch_size, const uint8_t* W_packed,
+                                 const float* scales, const float* x_batch, float* out_batch,
+                                 int64_t c_in, int64_t c_out);
+
 /* ------------------------------------------------------------- routing */
 /* compute_moe_lod_weights (moe_kernels.mojo:445-490) for `batch` tokens laid
  * out back to back (top_k entries each).  active_count[b] receives the count

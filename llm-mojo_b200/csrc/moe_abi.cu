@@ -7,6 +7,7 @@
 #include <chrono>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -1289,6 +1290,150 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
     c.post_w = ld.post_w;
     c.out_f16 = (flags & MOE_F_FP16_OUT) ? 1 : 0;
     TRY(run_experts(ctx, ld.w, M, K, d, F, E, L->activation, bb, &c, od));
+    return finish(ctx);
+}
+
+}  // extern "C"
+
+// ======================================================================
+// Dense Q4_0 matmul without allocation.
+//
+// moe_q4_matmul_batchN takes its fp16 activation copy and split-K partial
+// sums from the context workspace, which grows with cudaMalloc when a call
+// needs more than it holds, and it stages host buffers through the same
+// workspace.  Some callers must not allocate during a call: a serving loop
+// that hands out all of HBM to its own arenas when it starts (any later
+// cudaMalloc fails or evicts), and a latency-bound decode loop, where
+// cudaMalloc / cudaFree synchronise the device.  For them the variant below
+// keeps its scratch in one static device array per device, of fixed size,
+// created with the module; it makes no cudaMalloc, cudaFree or other
+// allocating call.
+namespace {
+
+// Fixed scratch: the fp16 copy of the activations (batch * c_in * 2 bytes)
+// and, when space is left, split-K partial sums.  No byte of it needs an
+// initial value: every byte a call reads is written earlier in that call.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch on the current device; looked up once per
+// device (with that device current) and cached.
+int noalloc_scratch(moe_ctx* ctx, void** out) {
+    *out = nullptr;
+    if (ctx->device < 0 || ctx->device >= kMaxDevices) return fail(ctx, MOE_E_ARG, "device ordinal too large");
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (!g_noalloc_ptr[ctx->device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();
+            return fail(ctx, MOE_E_CUDA, std::string("cudaGetSymbolAddress of the static scratch failed: ") +
+                                             cudaGetErrorString(e));
+        }
+        g_noalloc_ptr[ctx->device] = p;
+    }
+    *out = g_noalloc_ptr[ctx->device];
+    return MOE_OK;
+}
+
+// Device address of p without staging: a device (or managed) pointer, or a
+// host pointer inside a registered range.
+int dev_only(moe_ctx* ctx, const void* p, size_t bytes, const char* what, void** out) {
+    *out = nullptr;
+    const char* c = static_cast<const char*>(p);
+    for (const Reg& r : ctx->regs)
+        if (c >= r.host && c < r.host + r.bytes) {
+            if (c + bytes > r.host + r.bytes)
+                return fail(ctx, MOE_E_ARG, std::string(what) + " runs past the end of its registered range");
+            *out = r.dev + (c - r.host);
+            return MOE_OK;
+        }
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        at.type = cudaMemoryTypeUnregistered;
+    }
+    if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) {
+        *out = at.devicePointer ? at.devicePointer : const_cast<void*>(p);
+        return MOE_OK;
+    }
+    return fail(ctx, MOE_E_ARG,
+                std::string(what) + " must be device memory or inside a registered range (this entry point "
+                                    "does not stage host buffers)");
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_q4_matmul_batchN_noalloc(moe_ctx* ctx, int64_t batch, const uint8_t* W, const float* S,
+                                 const float* x, float* out, int64_t c_in, int64_t c_out) {
+    TRY(begin(ctx));
+    if (!W || !S || !x || !out) return fail(ctx, MOE_E_ARG, "null pointer");
+    TRY(check_q4_shape(ctx, c_in, c_out));
+    if (batch <= 0) return fail(ctx, MOE_E_SHAPE, "batch_size must be >= 1");
+    if (batch > (int64_t)(kNoAllocScratchBytes / 2) || batch * c_in * 2 > (int64_t)kNoAllocScratchBytes)
+        return fail(ctx, MOE_E_SHAPE,
+                    "batch_size * c_in * 2 bytes exceeds the no-alloc entry point's fixed scratch of 8 MiB "
+                    "(use moe_q4_matmul_batchN)");
+    void *w, *sc, *xd, *od, *scratch;
+    TRY(dev_only(ctx, W, c_out * c_in / 2, "W_packed", &w));
+    TRY(dev_only(ctx, S, c_out * c_in / 32 * 4, "scales", &sc));
+    TRY(dev_only(ctx, x, batch * c_in * 4, "x_batch", &xd));
+    TRY(dev_only(ctx, out, batch * c_out * 4, "out_batch", &od));
+    if (!al16(w)) return fail(ctx, MOE_E_ARG, "packed weights must be 16-byte aligned");
+    if (!al16(xd)) return fail(ctx, MOE_E_ARG, "x_batch must be 16-byte aligned");
+    TRY(noalloc_scratch(ctx, &scratch));
+    const bool tc = ctx->gemm_path != MOE_PATH_GEMV && moe::tc_supported(c_in, c_out, 0, 0) && al8(sc) &&
+                    (ctx->gemm_path == MOE_PATH_TC || batch >= ctx->dense_tc_min_tokens);
+    if (!tc) {
+        ctx->launches += moe::launch_gemv_wide((const uint8_t*)w, (const float*)sc, (const float*)xd, (float*)od,
+                                               c_out, (int)c_in, (int)batch, c_out, ctx->stream);
+        return finish(ctx);
+    }
+    __half* x16 = static_cast<__half*>(scratch);
+    const size_t x16_bytes = al(batch * c_in * 2);
+    moe::TcLaunch t;
+    t.a.Ws = (const float*)sc;
+    t.a.K = (int)c_in;
+    t.a.R = c_out;
+    t.a.dense_tokens = (int)batch;
+    t.a.y_out = (float*)od;
+    t.a.y_stride = c_out;
+    t.a.err_flag = ctx->err_flag;
+    t.a.timeout_ns = ctx->device_timeout_ns;
+    t.Wp = (const uint8_t*)w;
+    t.total_rows = c_out;
+    t.B = x16;
+    t.b_rows = batch;
+    int BN = 16;
+    while (BN < 256 && BN < batch) BN *= 2;
+    t.BN = BN;
+    t.max_items = ((c_out + 127) / 128) * ((batch + BN - 1) / BN);
+    t.a_in_smem = ctx->tc_a_in_smem;
+    // split-K partials go after the activation copy, as many splits as fit
+    int ks = choose_ksplit(ctx, t.max_items, c_in);
+    const size_t part_room = kNoAllocScratchBytes - x16_bytes;
+    while (ks > 1 && (size_t)ks * batch * c_out * 4 > part_room) --ks;
+    float* part = nullptr;
+    if (ks > 1) {
+        part = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) + x16_bytes);
+        t.a.y_out = part;
+        t.a.ksplit = ks;
+        t.a.split_stride = batch * c_out;
+        t.max_items *= ks;
+    }
+    ctx->launches += moe::launch_gather_f16((const float*)xd, c_in, nullptr, nullptr, batch, (int)batch, x16,
+                                            ctx->stream);
+    const int r = moe::launch_tc_gemm(moe::TC_PLAIN, t, ctx->num_sms, ctx->stream);
+    if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core GEMM setup failed");
+    ctx->launches += r;
+    if (ks > 1)
+        ctx->launches += moe::launch_reduce_splits(part, batch * c_out, ks, (float*)od, batch * c_out, ctx->stream);
     return finish(ctx);
 }
 

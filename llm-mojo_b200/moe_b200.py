@@ -41,6 +41,7 @@ EXPORTS = [
     "moe_compute_subbatch_set_cover_moe_weights", "moe_run_moe_experts_stage1",
     "moe_run_moe_experts_stage2", "moe_run_moe_coalesced_core",
     "moe_run_diffusion_moe_experts_parallel", "moe_route", "moe_layer_forward",
+    "moe_q4_matmul_batchN_noalloc",
 ]
 
 
@@ -97,6 +98,7 @@ def _declare(L):
     L.moe_quantize_fp32_to_q4_0.argtypes = [_p, _p, _p, _p, _i64]
     L.moe_q4_matmul_vec.argtypes = [_p, _p, _p, _p, _p, _i64, _i64]
     L.moe_q4_matmul_batchN.argtypes = [_p, _i64, _p, _p, _p, _p, _i64, _i64]
+    L.moe_q4_matmul_batchN_noalloc.argtypes = [_p, _i64, _p, _p, _p, _p, _i64, _i64]
     L.moe_compute_moe_lod_weights.argtypes = [_p, _i64, _p, _p, _p, _f, _p, _p, _p, _i64]
     L.moe_apply_moe_lod_and_set_cover.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64, _f, _p,
                                                   _p, _i64]
@@ -157,6 +159,9 @@ class Context:
     def check(self, rc: int):
         if rc != 0:
             raise MoeError(rc, self.lib.moe_last_error(self.h).decode())
+
+    def last_error(self) -> str:
+        return self.lib.moe_last_error(self.h).decode()
 
     @property
     def kernel_launches(self) -> int:
@@ -219,6 +224,13 @@ class Context:
         self.check(self.lib.moe_q4_matmul_batchN(self.h, batch_size, _addr(W_packed),
                                                  _addr(scales), _addr(x_batch), _addr(out_batch),
                                                  c_in, c_out))
+
+    def q4_matmul_batchN_noalloc(self, batch_size, W_packed, scales, x_batch, out_batch, c_in, c_out):
+        """q4_matmul_batchN on device buffers with the library's fixed static
+        scratch instead of the context workspace: no allocation during the call."""
+        self.check(self.lib.moe_q4_matmul_batchN_noalloc(self.h, batch_size, _addr(W_packed),
+                                                         _addr(scales), _addr(x_batch),
+                                                         _addr(out_batch), c_in, c_out))
 
     def compute_moe_lod_weights(self, top_idx, top_val, per_expert_scale, moe_top_p,
                                 active_idx, active_weights, top_k=8, batch=1, active_count=None):
