@@ -226,6 +226,7 @@ def workload_config(args, M):
             "l2": f"weights of {args.layers} distinct layers cycled per step ({args.layers * 476} MB > 126 MB L2)",
             "post_norm": True, "parallelism": f"replicas x{dist_setup()[0]}",
             "gemm_path": getattr(args, "path", "auto"),
+            "tc_kernel": getattr(args, "tc_kernel", "general"),
             "cuda_graph": not getattr(args, "no_graph", False)}
 
 
@@ -243,6 +244,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"],
                     help="expert/dense GEMM path: CUDA-core GEMV, tcgen05, or automatic")
+    ap.add_argument("--tc-kernel", default="general", choices=["stream", "general"],
+                    help="tensor-core kernel for token tiles <= 64: streaming or general")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = dist_setup()
@@ -266,6 +269,7 @@ def main():
     stream = torch.cuda.current_stream()
     ctx.set_stream(stream.cuda_stream)
     ctx.set_gemm_path({"auto": MB.PATH_AUTO, "gemv": MB.PATH_GEMV, "tc": MB.PATH_TC}[args.path])
+    ctx.set_option(MB.OPT_TC_STREAM, int(args.tc_kernel == "stream"))
     M = WORKLOADS[args.workload]
 
     layers, descs = [], []

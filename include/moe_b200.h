@@ -89,8 +89,10 @@ enum moe_option {
                                         many tokens (default 2) */
     MOE_OPT_TC_A_IN_SMEM = 5,      /* 1: stage the dequantised weights in shared memory even for token
                                       tiles <= 64 (default 0: tensor memory) */
-    MOE_OPT_ROUTER_TC_MIN_TOKENS = 6 /* router on tensor cores from this many tokens (default 2048;
+    MOE_OPT_ROUTER_TC_MIN_TOKENS = 6, /* router on tensor cores from this many tokens (default 2048;
                                         below it the router runs in fp32 like the reference) */
+    MOE_OPT_TC_STREAM = 7          /* 1: token tiles <= 64 (K % 128 == 0) use the streaming
+                                      tensor-core kernel; 0 (default): the general one */
 };
 enum moe_gemm_path {
     MOE_PATH_AUTO = 0, /* CUDA-core GEMV for few tokens, tensor cores above the threshold */

@@ -17,9 +17,10 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libmoe_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
-SOURCES = ["moe_abi.cu", "moe_kernels.cu", "moe_tc.cu"]
+SOURCES = ["moe_abi.cu", "moe_kernels.cu", "moe_tc.cu", "moe_tc_stream.cu"]
+OBJDIR = os.path.join(HERE, "_build")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
          "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include")]
 
 
@@ -39,9 +40,18 @@ def needs_build() -> bool:
 def build(verbose: bool = False, force: bool = False) -> str:
     if not force and not needs_build():
         return LIB
-    cmd = [NVCC, *ARCH, *FLAGS, *(["-Xptxas", "-v"] if verbose else []),
-           "-o", LIB + ".tmp", *sources(), "-lcuda"]
-    subprocess.run(cmd, check=True)
+    # one nvcc per translation unit, in parallel, then one link
+    os.makedirs(OBJDIR, exist_ok=True)
+    procs, objs = [], []
+    for src in sources():
+        obj = os.path.join(OBJDIR, os.path.basename(src) + ".o")
+        objs.append(obj)
+        cmd = [NVCC, *ARCH, *FLAGS, *(["-Xptxas", "-v"] if verbose else []), "-c", "-o", obj, src]
+        procs.append((src, subprocess.Popen(cmd)))
+    failed = [src for src, p in procs if p.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, f"nvcc {failed}")
+    subprocess.run([NVCC, *ARCH, "-shared", "-o", LIB + ".tmp", *objs, "-lcuda"], check=True)
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

@@ -58,6 +58,7 @@ struct moe_ctx {
     int dense_tc_min_tokens = 2;         // auto, dense projections
     int router_tc_min_tokens = 2048;     // router on tensor cores from this many tokens
     bool tc_a_in_smem = false;           // MOE_OPT_TC_A_IN_SMEM
+    bool tc_stream = false;              // MOE_OPT_TC_STREAM
     uint64_t device_timeout_ns = 4000000000ull;
     // profiling (moe_profile_enable)
     int profile = 0;
@@ -385,6 +386,7 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
         t1.BN = BN;
         t1.max_items = (int64_t)(F / 64) * (max_u + (P + BN - 1) / BN);
         t1.a_in_smem = ctx->tc_a_in_smem;
+        t1.stream = ctx->tc_stream;
         int r;
         {
             ProfScope ps(ctx, "tc_gate_up");
@@ -502,6 +504,7 @@ int dense_q4(moe_ctx* ctx, const uint8_t* w, const float* sc, const float* xd, f
         t.BN = BN;
         t.max_items = ((c_out + 127) / 128) * ((batch + BN - 1) / BN);
         t.a_in_smem = ctx->tc_a_in_smem;
+        t.stream = ctx->tc_stream;
         const int ks = choose_ksplit(ctx, t.max_items, c_in);
         float* part = nullptr;
         if (ks > 1) {
@@ -640,6 +643,9 @@ int moe_set_option(moe_ctx* ctx, int option, int64_t value) {
             return MOE_OK;
         case MOE_OPT_TC_A_IN_SMEM:
             ctx->tc_a_in_smem = value != 0;
+            return MOE_OK;
+        case MOE_OPT_TC_STREAM:
+            ctx->tc_stream = value != 0;
             return MOE_OK;
         case MOE_OPT_ROUTER_TC_MIN_TOKENS:
             if (value < 1) return fail(ctx, MOE_E_ARG, "bad token threshold");
@@ -1415,6 +1421,7 @@ int moe_q4_matmul_batchN_noalloc(moe_ctx* ctx, int64_t batch, const uint8_t* W, 
     t.BN = BN;
     t.max_items = ((c_out + 127) / 128) * ((batch + BN - 1) / BN);
     t.a_in_smem = ctx->tc_a_in_smem;
+    t.stream = ctx->tc_stream;
     // split-K partials go after the activation copy, as many splits as fit
     int ks = choose_ksplit(ctx, t.max_items, c_in);
     const size_t part_room = kNoAllocScratchBytes - x16_bytes;

@@ -1,5 +1,6 @@
 // moe_tc.h -- launch interface of the tcgen05 grouped Q4_0 GEMM (moe_tc.cu).
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -39,6 +40,7 @@ struct TcLaunch {
     int BN = 16;                  // token tile: 16, 32, 64, 128 or 256
     int64_t max_items = 0;        // upper bound on work items (limits the grid), 0 = none
     bool a_in_smem = false;       // force the shared-memory A operand for BN <= 64
+    bool stream = false;          // BN <= 64: the streaming kernel (moe_tc_stream.cu) where it applies
 };
 
 // Returns the number of kernels launched, or -1 when the shape or the tensor
@@ -48,6 +50,17 @@ int launch_tt_prefix(const int* meta, const int* seg_count, int BN, int* tt_pref
 int launch_gather_f16(const float* X, int64_t K, const int* pair_row, const int* meta, int64_t rows,
                       int dense_rows, __half* out, cudaStream_t s);
 bool tc_supported(int64_t K, int64_t R, int act_mode, int64_t F);
+
+// 2-D tensor map over a row-major matrix (driver entry point; false on error)
+bool tc_make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw);
+// Tensor map of any rank 1..5: dims[0] innermost; strides[i] is the byte
+// stride of dimension i + 1.
+bool tc_make_map_nd(CUtensorMap* m, CUtensorMapDataType dt, const void* base, int rank, const uint64_t* dims,
+                    const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle sw);
+// Streaming variant for token tiles of 16..64 (moe_tc_stream.cu); same
+// return convention as launch_tc_gemm.
+int launch_tc_stream(int mode, const TcLaunch& L, int num_sms, cudaStream_t s);
 int launch_reduce_splits(const float* part, int64_t stride, int splits, float* out, int64_t n,
                          cudaStream_t s);
 

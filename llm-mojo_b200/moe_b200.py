@@ -24,6 +24,7 @@ X_NATURAL, X_DEINT_HALVES, X_DEINT_BLOCK32 = 0, 1, 2
 F_POST_NORM, F_SET_COVER, F_FP16_OUT = 1, 4, 8
 OPT_GEMM_PATH, OPT_TC_MIN_TOKENS, OPT_DEVICE_TIMEOUT_NS = 1, 2, 3
 OPT_DENSE_TC_MIN_TOKENS, OPT_TC_A_IN_SMEM, OPT_ROUTER_TC_MIN_TOKENS = 4, 5, 6
+OPT_TC_STREAM = 7
 PATH_AUTO, PATH_GEMV, PATH_TC = 0, 1, 2
 
 STATUS = {0: "MOE_OK", 1: "MOE_E_ARG", 2: "MOE_E_SHAPE", 3: "MOE_E_UNREGISTERED",

@@ -17,14 +17,17 @@ from tolerances import assert_close, near_tie_tokens
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["a_tmem", "a_smem"])
+@pytest.fixture(params=["stream", "a_tmem", "a_smem"])
 def tc(ctx, request):
-    """Tensor-core path with the dequantised weights in TMEM (default for
-    token tiles <= 64) or staged in shared memory."""
+    """Tensor-core path: the streaming kernel (an option for token tiles <= 64),
+    the general kernel with the dequantised weights in TMEM (default), or the
+    general kernel with them staged in shared memory."""
     ctx.set_gemm_path(MB.PATH_TC)
+    ctx.set_option(MB.OPT_TC_STREAM, int(request.param == "stream"))
     ctx.set_option(MB.OPT_TC_A_IN_SMEM, int(request.param == "a_smem"))
     yield ctx
     ctx.set_option(MB.OPT_TC_A_IN_SMEM, 0)
+    ctx.set_option(MB.OPT_TC_STREAM, 0)
     ctx.set_gemm_path(MB.PATH_AUTO)
 
 
@@ -33,7 +36,8 @@ def _softmax_rows(s):
 
 
 @pytest.mark.parametrize("c_in,c_out,batch", [(2816, 4096, 16), (2816, 1024, 16), (4096, 2816, 16),
-                                              (704, 2816, 40), (2816, 128, 300)])
+                                              (704, 2816, 40), (2816, 128, 300), (192, 200, 16),
+                                              (2816, 67, 33)])
 def test_tc_dense_q4_matmul(tc, c_in, c_out, batch):
     import torch
     rng = np.random.default_rng(c_in * 7 + batch)
