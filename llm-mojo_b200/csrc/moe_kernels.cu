@@ -146,6 +146,8 @@ constexpr int DENSE_CHUNK = 4;
 
 template <int MODE, bool XS, int NBL, int RPW>
 __global__ void __launch_bounds__(128, 4) k_q4_gemv(GemvArgs a) {
+    pdl_wait();
+    pdl_trigger();
     GemvWarp W;
     W.lane = threadIdx.x & 31;
     W.g = W.lane >> 3;
@@ -277,7 +279,7 @@ static void gemv_launch_t(const GemvArgs& a, int num_sms, cudaStream_t s) {
     const int64_t cap = (int64_t)num_sms * 16;
     const int grid = (int)(blocks < cap ? blocks : cap);
     if (grid <= 0) return;
-    k_q4_gemv<MODE, XS, NBL, RPW><<<grid, 128, 0, s>>>(a);
+    launch_k(k_q4_gemv<MODE, XS, NBL, RPW>, dim3(grid), dim3(128), 0, s, a);
 }
 
 template <int MODE, bool XS>
@@ -307,6 +309,8 @@ int launch_gemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s) {
 // out[t][e] = W[e] . X[t]; one warp per (token, expert), float4 loads.
 __global__ void __launch_bounds__(128) k_gemv_f32(const float* W, const float* X, float* out,
                                                   int64_t M, int64_t E, int64_t d) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t gw = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
     if (gw >= M * E) return;
@@ -326,7 +330,7 @@ int launch_gemv_f32(const float* W, const float* X, float* out, int64_t M, int64
                     cudaStream_t s) {
     const int64_t warps = M * E;
     if (warps <= 0) return 0;
-    k_gemv_f32<<<(unsigned)((warps + 3) / 4), 128, 0, s>>>(W, X, out, M, E, d);
+    launch_k(k_gemv_f32, dim3((unsigned)((warps + 3) / 4)), dim3(128), 0, s, W, X, out, M, E, d);
     return 1;
 }
 
@@ -340,6 +344,8 @@ template <int T>
 __global__ void __launch_bounds__(256) k_gemv_wide(const uint8_t* __restrict__ W, const float* __restrict__ S,
                                                    const float* __restrict__ X, float* __restrict__ out,
                                                    int64_t rows, int K, int ntok, int64_t out_stride) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nb = K >> 5;
@@ -377,9 +383,9 @@ int launch_gemv_wide(const uint8_t* W, const float* S, const float* X, float* ou
     const int T = ntok >= 4 ? 4 : (ntok >= 2 ? 2 : 1);
     const int64_t warps = rows * ((ntok + T - 1) / T);
     const unsigned blocks = (unsigned)((warps + 7) / 8);
-    if (T == 4) k_gemv_wide<4><<<blocks, 256, 0, s>>>(W, S, X, out, rows, K, ntok, out_stride);
-    else if (T == 2) k_gemv_wide<2><<<blocks, 256, 0, s>>>(W, S, X, out, rows, K, ntok, out_stride);
-    else k_gemv_wide<1><<<blocks, 256, 0, s>>>(W, S, X, out, rows, K, ntok, out_stride);
+    if (T == 4) launch_k(k_gemv_wide<4>, dim3(blocks), dim3(256), 0, s, W, S, X, out, rows, K, ntok, out_stride);
+    else if (T == 2) launch_k(k_gemv_wide<2>, dim3(blocks), dim3(256), 0, s, W, S, X, out, rows, K, ntok, out_stride);
+    else launch_k(k_gemv_wide<1>, dim3(blocks), dim3(256), 0, s, W, S, X, out, rows, K, ntok, out_stride);
     return 1;
 }
 
@@ -389,6 +395,8 @@ int launch_gemv_wide(const uint8_t* W, const float* S, const float* X, float* ou
 // pre_w and scaled = x * inv * router_scale * r_scale_factor; and the
 // per-32-block sums (x1.5) the XS GEMV needs.
 __global__ void __launch_bounds__(512) k_prep(PrepArgs a) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float4 smem4[];
     float* xs = reinterpret_cast<float*>(smem4);
     __shared__ float red[33];
@@ -442,7 +450,7 @@ int launch_prep(const PrepArgs& a, int64_t M, cudaStream_t s) {
     if (M <= 0) return 0;
     const size_t smem = (size_t)a.K * sizeof(float);
     if (smem > 48 * 1024) cudaFuncSetAttribute(k_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_prep<<<(unsigned)M, 512, smem, s>>>(a);
+    launch_k(k_prep, dim3((unsigned)M), dim3(512), smem, s, a);
     return 1;
 }
 
@@ -452,6 +460,8 @@ int launch_prep(const PrepArgs& a, int64_t M, cudaStream_t s) {
 // values keep the lower index first) and, when a.lod,
 // compute_moe_lod_weights (moe_kernels.mojo:445-490).
 __global__ void __launch_bounds__(128) k_topk(TopkArgs a) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float4 smem4[];
     float* pr = reinterpret_cast<float*>(smem4);  // [E]
     __shared__ float red[33];
@@ -550,7 +560,7 @@ __global__ void __launch_bounds__(128) k_topk(TopkArgs a) {
 int launch_topk(const TopkArgs& a, int64_t M, cudaStream_t s) {
     if (M <= 0) return 0;
     const size_t smem = (size_t)a.E * sizeof(float);
-    k_topk<<<(unsigned)M, 128, smem, s>>>(a);
+    launch_k(k_topk, dim3((unsigned)M), dim3(128), smem, s, a);
     return 1;
 }
 
@@ -561,6 +571,8 @@ __global__ void k_set_cover(const int* ti, const float* tv, int64_t M, int K, in
                             const float* pes, float top_p, float core_top_p, float smp,
                             int sub_batch, int* slot_expert, float* slot_weight,
                             int64_t* tok_count, int64_t* tok_idx, float* tok_w) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t t0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * sub_batch;
     if (t0 >= M) return;
     const int sb = (int)min((int64_t)sub_batch, M - t0);
@@ -687,7 +699,7 @@ int launch_set_cover(const int* ti32, const float* tv, int64_t M, int K, int E, 
     const int64_t groups = (M + sub_batch - 1) / sub_batch;
     const int threads = 32;
     const int blocks = (int)((groups + threads - 1) / threads);
-    k_set_cover<<<blocks, threads, 0, s>>>(ti32, tv, M, K, E, pes, top_p, core_top_p, smp,
+    launch_k(k_set_cover, dim3(blocks), dim3(threads), 0, s, ti32, tv, M, K, E, pes, top_p, core_top_p, smp,
                                            sub_batch, slot_expert, slot_weight, tok_count,
                                            tok_idx, tok_w);
     return 1;
@@ -700,6 +712,8 @@ int launch_set_cover(const int* ti32, const float* tv, int64_t M, int K, int E, 
 __global__ void k_slots_from_lists(int64_t M, int K, const int64_t* count, int64_t count_scalar,
                                    const int64_t* idx, const float* w, int* slot_expert,
                                    float* slot_weight, int E, int* err_flag) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= M * K) return;
     const int64_t t = i / K;
@@ -725,7 +739,7 @@ int launch_slots_from_lists(int64_t M, int K, const int64_t* count, int64_t coun
                             float* slot_weight, int E, int* err_flag, cudaStream_t s) {
     const int64_t n = M * K;
     if (n <= 0) return 0;
-    k_slots_from_lists<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+    launch_k(k_slots_from_lists, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, 
         M, K, count, count_scalar, idx, w, slot_expert, slot_weight, E, err_flag);
     return 1;
 }
@@ -733,6 +747,8 @@ int launch_slots_from_lists(int64_t M, int K, const int64_t* count, int64_t coun
 // Diffusion convention (diffusion_kernels.mojo:263-266): slot active iff w > 0.
 __global__ void k_slots_from_topw(int64_t n, const int64_t* idx, const float* w, int* slot_expert,
                                   float* slot_weight, int E, int* err_flag) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     int e = -1;
@@ -754,7 +770,7 @@ int launch_slots_from_topw(int64_t M, int K, const int64_t* idx, const float* w,
                            float* slot_weight, int E, int* err_flag, cudaStream_t s) {
     const int64_t n = M * K;
     if (n <= 0) return 0;
-    k_slots_from_topw<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(n, idx, w, slot_expert,
+    launch_k(k_slots_from_topw, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, n, idx, w, slot_expert,
                                                                   slot_weight, E, err_flag);
     return 1;
 }
@@ -793,6 +809,8 @@ __device__ __forceinline__ int block_excl_scan(int v, int* wsum, int* total) {
 
 __global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t P, int K, int E,
                                                  BucketOut o) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int cnt[1024];
     __shared__ int cur[1024];
     __shared__ int wsum[32];
@@ -834,7 +852,7 @@ __global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t
 
 int launch_bucket(const int* slot_expert, int64_t P, int K, int E, const BucketOut& o,
                   cudaStream_t s) {
-    k_bucket<<<1, 1024, 0, s>>>(slot_expert, P, K, E, o);
+    launch_k(k_bucket, dim3(1), dim3(1024), 0, s, slot_expert, P, K, E, o);
     return 1;
 }
 
@@ -844,6 +862,8 @@ int launch_bucket(const int* slot_expert, int64_t P, int K, int E, const BucketO
 // rms_norm with post_feedforward_layernorm_2 (model_speculative_moe_batched
 // .mojo:1144-1150) and fp16 rounding.  float4 per thread, d % 4 == 0.
 __global__ void __launch_bounds__(512) k_combine(CombineArgs a) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[33];
     __shared__ int sp[32];
     __shared__ float sw[32];
@@ -912,7 +932,7 @@ __global__ void __launch_bounds__(512) k_combine(CombineArgs a) {
 
 int launch_combine(const CombineArgs& a, int64_t M, cudaStream_t s) {
     if (M <= 0) return 0;
-    k_combine<<<(unsigned)M, 512, 0, s>>>(a);
+    launch_k(k_combine, dim3((unsigned)M), dim3(512), 0, s, a);
     return 1;
 }
 
@@ -921,6 +941,8 @@ int launch_combine(const CombineArgs& a, int64_t M, cudaStream_t s) {
 // IEEE division (no fast-math) so scale and 1/scale match the reference bit
 // for bit; rint rounds exact ties to even like numpy.
 __global__ void k_quantize(const float* src, uint8_t* packed, float* scales, int64_t nblocks) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= nblocks) return;
     const float4* s4 = reinterpret_cast<const float4*>(src + b * 32);
@@ -956,7 +978,7 @@ __global__ void k_quantize(const float* src, uint8_t* packed, float* scales, int
 int launch_quantize(const float* src, uint8_t* packed, float* scales, int64_t nblocks,
                     cudaStream_t s) {
     if (nblocks <= 0) return 0;
-    k_quantize<<<(unsigned)((nblocks + 255) / 256), 256, 0, s>>>(src, packed, scales, nblocks);
+    launch_k(k_quantize, dim3((unsigned)((nblocks + 255) / 256)), dim3(256), 0, s, src, packed, scales, nblocks);
     return 1;
 }
 
@@ -964,6 +986,8 @@ int launch_quantize(const float* src, uint8_t* packed, float* scales, int64_t nb
 __global__ void k_lod(int64_t B, const int64_t* top_idx, const float* top_val, const float* pes,
                       float top_p, int64_t* act_idx, float* act_w, int64_t* act_count, int K,
                       int64_t E, int* err_flag) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= B) return;
     const int64_t* ti = top_idx + t * K;
@@ -1012,7 +1036,7 @@ int launch_lod(int64_t B, const int64_t* top_idx, const float* top_val, const fl
                float top_p, int64_t* act_idx, float* act_w, int64_t* act_count, int K,
                int64_t E, int* err_flag, cudaStream_t s) {
     if (B <= 0) return 0;
-    k_lod<<<(unsigned)((B + 127) / 128), 128, 0, s>>>(B, top_idx, top_val, pes, top_p, act_idx,
+    launch_k(k_lod, dim3((unsigned)((B + 127) / 128)), dim3(128), 0, s, B, top_idx, top_val, pes, top_p, act_idx,
                                                        act_w, act_count, K, E, err_flag);
     return 1;
 }
@@ -1021,6 +1045,8 @@ int launch_lod(int64_t B, const int64_t* top_idx, const float* top_val, const fl
 __global__ void k_apply_lod(const int64_t* top_idx, const float* top_val, const float* pes,
                             float* top_w, int64_t B, int K, int64_t eff_k, int64_t unacc_k,
                             const uint8_t* eb_mask, const int64_t* active_canvas_idx) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     const int64_t orig = active_canvas_idx ? active_canvas_idx[b] : b;
@@ -1048,7 +1074,7 @@ int launch_apply_lod(const int64_t* top_idx, const float* top_val, const float* 
     if (eff_k < 1) eff_k = 1;
     int64_t unacc = unaccepted_top_k <= eff_k ? unaccepted_top_k : eff_k;
     if (unacc < 1) unacc = 1;
-    k_apply_lod<<<(unsigned)((B + 127) / 128), 128, 0, s>>>(top_idx, top_val, pes, top_w, B, K,
+    launch_k(k_apply_lod, dim3((unsigned)((B + 127) / 128)), dim3(128), 0, s, top_idx, top_val, pes, top_w, B, K,
                                                              eff_k, unacc, eb_mask,
                                                              active_canvas_idx);
     return 1;

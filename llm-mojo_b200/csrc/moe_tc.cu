@@ -147,6 +147,8 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // barrier init, TMEM allocation and tensor-map prefetch overlap the previous kernel
+    pdl_trigger();
     Guard G{abort_flag, a.err_flag, globaltimer() + a.timeout_ns};
 
     if (warp == 0) {
@@ -391,6 +393,8 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
 // Token tiles per unique expert -> exclusive prefix (one CTA, U <= 1024).
 __global__ void __launch_bounds__(1024) k_tt_prefix(const int* meta, const int* seg_count, int BN,
                                                     int* tt_prefix) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int wsum[32];
     const int U = meta[0];
     const int tid = threadIdx.x;
@@ -423,6 +427,8 @@ __global__ void __launch_bounds__(1024) k_tt_prefix(const int* meta, const int* 
 // order; rows p >= meta[1] (no pair) are skipped.
 __global__ void __launch_bounds__(256) k_gather_f16(const float* X, int64_t K, const int* pair_row,
                                                     const int* meta, int dense_rows, __half* out) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t p = blockIdx.x;
     const int64_t P = dense_rows > 0 ? dense_rows : meta[1];
     if (p >= P) return;
@@ -515,7 +521,7 @@ int launch_t(const TcLaunch& L, int num_sms, cudaStream_t s) {
     int grid = num_sms * per_sm;
     if (L.max_items > 0 && L.max_items < grid) grid = (int)L.max_items;
     if (grid <= 0) return 0;
-    kern<<<grid, tc::THREADS, smem, s>>>(qmap, bmap, L.a);
+    launch_k(kern, dim3(grid), dim3(tc::THREADS), smem, s, qmap, bmap, L.a);
     return 1;
 }
 
@@ -553,6 +559,8 @@ int launch_tc_gemm(int mode, const TcLaunch& L, int num_sms, cudaStream_t s) {
 
 // out[i] = sum over s < splits of part[s * stride + i] (fixed order)
 __global__ void k_reduce_splits(const float* part, int64_t stride, int splits, float* out, int64_t n) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     float v = part[i];
@@ -563,19 +571,19 @@ __global__ void k_reduce_splits(const float* part, int64_t stride, int splits, f
 int launch_reduce_splits(const float* part, int64_t stride, int splits, float* out, int64_t n,
                          cudaStream_t s) {
     if (n <= 0) return 0;
-    k_reduce_splits<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, stride, splits, out, n);
+    launch_k(k_reduce_splits, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, part, stride, splits, out, n);
     return 1;
 }
 
 int launch_tt_prefix(const int* meta, const int* seg_count, int BN, int* tt_prefix, cudaStream_t s) {
-    tc::k_tt_prefix<<<1, 1024, 0, s>>>(meta, seg_count, BN, tt_prefix);
+    launch_k(tc::k_tt_prefix, dim3(1), dim3(1024), 0, s, meta, seg_count, BN, tt_prefix);
     return 1;
 }
 
 int launch_gather_f16(const float* X, int64_t K, const int* pair_row, const int* meta, int64_t rows,
                       int dense_rows, __half* out, cudaStream_t s) {
     if (rows <= 0) return 0;
-    tc::k_gather_f16<<<(unsigned)rows, 256, 0, s>>>(X, K, pair_row, meta, dense_rows, out);
+    launch_k(tc::k_gather_f16, dim3((unsigned)rows), dim3(256), 0, s, X, K, pair_row, meta, dense_rows, out);
     return 1;
 }
 

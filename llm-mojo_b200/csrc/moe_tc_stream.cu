@@ -175,6 +175,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // barrier init, TMEM allocation and tensor-map prefetch overlap the previous kernel
+    pdl_trigger();
     Guard G{abort_flag, a.err_flag, globaltimer() + a.timeout_ns};
 
     if (warp == 0) {
@@ -443,7 +445,7 @@ int launch_st(const TcLaunch& L, int num_sms, cudaStream_t s) {
     int grid = num_sms;  // one CTA per SM: it owns all 512 TMEM columns
     if (L.max_items > 0 && L.max_items < grid) grid = (int)L.max_items;
     if (grid <= 0) return 0;
-    kern<<<grid, tc::ST_THREADS, smem, s>>>(qmap, bmap, smap, L.a, L.Wp, L.total_rows);
+    launch_k(kern, dim3(grid), dim3(tc::ST_THREADS), smem, s, qmap, bmap, smap, L.a, L.Wp, L.total_rows);
     return 1;
 }
 
