@@ -224,7 +224,11 @@ def workload_config(args, M):
             "tokens_per_step": M, "embed_dim": D, "expert_mlp_dim": F, "num_experts": E, "top_k": K,
             "layers_cycled": args.layers,
             "l2": f"weights of {args.layers} distinct layers cycled per step ({args.layers * 476} MB > 126 MB L2)",
-            "post_norm": True, "parallelism": f"replicas x{dist_setup()[0]}",
+            "post_norm": True,
+            "parallelism": (f"ep{dist_setup()[0]}: 128/{dist_setup()[0]} experts per GPU, tokens replicated, "
+                            f"NCCL all-reduce of partial outputs; dense rows sharded"
+                            if dist_setup()[0] > 1 and getattr(args, "parallel", "ep") == "ep"
+                            else f"replicas x{dist_setup()[0]}"),
             "gemm_path": getattr(args, "path", "auto"),
             "tc_kernel": getattr(args, "tc_kernel", "general"),
             "cuda_graph": not getattr(args, "no_graph", False)}
@@ -244,6 +248,9 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"],
                     help="expert/dense GEMM path: CUDA-core GEMV, tcgen05, or automatic")
+    ap.add_argument("--parallel", default="ep", choices=["ep", "replicas"],
+                    help="N > 1: expert parallel (128/N experts per GPU, tokens replicated, one NCCL "
+                         "all-reduce per layer; dense projections row-sharded) or independent replicas")
     ap.add_argument("--tc-kernel", default="general", choices=["stream", "general"],
                     help="tensor-core kernel for token tiles <= 64: streaming or general")
     args = ap.parse_args()
@@ -254,6 +261,7 @@ def main():
 
     import numpy as np
     import torch
+    import ep as EP
     import moe_b200 as MB
     import synth
 
@@ -271,38 +279,54 @@ def main():
     ctx.set_gemm_path({"auto": MB.PATH_AUTO, "gemv": MB.PATH_GEMV, "tc": MB.PATH_TC}[args.path])
     ctx.set_option(MB.OPT_TC_STREAM, int(args.tc_kernel == "stream"))
     M = WORKLOADS[args.workload]
+    use_ep = ws > 1 and args.parallel == "ep"
+    # expert parallel: every rank holds the same layers and tokens and
+    # evaluates its own expert range; replicas: independent data per rank
+    seed_rank = 0 if use_ep else rank
 
     layers, descs = [], []
     for li in range(args.layers):
-        lw = synth.make_layer(ctx, seed=1000 * rank + li)
+        lw = synth.make_layer(ctx, seed=1000 * seed_rank + li)
         layers.append(lw)
         descs.append(MB.make_desc(lw))
     gen = torch.Generator(device="cuda")
-    gen.manual_seed(77 + rank)
+    gen.manual_seed(77 + seed_rank)
     dense = {}
     if M == 16:
         for name, ci, co in DENSE:
             wt = torch.randn(ci * co, generator=gen, device="cuda") * 0.02
             p, s = synth.quantize(ctx, wt)
+            if use_ep:  # row-sharded: this rank's slice of the output features
+                r0, r1 = EP.row_range(rank, ws, co)
+                p, s, co = p[r0 * ci // 2:r1 * ci // 2], s[r0 * ci // 32:r1 * ci // 32], r1 - r0
             dense[name] = (p, s, ci, co)
-    xs = [synth.make_x(M, seed=500 + 10 * rank + li) for li in range(args.layers)]
+    xs = [synth.make_x(M, seed=500 + 10 * seed_rank + li) for li in range(args.layers)]
     x_o = torch.randn((M, 4096), generator=gen, device="cuda")
     out = torch.empty((M, D), device="cuda")
     dense_out = {n: torch.empty((M, co), device="cuda") for n, (_, _, _, co) in dense.items()}
 
-    # routing per layer (unique experts -> algorithmic bytes)
+    # routing per layer (unique experts of this rank -> algorithmic bytes)
+    e_lo, e_hi = EP.expert_range(rank, ws, E) if use_ep else (0, E)
+    epl = EP.ExpertParallelLayer(ctx, E) if use_ep else None
     uniq = []
     for li in range(args.layers):
         cnt = np.zeros(M, np.int64)
         idx = np.zeros((M, K), np.int64)
         w = np.zeros((M, K), np.float32)
         ctx.layer_forward(descs[li], M, xs[li], out, MB.F_POST_NORM, cnt, idx, w)
-        uniq.append(len({int(idx[t, k]) for t in range(M) for k in range(cnt[t])}))
+        uniq.append(len({int(idx[t, k]) for t in range(M) for k in range(cnt[t])
+                         if e_lo <= int(idx[t, k]) < e_hi}))
         pairs = int(cnt.sum())
+
+    def moe_step(li, x, o):
+        if epl is not None:
+            epl.forward(descs[li], M, x, o, MB.F_POST_NORM, layers[li]["post_norm_w"])
+        else:
+            ctx.layer_forward(descs[li], M, x, o, MB.F_POST_NORM)
 
     def step(i):
         li = i % args.layers
-        ctx.layer_forward(descs[li], M, xs[li], out, MB.F_POST_NORM)
+        moe_step(li, xs[li], out)
         for name, (p, s, ci, co) in dense.items():
             ctx.q4_matmul_batchN(M, p, s, x_o if name == "o" else xs[li], dense_out[name], ci, co)
 
@@ -319,11 +343,12 @@ def main():
         ctx.set_stream(cap.cuda_stream)
         n_cap = ctx.kernel_launches
         for li in range(args.layers):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=cap):
+            graphs.append(torch.cuda.CUDAGraph())
+            with torch.cuda.graph(graphs[-1], stream=cap):
                 step(li)
-            graphs.append(g)
         launches_per_step = (ctx.kernel_launches - n_cap) / args.layers
+        if pg:
+            launches_per_step += 1  # the NCCL all-reduce kernel is not counted by the library
         ctx.set_stream(stream.cuda_stream)
         for i in range(args.warmup):
             graphs[i % args.layers].replay()
@@ -355,7 +380,9 @@ def main():
         pg.barrier()
     torch.cuda.synchronize()
     ms_per_step = ms / args.steps
-    value = ws * M * args.steps / (ms / 1e3)
+    # expert parallel: all ranks serve the same M tokens; replicas: M each
+    tokens_per_step = M if use_ep else ws * M
+    value = tokens_per_step * args.steps / (ms / 1e3)
 
     # profiled pass over the same steps: per-kernel device time
     ctx.profile_enable(True)
@@ -373,9 +400,16 @@ def main():
     h2d = M * D * 4 + sum((M * (4096 if n == "o" else D) * 4) for n in dense)
     d2h = M * D * 4 + sum(M * co * 4 for (_, _, _, co) in dense.values())
 
+    x_d = torch.empty((M, D), device="cuda")
+
     def step_e2e(i):
         li = i % args.layers
-        ctx.layer_forward(descs[li], M, x_h[li], out_h, MB.F_POST_NORM)
+        if epl is not None:  # the collective needs device buffers: copy in, reduce, copy out
+            x_d.copy_(x_h[li], non_blocking=True)
+            epl.forward(descs[li], M, x_d, out, MB.F_POST_NORM, layers[li]["post_norm_w"])
+            out_h.copy_(out, non_blocking=True)
+        else:
+            ctx.layer_forward(descs[li], M, x_h[li], out_h, MB.F_POST_NORM)
         for name, (p, s, ci, co) in dense.items():
             ctx.q4_matmul_batchN(M, p, s, xo_h if name == "o" else x_h[li], dout_h[name], ci, co)
 
@@ -396,7 +430,7 @@ def main():
         t = torch.tensor([e2e_ms], device="cuda")
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = ws * M * e2e_steps / (e2e_ms / 1e3)
+    e2e_value = tokens_per_step * e2e_steps / (e2e_ms / 1e3)
 
     # roofline of the dominant kernel (largest share of profiled time)
     hbm, _, src = peaks()
@@ -446,7 +480,7 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong" if use_ep else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": workload_config(args, M), "roofline": roof, "step_roofline": step_roof,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
@@ -454,9 +488,15 @@ def main():
             "gpu_launches": launches, "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
+    # graphs that hold NCCL calls must be gone before the process group is
+    graphs.clear()
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
     ctx.close()
     if pg:
         pg.barrier()
+        torch.cuda.synchronize()
         pg.destroy_process_group()
     return 0
 

@@ -91,8 +91,16 @@ enum moe_option {
                                       tiles <= 64 (default 0: tensor memory) */
     MOE_OPT_ROUTER_TC_MIN_TOKENS = 6, /* router on tensor cores from this many tokens (default 2048;
                                         below it the router runs in fp32 like the reference) */
-    MOE_OPT_TC_STREAM = 7          /* 1: token tiles <= 64 (K % 128 == 0) use the streaming
+    MOE_OPT_TC_STREAM = 7,         /* 1: token tiles <= 64 (K % 128 == 0) use the streaming
                                       tensor-core kernel; 0 (default): the general one */
+    /* Expert parallelism: moe_layer_forward, moe_run_moe_coalesced_core and
+       moe_run_diffusion_moe_experts_parallel evaluate only experts in
+       [BEGIN, END) (END 0: all, the default).  Routing still covers all
+       experts; a token's output is the sum over its local slots (sum the
+       partial outputs across ranks, then moe_rms_norm for the post-norm).
+       No counterpart in the reference (a single process). */
+    MOE_OPT_EXPERT_BEGIN = 8,
+    MOE_OPT_EXPERT_END = 9
 };
 enum moe_gemm_path {
     MOE_PATH_AUTO = 0, /* CUDA-core GEMV for few tokens, tensor cores above the threshold */
@@ -123,6 +131,11 @@ int moe_unregister_weights(moe_ctx* ctx, const void* host_base);
  * Bit-exact with the reference on every input without an exact .5 tie. */
 int moe_quantize_fp32_to_q4_0(moe_ctx* ctx, const float* src, uint8_t* dst_packed,
                               float* dst_scales, int64_t num_elements);
+
+/* rms_norm (model_speculative_moe_batched.mojo:857-879): out[m] = x[m] *
+ * (1 / sqrt(mean(x[m]^2) + 1e-6)) * w, for M rows of d (d % 32 == 0).  Used
+ * for the post-norm after partial expert outputs were summed across ranks. */
+int moe_rms_norm(moe_ctx* ctx, const float* x, const float* w, float* out, int64_t M, int64_t d);
 
 /* q4_matmul_vec (moe_kernels.mojo:59-67): out[c_out] = W[c_out x c_in] x[c_in]. */
 int moe_q4_matmul_vec(moe_ctx* ctx, const uint8_t* W_packed, const float* scales,

@@ -59,6 +59,8 @@ struct moe_ctx {
     int router_tc_min_tokens = 2048;     // router on tensor cores from this many tokens
     bool tc_a_in_smem = false;           // MOE_OPT_TC_A_IN_SMEM
     bool tc_stream = false;              // MOE_OPT_TC_STREAM
+    int64_t expert_begin = 0;            // MOE_OPT_EXPERT_BEGIN
+    int64_t expert_end = 0;              // MOE_OPT_EXPERT_END (0: all experts)
     uint64_t device_timeout_ns = 4000000000ull;
     // profiling (moe_profile_enable)
     int profile = 0;
@@ -349,7 +351,9 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     const int64_t P = M * K;
     {
         ProfScope ps(ctx, "bucket");
-        ctx->launches += moe::launch_bucket(bb.slot_expert, P, (int)K, (int)E, bb.b, s);
+        const int e_lo = (int)std::min<int64_t>(ctx->expert_begin, E);
+        const int e_hi = ctx->expert_end > 0 ? (int)std::min<int64_t>(ctx->expert_end, E) : (int)E;
+        ctx->launches += moe::launch_bucket(bb.slot_expert, P, (int)K, (int)E, e_lo, e_hi, bb.b, s);
     }
     const int max_u = (int)std::min<int64_t>(E, P);
     const int max_t = (int)std::max<int64_t>(1, M);
@@ -647,6 +651,14 @@ int moe_set_option(moe_ctx* ctx, int option, int64_t value) {
         case MOE_OPT_TC_STREAM:
             ctx->tc_stream = value != 0;
             return MOE_OK;
+        case MOE_OPT_EXPERT_BEGIN:
+            if (value < 0) return fail(ctx, MOE_E_ARG, "bad expert index");
+            ctx->expert_begin = value;
+            return MOE_OK;
+        case MOE_OPT_EXPERT_END:
+            if (value < 0) return fail(ctx, MOE_E_ARG, "bad expert index");
+            ctx->expert_end = value;
+            return MOE_OK;
         case MOE_OPT_ROUTER_TC_MIN_TOKENS:
             if (value < 1) return fail(ctx, MOE_E_ARG, "bad token threshold");
             ctx->router_tc_min_tokens = (int)value;
@@ -771,6 +783,29 @@ int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch, const uint8_t* W, const fl
     }
     TRY(dense_q4(ctx, (const uint8_t*)w, (const float*)sc, (const float*)xd, (float*)od, c_in, c_out,
                  batch, "q4_matmul"));
+    return finish(ctx);
+}
+
+int moe_rms_norm(moe_ctx* ctx, const float* x, const float* w, float* out, int64_t M, int64_t d) {
+    TRY(begin(ctx));
+    if (!x || !w || !out) return fail(ctx, MOE_E_ARG, "null pointer");
+    if (M < 0 || d <= 0 || d % 32) return fail(ctx, MOE_E_SHAPE, "d must be a positive multiple of 32");
+    if (M == 0) return MOE_OK;
+    TRY(ws_reserve(ctx, al(M * d * 4) * 2 + al(d * 4)));
+    void *xd, *wd, *od;
+    TRY(dev_ptr(ctx, x, M * d * 4, K_IN, &xd));
+    TRY(dev_ptr(ctx, w, d * 4, K_IN, &wd));
+    TRY(dev_ptr(ctx, out, M * d * 4, K_OUT, &od));
+    moe::PrepArgs pa;
+    pa.x = xd;
+    pa.K = d;
+    pa.norm = 1;
+    pa.pre_w = (const float*)wd;
+    pa.out = (float*)od;
+    {
+        ProfScope ps(ctx, "rms_norm");
+        ctx->launches += moe::launch_prep(pa, M, ctx->stream);
+    }
     return finish(ctx);
 }
 
@@ -909,7 +944,7 @@ int moe_run_moe_experts_stage1(moe_ctx* ctx, const uint8_t* gu_p, const float* g
     ctx->launches += moe::launch_slots_from_lists(1, (int)count, nullptr, count,
                                                   (const int64_t*)ai, nullptr, bb.slot_expert,
                                                   bb.slot_weight, (int)E, ctx->err_flag, s);
-    ctx->launches += moe::launch_bucket(bb.slot_expert, count, (int)count, (int)E, bb.b, s);
+    ctx->launches += moe::launch_bucket(bb.slot_expert, count, (int)count, (int)E, 0, (int)E, bb.b, s);
     TRY(prep_rows(ctx, xi, MOE_X_NATURAL, 0, 1, d, bb.x32, bb.xsum));
     moe::GemvArgs g;
     g.Wp = (const uint8_t*)wp;
@@ -969,7 +1004,7 @@ int moe_run_moe_experts_stage2(moe_ctx* ctx, const uint8_t* dn_p, const float* d
                                                   (const int64_t*)ai, (const float*)aw,
                                                   bb.slot_expert, bb.slot_weight, (int)E,
                                                   ctx->err_flag, s);
-    ctx->launches += moe::launch_bucket(bb.slot_expert, count, (int)count, (int)E, bb.b, s);
+    ctx->launches += moe::launch_bucket(bb.slot_expert, count, (int)count, (int)E, 0, (int)E, bb.b, s);
     if (!al16(aa)) {
         float* ac = (float*)ws_take(ctx, count * F * 4);
         TRY(prep_rows(ctx, aa, MOE_X_NATURAL, 0, count, F, ac, nullptr));

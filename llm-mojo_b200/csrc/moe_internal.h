@@ -107,7 +107,7 @@ int launch_slots_from_lists(int64_t M, int K, const int64_t* count, int64_t coun
 int launch_slots_from_topw(int64_t M, int K, const int64_t* idx, const float* w,
                            int* slot_expert, float* slot_weight, int E, int* err_flag,
                            cudaStream_t s);
-int launch_bucket(const int* slot_expert, int64_t P, int K, int E, const BucketOut& o,
+int launch_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo, int e_hi, const BucketOut& o,
                   cudaStream_t s);
 int launch_gemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);
 int launch_gemv_wide(const uint8_t* W, const float* S, const float* X, float* out, int64_t rows, int K,

@@ -807,8 +807,10 @@ __device__ __forceinline__ int block_excl_scan(int v, int* wsum, int* total) {
     return base + x - v;
 }
 
-__global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t P, int K, int E,
-                                                 BucketOut o) {
+// Pairs whose expert lies outside [e_lo, e_hi) are left out (expert
+// parallelism: this rank holds only those experts); their slots get no pair.
+__global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo,
+                                                 int e_hi, BucketOut o) {
     pdl_wait();
     pdl_trigger();
     __shared__ int cnt[1024];
@@ -819,7 +821,7 @@ __global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t
     __syncthreads();
     for (int64_t p = tid; p < P; p += blockDim.x) {
         const int e = slot_expert[p];
-        if (e >= 0) atomicAdd(&cnt[e], 1);
+        if (e >= e_lo && e < e_hi) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
     const int c = tid < E ? cnt[tid] : 0;
@@ -839,7 +841,7 @@ __global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t
     __syncthreads();
     for (int64_t p = tid; p < P; p += blockDim.x) {
         const int e = slot_expert[p];
-        if (e >= 0) {
+        if (e >= e_lo && e < e_hi) {
             const int pos = atomicAdd(&cur[e], 1);
             o.pair_token[pos] = (int)(p / K);
             o.pair_slot[pos] = (int)p;
@@ -850,9 +852,9 @@ __global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t
     }
 }
 
-int launch_bucket(const int* slot_expert, int64_t P, int K, int E, const BucketOut& o,
+int launch_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo, int e_hi, const BucketOut& o,
                   cudaStream_t s) {
-    launch_k(k_bucket, dim3(1), dim3(1024), 0, s, slot_expert, P, K, E, o);
+    launch_k(k_bucket, dim3(1), dim3(1024), 0, s, slot_expert, P, K, E, e_lo, e_hi, o);
     return 1;
 }
 

@@ -25,6 +25,7 @@ F_POST_NORM, F_SET_COVER, F_FP16_OUT = 1, 4, 8
 OPT_GEMM_PATH, OPT_TC_MIN_TOKENS, OPT_DEVICE_TIMEOUT_NS = 1, 2, 3
 OPT_DENSE_TC_MIN_TOKENS, OPT_TC_A_IN_SMEM, OPT_ROUTER_TC_MIN_TOKENS = 4, 5, 6
 OPT_TC_STREAM = 7
+OPT_EXPERT_BEGIN, OPT_EXPERT_END = 8, 9
 PATH_AUTO, PATH_GEMV, PATH_TC = 0, 1, 2
 
 STATUS = {0: "MOE_OK", 1: "MOE_E_ARG", 2: "MOE_E_SHAPE", 3: "MOE_E_UNREGISTERED",
@@ -42,7 +43,7 @@ EXPORTS = [
     "moe_compute_subbatch_set_cover_moe_weights", "moe_run_moe_experts_stage1",
     "moe_run_moe_experts_stage2", "moe_run_moe_coalesced_core",
     "moe_run_diffusion_moe_experts_parallel", "moe_route", "moe_layer_forward",
-    "moe_q4_matmul_batchN_noalloc",
+    "moe_q4_matmul_batchN_noalloc", "moe_rms_norm",
 ]
 
 
@@ -100,6 +101,7 @@ def _declare(L):
     L.moe_q4_matmul_vec.argtypes = [_p, _p, _p, _p, _p, _i64, _i64]
     L.moe_q4_matmul_batchN.argtypes = [_p, _i64, _p, _p, _p, _p, _i64, _i64]
     L.moe_q4_matmul_batchN_noalloc.argtypes = [_p, _i64, _p, _p, _p, _p, _i64, _i64]
+    L.moe_rms_norm.argtypes = [_p, _p, _p, _p, _i64, _i64]
     L.moe_compute_moe_lod_weights.argtypes = [_p, _i64, _p, _p, _p, _f, _p, _p, _p, _i64]
     L.moe_apply_moe_lod_and_set_cover.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64, _f, _p,
                                                   _p, _i64]
@@ -179,6 +181,16 @@ class Context:
 
     def set_option(self, option: int, value: int):
         self.check(self.lib.moe_set_option(self.h, option, value))
+
+    def set_expert_range(self, begin: int = 0, end: int = 0):
+        """Evaluate only experts [begin, end) in the multi-token expert paths
+        (expert parallelism); end 0 selects all experts."""
+        self.set_option(OPT_EXPERT_BEGIN, begin)
+        self.set_option(OPT_EXPERT_END, end)
+
+    def rms_norm(self, x, w, out, M, d):
+        """model_speculative_moe_batched.mojo:857-879."""
+        self.check(self.lib.moe_rms_norm(self.h, _addr(x), _addr(w), _addr(out), M, d))
 
     def set_gemm_path(self, path: int):
         """PATH_AUTO, PATH_GEMV (CUDA cores, fp32) or PATH_TC (tcgen05, fp16 operands)."""

@@ -1,0 +1,51 @@
+"""One rank of the multi-GPU expert-parallel check (launched by
+tests/test_gpu_ep.py through torch.distributed.run, one process per GPU).
+
+Every rank builds the same seeded full-size layer and token batch, evaluates
+its expert range, and the partial outputs are all-reduced over NCCL; each
+rank then compares the result with its own one-GPU evaluation of the whole
+layer.  Exit status 0 means the outputs agree within the parity tolerance."""
+import datetime
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(HERE, "..", "llm-mojo_b200"), HERE]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import ep  # noqa: E402
+import moe_b200 as MB  # noqa: E402
+import synth  # noqa: E402
+from tolerances import errors  # noqa: E402
+
+
+def main():
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
+    ctx = MB.Context(local)
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    layer = synth.make_layer(ctx, seed=0)
+    layer["post_norm_w"] = (1.0 + 0.1 * torch.randn(layer["d"], generator=torch.Generator().manual_seed(3))).cuda()
+    desc = MB.make_desc(layer)
+    ok = True
+    for M in (1, 16, 64):
+        x = synth.make_x(M, seed=40 + M)
+        out = torch.zeros((M, layer["d"]), device="cuda")
+        ep.ExpertParallelLayer(ctx, layer["E"]).forward(desc, M, x, out, MB.F_POST_NORM, layer["post_norm_w"])
+        ref = torch.zeros_like(out)
+        ctx.layer_forward(desc, M, x, ref, MB.F_POST_NORM)
+        torch.cuda.synchronize()
+        mx, rel = errors(out.cpu().numpy(), ref.cpu().numpy())
+        print(f"rank {dist.get_rank()} M={M}: max_abs={mx:.2e} rel_l2={rel:.2e}", flush=True)
+        ok = ok and mx <= 1e-4 and rel <= 1e-5
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0 if ok else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

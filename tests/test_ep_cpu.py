@@ -1,0 +1,98 @@
+"""Expert parallelism, host side, on CPU: two gloo ranks each evaluate their
+contiguous expert range with the oracle and all-reduce the partial outputs;
+the sum must equal the one-process result.  No GPU is involved."""
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import ep
+
+
+def test_expert_ranges_partition_all_experts():
+    for world in (1, 2, 3, 4, 8):
+        seen = []
+        for r in range(world):
+            lo, hi = ep.expert_range(r, world, 128)
+            assert lo <= hi
+            seen.extend(range(lo, hi))
+        assert seen == list(range(128))
+    assert ep.expert_range(7, 8, 128) == (112, 128)
+    with pytest.raises(ValueError):
+        ep.expert_range(2, 2, 128)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _layer(d, F, E, K, seed):
+    import oracle as O
+    rng = np.random.default_rng(seed)
+    w = dict(d=d, F=F, E=E, top_k=K)
+    w["router_f32"] = rng.normal(0, 0.02, (E, d)).astype(np.float32)
+    w["router_p"], w["router_s"], _ = O.quantize_q4_0(w["router_f32"])
+    w["gu_p"], w["gu_s"], _ = O.quantize_q4_0(rng.normal(0, 0.02, E * 2 * F * d).astype(np.float32))
+    w["dn_p"], w["dn_s"], _ = O.quantize_q4_0(rng.normal(0, 0.02, E * d * F).astype(np.float32))
+    for k in ("router_scale", "pre_norm_w", "post_norm_w"):
+        w[k] = np.ones(d, np.float32)
+    w["per_expert_scale"] = np.ones(E, np.float32)
+    return w
+
+
+def _worker(rank, world, port, q):
+    try:
+        import torch
+        import torch.distributed as dist
+        import oracle as O
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        import datetime
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        d, F, E, K, M = 256, 64, 16, 4, 6
+        w = _layer(d, F, E, K, seed=11)
+        L = O.make_layer(w)
+        x = np.random.default_rng(12).standard_normal((M, d)).astype(np.float32)
+        r = O.route(L, x)
+        lo, hi = ep.expert_range(rank, world, E)
+        local = (r["idx"] >= lo) & (r["idx"] < hi)
+        w_local = np.where(local, r["w"], 0.0).astype(np.float32)
+        part = O.experts_forward(L, r["moe_in"], r["count"], r["idx"], w_local, prec=O.F64)
+        t = torch.from_numpy(part.astype(np.float64))
+        dist.all_reduce(t)
+        full = O.experts_forward(L, r["moe_in"], r["count"], r["idx"], r["w"], prec=O.F64)
+        err = float(np.max(np.abs(t.numpy() - full)))
+        # post-norm after the reduction, as ep.ExpertParallelLayer applies it
+        s = t.numpy()
+        normed = s / np.sqrt((s ** 2).mean(1, keepdims=True) + 1e-6)
+        ref, _, _, _ = O.layer_forward(L, x, post_norm=True, prec=O.F64)
+        err_norm = float(np.max(np.abs(normed - ref)))
+        n_local = int(local.sum())
+        dist.destroy_process_group()
+        q.put((rank, err, err_norm, n_local))
+    except Exception as e:  # reported to the parent
+        q.put((rank, repr(e), None, None))
+
+
+def test_two_gloo_ranks_reproduce_the_full_layer():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    res.sort()
+    for rank, err, err_norm, n_local in res:
+        assert not isinstance(err, str), err
+        assert err < 1e-6 and err_norm < 1e-5, (rank, err, err_norm)
+    assert res[0][3] + res[1][3] > 0
