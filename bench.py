@@ -41,7 +41,21 @@ GU_BYTES = 2 * F * D // 2 + 2 * F * D // 32 * 4   # 2,478,080 per expert
 DN_BYTES = D * F // 2 + D * F // 32 * 4           # 1,239,040 per expert
 ROUTER_BYTES = E * D // 2 + E * D // 32 * 4       # 225,280
 DENSE = [("q", D, 4096), ("k", D, 1024), ("v", D, 1024), ("o", 4096, D)]
-WORKLOADS = {"decode16": 16, "decode1": 1, "block256": 256}
+# tokens per step, distinct layers cycled (default), skewed routing, step count (default)
+WORKLOADS = {
+    "decode16": dict(M=16, layers=4),
+    "decode1": dict(M=1, layers=4),
+    "block256": dict(M=256, layers=4),
+    "decode64": dict(M=64, layers=30),
+    "prefill8k": dict(M=8192, layers=2, skew=True, steps=50),
+}
+WORKLOAD_NAMES = {
+    "decode16": "cfg2: M=16 decode MoE layer + dense q/k/v/o",
+    "decode1": "cfg1: M=1 decode MoE layer",
+    "block256": "cfg3: M=256 block through the MoE layer",
+    "decode64": "cfg4: M=64 decode, one layer step of a 30-layer stack (independent seeded layers)",
+    "prefill8k": "cfg5: M=8192 (4 x 2048) through the MoE layer, Zipf(1.1)-skewed router",
+}
 METRIC = "moe_layer_tokens_per_s"
 
 
@@ -50,12 +64,43 @@ def q4_bytes(c_in, c_out):
 
 
 def peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, source)."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             j = json.load(f)
-        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return (float(j["hbm_gbs"]), float(j["bf16_tflops"]),
+                float(j.get("bf16_tflops_sustained", j["bf16_tflops"])), "measured")
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def calibrate_skew(ctx, MB, synth, layer, x, M, target=5.0):
+    """Zipf(1.1) router-logit bias scaled so that the busiest expert takes
+    `target` x the mean load (active slots after the LOD prune); bisection
+    on the scale alpha with the library's own router."""
+    import numpy as np
+    import torch
+    cnt = np.zeros(M, np.int64)
+    idx = np.zeros((M, K), np.int64)
+    w = np.zeros((M, K), np.float32)
+
+    def ratio(alpha):
+        b = torch.from_numpy(synth.zipf_bias(E, 1.1, alpha, seed=0)).cuda()
+        ctx.route(MB.make_desc(layer, bias=b), M, x, cnt, idx, w)
+        act = idx[np.arange(K)[None, :] < cnt[:, None]]
+        loads = np.bincount(act, minlength=E)
+        return float(loads.max() / loads.mean()), b
+
+    lo, hi = 0.0, 1.0
+    for _ in range(14):
+        mid = 0.5 * (lo + hi)
+        if ratio(mid)[0] < target:
+            lo = mid
+        else:
+            hi = mid
+    alpha = 0.5 * (lo + hi)
+    r, b = ratio(alpha)
+    return alpha, r, b
 
 
 class ClockSampler:
@@ -178,7 +223,7 @@ def run_reference(args, ws, rank):
     moe_kernels.mojo; the Mojo toolchain is absent) on the host cores."""
     if rank != 0:
         return 0
-    M = WORKLOADS[args.workload]
+    M = WORKLOADS[args.workload]["M"]
     nthreads = os.cpu_count() or 1
     w, dense = host_layer(seed=0)
     # bounded sample: at most ~120 s for the K timed steps
@@ -218,9 +263,7 @@ def run_reference(args, ws, rank):
 
 
 def workload_config(args, M):
-    return {"workload": {"decode16": "cfg2: M=16 decode MoE layer + dense q/k/v/o",
-                         "decode1": "cfg1: M=1 decode MoE layer",
-                         "block256": "cfg3: M=256 block through the MoE layer"}[args.workload],
+    return {"workload": WORKLOAD_NAMES[args.workload],
             "tokens_per_step": M, "embed_dim": D, "expert_mlp_dim": F, "num_experts": E, "top_k": K,
             "layers_cycled": args.layers,
             "l2": f"weights of {args.layers} distinct layers cycled per step ({args.layers * 476} MB > 126 MB L2)",
@@ -238,11 +281,11 @@ def workload_config(args, M):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (workload default)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode16", choices=sorted(WORKLOADS))
-    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--layers", type=int, default=None, help="distinct layers cycled (workload default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
@@ -255,6 +298,11 @@ def main():
                     help="tensor-core kernel for token tiles <= 64: streaming or general")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    wl = WORKLOADS[args.workload]
+    if args.layers is None:
+        args.layers = wl["layers"]
+    if args.steps is None:
+        args.steps = wl.get("steps", 2000)
     ws, rank, local = dist_setup()
     if args.impl == "reference":
         return run_reference(args, ws, rank)
@@ -278,7 +326,7 @@ def main():
     ctx.set_stream(stream.cuda_stream)
     ctx.set_gemm_path({"auto": MB.PATH_AUTO, "gemv": MB.PATH_GEMV, "tc": MB.PATH_TC}[args.path])
     ctx.set_option(MB.OPT_TC_STREAM, int(args.tc_kernel == "stream"))
-    M = WORKLOADS[args.workload]
+    M = wl["M"]
     use_ep = ws > 1 and args.parallel == "ep"
     # expert parallel: every rank holds the same layers and tokens and
     # evaluates its own expert range; replicas: independent data per rank
@@ -289,6 +337,12 @@ def main():
         lw = synth.make_layer(ctx, seed=1000 * seed_rank + li)
         layers.append(lw)
         descs.append(MB.make_desc(lw))
+    skew = None
+    if wl.get("skew"):
+        x_cal = synth.make_x(M, seed=499)
+        alpha, ratio, bias = calibrate_skew(ctx, MB, synth, layers[0], x_cal, M)
+        descs = [MB.make_desc(lw, bias=bias) for lw in layers]
+        skew = {"zipf_s": 1.1, "alpha": alpha, "max_over_mean_load": ratio}
     gen = torch.Generator(device="cuda")
     gen.manual_seed(77 + seed_rank)
     dense = {}
@@ -308,7 +362,7 @@ def main():
     # routing per layer (unique experts of this rank -> algorithmic bytes)
     e_lo, e_hi = EP.expert_range(rank, ws, E) if use_ep else (0, E)
     epl = EP.ExpertParallelLayer(ctx, E) if use_ep else None
-    uniq = []
+    uniq, pairs_l = [], []
     for li in range(args.layers):
         cnt = np.zeros(M, np.int64)
         idx = np.zeros((M, K), np.int64)
@@ -317,6 +371,7 @@ def main():
         uniq.append(len({int(idx[t, k]) for t in range(M) for k in range(cnt[t])
                          if e_lo <= int(idx[t, k]) < e_hi}))
         pairs = int(cnt.sum())
+        pairs_l.append(pairs)
 
     def moe_step(li, x, o):
         if epl is not None:
@@ -433,7 +488,8 @@ def main():
     e2e_value = tokens_per_step * e2e_steps / (e2e_ms / 1e3)
 
     # roofline of the dominant kernel (largest share of profiled time)
-    hbm, _, src = peaks()
+    hbm, tf_burst, tf_sust, src = peaks()
+    pairs_mean = sum(pairs_l) / len(pairs_l)
     u_mean = sum(uniq) / len(uniq)
     dom = max((kv for kv in prof.items() if kv[0] in ("gemv_gate_up", "gemv_down", "q4_matmul",
                                                        "tc_gate_up", "tc_down")),
@@ -448,7 +504,15 @@ def main():
         "prep": 4 * M * D * 4,
     }
     roof = None
-    if dom in alg and prof[dom][1] > 0:
+    if wl.get("skew") and dom in ("tc_gate_up", "tc_down") and prof[dom][1] > 0:
+        # prefill scale: tensor-bound; FLOPs of the dominant grouped GEMM per launch
+        flops = pairs_mean * 2 * (2 * F * D if dom == "tc_gate_up" else D * F)
+        avg_ms = prof[dom][0] / prof[dom][1]
+        achieved = flops / (avg_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": tf_sust, "unit": "TFLOP/s",
+                "frac": achieved / tf_sust, "traffic": None, "flops_per_launch": flops, "avg_launch_ms": avg_ms,
+                "peak_source": f"MEASURED_PEAKS.json bf16_tflops_sustained ({'of measured' if src == 'measured' else 'of fallback'})"}
+    elif dom in alg and prof[dom][1] > 0:
         avg_ms = prof[dom][0] / prof[dom][1]
         achieved = alg[dom] / (avg_ms / 1e3) / 1e9
         traffic = None
@@ -481,7 +545,8 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong" if use_ep else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(args, M), "roofline": roof, "step_roofline": step_roof,
+            "config": dict(workload_config(args, M), **({"skew": skew} if skew else {})),
+            "roofline": roof, "step_roofline": step_roof,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
