@@ -273,7 +273,7 @@ def workload_config(args, M):
                             if dist_setup()[0] > 1 and getattr(args, "parallel", "ep") == "ep"
                             else f"replicas x{dist_setup()[0]}"),
             "gemm_path": getattr(args, "path", "auto"),
-            "tc_kernel": getattr(args, "tc_kernel", "general"),
+            "tc_kernel": getattr(args, "tc_kernel", "stream"),
             "cuda_graph": not getattr(args, "no_graph", False)}
 
 
@@ -294,8 +294,9 @@ def main():
     ap.add_argument("--parallel", default="ep", choices=["ep", "replicas"],
                     help="N > 1: expert parallel (128/N experts per GPU, tokens replicated, one NCCL "
                          "all-reduce per layer; dense projections row-sharded) or independent replicas")
-    ap.add_argument("--tc-kernel", default="general", choices=["stream", "general"],
-                    help="tensor-core kernel for token tiles <= 64: streaming or general")
+    ap.add_argument("--tc-kernel", default="stream", choices=["stream", "stream-all", "general"],
+                    help="tensor-core kernel for token tiles <= 64: streaming for the expert GEMMs "
+                         "(default), streaming also for dense projections, or general")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = WORKLOADS[args.workload]
@@ -325,7 +326,7 @@ def main():
     stream = torch.cuda.current_stream()
     ctx.set_stream(stream.cuda_stream)
     ctx.set_gemm_path({"auto": MB.PATH_AUTO, "gemv": MB.PATH_GEMV, "tc": MB.PATH_TC}[args.path])
-    ctx.set_option(MB.OPT_TC_STREAM, int(args.tc_kernel == "stream"))
+    ctx.set_option(MB.OPT_TC_STREAM, {"general": 0, "stream": 1, "stream-all": 2}[args.tc_kernel])
     M = wl["M"]
     use_ep = ws > 1 and args.parallel == "ep"
     # expert parallel: every rank holds the same layers and tokens and

@@ -58,7 +58,7 @@ struct moe_ctx {
     int dense_tc_min_tokens = 2;         // auto, dense projections
     int router_tc_min_tokens = 2048;     // router on tensor cores from this many tokens
     bool tc_a_in_smem = false;           // MOE_OPT_TC_A_IN_SMEM
-    bool tc_stream = false;              // MOE_OPT_TC_STREAM
+    int tc_stream = 1;                   // MOE_OPT_TC_STREAM
     int64_t expert_begin = 0;            // MOE_OPT_EXPERT_BEGIN
     int64_t expert_end = 0;              // MOE_OPT_EXPERT_END (0: all experts)
     uint64_t device_timeout_ns = 4000000000ull;
@@ -390,7 +390,7 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
         t1.BN = BN;
         t1.max_items = (int64_t)(F / 64) * (max_u + (P + BN - 1) / BN);
         t1.a_in_smem = ctx->tc_a_in_smem;
-        t1.stream = ctx->tc_stream;
+        t1.stream = ctx->tc_stream >= 1;
         int r;
         {
             ProfScope ps(ctx, "tc_gate_up");
@@ -508,7 +508,7 @@ int dense_q4(moe_ctx* ctx, const uint8_t* w, const float* sc, const float* xd, f
         t.BN = BN;
         t.max_items = ((c_out + 127) / 128) * ((batch + BN - 1) / BN);
         t.a_in_smem = ctx->tc_a_in_smem;
-        t.stream = ctx->tc_stream;
+        t.stream = ctx->tc_stream >= 2;
         const int ks = choose_ksplit(ctx, t.max_items, c_in);
         float* part = nullptr;
         if (ks > 1) {
@@ -649,7 +649,8 @@ int moe_set_option(moe_ctx* ctx, int option, int64_t value) {
             ctx->tc_a_in_smem = value != 0;
             return MOE_OK;
         case MOE_OPT_TC_STREAM:
-            ctx->tc_stream = value != 0;
+            if (value < 0 || value > 2) return fail(ctx, MOE_E_ARG, "MOE_OPT_TC_STREAM is 0, 1 or 2");
+            ctx->tc_stream = (int)value;
             return MOE_OK;
         case MOE_OPT_EXPERT_BEGIN:
             if (value < 0) return fail(ctx, MOE_E_ARG, "bad expert index");
@@ -1456,7 +1457,7 @@ int moe_q4_matmul_batchN_noalloc(moe_ctx* ctx, int64_t batch, const uint8_t* W, 
     t.BN = BN;
     t.max_items = ((c_out + 127) / 128) * ((batch + BN - 1) / BN);
     t.a_in_smem = ctx->tc_a_in_smem;
-    t.stream = ctx->tc_stream;
+    t.stream = ctx->tc_stream >= 2;
     // split-K partials go after the activation copy, as many splits as fit
     int ks = choose_ksplit(ctx, t.max_items, c_in);
     const size_t part_room = kNoAllocScratchBytes - x16_bytes;

@@ -40,7 +40,7 @@ struct TcLaunch {
     int BN = 16;                  // token tile: 16, 32, 64, 128 or 256
     int64_t max_items = 0;        // upper bound on work items (limits the grid), 0 = none
     bool a_in_smem = false;       // force the shared-memory A operand for BN <= 64
-    bool stream = false;          // BN <= 64: the streaming kernel (moe_tc_stream.cu) where it applies
+    bool stream = false;          // BN <= 64, K % 128 == 0: the streaming kernel (moe_tc_stream.cu)
 };
 
 // Returns the number of kernels launched, or -1 when the shape or the tensor

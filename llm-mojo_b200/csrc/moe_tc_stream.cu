@@ -1,9 +1,11 @@
 // moe_tc_stream.cu -- streaming variant of the tcgen05 grouped Q4_0 GEMM
-// for token tiles of 16..64 tokens and K % 128 == 0 (MOE_OPT_TC_STREAM;
-// off by default).
+// for token tiles of 16..64 tokens and K % 128 == 0 (MOE_OPT_TC_STREAM:
+// by default the expert GEMMs whose K allows it, i.e. gate/up).
 //
 // Same contraction, work list, K order and epilogues as k_tc_gemm
-// (moe_tc.cu), organised as one CTA per SM with all 512 TMEM columns:
+// (moe_tc.cu), organised as one CTA per SM with all 512 TMEM columns
+// (measured 12-18 % faster than k_tc_gemm on the gate/up GEMM at 16-256
+// tokens):
 //  - a stage covers 256 K: the 128 weight rows' 128 packed bytes (two TMA
 //    boxes of 128 B x 64 rows, SWIZZLE_128B), their eight block scales (two
 //    TMA boxes of 8 fp32 x 64 rows) and the token tile's activations (one 3-D
@@ -16,11 +18,10 @@
 //    is 1024 + n and (w & 0x00F000F0) | 0x54005400 is 64 + n, so (n - 8) is
 //    one exact fp16 subtraction, then one multiply by the fp16 scale;
 //  - epilogue warps wait with back-off.
-// Measured on B200 at decode sizes it is slower than k_tc_gemm: with the A
-// operand in TMEM a tcgen05.mma of M=128, N=16, K=16 occupies the issuing
-// thread for about 100 cycles, so one MMA issuer per SM bounds the stream at
-// about 20 weights per cycle, and the general kernel's two CTAs per SM hide
-// more of the dequantisation latency.
+//  - with the A operand in TMEM a tcgen05.mma of M=128, N=16, K=16 holds
+//    its issuing thread for about 100 cycles, so two threads (warps 1 and
+//    14) issue the MMAs of alternate stages into separate accumulators,
+//    which the epilogue adds.
 //
 // Every mbarrier wait is bounded (globaltimer deadline); on expiry the kernel
 // raises err_flag = 2, every role drains what it issued and the CTA frees
@@ -39,11 +40,13 @@ constexpr int ST_Q = 128 * ST_K / 2;            // packed bytes per stage (16384
 constexpr int ST_S = 128 * 32;                  // scale bytes per stage (8 fp32 per row)
 constexpr int ST_DQ0 = 2;                       // warps 2-9: dequant, two groups of four
 constexpr int ST_EPI0 = ST_DQ0 + 8;             // warps 10-13: epilogue
-constexpr int ST_THREADS = 32 * (ST_EPI0 + 4);  // 448
+constexpr int ST_MMA2 = ST_EPI0 + 4;            // warp 14: second MMA issuer
+constexpr int ST_NMMA = 2;                      // MMA issuers: warp 1 (even stages), warp 14 (odd)
+constexpr int ST_THREADS = 32 * (ST_MMA2 + 1);  // 480
 
 template <int BN>
 struct StLayout {
-    static constexpr int ACC = ((2 * BN + 31) / 32) * 32;  // two accumulator buffers
+    static constexpr int ACC = ((2 * ST_NMMA * BN + 31) / 32) * 32;  // two buffers x two issuers
     static constexpr int SA = (512 - ACC) / 64 > 7 ? 7 : (512 - ACC) / 64;  // 128-K fp16 A slots in TMEM
     static constexpr int B_BYTES = BN * ST_K * 2;
     static constexpr int SLOT = ST_Q + B_BYTES + ST_S;
@@ -52,7 +55,7 @@ struct StLayout {
     static constexpr int OFF_B = OFF_Q + SQ * ST_Q;
     static constexpr int OFF_S = OFF_B + SQ * B_BYTES;
     static constexpr int OFF_BAR = OFF_S + SQ * ST_S;
-    static constexpr int N_BAR = 2 * SQ + 2 * SA + 4 + 1;
+    static constexpr int N_BAR = 2 * SQ + 2 * SA + 4 + ST_NMMA;
     static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
     static constexpr int TOTAL = OFF_MISC + 16 + 1024;  // + alignment slack
 };
@@ -122,7 +125,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     auto a_empty = [&](int s) { return bar0 + 8u * (2 * SQ + SA + s); };
     auto acc_full = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + s); };
     auto acc_empty = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + 2 + s); };
-    const uint32_t drain_bar = bar0 + 8u * (2 * SQ + 2 * SA + 4);
+    auto drain_bar = [&](int j) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + j); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -155,10 +158,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             mbar_init(a_empty(s), 1);
         }
         for (int s = 0; s < 2; ++s) {
-            mbar_init(acc_full(s), 1);
+            mbar_init(acc_full(s), ST_NMMA);
             mbar_init(acc_empty(s), 4);
         }
-        mbar_init(drain_bar, 1);
+        for (int j = 0; j < ST_NMMA; ++j) mbar_init(drain_bar(j), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         prefetch_tmap(&qmap);
@@ -238,8 +241,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 if (q_armed & (1u << s)) mbar_wait(q_full(s), (q_par >> s) & 1u, Gd);
         }
         __syncwarp();
-    } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
+    } else if (warp == 1 || warp == ST_MMA2) {
+        // ------------------------------------------------ MMA issuers
+        // A tcgen05.mma of N <= 64 with A in TMEM holds its issuing thread for
+        // about 100 cycles, so two threads issue: stage st goes to issuer
+        // st % 2, each into its own accumulator, summed by the epilogue.
+        const int me = (warp == 1) ? 0 : 1;
         if (lane == 0) {
             uint32_t st = 0;
             int ab = 0;
@@ -250,9 +257,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
                 if (!(ok = mbar_wait(acc_empty(ab), accp ^ 1u, G))) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(ab * BN);
+                const uint32_t d_tmem = tmem_base + (uint32_t)((ab * ST_NMMA + me) * BN);
+                bool first = true;
                 const int sb = s_begin(it), se = s_end(it);
                 for (int s = sb; s < se && ok; ++s, ++st) {
+                    if ((int)(st % ST_NMMA) != me) continue;
                     const int qs = (int)(st % SQ);
                     if (!(ok = mbar_wait(q_full(qs), (st / SQ) & 1u, G))) break;  // activations landed
                     const uint32_t bd = smem_u32(smem + L::OFF_B + qs * L::B_BYTES);
@@ -267,10 +276,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                         for (int k = 0; k < nk; ++k)
                             tc_mma_ts(d_tmem, ta + 8u * k,
                                       kmajor_plain_desc(bd + (uint32_t)((16 * h + 2 * k) * BN * 16), BN * 16, 128),
-                                      IDESC, (s != sb) || h || k);
+                                      IDESC, (!first) || h || k);
                         issued = true;
                         tc_commit(a_empty(as));
                     }
+                    first = false;
                     if (!ok) break;
                     tc_commit(q_empty(qs));
                 }
@@ -281,12 +291,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                     accp ^= 1u;
                 }
             }
-            if (issued) {  // all MMAs complete before TMEM is released
-                tc_commit(drain_bar);
+            if (issued) {  // all of this thread's MMAs complete before TMEM is released
+                tc_commit(drain_bar(me));
                 Guard Gd{abort_flag, a.err_flag, globaltimer() + drain_ns};
                 volatile int no_abort = 0;
                 Gd.abort = &no_abort;
-                mbar_wait(drain_bar, 0, Gd);
+                mbar_wait(drain_bar(me), 0, Gd);
             }
         }
         __syncwarp();
@@ -357,11 +367,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             }
             st += (uint32_t)ns;
         }
-    } else {
+    } else if (warp < ST_MMA2) {
         // ------------------------------------------------ epilogue
         const int q = warp & 3;       // TMEM lane quarter this warp may access
         const int i = q * 32 + lane;  // accumulator row (A-tile row)
         constexpr int CW = BN < 32 ? BN : 32;
+        uint32_t est = 0;             // global stage counter at the item's first stage
         int ab = 0;
         uint32_t accp = 0;
         Item it;
@@ -371,10 +382,19 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             if (!ok) break;
             tc_fence_after();
             const int nv = min(BN, it.n - it.tt * BN);
-            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * ST_NMMA * BN);
+            const int ns = s_end(it) - s_begin(it);
             for (int c0 = 0; c0 < nv; c0 += CW) {
                 float v[CW];
-                tmem_ld<CW>(tbase + c0, v);
+#pragma unroll
+                for (int cc = 0; cc < CW; ++cc) v[cc] = 0.f;
+                for (int j = 0; j < ST_NMMA; ++j) {  // the issuers that had a stage of this item
+                    if ((j - (int)(est % ST_NMMA) + ST_NMMA) % ST_NMMA >= ns) continue;
+                    float v2[CW];
+                    tmem_ld<CW>(tbase + (uint32_t)(j * BN) + c0, v2);
+#pragma unroll
+                    for (int cc = 0; cc < CW; ++cc) v[cc] += v2[cc];
+                }
                 if (MODE == TC_ACT) {
                     const int j = it.rt * 64 + 16 * q + (lane & 15);  // act row
                     const int jp = (j & ~7) | kpos(j & 7);
@@ -400,6 +420,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                     }
                 }
             }
+            est += (uint32_t)(s_end(it) - s_begin(it));
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty(ab));

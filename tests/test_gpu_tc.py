@@ -19,15 +19,16 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(params=["stream", "a_tmem", "a_smem"])
 def tc(ctx, request):
-    """Tensor-core path: the streaming kernel (an option for token tiles <= 64),
-    the general kernel with the dequantised weights in TMEM (default), or the
-    general kernel with them staged in shared memory."""
+    """Tensor-core path: the streaming kernel for every GEMM it supports (the
+    default uses it for the expert GEMMs), the general kernel with the
+    dequantised weights in TMEM, or the general kernel with them staged in
+    shared memory."""
     ctx.set_gemm_path(MB.PATH_TC)
-    ctx.set_option(MB.OPT_TC_STREAM, int(request.param == "stream"))
+    ctx.set_option(MB.OPT_TC_STREAM, 2 if request.param == "stream" else 0)
     ctx.set_option(MB.OPT_TC_A_IN_SMEM, int(request.param == "a_smem"))
     yield ctx
     ctx.set_option(MB.OPT_TC_A_IN_SMEM, 0)
-    ctx.set_option(MB.OPT_TC_STREAM, 0)
+    ctx.set_option(MB.OPT_TC_STREAM, 1)
     ctx.set_gemm_path(MB.PATH_AUTO)
 
 
