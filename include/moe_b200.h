@@ -101,7 +101,12 @@ enum moe_option {
        partial outputs across ranks, then moe_rms_norm for the post-norm).
        No counterpart in the reference (a single process). */
     MOE_OPT_EXPERT_BEGIN = 8,
-    MOE_OPT_EXPERT_END = 9
+    MOE_OPT_EXPERT_END = 9,
+    MOE_OPT_FUSED_ROUTE = 10,      /* 1: moe_layer_forward routes batches of <= 16 tokens (Q4_0
+                                      router, LOD routing) in one fused cluster launch; 0 (default):
+                                      the separate norm / router / top-k / bucket / gather kernels */
+    MOE_OPT_DENSE_KSPLIT = 11      /* dense tensor-core GEMMs: split K into this many partial sums
+                                      (0, the default: enough work items for two per SM) */
 };
 enum moe_gemm_path {
     MOE_PATH_AUTO = 0, /* CUDA-core GEMV for few tokens, tensor cores above the threshold */

@@ -61,6 +61,8 @@ struct moe_ctx {
     int tc_stream = 1;                   // MOE_OPT_TC_STREAM
     int64_t expert_begin = 0;            // MOE_OPT_EXPERT_BEGIN
     int64_t expert_end = 0;              // MOE_OPT_EXPERT_END (0: all experts)
+    bool fused_route = false;            // MOE_OPT_FUSED_ROUTE
+    int dense_ksplit = 0;                // MOE_OPT_DENSE_KSPLIT (0: automatic)
     uint64_t device_timeout_ns = 4000000000ull;
     // profiling (moe_profile_enable)
     int profile = 0;
@@ -343,16 +345,34 @@ bool use_tc(moe_ctx* ctx, int64_t M, int64_t d, int64_t F, const ExpertWeights& 
     return M >= ctx->tc_min_tokens;
 }
 
+// Local expert range [lo, hi) of the context (expert parallelism).
+void expert_range(moe_ctx* ctx, int64_t E, int* lo, int* hi) {
+    *lo = (int)std::min<int64_t>(ctx->expert_begin, E);
+    *hi = ctx->expert_end > 0 ? (int)std::min<int64_t>(ctx->expert_end, E) : (int)E;
+}
+
+// Token tile of the expert GEMMs from the mean load of an active expert.
+int expert_token_tile(int64_t P, int64_t E) {
+    const int64_t max_u = std::min<int64_t>(E, P);
+    const int64_t mean = (P + max_u - 1) / max_u;
+    int BN = 16;
+    while (BN < 256 && BN < mean) BN *= 2;
+    return BN;
+}
+
 // slot table -> bucket -> gate/up (+act) -> down -> combine.  bb.x32 and
 // bb.xsum must hold the gate/up input (prep_rows or the router's prep).
+// `prebucketed`: the fused routing kernel already wrote the buckets, the
+// token-tile prefix and (tensor-core path) the fp16 pair rows.
 int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int64_t d, int64_t F,
-                int64_t E, int act, ExpertBufs& bb, const moe::CombineArgs* comb_tmpl, void* out) {
+                int64_t E, int act, ExpertBufs& bb, const moe::CombineArgs* comb_tmpl, void* out,
+                bool prebucketed = false) {
     cudaStream_t s = ctx->stream;
     const int64_t P = M * K;
-    {
+    if (!prebucketed) {
         ProfScope ps(ctx, "bucket");
-        const int e_lo = (int)std::min<int64_t>(ctx->expert_begin, E);
-        const int e_hi = ctx->expert_end > 0 ? (int)std::min<int64_t>(ctx->expert_end, E) : (int)E;
+        int e_lo, e_hi;
+        expert_range(ctx, E, &e_lo, &e_hi);
         ctx->launches += moe::launch_bucket(bb.slot_expert, P, (int)K, (int)E, e_lo, e_hi, bb.b, s);
     }
     const int max_u = (int)std::min<int64_t>(E, P);
@@ -360,12 +380,9 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
 
     int ksplit = 1;
     if (use_tc(ctx, M, d, F, w)) {
-        // token tile from the mean load of an active expert
-        const int64_t mean = (P + max_u - 1) / max_u;
-        int BN = 16;
-        while (BN < 256 && BN < mean) BN *= 2;
-        ctx->launches += moe::launch_tt_prefix(bb.b.meta, bb.b.seg_count, BN, bb.tt_prefix, s);
-        {
+        const int BN = expert_token_tile(P, E);
+        if (!prebucketed) {
+            ctx->launches += moe::launch_tt_prefix(bb.b.meta, bb.b.seg_count, BN, bb.tt_prefix, s);
             ProfScope ps(ctx, "gather");
             ctx->launches += moe::launch_gather_f16(bb.x32, d, bb.b.pair_token, bb.b.meta, P, 0, bb.x16, s);
         }
@@ -509,7 +526,8 @@ int dense_q4(moe_ctx* ctx, const uint8_t* w, const float* sc, const float* xd, f
         t.max_items = ((c_out + 127) / 128) * ((batch + BN - 1) / BN);
         t.a_in_smem = ctx->tc_a_in_smem;
         t.stream = ctx->tc_stream >= 2;
-        const int ks = choose_ksplit(ctx, t.max_items, c_in);
+        const int ks = ctx->dense_ksplit > 0 ? (int)std::min<int64_t>(ctx->dense_ksplit, std::max<int64_t>(1, c_in / 256))
+                                             : choose_ksplit(ctx, t.max_items, c_in);
         float* part = nullptr;
         if (ks > 1) {
             part = (float*)ws_take(ctx, (size_t)ks * batch * c_out * 4);
@@ -659,6 +677,13 @@ int moe_set_option(moe_ctx* ctx, int option, int64_t value) {
         case MOE_OPT_EXPERT_END:
             if (value < 0) return fail(ctx, MOE_E_ARG, "bad expert index");
             ctx->expert_end = value;
+            return MOE_OK;
+        case MOE_OPT_FUSED_ROUTE:
+            ctx->fused_route = value != 0;
+            return MOE_OK;
+        case MOE_OPT_DENSE_KSPLIT:
+            if (value < 0 || value > 64) return fail(ctx, MOE_E_ARG, "MOE_OPT_DENSE_KSPLIT is 0..64");
+            ctx->dense_ksplit = (int)value;
             return MOE_OK;
         case MOE_OPT_ROUTER_TC_MIN_TOKENS:
             if (value < 1) return fail(ctx, MOE_E_ARG, "bad token threshold");
@@ -1324,14 +1349,56 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
     if (tw) TRY(dev_ptr(ctx, tw, P * 4, K_OUT, &dtw));
     ExpertBufs bb;
     TRY(take_expert_bufs(ctx, M, K, d, F, E, &bb));
-    TRY(route_dev(ctx, L, ld, M, (const float*)xd, flags, bb.x32, bb.xsum, bb.slot_expert,
-                  bb.slot_weight, nullptr, nullptr, nullptr, (int64_t*)dtc, (int64_t*)dti,
-                  (float*)dtw));
+    int C = 0;
+    const bool fused = ctx->fused_route && ld.rp && !(flags & MOE_F_SET_COVER) &&
+                       M < ctx->router_tc_min_tokens && al16(xd) &&
+                       moe::route_fused_supported((int)M, (int)E, (int)K, (int)d, &C);
+    if (fused) {
+        const bool tc_path = use_tc(ctx, M, d, F, ld.w);
+        moe::RouteFusedArgs ra;
+        ra.x = (const float*)xd;
+        ra.M = (int)M;
+        ra.d = (int)d;
+        ra.E = (int)E;
+        ra.K = (int)K;
+        ra.C = C;
+        ra.rp = ld.rp;
+        ra.rs = ld.rs;
+        ra.rscale = ld.router_scale;
+        ra.rsf = L->r_scale_factor;
+        ra.pre_w = ld.pre_w;
+        ra.bias = ld.bias;
+        ra.pes = ld.pes;
+        ra.top_p = L->moe_top_p;
+        expert_range(ctx, E, &ra.e_lo, &ra.e_hi);
+        ra.BN = tc_path ? expert_token_tile(P, E) : 0;
+        ra.x32 = bb.x32;
+        ra.xsum = bb.xsum;
+        ra.x16 = tc_path ? bb.x16 : nullptr;
+        ra.slot_expert = bb.slot_expert;
+        ra.slot_weight = bb.slot_weight;
+        ra.tok_count = (int64_t*)dtc;
+        ra.tok_idx = (int64_t*)dti;
+        ra.tok_w = (float*)dtw;
+        ra.b = bb.b;
+        ra.tt_prefix = tc_path ? bb.tt_prefix : nullptr;
+        int r;
+        {
+            ProfScope ps(ctx, "route_fused");
+            r = moe::launch_route_fused(ra, ctx->stream);
+        }
+        if (r < 0) return fail(ctx, MOE_E_CUDA, "fused routing launch failed");
+        ctx->launches += r;
+    } else {
+        TRY(route_dev(ctx, L, ld, M, (const float*)xd, flags, bb.x32, bb.xsum, bb.slot_expert,
+                      bb.slot_weight, nullptr, nullptr, nullptr, (int64_t*)dtc, (int64_t*)dti,
+                      (float*)dtw));
+    }
     moe::CombineArgs c;
     c.post_norm = (flags & MOE_F_POST_NORM) ? 1 : 0;
     c.post_w = ld.post_w;
     c.out_f16 = (flags & MOE_F_FP16_OUT) ? 1 : 0;
-    TRY(run_experts(ctx, ld.w, M, K, d, F, E, L->activation, bb, &c, od));
+    TRY(run_experts(ctx, ld.w, M, K, d, F, E, L->activation, bb, &c, od, fused));
     return finish(ctx);
 }
 

@@ -1,6 +1,7 @@
 // moe_internal.h -- launch interface between the C ABI (moe_abi.cu) and the
 // kernels (moe_kernels.cu).  Internal to libmoe_b200.so.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -107,6 +108,39 @@ int launch_slots_from_lists(int64_t M, int K, const int64_t* count, int64_t coun
 int launch_slots_from_topw(int64_t M, int K, const int64_t* idx, const float* w,
                            int* slot_expert, float* slot_weight, int E, int* err_flag,
                            cudaStream_t s);
+// Fused routing of a small batch (moe_route.cu): norms, Q4_0 router, softmax,
+// top-k, LOD weights, buckets, token-tile prefix and fp16 gather in one
+// thread-block cluster of C CTAs.
+struct RouteFusedArgs {
+    const float* x = nullptr;        // [M][d] fp32, 16-byte aligned
+    int M = 0, d = 0, E = 0, K = 0, C = 1;
+    const uint8_t* rp = nullptr;     // Q4_0 router [E][d]
+    const float* rs = nullptr;
+    const float* rscale = nullptr;   // router_scale [d]
+    float rsf = 0.f;                 // r_scale_factor
+    const float* pre_w = nullptr;    // [d]
+    const float* bias = nullptr;     // optional [E]
+    const float* pes = nullptr;      // per_expert_scale [E]
+    float top_p = 1.f;
+    int e_lo = 0, e_hi = 0;          // local expert range for the buckets
+    int BN = 0;                      // token tile for the prefix (0: no prefix)
+    float* x32 = nullptr;            // moe_in [M][d] (nullable)
+    float* xsum = nullptr;           // [M][d/32] 1.5 * block sums (nullable)
+    __half* x16 = nullptr;           // [pairs][d] fp16 in bucket order (nullable)
+    float* probs_out = nullptr;
+    int64_t* top_idx = nullptr;
+    float* top_val = nullptr;
+    int* slot_expert = nullptr;
+    float* slot_weight = nullptr;
+    int64_t* tok_count = nullptr;
+    int64_t* tok_idx = nullptr;
+    float* tok_w = nullptr;
+    BucketOut b;
+    int* tt_prefix = nullptr;
+};
+bool route_fused_supported(int M, int E, int K, int d, int* C_out);
+int launch_route_fused(const RouteFusedArgs& a, cudaStream_t s);
+
 int launch_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo, int e_hi, const BucketOut& o,
                   cudaStream_t s);
 int launch_gemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);

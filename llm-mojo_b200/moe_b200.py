@@ -26,6 +26,8 @@ OPT_GEMM_PATH, OPT_TC_MIN_TOKENS, OPT_DEVICE_TIMEOUT_NS = 1, 2, 3
 OPT_DENSE_TC_MIN_TOKENS, OPT_TC_A_IN_SMEM, OPT_ROUTER_TC_MIN_TOKENS = 4, 5, 6
 OPT_TC_STREAM = 7
 OPT_EXPERT_BEGIN, OPT_EXPERT_END = 8, 9
+OPT_FUSED_ROUTE = 10
+OPT_DENSE_KSPLIT = 11
 PATH_AUTO, PATH_GEMV, PATH_TC = 0, 1, 2
 
 STATUS = {0: "MOE_OK", 1: "MOE_E_ARG", 2: "MOE_E_SHAPE", 3: "MOE_E_UNREGISTERED",

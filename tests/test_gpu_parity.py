@@ -360,3 +360,36 @@ def test_kernel_launch_counter_advances(ctx):
     x = np.ones(32 * 4, np.float32)
     ctx.quantize_fp32_to_q4_0(x, np.zeros(64, np.uint8), np.zeros(4, np.float32), x.size)
     assert ctx.kernel_launches == n0 + 1
+
+
+@pytest.mark.parametrize("M", [1, 7, 16])
+def test_fused_routing_matches_separate_kernels(ctx, full_layer, M):
+    """The fused cluster launch (MOE_OPT_FUSED_ROUTE=1) and the separate
+    routing kernels must give the same routing and, within fp32
+    reassociation, the same output, also on an expert range."""
+    dev, host, L = full_layer
+    desc = MB.make_desc(dev)
+    x = synth.make_x(M, seed=300 + M).cpu().numpy()
+    res = []
+    for fused in (1, 0):
+        ctx.set_option(MB.OPT_FUSED_ROUTE, fused)
+        try:
+            for lo, hi in ((0, 0), (32, 96)):
+                ctx.set_expert_range(lo, hi)
+                out = np.zeros((M, 2816), np.float32)
+                cnt = np.zeros(M, np.int64)
+                idx = np.zeros((M, 8), np.int64)
+                w = np.zeros((M, 8), np.float32)
+                ctx.layer_forward(desc, M, x, out, MB.F_POST_NORM if hi == 0 else 0, cnt, idx, w)
+                res.append((out, cnt, idx, w))
+        finally:
+            ctx.set_expert_range(0, 0)
+            ctx.set_option(MB.OPT_FUSED_ROUTE, 0)
+    r = O.route(L, x)
+    ties = set(near_tie_tokens(np.stack([O.softmax(s) for s in r["scores"]]), 8).tolist())
+    for a, b in ((res[0], res[2]), (res[1], res[3])):
+        keep = [t for t in range(M) if t not in ties]
+        assert np.array_equal(a[1][keep], b[1][keep])
+        assert np.array_equal(a[2][keep], b[2][keep])
+        np.testing.assert_allclose(a[3][keep], b[3][keep], rtol=1e-5, atol=1e-7)
+        assert_close(a[0][keep], b[0][keep], max_abs=1e-4, rel_l2=1e-5, what=f"fused vs separate M={M}")
