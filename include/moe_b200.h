@@ -83,7 +83,8 @@ int moe_wait(moe_ctx* ctx, uint64_t timeout_ns);
 /* Context options (moe_set_option). */
 enum moe_option {
     MOE_OPT_GEMM_PATH = 1,        /* value: moe_gemm_path */
-    MOE_OPT_TC_MIN_TOKENS = 2,    /* auto path, expert GEMMs: tensor cores from this many tokens (default 1) */
+    MOE_OPT_TC_MIN_TOKENS = 2,    /* auto path, expert GEMMs: tensor cores from this many tokens in
+                                     the batch (default 2: a single token uses the CUDA-core GEMV) */
     MOE_OPT_DEVICE_TIMEOUT_NS = 3, /* deadline of every device-side wait (default 4 s) */
     MOE_OPT_DENSE_TC_MIN_TOKENS = 4, /* auto path, dense projections and router: tensor cores from this
                                         many tokens (default 2) */

@@ -54,7 +54,7 @@ struct moe_ctx {
     std::vector<CopyBack> pending;
     cudaEvent_t done = nullptr;
     int gemm_path = MOE_PATH_AUTO;       // moe_set_option(MOE_OPT_GEMM_PATH)
-    int tc_min_tokens = 1;               // auto: tensor cores from this many tokens
+    int tc_min_tokens = 2;               // auto: tensor cores from this many tokens (one token: CUDA-core GEMV)
     int dense_tc_min_tokens = 2;         // auto, dense projections
     int router_tc_min_tokens = 2048;     // router on tensor cores from this many tokens
     bool tc_a_in_smem = false;           // MOE_OPT_TC_A_IN_SMEM
@@ -457,7 +457,8 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     g1.max_unique = max_u;
     {
         ProfScope ps(ctx, "gemv_gate_up");
-        ctx->launches += moe::launch_gemv(moe::GEMV_ACT, g1, ctx->num_sms, s);
+        ctx->launches += moe::dgemv_supported(g1) ? moe::launch_dgemv(moe::GEMV_ACT, g1, ctx->num_sms, s)
+                                                   : moe::launch_gemv(moe::GEMV_ACT, g1, ctx->num_sms, s);
     }
 
     moe::GemvArgs g2 = g1;
@@ -472,7 +473,8 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     g2.out_stride = d;
     {
         ProfScope ps(ctx, "gemv_down");
-        ctx->launches += moe::launch_gemv(moe::GEMV_PLAIN, g2, ctx->num_sms, s);
+        ctx->launches += moe::dgemv_supported(g2) ? moe::launch_dgemv(moe::GEMV_PLAIN, g2, ctx->num_sms, s)
+                                                   : moe::launch_gemv(moe::GEMV_PLAIN, g2, ctx->num_sms, s);
     }
     }
 

@@ -141,6 +141,11 @@ struct RouteFusedArgs {
 bool route_fused_supported(int M, int E, int K, int d, int* C_out);
 int launch_route_fused(const RouteFusedArgs& a, cudaStream_t s);
 
+// CUDA-core grouped GEMV for few tokens per expert (moe_gemv.cu); expert
+// work lists only (dense_tokens == 0).
+bool dgemv_supported(const GemvArgs& a);
+int launch_dgemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);
+
 int launch_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo, int e_hi, const BucketOut& o,
                   cudaStream_t s);
 int launch_gemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);

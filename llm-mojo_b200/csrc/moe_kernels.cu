@@ -14,20 +14,6 @@
 
 namespace moe {
 
-// ------------------------------------------------------------------ loads
-__device__ __forceinline__ uint4 ldg_stream(const void* p) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
-    return r;
-}
-__device__ __forceinline__ float ldg_stream_f(const float* p) {
-    float r;
-    asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(r) : "l"(p));
-    return r;
-}
-
 // Dot products of one Q4_0 block (16 bytes = 32 weights) with the
 // matching 32 activations of T rows, one 32-bit word (8 weights) at a time.
 // XS = true: weights as 1 + n/16 (shift + LOP3 per weight, see nib_1p); the
