@@ -289,6 +289,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
+    ap.add_argument("--graph", action="store_true",
+                    help="with N > 1, capture steps (NCCL all-reduce included) in CUDA graphs; "
+                         "by default N > 1 launches eagerly")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"],
                     help="expert/dense GEMM path: CUDA-core GEMV, tcgen05, or automatic")
     ap.add_argument("--parallel", default="ep", choices=["ep", "replicas"],
@@ -300,6 +303,10 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = WORKLOADS[args.workload]
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and not args.graph:
+        # replaying graphs that hold the NCCL all-reduce was slower than eager
+        # launches at 8 ranks (825 vs < 300 us per step), so N > 1 runs eagerly
+        args.no_graph = True
     if args.layers is None:
         args.layers = wl["layers"]
     if args.steps is None:
