@@ -305,7 +305,8 @@ def main():
     wl = WORKLOADS[args.workload]
     if int(os.environ.get("WORLD_SIZE", "1")) > 1 and not args.graph:
         # replaying graphs that hold the NCCL all-reduce was slower than eager
-        # launches at 8 ranks (825 vs < 300 us per step), so N > 1 runs eagerly
+        # launches at 8 ranks (825 us per step replayed, 462 us per step for
+        # eager calls even with host copies), so N > 1 runs eagerly
         args.no_graph = True
     if args.layers is None:
         args.layers = wl["layers"]
