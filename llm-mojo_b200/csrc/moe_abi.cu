@@ -1227,7 +1227,8 @@ int layer_dev(moe_ctx* ctx, const moe_layer_desc* L, int flags, LayerDev* o) {
 
 // Bytes route_dev takes from the workspace.
 size_t route_bytes(int64_t M, int64_t d, int64_t E, int64_t K) {
-    return al(M * K * 4) * 2 + al(M * d * 4) * 2 + al(M * d / 32 * 4) + al(M * E * 4) + dense_bytes(M, d, E);
+    return al(M * K * 4) * 2 + al(M * d * 4) * 2 + al(M * d / 32 * 4) + al(M * E * 4) + dense_bytes(M, d, E) +
+           al(M * E * 4 * (d / 128 + 1));  // router partial sums (few tokens)
 }
 
 // Router: prep (norms, router input, block sums) -> router GEMV -> softmax /
@@ -1260,8 +1261,17 @@ int route_dev(moe_ctx* ctx, const moe_layer_desc* L, const LayerDev& ld, int64_t
         ProfScope ps(ctx, "prep");
         ctx->launches += moe::launch_prep(pa, M, s);
     }
+    float* part = nullptr;
+    int part_n = 0;
     if (ld.rp && M >= ctx->router_tc_min_tokens && ctx->gemm_path != MOE_PATH_GEMV) {
         TRY(dense_q4(ctx, ld.rp, ld.rs, scaled, scores, d, E, M, "router"));
+    } else if (ld.rp && moe::router_part_supported((int)M, (int)d)) {
+        // few tokens: fp32 partial sums over 128-wide K slices, added by k_topk
+        part_n = (int)(d / 128);
+        part = (float*)ws_take(ctx, (size_t)part_n * M * E * 4);
+        if (!part) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+        ProfScope ps(ctx, "router");
+        ctx->launches += moe::launch_router_part(ld.rp, ld.rs, scaled, (int)M, (int)d, (int)E, part, s);
     } else if (ld.rp) {  // fp32 router: routing follows the reference's arithmetic
         ProfScope ps(ctx, "router");
         ctx->launches += moe::launch_gemv_wide(ld.rp, ld.rs, scaled, scores, E, (int)d, (int)M, E, s);
@@ -1271,6 +1281,9 @@ int route_dev(moe_ctx* ctx, const moe_layer_desc* L, const LayerDev& ld, int64_t
     }
     moe::TopkArgs a;
     a.scores = scores;
+    a.part = part;
+    a.part_n = part_n;
+    a.M = (int)M;
     a.bias = ld.bias;
     a.E = (int)E;
     a.K = (int)K;

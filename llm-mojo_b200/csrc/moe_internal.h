@@ -51,6 +51,10 @@ struct PrepArgs {
 
 struct TopkArgs {
     const float* scores = nullptr;  // [M][E] router logits
+    const float* part = nullptr;    // or: [part_n][M][E] partial logits (k_router_part)
+    int part_n = 0;
+    int M = 0;
+    float* scores_out = nullptr;    // with part: the summed logits (nullable)
     const float* bias = nullptr;
     int E = 0, K = 0;
     const float* pes = nullptr;
@@ -140,6 +144,11 @@ struct RouteFusedArgs {
 };
 bool route_fused_supported(int M, int E, int K, int d, int* C_out);
 int launch_route_fused(const RouteFusedArgs& a, cudaStream_t s);
+
+// Router logits of <= 16 tokens as per-K-slice partial sums (moe_kernels.cu).
+bool router_part_supported(int M, int K);
+int launch_router_part(const uint8_t* W, const float* S, const float* X, int M, int K, int E, float* part,
+                       cudaStream_t s);
 
 // CUDA-core grouped GEMV for few tokens per expert (moe_gemv.cu); expert
 // work lists only (dense_tokens == 0).

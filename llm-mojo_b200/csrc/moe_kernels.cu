@@ -375,6 +375,81 @@ int launch_gemv_wide(const uint8_t* W, const float* S, const float* X, float* ou
     return 1;
 }
 
+// ------------------------------------------------------------ router (few tokens)
+// Router logits of M <= 16 tokens as partial sums over K slices: CTA c takes
+// the slice [c*RS, (c+1)*RS) of every token (staged in shared memory) and
+// thread (e, token group) dots router row e's slice with the group's tokens;
+// every thread loads its row's blocks before using them, and the 32 threads
+// of a warp read the same activations (broadcast).  part[c][t][e] is summed
+// over c, in c order, by k_topk.
+constexpr int RS = 128;  // K slice per CTA (4 Q4 blocks)
+__global__ void __launch_bounds__(512) k_router_part(const uint8_t* __restrict__ W, const float* __restrict__ S,
+                                                     const float* __restrict__ X, int M, int K, int E,
+                                                     float* __restrict__ part) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ __align__(16) float xs[16][RS];
+    const int c = blockIdx.x, k0 = c * RS, tid = threadIdx.x;
+    for (int i = tid; i < M * RS / 4; i += blockDim.x) {
+        const int t = (i * 4) / RS, k = (i * 4) % RS;
+        reinterpret_cast<float4*>(&xs[t][0])[k / 4] = __ldg(reinterpret_cast<const float4*>(X + (int64_t)t * K + k0 + k));
+    }
+    __syncthreads();
+    const int tg = tid >> 7, TG = blockDim.x >> 7;
+    for (int e0 = 0; e0 < E; e0 += 128) {
+        const int e = e0 + (tid & 127);
+        if (e >= E) continue;
+        uint4 q[RS / 32];
+        float sc[RS / 32];
+#pragma unroll
+        for (int b = 0; b < RS / 32; ++b) {
+            q[b] = ldg_stream(W + (int64_t)e * (K / 2) + k0 / 2 + b * 16);
+            sc[b] = ldg_stream_f(S + (int64_t)e * (K / 32) + k0 / 32 + b);
+        }
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int b = 0; b < RS / 32; ++b) {
+            const uint32_t w4[4] = {q[b].x, q[b].y, q[b].z, q[b].w};
+            float wv[32];
+#pragma unroll
+            for (int w = 0; w < 4; ++w)
+#pragma unroll
+                for (int n = 0; n < 8; ++n)  // element 8w+n: nibble n of word w
+                    wv[8 * w + n] = (float)((int)((w4[w] >> (4 * n)) & 15u) - 8);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int t = tg + TG * j;
+                if (t < M) {
+                    const float4* xp = reinterpret_cast<const float4*>(&xs[t][b * 32]);
+                    float d = 0.f;
+#pragma unroll
+                    for (int v = 0; v < 8; ++v) {
+                        const float4 x4 = xp[v];
+                        d = fmaf(wv[4 * v], x4.x, d);
+                        d = fmaf(wv[4 * v + 1], x4.y, d);
+                        d = fmaf(wv[4 * v + 2], x4.z, d);
+                        d = fmaf(wv[4 * v + 3], x4.w, d);
+                    }
+                    acc[j] = fmaf(sc[b], d, acc[j]);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int t = tg + TG * j;
+            if (t < M) part[((int64_t)c * M + t) * E + e] = acc[j];
+        }
+    }
+}
+
+bool router_part_supported(int M, int K) { return M >= 1 && M <= 16 && K % RS == 0; }
+
+int launch_router_part(const uint8_t* W, const float* S, const float* X, int M, int K, int E, float* part,
+                       cudaStream_t s) {
+    launch_k(k_router_part, dim3(K / RS), dim3(512), 0, s, W, S, X, M, K, E, part);
+    return 1;
+}
+
 // ------------------------------------------------------------ row prep
 // One CTA per row: layout conversion (moe_x_layout), fp16 -> fp32, optional
 // rms norms (model_speculative_moe_batched.mojo:857-879): out = x * inv *
@@ -457,7 +532,23 @@ __global__ void __launch_bounds__(128) k_topk(TopkArgs a) {
     const int64_t t = blockIdx.x;
     float m = -INFINITY;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const float v = a.scores[t * E + e] + (a.bias ? a.bias[e] : 0.f);
+        float sc;
+        if (a.part_n > 0) {  // router partial sums over K slices, in slice order
+            sc = 0.f;
+            for (int c0 = 0; c0 < a.part_n; c0 += 8) {  // 8 loads in flight, then the ordered sum
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    v[j] = c0 + j < a.part_n ? __ldg(a.part + ((int64_t)(c0 + j) * a.M + t) * E + e) : 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (c0 + j < a.part_n) sc += v[j];
+            }
+            if (a.scores_out) a.scores_out[t * E + e] = sc;
+        } else {
+            sc = a.scores[t * E + e];
+        }
+        const float v = sc + (a.bias ? a.bias[e] : 0.f);
         pr[e] = v;
         m = fmaxf(m, v);
     }
@@ -918,8 +1009,110 @@ __global__ void __launch_bounds__(512) k_combine(CombineArgs a) {
     }
 }
 
+// The same per-token combine with a token's row split over a cluster of
+// CW_CL CTAs (more CTAs in flight for small batches); the post-norm's sum of
+// squares is added across the cluster through distributed shared memory, in
+// cluster-rank order.
+constexpr int CW_CL = 4;
+__global__ void __launch_bounds__(256) k_combine_cl(CombineArgs a) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ float red[33];
+    __shared__ int sp[32];
+    __shared__ float sw[32];
+    __shared__ float parts[CW_CL];
+    const uint32_t r = cl_rank();
+    const int64_t t = blockIdx.x / CW_CL;
+    const int K = a.K;
+    if (threadIdx.x < K) {
+        sp[threadIdx.x] = a.slot_pair[t * K + threadIdx.x];
+        sw[threadIdx.x] = a.slot_weight[t * K + threadIdx.x];
+    }
+    cl_sync();  // every CTA of the cluster runs before shared memory is exchanged
+    const int64_t d4 = a.d / 4, per = d4 / CW_CL, j0 = (int64_t)r * per;
+    constexpr int MAXV = 3;  // 256 threads x 3 float4 x 4 CTAs: d <= 12288
+    float4 acc[MAXV];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int64_t jj = threadIdx.x + (int64_t)i * blockDim.x;
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (jj < per) {
+            const int64_t j = j0 + jj;
+#pragma unroll 8
+            for (int k = 0; k < K; ++k) {
+                const int p = sp[k];
+                if (p < 0) continue;
+                float4 y = __ldg(reinterpret_cast<const float4*>(a.y + (size_t)p * a.d) + j);
+                for (int ks = 1; ks < a.ksplit; ++ks) {  // split-K partials, fixed order
+                    const float4 z = __ldg(reinterpret_cast<const float4*>(a.y + ks * a.split_stride +
+                                                                           (size_t)p * a.d) + j);
+                    y.x += z.x; y.y += z.y; y.z += z.z; y.w += z.w;
+                }
+                const float w = sw[k];
+                if (a.fma_mode) {
+                    s.x = fmaf(y.x, w, s.x); s.y = fmaf(y.y, w, s.y);
+                    s.z = fmaf(y.z, w, s.z); s.w = fmaf(y.w, w, s.w);
+                } else {
+                    s.x = __fadd_rn(s.x, __fmul_rn(y.x, w)); s.y = __fadd_rn(s.y, __fmul_rn(y.y, w));
+                    s.z = __fadd_rn(s.z, __fmul_rn(y.z, w)); s.w = __fadd_rn(s.w, __fmul_rn(y.w, w));
+                }
+            }
+            ss += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+        }
+        acc[i] = s;
+    }
+    float inv = 1.f;
+    if (a.post_norm) {
+        ss = block_sum(ss, red);
+        if (threadIdx.x == 0) cl_st(cl_map(&parts[r], 0), ss);
+    }
+    cl_sync();
+    if (a.post_norm) {
+        float tot = 0.f;
+        for (int i = 0; i < CW_CL; ++i) tot += cl_ldf(cl_map(&parts[i], 0));
+        inv = 1.0f / sqrtf(tot / (float)a.d + 1e-6f);
+    }
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int64_t jj = threadIdx.x + (int64_t)i * blockDim.x;
+        if (jj >= per) continue;
+        const int64_t j = j0 + jj;
+        float4 v = acc[i];
+        if (a.post_norm) {
+            const float4 w = __ldg(reinterpret_cast<const float4*>(a.post_w) + j);
+            v.x = v.x * inv * w.x; v.y = v.y * inv * w.y; v.z = v.z * inv * w.z; v.w = v.w * inv * w.w;
+        }
+        if (a.out_f16) {
+            __half2* o = reinterpret_cast<__half2*>(a.out) + (t * a.d) / 2 + 2 * j;
+            o[0] = __floats2half2_rn(v.x, v.y);
+            o[1] = __floats2half2_rn(v.z, v.w);
+        } else {
+            reinterpret_cast<float4*>(a.out)[(t * a.d) / 4 + j] = v;
+        }
+    }
+    cl_sync();  // CTA 0's shared memory stays alive until every CTA has read it
+}
+
 int launch_combine(const CombineArgs& a, int64_t M, cudaStream_t s) {
     if (M <= 0) return 0;
+    if (M <= 64 && (a.d / 4) % CW_CL == 0 && a.d <= 12288) {  // small batches: more CTAs per token
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(M * CW_CL));
+        cfg.blockDim = dim3(256);
+        cfg.stream = s;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = CW_CL;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        cudaLaunchKernelEx(&cfg, k_combine_cl, a);
+        return 1;
+    }
     launch_k(k_combine, dim3((unsigned)M), dim3(512), 0, s, a);
     return 1;
 }

@@ -30,35 +30,6 @@ namespace moe {
 
 namespace {
 
-__device__ __forceinline__ uint32_t cl_map(const void* p, uint32_t cta) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
-                 : "=r"(r)
-                 : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"(cta));
-    return r;
-}
-__device__ __forceinline__ void cl_st(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-__device__ __forceinline__ float cl_ldf(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
-}
-__device__ __forceinline__ int cl_ldi(uint32_t addr) {
-    int v;
-    asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
-    return v;
-}
-__device__ __forceinline__ void cl_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t cl_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
 constexpr int RF_THREADS = 512;
 constexpr int RF_MAXB = 12;  // Q4 blocks per K slice (S <= 384)
 constexpr int RF_MAXM = 16;  // tokens
