@@ -1,27 +1,36 @@
 // moe_tc_stream.cu -- streaming variant of the tcgen05 grouped Q4_0 GEMM
-// for token tiles of 16..64 tokens and K % 128 == 0 (MOE_OPT_TC_STREAM:
-// by default the expert GEMMs whose K allows it, i.e. gate/up).
+// for token tiles of 16..64 tokens and K % 64 == 0 (MOE_OPT_TC_STREAM: by
+// default the expert GEMMs).
 //
 // Same contraction, work list, K order and epilogues as k_tc_gemm
-// (moe_tc.cu), organised as one CTA per SM with all 512 TMEM columns
-// (measured 12-18 % faster than k_tc_gemm on the gate/up GEMM at 16-256
-// tokens):
+// (moe_tc.cu), organised as one CTA per SM with all 512 TMEM columns:
 //  - a stage covers 256 K: the 128 weight rows' 128 packed bytes (two TMA
 //    boxes of 128 B x 64 rows, SWIZZLE_128B), their eight block scales (two
 //    TMA boxes of 8 fp32 x 64 rows) and the token tile's activations (one 3-D
-//    TMA box that lands in the UMMA no-swizzle K-major layout);
-//  - the producer prefetches the CTA's next work item into L2 as whole
-//    contiguous row blocks (cp.async.bulk.prefetch.L2);
+//    TMA box of four K-major SWIZZLE_128B tiles, BN rows x 64 K each);
+//  - when K % 128 == 64 a scale row (K/8 bytes) is no multiple of 16 bytes
+//    and no tensor map can describe it: the producer then copies each work
+//    item's scale rows, which are contiguous, with one or two bulk copies;
 //  - two groups of four dequant warps take alternate stages; the thread that
-//    owns A-tile row t turns the row's 256 weights into fp16 in TMEM with
-//    tcgen05.st.32x32b.x32 (128-K A slots).  (w & 0x000F000F) | 0x64006400
-//    is 1024 + n and (w & 0x00F000F0) | 0x54005400 is 64 + n, so (n - 8) is
-//    one exact fp16 subtraction, then one multiply by the fp16 scale;
-//  - epilogue warps wait with back-off.
+//    owns A-tile row t reads the row's 128 bytes of the stage into registers,
+//    hands the slot back to the producer, and turns the 256 weights into
+//    fp16 in TMEM with tcgen05.st.32x32b.x32 (128-K A slots).
+//    (w & 0x000F000F) | 0x64006400 is 1024 + n and (w & 0x00F000F0) |
+//    0x54005400 is 64 + n, so (n - 8) is one exact fp16 subtraction, then
+//    one multiply by the fp16 scale;
+//  - the activation tile has its own barriers: it stays until the stage's
+//    MMAs have read it, while the weight bytes go back as soon as they are in
+//    registers;
 //  - with the A operand in TMEM a tcgen05.mma of M=128, N=16, K=16 holds
 //    its issuing thread for about 100 cycles, so two threads (warps 1 and
 //    14) issue the MMAs of alternate stages into separate accumulators,
-//    which the epilogue adds.
+//    which the epilogue adds;
+//  - every ring (stages, TMEM A slots) has one producer order and one
+//    consumer order: stage st belongs to dequant group and issuer st % 2,
+//    the stage ring has an even number of slots and each group has its own
+//    A slots.  An mbarrier parity wait cannot tell phase p from p - 2, so a
+//    consumer that could reach a slot before its previous user had filled it
+//    would pass the wait early.
 //
 // Every mbarrier wait is bounded (globaltimer deadline); on expiry the kernel
 // raises err_flag = 2, every role drains what it issued and the CTA frees
@@ -48,29 +57,29 @@ template <int BN>
 struct StLayout {
     static constexpr int ACC = ((2 * ST_NMMA * BN + 31) / 32) * 32;  // two buffers x two issuers
     static constexpr int SA = (512 - ACC) / 64 > 7 ? 7 : (512 - ACC) / 64;  // 128-K fp16 A slots in TMEM
+    // The slots form one ring per dequant group / MMA issuer pair (stage
+    // parity), SAG slots each: a ring shared by both groups lets an issuer
+    // wait on a slot whose previous writer (the other group) has not arrived
+    // yet, where the mbarrier parity test matches the phase before and passes.
+    static constexpr int SAG = SA / 2;
     static constexpr int B_BYTES = BN * ST_K * 2;
     static constexpr int SLOT = ST_Q + B_BYTES + ST_S;
-    static constexpr int SQ = (227 * 1024 - 2048) / SLOT > 8 ? 8 : (227 * 1024 - 2048) / SLOT;
+    // even, so that stage slot qs is always used by the same dequant group and
+    // MMA issuer (stage parity): each ring then has one producer and one
+    // consumer order, which the mbarrier parity waits rely on
+    static constexpr int SQ = ((227 * 1024 - 2048) / SLOT > 8 ? 8 : (227 * 1024 - 2048) / SLOT) & ~1;
+    static_assert(SQ >= 2 && SQ % ST_NMMA == 0, "stage ring must split evenly between the two issuers");
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_B = OFF_Q + SQ * ST_Q;
     static constexpr int OFF_S = OFF_B + SQ * B_BYTES;
     static constexpr int OFF_BAR = OFF_S + SQ * ST_S;
-    static constexpr int N_BAR = 2 * SQ + 2 * SA + 4 + ST_NMMA;
+    static constexpr int N_BAR = 2 * SQ + 2 * SA + 4 + ST_NMMA + 4 + 2 * SQ;
+    // item-scale mode (K % 128 == 64): the scale area holds two item buffers
+    static constexpr int ISCALE_BYTES = SQ * ST_S / 2;
     static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
     static constexpr int TOTAL = OFF_MISC + 16 + 1024;  // + alignment slack
 };
 
-// L2 prefetch of [p, p + bytes), trimmed inwards to 16-byte boundaries, in
-// pieces of at most 64 KB.
-__device__ __forceinline__ void l2_prefetch_range(const uint8_t* p, int64_t bytes) {
-    uintptr_t b = (reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15);
-    const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + (uintptr_t)bytes) & ~uintptr_t(15);
-    while (b < e) {
-        const uint32_t n = (uint32_t)((e - b) < 65536u ? (e - b) : 65536u);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(b), "r"(n) : "memory");
-        b += n;
-    }
-}
 // Whole-warp wait: every lane waits, and the warp leaves together (a lane
 // that saw the deadline makes all of them give up), so .sync.aligned
 // instructions after it always run with the full warp.
@@ -112,10 +121,12 @@ __device__ __forceinline__ uint32_t deq_pair(uint32_t w, __half2 sc) {
 template <int MODE, int BN>
 __global__ void __launch_bounds__(ST_THREADS, 1)
     k_tc_stream(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap bmap,
-                const __grid_constant__ CUtensorMap smap, TcArgs a, const uint8_t* wp, int64_t total_rows) {
+                const __grid_constant__ CUtensorMap smap, TcArgs a, int64_t total_rows,
+                int iscale) {
     using L = StLayout<BN>;
     constexpr int SQ = L::SQ;
     constexpr int SA = L::SA;
+    constexpr int SAG = L::SAG;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t bar0 = smem_u32(smem + L::OFF_BAR);
@@ -126,6 +137,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     auto acc_full = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + s); };
     auto acc_empty = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + 2 + s); };
     auto drain_bar = [&](int j) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + j); };
+    // item scales: all of an item's scale rows in one bulk copy (K % 128 == 64,
+    // where the 2-D scale tensor map cannot exist); buffers b = 0, 1
+    auto is_full = [&](int b) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + ST_NMMA + b); };
+    auto is_empty = [&](int b) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + ST_NMMA + 2 + b); };
+    // activation tiles: same slot index as the stage, own barriers, so a
+    // stage's weight bytes are released by the dequant group alone and the
+    // tile stays until the stage's MMAs have read it
+    auto b_full = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + 8 + ST_NMMA + s); };
+    auto b_empty = [&](int s) { return bar0 + 8u * (3 * SQ + 2 * SA + 8 + ST_NMMA + s); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -150,8 +170,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SQ; ++s) {
-            mbar_init(q_full(s), 1);       // TMA: Q4 tile, its scales, activations
-            mbar_init(q_empty(s), 4 + 1);  // the dequant group's four warps + the MMAs reading the activations
+            mbar_init(q_full(s), 1);   // TMA: Q4 tile and its scales
+            mbar_init(q_empty(s), 4);  // the dequant group's four warps
+            mbar_init(b_full(s), 1);   // TMA: activation tile
+            mbar_init(b_empty(s), 1);  // the MMAs that read it
         }
         for (int s = 0; s < SA; ++s) {
             mbar_init(a_full(s), 4);
@@ -162,11 +184,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             mbar_init(acc_empty(s), 4);
         }
         for (int j = 0; j < ST_NMMA; ++j) mbar_init(drain_bar(j), 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(is_full(b), 1);
+            mbar_init(is_empty(b), 8);  // the eight dequant warps
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         prefetch_tmap(&qmap);
         prefetch_tmap(&bmap);
-        prefetch_tmap(&smap);
+        if (!iscale) prefetch_tmap(&smap);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -184,61 +210,73 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer (one thread)
-        // An item's weight rows are one (PLAIN) or two (ACT: gate and up)
-        // contiguous blocks of rows x K/2 bytes, plus their scale rows;
-        // prefetching the next item into L2 in one piece keeps DRAM accesses
-        // long and sequential while the ring's TMA boxes (128 bytes of each
-        // of 128 rows per stage) read from L2.
-        auto prefetch_item = [&](int64_t item) {
-            Item pi;
-            if (!decode_item(a, item, row_tiles, BN, pi) || pi.ks != 0) return;
-            int ra, rb;
-            box_rows(pi, ra, rb);
-            const int64_t nrow = (MODE == TC_ACT) ? 64 : 128;
-            const int nblk = (MODE == TC_ACT) ? 2 : 1;
-            for (int b = 0; b < nblk; ++b) {
-                const int64_t r0 = (b == 0) ? ra : rb;
-                const int64_t r1 = (r0 + nrow < total_rows) ? r0 + nrow : total_rows;
-                if (r1 <= r0) continue;
-                l2_prefetch_range(wp + r0 * (K / 2), (r1 - r0) * (K / 2));
-                l2_prefetch_range(reinterpret_cast<const uint8_t*>(a.Ws + r0 * nb), (r1 - r0) * nb * 4);
-            }
-        };
+        // (a whole-item L2 prefetch ahead of the ring, tried here, cost 10-12 %:
+        // the TMA ring alone keeps enough bytes in flight)
         if (lane == 0) {
-            prefetch_item(blockIdx.x);
             uint32_t st = 0;
             uint32_t q_armed = 0;  // stages armed in their current phase
-            uint32_t q_par = 0;    // their parity, one bit per stage
+            uint32_t q_par = 0;    // their parity, one bit per stage (activation tiles: the same)
+            uint32_t b_armed = 0;
+            uint32_t is_armed = 0, is_par = 0;
+            uint32_t ii = 0;       // items of this CTA so far
             Item it;
             bool ok = true;
-            for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
+            for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x, ++ii) {
                 int row_a, row_b;
                 box_rows(it, row_a, row_b);
-                prefetch_item(item + gridDim.x);
                 const int tok_row = it.s0 + it.tt * BN;
+                if (iscale) {
+                    const int b = (int)(ii & 1u);
+                    const uint32_t ph = (ii >> 1) & 1u;
+                    if (!(ok = mbar_wait(is_empty(b), ph ^ 1u, G))) break;
+                    const uint32_t dst = smem_u32(smem + L::OFF_S + b * L::ISCALE_BYTES);
+                    const uint32_t blk = (MODE == TC_ACT ? 64u : 128u) * (uint32_t)nb * 4u;
+                    mbar_expect_tx(is_full(b), (MODE == TC_ACT ? 2u : 1u) * blk);
+                    asm volatile(
+                        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                        "l"(a.Ws + (int64_t)row_a * nb), "r"(blk), "r"(is_full(b))
+                        : "memory");
+                    if (MODE == TC_ACT)
+                        asm volatile(
+                            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                                dst + blk),
+                            "l"(a.Ws + (int64_t)row_b * nb), "r"(blk), "r"(is_full(b))
+                            : "memory");
+                    is_armed |= 1u << b;
+                    is_par = (is_par & ~(1u << b)) | (ph << b);
+                }
                 for (int s = s_begin(it); s < s_end(it); ++s, ++st) {
                     const int qs = (int)(st % SQ);
                     const uint32_t qp = (st / SQ) & 1u;
                     if (!(ok = mbar_wait(q_empty(qs), qp ^ 1u, G))) break;
                     const uint32_t qd = smem_u32(smem + L::OFF_Q + qs * ST_Q);
                     const uint32_t sd = smem_u32(smem + L::OFF_S + qs * ST_S);
-                    mbar_expect_tx(q_full(qs), ST_Q + ST_S + L::B_BYTES);
+                    mbar_expect_tx(q_full(qs), ST_Q + (iscale ? 0 : ST_S));
                     tma_load_2d(qd, &qmap, q_full(qs), s * (ST_K / 2), row_a);
                     tma_load_2d(qd + ST_Q / 2, &qmap, q_full(qs), s * (ST_K / 2), row_b);
-                    tma_load_2d(sd, &smap, q_full(qs), s * (ST_K / 32), row_a);
-                    tma_load_2d(sd + ST_S / 2, &smap, q_full(qs), s * (ST_K / 32), row_b);
-                    tma_load_3d(smem_u32(smem + L::OFF_B + qs * L::B_BYTES), &bmap, q_full(qs), 0, tok_row,
-                                s * (ST_K / 8));
+                    if (!iscale) {
+                        tma_load_2d(sd, &smap, q_full(qs), s * (ST_K / 32), row_a);
+                        tma_load_2d(sd + ST_S / 2, &smap, q_full(qs), s * (ST_K / 32), row_b);
+                    }
                     q_armed |= 1u << qs;
                     q_par = (q_par & ~(1u << qs)) | (qp << qs);
+                    if (!(ok = mbar_wait(b_empty(qs), qp ^ 1u, G))) break;
+                    mbar_expect_tx(b_full(qs), L::B_BYTES);
+                    tma_load_3d(smem_u32(smem + L::OFF_B + qs * L::B_BYTES), &bmap, b_full(qs), 0, tok_row,
+                                s * (ST_K / 64));
+                    b_armed |= 1u << qs;
                 }
             }
             // every armed stage's bytes must have landed before exit
             Guard Gd{abort_flag, a.err_flag, globaltimer() + drain_ns};
             volatile int no_abort = 0;
             Gd.abort = &no_abort;
-            for (int s = 0; s < SQ; ++s)
+            for (int s = 0; s < SQ; ++s) {
                 if (q_armed & (1u << s)) mbar_wait(q_full(s), (q_par >> s) & 1u, Gd);
+                if (b_armed & (1u << s)) mbar_wait(b_full(s), (q_par >> s) & 1u, Gd);
+            }
+            for (int b = 0; b < 2; ++b)
+                if (is_armed & (1u << b)) mbar_wait(is_full(b), (is_par >> b) & 1u, Gd);
         }
         __syncwarp();
     } else if (warp == 1 || warp == ST_MMA2) {
@@ -263,26 +301,26 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 for (int s = sb; s < se && ok; ++s, ++st) {
                     if ((int)(st % ST_NMMA) != me) continue;
                     const int qs = (int)(st % SQ);
-                    if (!(ok = mbar_wait(q_full(qs), (st / SQ) & 1u, G))) break;  // activations landed
+                    if (!(ok = mbar_wait(b_full(qs), (st / SQ) & 1u, G))) break;  // activations landed
                     const uint32_t bd = smem_u32(smem + L::OFF_B + qs * L::B_BYTES);
                     for (int h = 0; h < 2; ++h) {
-                        const uint32_t ag = 2u * st + (uint32_t)h;
-                        const int as = (int)(ag % SA);
-                        if (!(ok = mbar_wait(a_full(as), (ag / SA) & 1u, G))) break;
+                        const uint32_t la = 2u * (st >> 1) + (uint32_t)h;  // place in this issuer's ring
+                        const int as = me * SAG + (int)(la % SAG);
+                        if (!(ok = mbar_wait(a_full(as), (la / SAG) & 1u, G))) break;
                         tc_fence_after();
                         const int kv = K - s * ST_K - 128 * h;
                         const int nk = kv >= 128 ? 8 : (kv > 0 ? kv / 16 : 0);
                         const uint32_t ta = tmem_base + ACOL + (uint32_t)(as * 64);
                         for (int k = 0; k < nk; ++k)
                             tc_mma_ts(d_tmem, ta + 8u * k,
-                                      kmajor_plain_desc(bd + (uint32_t)((16 * h + 2 * k) * BN * 16), BN * 16, 128),
+                                      sw128_desc(bd + (uint32_t)((2 * h + k / 4) * BN * 128 + 32 * (k % 4))),
                                       IDESC, (!first) || h || k);
                         issued = true;
                         tc_commit(a_empty(as));
                     }
                     first = false;
                     if (!ok) break;
-                    tc_commit(q_empty(qs));
+                    tc_commit(b_empty(qs));
                 }
                 if (!ok) break;
                 tc_commit(acc_full(ab));
@@ -308,24 +346,49 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         const int sr = (MODE == TC_ACT) ? ((lane < 16) ? 16 * q + lane : 64 + 16 * q + (lane - 16)) : t;
         const int swz = sr & 7;                // SWIZZLE_128B: 16-byte chunk ^= row % 8
         const uint32_t tl = tmem_base + ((uint32_t)(q * 32) << 16) + ACOL;
-        uint32_t st = 0;
+        uint32_t st = 0, ii = 0;
         Item it;
         bool ok = true;
-        for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
+        for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x, ++ii) {
             const int ns = s_end(it) - s_begin(it);
+            const float* iscl = nullptr;  // item-scale mode: this row's scales
+            if (iscale) {
+                const int b = (int)(ii & 1u);
+                if (!(ok = mbar_wait_warp(is_full(b), (ii >> 1) & 1u, G))) break;
+                iscl = reinterpret_cast<const float*>(smem + L::OFF_S + b * L::ISCALE_BYTES) + sr * nb;
+            }
             for (int i = (int)((uint32_t)(grp - (int)st) & 1u); i < ns && ok; i += 2) {
                 const uint32_t gs = st + (uint32_t)i;
                 const int qs = (int)(gs % SQ);
                 if (!(ok = mbar_wait_warp(q_full(qs), (gs / SQ) & 1u, G))) break;
                 const uint8_t* qrow = smem + L::OFF_Q + qs * ST_Q + sr * 128;
-                const float4* sp = reinterpret_cast<const float4*>(smem + L::OFF_S + qs * ST_S + sr * 32);
-                const float4 s0 = sp[0], s1 = sp[1];
-                const float scl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                float scl[8];
+                if (iscale) {  // 8-byte aligned: nb is even
+                    const float2* sp2 = reinterpret_cast<const float2*>(iscl + 8 * (s_begin(it) + i));
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        const float2 f = sp2[v];
+                        scl[2 * v] = f.x;
+                        scl[2 * v + 1] = f.y;
+                    }
+                } else {
+                    const float4* sp = reinterpret_cast<const float4*>(smem + L::OFF_S + qs * ST_S + sr * 32);
+                    const float4 s0 = sp[0], s1 = sp[1];
+                    scl[0] = s0.x; scl[1] = s0.y; scl[2] = s0.z; scl[3] = s0.w;
+                    scl[4] = s1.x; scl[5] = s1.y; scl[6] = s1.z; scl[7] = s1.w;
+                }
+                // the row's 128 bytes of this stage into registers: the slot
+                // goes back to the producer before any wait on the MMAs
+                uint4 wq[8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) wq[c] = *reinterpret_cast<const uint4*>(qrow + ((c ^ swz) << 4));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(q_empty(qs));
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const uint32_t ag = 2u * gs + (uint32_t)h;
-                    const int as = (int)(ag % SA);
-                    if (!(ok = mbar_wait_warp(a_empty(as), ((ag / SA) & 1u) ^ 1u, G))) break;
+                    const uint32_t la = 2u * (gs >> 1) + (uint32_t)h;  // place in this group's ring
+                    const int as = grp * SAG + (int)(la % SAG);
+                    if (!(ok = mbar_wait_warp(a_empty(as), ((la / SAG) & 1u) ^ 1u, G))) break;
                     tc_fence_after();
 #pragma unroll
                     for (int p2 = 0; p2 < 2; ++p2) {
@@ -333,7 +396,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 #pragma unroll
                         for (int cc = 0; cc < 2; ++cc) {
                             const int c = 4 * h + 2 * p2 + cc;  // chunk = Q4 block 8s + c
-                            const uint4 wv = *reinterpret_cast<const uint4*>(qrow + ((c ^ swz) << 4));
+                            const uint4 wv = wq[c];
                             const __half2 sc = __float2half2_rn(scl[c]);
                             const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
@@ -362,8 +425,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                     if (lane == 0) mbar_arrive(a_full(as));
                 }
                 if (!ok) break;
+            }
+            if (!ok) break;
+            if (iscale) {
                 __syncwarp();
-                if (lane == 0) mbar_arrive(q_empty(qs));
+                if (lane == 0) mbar_arrive(is_empty((int)(ii & 1u)));
             }
             st += (uint32_t)ns;
         }
@@ -448,25 +514,39 @@ int launch_st(const TcLaunch& L, int num_sms, cudaStream_t s) {
     if (!tc_make_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.Wp, (uint64_t)L.a.K / 2, (uint64_t)L.total_rows,
                      (uint64_t)L.a.K / 2, tc::ST_K / 2, 64, CU_TENSOR_MAP_SWIZZLE_128B))
         return -1;
-    // activations as [K/8 chunks][rows][8 fp16]: one box per stage lands in the
-    // UMMA no-swizzle K-major layout (8x8 core matrices of 128 contiguous bytes)
-    const uint64_t bdims[3] = {8, (uint64_t)L.b_rows, (uint64_t)L.a.K / 8};
-    const uint64_t bstr[2] = {(uint64_t)L.a.K * 2, 16};
-    const uint32_t bbox[3] = {8, (uint32_t)BN, tc::ST_K / 8};
-    if (!tc_make_map_nd(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.B, 3, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_NONE))
+    // activations as [K/64 chunks][rows][64 fp16]: one box per stage lands as
+    // four UMMA K-major SWIZZLE_128B tiles of BN rows x 64 K (128-byte rows,
+    // so the TMA moves whole 128-byte lines)
+    const uint64_t bdims[3] = {64, (uint64_t)L.b_rows, (uint64_t)L.a.K / 64};
+    const uint64_t bstr[2] = {(uint64_t)L.a.K * 2, 128};
+    const uint32_t bbox[3] = {64, (uint32_t)BN, tc::ST_K / 64};
+    if (!tc_make_map_nd(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.B, 3, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B))
         return -1;
-    // scales [rows][K/32] fp32: 8 blocks (one stage) of 64 rows per box
-    CUtensorMap smap;
-    if (!tc_make_map(&smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, L.a.Ws, (uint64_t)L.a.K / 32, (uint64_t)L.total_rows,
-                     (uint64_t)L.a.K / 32 * 4, tc::ST_K / 32, 64, CU_TENSOR_MAP_SWIZZLE_NONE))
+    // scales [rows][K/32] fp32: 8 blocks (one stage) of 64 rows per box; when
+    // the row stride is not a multiple of 16 bytes (K % 128 == 64) the kernel
+    // copies each item's scale rows in one piece instead
+    const int iscale = (L.a.K % 128) != 0;
+    CUtensorMap smap = qmap;
+    if (!iscale && !tc_make_map(&smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, L.a.Ws, (uint64_t)L.a.K / 32,
+                                (uint64_t)L.total_rows, (uint64_t)L.a.K / 32 * 4, tc::ST_K / 32, 64,
+                                CU_TENSOR_MAP_SWIZZLE_NONE))
         return -1;
+    if (iscale) {
+        const int64_t nb = L.a.K / 32;
+        if (128 * nb * 4 > tc::StLayout<BN>::ISCALE_BYTES) return -1;
+        // every item's scale block starts on a 16-byte boundary and is whole
+        // (each copy covers 64 or 128 whole rows of one expert)
+        if (MODE == TC_PLAIN && L.a.R % 128 != 0) return -1;
+        if (MODE == TC_ACT && L.a.F % 64 != 0) return -1;
+        if ((L.a.R * nb) % 4 != 0) return -1;
+    }
     const int smem = tc::StLayout<BN>::TOTAL;
     auto kern = tc::k_tc_stream<MODE, BN>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -1;
     int grid = num_sms;  // one CTA per SM: it owns all 512 TMEM columns
     if (L.max_items > 0 && L.max_items < grid) grid = (int)L.max_items;
     if (grid <= 0) return 0;
-    launch_k(kern, dim3(grid), dim3(tc::ST_THREADS), smem, s, qmap, bmap, smap, L.a, L.Wp, L.total_rows);
+    launch_k(kern, dim3(grid), dim3(tc::ST_THREADS), smem, s, qmap, bmap, smap, L.a, L.total_rows, iscale);
     return 1;
 }
 
@@ -484,8 +564,7 @@ int launch_st_mode(const TcLaunch& L, int num_sms, cudaStream_t s) {
 
 int launch_tc_stream(int mode, const TcLaunch& L, int num_sms, cudaStream_t s) {
     const int nst = (L.a.K + tc::ST_K - 1) / tc::ST_K;
-    // the scale rows are read by TMA: their stride (K/8 bytes) must be a multiple of 16
-    if (L.a.K < 128 || L.a.K % 128 != 0 || L.a.ksplit > nst) return -1;
+    if (L.a.K < 128 || L.a.K % 64 != 0 || L.a.ksplit > nst) return -1;
     if ((reinterpret_cast<uintptr_t>(L.a.Ws) & 15u) != 0) return -1;
     return mode == TC_ACT ? launch_st_mode<TC_ACT>(L, num_sms, s) : launch_st_mode<TC_PLAIN>(L, num_sms, s);
 }

@@ -71,6 +71,39 @@ def test_tc_layer_forward_vs_oracle(tc, full_layer, M):
     assert_close(out[keep], moe_ref[keep], what=f"tc layer M={M}")
 
 
+@pytest.fixture(scope="module", params=[(320, 192), (384, 192)], ids=["act_k64", "plain_k64"])
+def odd_k_layer(ctx, request):
+    """Layers whose GEMMs have K % 128 == 64: d=320 gives the gate/up GEMM
+    K=320 (scale rows 40 bytes long), F=192 gives the down GEMM K=192 over
+    d=384 output rows.  The streaming kernel copies each work item's scale rows
+    in one piece for them."""
+    d, F_ = request.param
+    dev = synth.make_layer(ctx, d=d, F_=F_, E_=16, top_k=4, seed=5)
+    host = synth.to_host(dev)
+    return dev, host, O.make_layer(host)
+
+
+@pytest.mark.parametrize("M", [16, 64])
+def test_tc_layer_forward_odd_k(tc, odd_k_layer, M):
+    dev, host, L = odd_k_layer
+    d = dev["d"]
+    desc = MB.make_desc(dev)
+    x = synth.make_x(M, d=d, seed=900 + M).cpu().numpy()
+    out = np.zeros((M, d), np.float32)
+    cnt = np.zeros(M, np.int64)
+    idx = np.zeros((M, 4), np.int64)
+    w = np.zeros((M, 4), np.float32)
+    tc.layer_forward(desc, M, x, out, flags=0, tok_active_count=cnt, tok_active_idx=idx,
+                     tok_active_weights=w)
+    ref = O.route(L, x)
+    ties = set(near_tie_tokens(_softmax_rows(ref["scores"]), 4).tolist())
+    keep = [t for t in range(M) if t not in ties and cnt[t] == ref["count"][t]
+            and np.array_equal(idx[t, :cnt[t]], ref["idx"][t, :cnt[t]])]
+    assert len(keep) >= M - len(ties)
+    moe_ref = O.experts_forward(L, ref["moe_in"], ref["count"], ref["idx"], ref["w"], prec=O.F64)
+    assert_close(out[keep], moe_ref[keep], what=f"tc layer d={d} F={dev['F']} M={M}")
+
+
 def test_tc_diffusion_block_vs_oracle(tc, full_layer):
     dev, host, L = full_layer
     B = 256
