@@ -302,19 +302,30 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                     if ((int)(st % ST_NMMA) != me) continue;
                     const int qs = (int)(st % SQ);
                     if (!(ok = mbar_wait(b_full(qs), (st / SQ) & 1u, G))) break;  // activations landed
-                    const uint32_t bd = smem_u32(smem + L::OFF_B + qs * L::B_BYTES);
+                    // One thread issues every MMA, so the loop is unrolled with the
+                    // descriptors as constant offsets of one base: computed per MMA,
+                    // they held the issuer ~190 cycles per tcgen05.mma instead of ~55.
+                    const uint64_t bdesc = sw128_desc(smem_u32(smem + L::OFF_B + qs * L::B_BYTES));
+#pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const uint32_t la = 2u * (st >> 1) + (uint32_t)h;  // place in this issuer's ring
                         const int as = me * SAG + (int)(la % SAG);
                         if (!(ok = mbar_wait(a_full(as), (la / SAG) & 1u, G))) break;
                         tc_fence_after();
                         const int kv = K - s * ST_K - 128 * h;
-                        const int nk = kv >= 128 ? 8 : (kv > 0 ? kv / 16 : 0);
                         const uint32_t ta = tmem_base + ACOL + (uint32_t)(as * 64);
-                        for (int k = 0; k < nk; ++k)
-                            tc_mma_ts(d_tmem, ta + 8u * k,
-                                      sw128_desc(bd + (uint32_t)((2 * h + k / 4) * BN * 128 + 32 * (k % 4))),
-                                      IDESC, (!first) || h || k);
+                        const uint32_t acc = (!first || h) ? 1u : 0u;
+                        // B sub-tile of k: 64-K chunk 2h + k/4, 32 bytes per 16 K inside its rows
+                        auto boff = [&](int k) { return (uint64_t)(((2 * h + k / 4) * BN * 128 + 32 * (k % 4)) >> 4); };
+                        if (kv >= 128) {
+#pragma unroll
+                            for (int k = 0; k < 8; ++k)
+                                tc_mma_ts(d_tmem, ta + 8u * k, bdesc + boff(k), IDESC, acc | (k > 0 ? 1u : 0u));
+                        } else {  // the K tail (kv is a multiple of 64)
+                            const int nk = kv > 0 ? kv / 16 : 0;
+                            for (int k = 0; k < nk; ++k)
+                                tc_mma_ts(d_tmem, ta + 8u * k, bdesc + boff(k), IDESC, acc | (k > 0 ? 1u : 0u));
+                        }
                         issued = true;
                         tc_commit(a_empty(as));
                     }
