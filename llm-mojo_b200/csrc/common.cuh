@@ -144,6 +144,19 @@ __device__ __forceinline__ float act_fn(float g, float u, int kind) {
     return (g * sig) * u;
 }
 
+// The q layout of an activation row read by the CUDA-core expert kernels
+// (moe_gemv.cu): element j is stored pre-scaled by 16^-(j % 4) at float
+// position 4 * xunit(j / 4) + j % 4, where xunit XOR-swizzles the eight float4
+// units of each 32-element chunk by the chunk index.
+__host__ __device__ __forceinline__ int xunit(int u) {
+    const int c = u >> 3;
+    return (c << 3) | ((u & 7) ^ (c & 7));
+}
+__device__ __forceinline__ int64_t qpos(int64_t j) { return 4 * xunit((int)(j >> 2)) + (j & 3); }
+__device__ __forceinline__ float qscale(int64_t j) {
+    return (j & 3) == 0 ? 1.f : (j & 3) == 1 ? 0.0625f : (j & 3) == 2 ? 0.00390625f : 0.000244140625f;
+}
+
 // Position of natural element j of a K-long row inside each input layout.
 __device__ __forceinline__ int64_t x_src_index(int64_t j, int64_t K, int layout) {
     if (layout == 0) return j;

@@ -266,6 +266,8 @@ struct ExpertBufs {
     moe::BucketOut b;
     float* x32;   // [M][d] gate/up input, fp32 natural
     float* xsum;  // [M][d/32] 1.5 * block sums of x32
+    float* x32q;  // [M][d]   CUDA-core path: x32 in the q layout
+    bool x32q_ready;  // x32q already written (by the router's prep)
     float* act;   // [P][F]
     float* y;     // [P][d]
     __half* x16;  // [P][d]   tensor-core path: gathered gate/up input
@@ -276,7 +278,7 @@ struct ExpertBufs {
 size_t expert_bufs_bytes(int64_t M, int64_t K, int64_t d, int64_t F, int64_t E) {
     const int64_t P = M * K;
     return al(P * 4) * 2 + al(16) + al(E * 4) * 3 + al(P * 4) * 3 + al(M * d * 4) +
-           al(M * d / 32 * 4) + al(P * F * 4) + al(P * d * 4 * kMaxSplitY) + al(P * d * 2) +
+           al(M * d / 32 * 4) + al(M * d * 4) + al(P * F * 4) + al(P * d * 4 * kMaxSplitY) + al(P * d * 2) +
            al(P * F * 2) + al((E + 1) * 4);
 }
 
@@ -294,6 +296,8 @@ int take_expert_bufs(moe_ctx* ctx, int64_t M, int64_t K, int64_t d, int64_t F, i
     o->b.slot_pair = (int*)ws_take(ctx, P * 4);
     o->x32 = (float*)ws_take(ctx, M * d * 4);
     o->xsum = (float*)ws_take(ctx, M * d / 32 * 4);
+    o->x32q = (float*)ws_take(ctx, M * d * 4);
+    o->x32q_ready = false;
     o->act = (float*)ws_take(ctx, P * F * 4);
     o->y = (float*)ws_take(ctx, P * d * 4 * kMaxSplitY);
     o->x16 = (__half*)ws_take(ctx, P * d * 2);
@@ -455,11 +459,8 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     g1.act = act;
     g1.max_tokens = max_t;
     g1.max_unique = max_u;
-    {
-        ProfScope ps(ctx, "gemv_gate_up");
-        ctx->launches += moe::dgemv_supported(g1) ? moe::launch_dgemv(moe::GEMV_ACT, g1, ctx->num_sms, s)
-                                                   : moe::launch_gemv(moe::GEMV_ACT, g1, ctx->num_sms, s);
-    }
+    g1.err_flag = ctx->err_flag;
+    g1.timeout_ns = ctx->device_timeout_ns;
 
     moe::GemvArgs g2 = g1;
     g2.Wp = w.dn_p;
@@ -471,10 +472,33 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     g2.pair_row = nullptr;
     g2.out = bb.y;
     g2.out_stride = d;
+
+    // The streaming kernel pair (k_dgemv) reads its inputs in the q layout:
+    // the gate/up input is converted once, the activations come out of stage
+    // 1 in it.  Both stages take it or neither does.
+    moe::GemvArgs q1 = g1, q2 = g2;
+    q1.X = bb.x32q;
+    q1.x_qlayout = 1;
+    q1.out_qlayout = 1;
+    q2.x_qlayout = 1;
+    const bool stream = moe::dgemv_supported(q1, moe::GEMV_ACT) && moe::dgemv_supported(q2, moe::GEMV_PLAIN);
+    if (stream && !bb.x32q_ready) {
+        ProfScope ps(ctx, "qlayout");
+        ctx->launches += moe::launch_to_qlayout(bb.x32, bb.x32q, M, (int)d, ctx->num_sms, s);
+    }
+    {
+        ProfScope ps(ctx, "gemv_gate_up");
+        const int r = stream ? moe::launch_dgemv(moe::GEMV_ACT, q1, ctx->num_sms, s)
+                             : moe::launch_gemv(moe::GEMV_ACT, g1, ctx->num_sms, s);
+        if (r < 0) return fail(ctx, MOE_E_CUDA, "expert GEMV launch failed (gate/up)");
+        ctx->launches += r;
+    }
     {
         ProfScope ps(ctx, "gemv_down");
-        ctx->launches += moe::dgemv_supported(g2) ? moe::launch_dgemv(moe::GEMV_PLAIN, g2, ctx->num_sms, s)
-                                                   : moe::launch_gemv(moe::GEMV_PLAIN, g2, ctx->num_sms, s);
+        const int r = stream ? moe::launch_dgemv(moe::GEMV_PLAIN, q2, ctx->num_sms, s)
+                             : moe::launch_gemv(moe::GEMV_PLAIN, g2, ctx->num_sms, s);
+        if (r < 0) return fail(ctx, MOE_E_CUDA, "expert GEMV launch failed (down)");
+        ctx->launches += r;
     }
     }
 
@@ -1236,7 +1260,7 @@ size_t route_bytes(int64_t M, int64_t d, int64_t E, int64_t K) {
 int route_dev(moe_ctx* ctx, const moe_layer_desc* L, const LayerDev& ld, int64_t M,
               const float* xd, int flags, float* moe_in, float* moe_in_sum, int* slot_expert,
               float* slot_weight, float* probs, int64_t* top_idx, float* top_val, int64_t* tc,
-              int64_t* ti, float* tw) {
+              int64_t* ti, float* tw, float* moe_in_q = nullptr) {
     const int64_t K = L->top_k, d = L->embed_dim, E = L->num_experts;
     int* ti32 = (int*)ws_take(ctx, M * K * 4);
     float* tv = (float*)ws_take(ctx, M * K * 4);
@@ -1256,6 +1280,7 @@ int route_dev(moe_ctx* ctx, const moe_layer_desc* L, const LayerDev& ld, int64_t
     pa.rsf = L->r_scale_factor;
     pa.out = moe_in;
     pa.out_sum = moe_in_sum;
+    pa.out_q = moe_in_q;
     pa.scaled = scaled;
     {
         ProfScope ps(ctx, "prep");
@@ -1405,9 +1430,13 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
         if (r < 0) return fail(ctx, MOE_E_CUDA, "fused routing launch failed");
         ctx->launches += r;
     } else {
+        // the CUDA-core expert kernels read the gate/up input in the q layout:
+        // the router's prep writes it alongside
+        const bool cc = !use_tc(ctx, M, d, F, ld.w);
         TRY(route_dev(ctx, L, ld, M, (const float*)xd, flags, bb.x32, bb.xsum, bb.slot_expert,
                       bb.slot_weight, nullptr, nullptr, nullptr, (int64_t*)dtc, (int64_t*)dti,
-                      (float*)dtw));
+                      (float*)dtw, cc ? bb.x32q : nullptr));
+        bb.x32q_ready = cc;
     }
     moe::CombineArgs c;
     c.post_norm = (flags & MOE_F_POST_NORM) ? 1 : 0;

@@ -30,6 +30,10 @@ struct GemvArgs {
     int act = 0;
     int max_tokens = 1;             // upper bound on tokens per expert (host side)
     int max_unique = 1;             // upper bound on U (host side)
+    int x_qlayout = 0;              // X rows in the q layout (k_dgemv; see moe_gemv.cu)
+    int out_qlayout = 0;            // ACT: write the activations in the q layout
+    int* err_flag = nullptr;        // k_dgemv: set to 2 when a bounded wait expires
+    uint64_t timeout_ns = 0;
 };
 
 enum GemvMode { GEMV_PLAIN = 0, GEMV_ACT = 1 };
@@ -47,6 +51,7 @@ struct PrepArgs {
     float* out = nullptr;           // [M][K] fp32
     float* out_sum = nullptr;       // [M][K/32] 1.5 * block sums of out (nullable)
     float* scaled = nullptr;        // [M][K] x*inv*router_scale*rsf (nullable)
+    float* out_q = nullptr;         // [M][K] out in the q layout (nullable; common.cuh)
 };
 
 struct TopkArgs {
@@ -152,8 +157,10 @@ int launch_router_part(const uint8_t* W, const float* S, const float* X, int M, 
 
 // CUDA-core grouped GEMV for few tokens per expert (moe_gemv.cu); expert
 // work lists only (dense_tokens == 0).
-bool dgemv_supported(const GemvArgs& a);
+bool dgemv_supported(const GemvArgs& a, int mode);
 int launch_dgemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);
+// rows x K fp32 -> the q layout k_dgemv reads (pre-scaled, swizzled per row)
+int launch_to_qlayout(const float* x, float* xq, int64_t rows, int K, int num_sms, cudaStream_t s);
 
 int launch_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo, int e_hi, const BucketOut& o,
                   cudaStream_t s);

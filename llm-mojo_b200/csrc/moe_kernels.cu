@@ -496,6 +496,7 @@ __global__ void __launch_bounds__(512) k_prep(PrepArgs a) {
         const float o = a.norm ? v * inv * __ldg(a.pre_w + j) : v;
         xs[j] = o;
         a.out[t * K + j] = o;
+        if (a.out_q) a.out_q[t * K + qpos(j)] = o * qscale(j);
     }
     if (a.out_sum) {
         __syncthreads();

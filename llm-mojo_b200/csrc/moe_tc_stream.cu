@@ -87,6 +87,16 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t a, uint32_t parity, cons
     const bool ok = mbar_wait(a, parity, g);
     return __all_sync(0xffffffffu, ok) != 0;
 }
+// Whole-warp wait where lane 0 alone polls: for barriers that guard no data
+// the lanes read afterwards (a TMEM slot freed by MMAs; the tcgen05 fence
+// after it orders the warp's stores).  32 lanes polling one barrier cost a
+// few hundred cycles per wait.
+__device__ __forceinline__ bool mbar_wait_warp1(uint32_t a, uint32_t parity, const Guard& g) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(a, parity, g) ? 1 : 0;
+    __syncwarp();
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
 
 // Wait with back-off for roles that are far from the critical path.
 __device__ __forceinline__ bool mbar_wait_sleep(uint32_t a, uint32_t parity, const Guard& g) {
@@ -397,16 +407,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 if (lane == 0) mbar_arrive(q_empty(qs));
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const uint32_t la = 2u * (gs >> 1) + (uint32_t)h;  // place in this group's ring
-                    const int as = grp * SAG + (int)(la % SAG);
-                    if (!(ok = mbar_wait_warp(a_empty(as), ((la / SAG) & 1u) ^ 1u, G))) break;
-                    tc_fence_after();
-#pragma unroll
-                    for (int p2 = 0; p2 < 2; ++p2) {
-                        uint32_t hv[32];
+                    // Two 32-column quarters: the first quarter's TMEM store runs
+                    // while the second is computed, one wait for both.  The math of
+                    // the first quarter comes before the wait for the A slot.
+                    auto deq_quarter = [&](int c0, uint32_t (&hv)[32]) {
 #pragma unroll
                         for (int cc = 0; cc < 2; ++cc) {
-                            const int c = 4 * h + 2 * p2 + cc;  // chunk = Q4 block 8s + c
+                            const int c = c0 + cc;  // chunk = Q4 block 8s + c
                             const uint4 wv = wq[c];
                             const __half2 sc = __float2half2_rn(scl[c]);
                             const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
@@ -418,19 +425,30 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                                 hv[16 * cc + 4 * w + 3] = deq_pair<3>(w4[w], sc);
                             }
                         }
-                        // store and wait in one statement: the 32 source registers stay untouched
-                        // until the store has completed
-                        asm volatile(
-                            "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
-                            "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
-                            "tcgen05.wait::st.sync.aligned;" ::"r"(tl + (uint32_t)(as * 64 + 32 * p2)),
-                            "r"(hv[0]), "r"(hv[1]), "r"(hv[2]), "r"(hv[3]), "r"(hv[4]), "r"(hv[5]), "r"(hv[6]),
-                            "r"(hv[7]), "r"(hv[8]), "r"(hv[9]), "r"(hv[10]), "r"(hv[11]), "r"(hv[12]), "r"(hv[13]),
-                            "r"(hv[14]), "r"(hv[15]), "r"(hv[16]), "r"(hv[17]), "r"(hv[18]), "r"(hv[19]),
-                            "r"(hv[20]), "r"(hv[21]), "r"(hv[22]), "r"(hv[23]), "r"(hv[24]), "r"(hv[25]),
-                            "r"(hv[26]), "r"(hv[27]), "r"(hv[28]), "r"(hv[29]), "r"(hv[30]), "r"(hv[31])
-                            : "memory");
-                    }
+                    };
+                    uint32_t hA[32], hB[32];
+                    deq_quarter(4 * h, hA);
+                    const uint32_t la = 2u * (gs >> 1) + (uint32_t)h;  // place in this group's ring
+                    const int as = grp * SAG + (int)(la % SAG);
+                    if (!(ok = mbar_wait_warp1(a_empty(as), ((la / SAG) & 1u) ^ 1u, G))) break;
+                    tc_fence_after();
+                    asm volatile(
+                        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(tl + (uint32_t)(as * 64)),
+                        "r"(hA[0]), "r"(hA[1]), "r"(hA[2]), "r"(hA[3]), "r"(hA[4]), "r"(hA[5]), "r"(hA[6]), "r"(hA[7]),
+                        "r"(hA[8]), "r"(hA[9]), "r"(hA[10]), "r"(hA[11]), "r"(hA[12]), "r"(hA[13]), "r"(hA[14]), "r"(hA[15]),
+                        "r"(hA[16]), "r"(hA[17]), "r"(hA[18]), "r"(hA[19]), "r"(hA[20]), "r"(hA[21]), "r"(hA[22]), "r"(hA[23]),
+                        "r"(hA[24]), "r"(hA[25]), "r"(hA[26]), "r"(hA[27]), "r"(hA[28]), "r"(hA[29]), "r"(hA[30]), "r"(hA[31])
+                        : "memory");
+                    deq_quarter(4 * h + 2, hB);
+                    // the wait covers both stores: the MMAs may read the slot after it
+                    asm volatile(
+                        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
+                        "tcgen05.wait::st.sync.aligned;" ::"r"(tl + (uint32_t)(as * 64 + 32)),
+                        "r"(hB[0]), "r"(hB[1]), "r"(hB[2]), "r"(hB[3]), "r"(hB[4]), "r"(hB[5]), "r"(hB[6]), "r"(hB[7]),
+                        "r"(hB[8]), "r"(hB[9]), "r"(hB[10]), "r"(hB[11]), "r"(hB[12]), "r"(hB[13]), "r"(hB[14]), "r"(hB[15]),
+                        "r"(hB[16]), "r"(hB[17]), "r"(hB[18]), "r"(hB[19]), "r"(hB[20]), "r"(hB[21]), "r"(hB[22]), "r"(hB[23]),
+                        "r"(hB[24]), "r"(hB[25]), "r"(hB[26]), "r"(hB[27]), "r"(hB[28]), "r"(hB[29]), "r"(hB[30]), "r"(hB[31])
+                        : "memory");
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(a_full(as));
