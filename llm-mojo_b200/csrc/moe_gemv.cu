@@ -120,14 +120,6 @@ struct QRows {
     static constexpr int ITEM = (MODE == GEMV_ACT) ? IROWS / 2 : IROWS;  // act rows / rows per item
 };
 
-// (a & b) | c in one LOP3: with both constants in registers, the mask and
-// the magic exponent do not compete for the instruction's one immediate.
-__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t d;
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-
 // Dot products of the warp's RW rows (slot rows lr[], packed rows sq, scale
 // rows ss; every row of an item exists) with NT staged tokens over the whole
 // K.  res[r][t] is complete in every lane afterwards.
@@ -184,8 +176,8 @@ __device__ __forceinline__ void rows_dot(const uint8_t* sq, const float* ss, con
                 for (int r = 0; r < RW; ++r) {
                     const uint32_t word = w == 0 ? q[r].x : w == 1 ? q[r].y : w == 2 ? q[r].z : q[r].w;
                     const uint32_t u = h ? (word >> 16) : word;
-                    v01[r] = fadd2(pk2(and_or(u, mk[0], magic), and_or(u, mk[1], magic)), m01);
-                    v23[r] = fadd2(pk2(and_or(u, mk[2], magic), and_or(u, mk[3], magic)), m23);
+                    v01[r] = fadd2(pk2(tc::and_or(u, mk[0], magic), tc::and_or(u, mk[1], magic)), m01);
+                    v23[r] = fadd2(pk2(tc::and_or(u, mk[2], magic), tc::and_or(u, mk[3], magic)), m23);
                 }
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {

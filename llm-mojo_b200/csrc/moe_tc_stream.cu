@@ -119,9 +119,8 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint32_t a, uint32_t parity, con
 template <int P>
 __device__ __forceinline__ uint32_t deq_pair(uint32_t w, __half2 sc) {
     const uint32_t v = (P < 2 ? w : (w >> 8));
-    uint32_t m;
-    if (P % 2 == 0) m = (v & 0x000F000Fu) | 0x64006400u;  // 1024 + n
-    else m = (v & 0x00F000F0u) | 0x54005400u;             // 64 + n
+    // one LOP3 each (and_or): 1024 + n, or 64 + n
+    const uint32_t m = (P % 2 == 0) ? and_or(v, 0x000F000Fu, 0x64006400u) : and_or(v, 0x00F000F0u, 0x54005400u);
     const __half2 off = (P % 2 == 0) ? __half2(__float2half(1032.0f), __float2half(1032.0f))
                                      : __half2(__float2half(72.0f), __float2half(72.0f));
     const __half2 x = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&m), off), sc);

@@ -29,16 +29,29 @@ __device__ __forceinline__ void mbar_arrive(uint32_t a) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
 }
+// A thread whose phase is not complete sleeps in the hardware until it
+// completes or `kSuspendNs` pass: without the hint the time limit is short and
+// the waiting loops spin, taking issue slots from the warps that work.
+constexpr uint32_t kSuspendNs = 20000;
 __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(a), "r"(parity)
+        : "r"(a), "r"(parity), "r"(kSuspendNs)
         : "memory");
     return ok != 0;
+}
+
+// (a & b) | c as one LOP3: with both constants in registers the mask and the
+// magic exponent do not compete for the instruction's one immediate (written
+// in C++ the pair compiles to two LOP3s).
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
 struct Guard {
@@ -52,7 +65,7 @@ struct Guard {
 __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, const Guard& g) {
     for (uint32_t it = 0;; ++it) {
         if (mbar_try(a, parity)) return true;
-        if ((it & 255u) == 255u) {
+        if ((it & 15u) == 15u) {
             if (*g.abort) return false;
             if (globaltimer() > g.deadline) {
                 *g.abort = 1;
