@@ -160,8 +160,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = a.K, nb = K / 32, nst = (K + ST_K - 1) / ST_K;
-    auto s_begin = [&](const Item& it) { return (int)((int64_t)it.ks * nst / a.ksplit); };
-    auto s_end = [&](const Item& it) { return (int)((int64_t)(it.ks + 1) * nst / a.ksplit); };
+    // 32-bit: every role evaluates these per item (ks < ksplit <= 16, nst < 2^16)
+    auto s_begin = [&](const Item& it) { return it.ks * nst / a.ksplit; };
+    auto s_end = [&](const Item& it) { return (it.ks + 1) * nst / a.ksplit; };
     const int row_tiles = (MODE == TC_ACT) ? (a.F / 64) : (int)((a.R + 127) / 128);
     // TMA rows of the two 64-row boxes of an item
     auto box_rows = [&](const Item& it, int& ra, int& rb) {

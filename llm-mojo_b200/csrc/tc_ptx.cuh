@@ -218,37 +218,47 @@ struct Item {
     int u, e, rt, tt, n, s0, ks;
 };
 
-__device__ __forceinline__ bool decode_item(const TcArgs& a, int64_t item, int row_tiles, int BN,
+// Every role of a kernel decodes every work item, so the arithmetic is 32-bit
+// (work lists stay far below 2^31 items): 64-bit division by a run-time value
+// is a long instruction sequence.
+__device__ __forceinline__ bool decode_item(const TcArgs& a, int64_t item64, int row_tiles, int BN,
                                             Item& it) {
-    it.ks = (int)(item % a.ksplit);  // split-K index (PLAIN mode), fastest varying
-    item /= a.ksplit;
+    if (item64 >= 0x7FFFFFFF) return false;
+    int item = (int)item64;
+    if (a.ksplit > 1) {
+        it.ks = item % a.ksplit;  // split-K index (PLAIN mode), fastest varying
+        item /= a.ksplit;
+    } else {
+        it.ks = 0;
+    }
     if (a.dense_tokens > 0) {
         const int ntt = (a.dense_tokens + BN - 1) / BN;
-        if (item >= (int64_t)row_tiles * ntt) return false;
+        if (item >= row_tiles * ntt) return false;
         it.u = 0;
         it.e = 0;
-        it.rt = (int)(item / ntt);
-        it.tt = (int)(item - (int64_t)it.rt * ntt);
+        it.rt = item / ntt;
+        it.tt = item - it.rt * ntt;
         it.n = a.dense_tokens;
         it.s0 = 0;
         return true;
     }
     const int U = a.meta[0];
-    const int64_t total = (int64_t)row_tiles * a.tt_prefix[U];
+    const int total = row_tiles * a.tt_prefix[U];
     if (item >= total) return false;
     int lo = 0, hi = U - 1;  // last u with row_tiles * tt_prefix[u] <= item
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if ((int64_t)row_tiles * a.tt_prefix[mid] <= item) lo = mid;
+        if (row_tiles * a.tt_prefix[mid] <= item) lo = mid;
         else hi = mid - 1;
     }
     const int u = lo;
-    const int ntt = a.tt_prefix[u + 1] - a.tt_prefix[u];
-    const int64_t rem = item - (int64_t)row_tiles * a.tt_prefix[u];
+    const int p0 = a.tt_prefix[u];
+    const int ntt = a.tt_prefix[u + 1] - p0;
+    const int rem = item - row_tiles * p0;
     it.u = u;
     it.e = a.unique_expert[u];
-    it.rt = (int)(rem / ntt);
-    it.tt = (int)(rem - (int64_t)it.rt * ntt);
+    it.rt = rem / ntt;
+    it.tt = rem - it.rt * ntt;
     it.n = a.seg_count[u];
     it.s0 = a.seg_start[u];
     return true;
