@@ -47,33 +47,39 @@ namespace tc {
 constexpr int ST_K = 256;                       // K per stage
 constexpr int ST_Q = 128 * ST_K / 2;            // packed bytes per stage (16384)
 constexpr int ST_S = 128 * 32;                  // scale bytes per stage (8 fp32 per row)
-constexpr int ST_DQ0 = 2;                       // warps 2-9: dequant, two groups of four
-constexpr int ST_EPI0 = ST_DQ0 + 8;             // warps 10-13: epilogue
-constexpr int ST_MMA2 = ST_EPI0 + 4;            // warp 14: second MMA issuer
-constexpr int ST_NMMA = 2;                      // MMA issuers: warp 1 (even stages), warp 14 (odd)
-constexpr int ST_THREADS = 32 * (ST_MMA2 + 1);  // 480
+constexpr int ST_DQ0 = 2;  // warp 0: TMA producer, warp 1: MMA issuer 0, then the dequant groups
 
 template <int BN>
 struct StLayout {
-    static constexpr int ACC = ((2 * ST_NMMA * BN + 31) / 32) * 32;  // two buffers x two issuers
+    // NG dequant groups of four warps and NG MMA issuers; stage st belongs to
+    // group and issuer st % NG.  Three for 16-token tiles (the dequant warps
+    // are latency-bound, 2 groups ran 1.36x faster than one); TMEM holds the
+    // accumulators of only two issuers at wider tiles.
+    static constexpr int NG = BN <= 16 ? 3 : 2;
+    static constexpr int EPI0 = ST_DQ0 + 4 * NG;  // four epilogue warps
+    static constexpr int MMAX = EPI0 + 4;         // MMA issuers 1 .. NG-1
+    static constexpr int THREADS = 32 * (MMAX + NG - 1);
+    static constexpr int ACC = ((2 * NG * BN + 31) / 32) * 32;  // two buffers x NG issuers
     static constexpr int SA = (512 - ACC) / 64 > 7 ? 7 : (512 - ACC) / 64;  // 128-K fp16 A slots in TMEM
-    // The slots form one ring per dequant group / MMA issuer pair (stage
-    // parity), SAG slots each: a ring shared by both groups lets an issuer
-    // wait on a slot whose previous writer (the other group) has not arrived
-    // yet, where the mbarrier parity test matches the phase before and passes.
-    static constexpr int SAG = SA / 2;
+    // The slots form one ring per dequant group / MMA issuer pair, SAG slots
+    // each: a ring shared by two groups lets an issuer wait on a slot whose
+    // previous writer (the other group) has not arrived yet, where the
+    // mbarrier parity test matches the phase before and passes.
+    static constexpr int SAG = SA / NG;
+    static_assert(SAG >= 2, "each group needs two A slots");
     static constexpr int B_BYTES = BN * ST_K * 2;
     static constexpr int SLOT = ST_Q + B_BYTES + ST_S;
-    // even, so that stage slot qs is always used by the same dequant group and
-    // MMA issuer (stage parity): each ring then has one producer and one
+    // a multiple of NG, so that stage slot qs is always used by the same
+    // dequant group and MMA issuer: each ring then has one producer and one
     // consumer order, which the mbarrier parity waits rely on
-    static constexpr int SQ = ((227 * 1024 - 2048) / SLOT > 8 ? 8 : (227 * 1024 - 2048) / SLOT) & ~1;
-    static_assert(SQ >= 2 && SQ % ST_NMMA == 0, "stage ring must split evenly between the two issuers");
+    static constexpr int SQ0 = (227 * 1024 - 2048) / SLOT > 8 ? 8 : (227 * 1024 - 2048) / SLOT;
+    static constexpr int SQ = (SQ0 / NG) * NG;
+    static_assert(SQ >= NG, "stage ring must split evenly between the issuers");
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_B = OFF_Q + SQ * ST_Q;
     static constexpr int OFF_S = OFF_B + SQ * B_BYTES;
     static constexpr int OFF_BAR = OFF_S + SQ * ST_S;
-    static constexpr int N_BAR = 2 * SQ + 2 * SA + 4 + ST_NMMA + 4 + 2 * SQ;
+    static constexpr int N_BAR = 2 * SQ + 2 * SA + 4 + NG + 4 + 2 * SQ;
     // item-scale mode (K % 128 == 64): the scale area holds two item buffers
     static constexpr int ISCALE_BYTES = SQ * ST_S / 2;
     static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
@@ -128,11 +134,12 @@ __device__ __forceinline__ uint32_t deq_pair(uint32_t w, __half2 sc) {
 }
 
 template <int MODE, int BN>
-__global__ void __launch_bounds__(ST_THREADS, 1)
+__global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
     k_tc_stream(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap bmap,
                 const __grid_constant__ CUtensorMap smap, TcArgs a, int64_t total_rows,
                 int iscale) {
     using L = StLayout<BN>;
+    constexpr int NG = L::NG;
     constexpr int SQ = L::SQ;
     constexpr int SA = L::SA;
     constexpr int SAG = L::SAG;
@@ -148,13 +155,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     auto drain_bar = [&](int j) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + j); };
     // item scales: all of an item's scale rows in one bulk copy (K % 128 == 64,
     // where the 2-D scale tensor map cannot exist); buffers b = 0, 1
-    auto is_full = [&](int b) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + ST_NMMA + b); };
-    auto is_empty = [&](int b) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + ST_NMMA + 2 + b); };
+    auto is_full = [&](int b) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + NG + b); };
+    auto is_empty = [&](int b) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + NG + 2 + b); };
     // activation tiles: same slot index as the stage, own barriers, so a
     // stage's weight bytes are released by the dequant group alone and the
     // tile stays until the stage's MMAs have read it
-    auto b_full = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + 8 + ST_NMMA + s); };
-    auto b_empty = [&](int s) { return bar0 + 8u * (3 * SQ + 2 * SA + 8 + ST_NMMA + s); };
+    auto b_full = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + 8 + NG + s); };
+    auto b_empty = [&](int s) { return bar0 + 8u * (3 * SQ + 2 * SA + 8 + NG + s); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -190,13 +197,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             mbar_init(a_empty(s), 1);
         }
         for (int s = 0; s < 2; ++s) {
-            mbar_init(acc_full(s), ST_NMMA);
+            mbar_init(acc_full(s), NG);
             mbar_init(acc_empty(s), 4);
         }
-        for (int j = 0; j < ST_NMMA; ++j) mbar_init(drain_bar(j), 1);
+        for (int j = 0; j < NG; ++j) mbar_init(drain_bar(j), 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(is_full(b), 1);
-            mbar_init(is_empty(b), 8);  // the eight dequant warps
+            mbar_init(is_empty(b), 4 * NG);  // every dequant warp
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -289,12 +296,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 if (is_armed & (1u << b)) mbar_wait(is_full(b), (is_par >> b) & 1u, Gd);
         }
         __syncwarp();
-    } else if (warp == 1 || warp == ST_MMA2) {
+    } else if (warp == 1 || (warp >= L::MMAX && warp < L::MMAX + NG - 1)) {
         // ------------------------------------------------ MMA issuers
         // A tcgen05.mma of N <= 64 with A in TMEM holds its issuing thread for
         // about 100 cycles, so two threads issue: stage st goes to issuer
         // st % 2, each into its own accumulator, summed by the epilogue.
-        const int me = (warp == 1) ? 0 : 1;
+        const int me = (warp == 1) ? 0 : warp - L::MMAX + 1;
         if (lane == 0) {
             uint32_t st = 0;
             int ab = 0;
@@ -305,11 +312,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
                 if (!(ok = mbar_wait(acc_empty(ab), accp ^ 1u, G))) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)((ab * ST_NMMA + me) * BN);
+                const uint32_t d_tmem = tmem_base + (uint32_t)((ab * NG + me) * BN);
                 bool first = true;
                 const int sb = s_begin(it), se = s_end(it);
                 for (int s = sb; s < se && ok; ++s, ++st) {
-                    if ((int)(st % ST_NMMA) != me) continue;
+                    if ((int)(st % NG) != me) continue;
                     const int qs = (int)(st % SQ);
                     if (!(ok = mbar_wait(b_full(qs), (st / SQ) & 1u, G))) break;  // activations landed
                     // One thread issues every MMA, so the loop is unrolled with the
@@ -318,7 +325,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                     const uint64_t bdesc = sw128_desc(smem_u32(smem + L::OFF_B + qs * L::B_BYTES));
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const uint32_t la = 2u * (st >> 1) + (uint32_t)h;  // place in this issuer's ring
+                        const uint32_t la = 2u * (st / NG) + (uint32_t)h;  // place in this issuer's ring
                         const int as = me * SAG + (int)(la % SAG);
                         if (!(ok = mbar_wait(a_full(as), (la / SAG) & 1u, G))) break;
                         tc_fence_after();
@@ -359,9 +366,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             }
         }
         __syncwarp();
-    } else if (warp < ST_EPI0) {
+    } else if (warp < L::EPI0) {
         // ------------------------------------------------ dequant
-        const int grp = (warp - ST_DQ0) >> 2;  // 0: even stages, 1: odd stages
+        const int grp = (warp - ST_DQ0) >> 2;  // takes the stages st with st % NG == grp
         const int q = warp & 3;                // TMEM lane quarter
         const int t = q * 32 + lane;           // A-tile row = TMEM lane
         const int sr = (MODE == TC_ACT) ? ((lane < 16) ? 16 * q + lane : 64 + 16 * q + (lane - 16)) : t;
@@ -378,7 +385,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 if (!(ok = mbar_wait_warp(is_full(b), (ii >> 1) & 1u, G))) break;
                 iscl = reinterpret_cast<const float*>(smem + L::OFF_S + b * L::ISCALE_BYTES) + sr * nb;
             }
-            for (int i = (int)((uint32_t)(grp - (int)st) & 1u); i < ns && ok; i += 2) {
+            for (int i = (grp - (int)(st % NG) + NG) % NG; i < ns && ok; i += NG) {
                 const uint32_t gs = st + (uint32_t)i;
                 const int qs = (int)(gs % SQ);
                 if (!(ok = mbar_wait_warp(q_full(qs), (gs / SQ) & 1u, G))) break;
@@ -428,7 +435,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                     };
                     uint32_t hA[32], hB[32];
                     deq_quarter(4 * h, hA);
-                    const uint32_t la = 2u * (gs >> 1) + (uint32_t)h;  // place in this group's ring
+                    const uint32_t la = 2u * (gs / NG) + (uint32_t)h;  // place in this group's ring
                     const int as = grp * SAG + (int)(la % SAG);
                     if (!(ok = mbar_wait_warp1(a_empty(as), ((la / SAG) & 1u) ^ 1u, G))) break;
                     tc_fence_after();
@@ -462,7 +469,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             }
             st += (uint32_t)ns;
         }
-    } else if (warp < ST_MMA2) {
+    } else if (warp < L::EPI0 + 4) {
         // ------------------------------------------------ epilogue
         const int q = warp & 3;       // TMEM lane quarter this warp may access
         const int i = q * 32 + lane;  // accumulator row (A-tile row)
@@ -477,14 +484,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             if (!ok) break;
             tc_fence_after();
             const int nv = min(BN, it.n - it.tt * BN);
-            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * ST_NMMA * BN);
+            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * NG * BN);
             const int ns = s_end(it) - s_begin(it);
             for (int c0 = 0; c0 < nv; c0 += CW) {
                 float v[CW];
 #pragma unroll
                 for (int cc = 0; cc < CW; ++cc) v[cc] = 0.f;
-                for (int j = 0; j < ST_NMMA; ++j) {  // the issuers that had a stage of this item
-                    if ((j - (int)(est % ST_NMMA) + ST_NMMA) % ST_NMMA >= ns) continue;
+                for (int j = 0; j < NG; ++j) {  // the issuers that had a stage of this item
+                    if ((j - (int)(est % NG) + NG) % NG >= ns) continue;
                     float v2[CW];
                     tmem_ld<CW>(tbase + (uint32_t)(j * BN) + c0, v2);
 #pragma unroll
@@ -575,7 +582,7 @@ int launch_st(const TcLaunch& L, int num_sms, cudaStream_t s) {
     int grid = num_sms;  // one CTA per SM: it owns all 512 TMEM columns
     if (L.max_items > 0 && L.max_items < grid) grid = (int)L.max_items;
     if (grid <= 0) return 0;
-    launch_k(kern, dim3(grid), dim3(tc::ST_THREADS), smem, s, qmap, bmap, smap, L.a, L.total_rows, iscale);
+    launch_k(kern, dim3(grid), dim3(tc::StLayout<BN>::THREADS), smem, s, qmap, bmap, smap, L.a, L.total_rows, iscale);
     return 1;
 }
 

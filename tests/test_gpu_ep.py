@@ -48,10 +48,12 @@ def test_expert_ranges_sum_to_the_full_layer(ctx, full_layer, M):
     torch.cuda.synchronize()
     # A launch over fewer experts hands the CTAs different work items, and the
     # tensor-core kernel splits an item's K stages between accumulators by the
-    # CTA's running stage count, so the fp32 sums agree to rounding (~1e-5),
-    # not bit for bit.  One expert's share of an output is ~5e-2: a missing or
+    # CTA's running stage count, so the fp32 sums agree to rounding, not bit
+    # for bit; a reordered gate/up sum can also move an activation across an
+    # fp16 rounding boundary (one ulp, ~5e-4 relative) before the down
+    # projection.  One expert's share of an output is ~5e-2: a missing or
     # doubled expert fails this bar by orders of magnitude.
-    assert_close(acc.cpu().numpy(), full.cpu().numpy(), max_abs=1e-4, rel_l2=1e-5, what=f"ranges M={M}")
+    assert_close(acc.cpu().numpy(), full.cpu().numpy(), max_abs=1e-4, rel_l2=1e-4, what=f"ranges M={M}")
     # post-norm of the reduced sum = the layer's own post-norm
     w = (1.0 + 0.1 * torch.randn(2816, generator=torch.Generator().manual_seed(1))).cuda()
     d2 = dict(dev)
@@ -62,7 +64,7 @@ def test_expert_ranges_sum_to_the_full_layer(ctx, full_layer, M):
     ctx.rms_norm(acc, w, normed, M, 2816)
     torch.cuda.synchronize()
     # normalised outputs are ~7x the layer's (rms 1), the rounding above with them
-    assert_close(normed.cpu().numpy(), normed_ref.cpu().numpy(), max_abs=5e-4, rel_l2=1e-5, what="post-norm")
+    assert_close(normed.cpu().numpy(), normed_ref.cpu().numpy(), max_abs=5e-4, rel_l2=1e-4, what="post-norm")
 
 
 def _free_port():
