@@ -11,8 +11,9 @@
 //  - when K % 128 == 64 a scale row (K/8 bytes) is no multiple of 16 bytes
 //    and no tensor map can describe it: the producer then copies each work
 //    item's scale rows, which are contiguous, with one or two bulk copies;
-//  - two groups of four dequant warps take alternate stages; the thread that
-//    owns A-tile row t reads the row's 128 bytes of the stage into registers,
+//  - NG groups of four dequant warps (three for 16-token tiles, two for
+//    wider ones) take the stages in turn; the thread that owns A-tile row t
+//    reads the row's 128 bytes of the stage into registers,
 //    hands the slot back to the producer, and turns the 256 weights into
 //    fp16 in TMEM with tcgen05.st.32x32b.x32 (128-K A slots).
 //    (w & 0x000F000F) | 0x64006400 is 1024 + n and (w & 0x00F000F0) |
@@ -21,14 +22,13 @@
 //  - the activation tile has its own barriers: it stays until the stage's
 //    MMAs have read it, while the weight bytes go back as soon as they are in
 //    registers;
-//  - with the A operand in TMEM a tcgen05.mma of M=128, N=16, K=16 holds
-//    its issuing thread for about 100 cycles, so two threads (warps 1 and
-//    14) issue the MMAs of alternate stages into separate accumulators,
-//    which the epilogue adds;
+//  - a tcgen05.mma holds its issuing thread for ~55 cycles whatever N is,
+//    so NG threads (warp 1 and the warps after the epilogue) issue the MMAs
+//    of their stages into separate accumulators, which the epilogue adds;
 //  - every ring (stages, TMEM A slots) has one producer order and one
-//    consumer order: stage st belongs to dequant group and issuer st % 2,
-//    the stage ring has an even number of slots and each group has its own
-//    A slots.  An mbarrier parity wait cannot tell phase p from p - 2, so a
+//    consumer order: stage st belongs to dequant group and issuer st % NG,
+//    the stage ring is a multiple of NG slots and each group has its own A
+//    slots.  An mbarrier parity wait cannot tell phase p from p - 2, so a
 //    consumer that could reach a slot before its previous user had filled it
 //    would pass the wait early.
 //
