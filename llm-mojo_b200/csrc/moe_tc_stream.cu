@@ -433,11 +433,20 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
                             }
                         }
                     };
-                    uint32_t hA[32], hB[32];
-                    deq_quarter(4 * h, hA);
                     const uint32_t la = 2u * (gs / NG) + (uint32_t)h;  // place in this group's ring
                     const int as = grp * SAG + (int)(la % SAG);
-                    if (!(ok = mbar_wait_warp1(a_empty(as), ((la / SAG) & 1u) ^ 1u, G))) break;
+                    const uint32_t apar = ((la / SAG) & 1u) ^ 1u;
+                    // the slot is nearly always free by now: a non-blocking test
+                    // ahead of the math hides its latency; the bounded wait only
+                    // when it was not
+                    const uint32_t early = (lane == 0) ? (mbar_test(a_empty(as), apar) ? 1u : 0u) : 0u;
+                    uint32_t hA[32], hB[32];
+                    deq_quarter(4 * h, hA);
+                    if (__shfl_sync(0xffffffffu, early, 0) == 0u) {
+                        if (!(ok = mbar_wait_warp1(a_empty(as), apar, G))) break;
+                    } else {
+                        __syncwarp();
+                    }
                     tc_fence_after();
                     asm volatile(
                         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(tl + (uint32_t)(as * 64)),

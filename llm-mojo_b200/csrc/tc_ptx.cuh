@@ -29,6 +29,19 @@ __device__ __forceinline__ void mbar_arrive(uint32_t a) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
 }
+// Non-blocking test of a phase (no suspension): issued ahead of other work
+// its latency overlaps that work.
+__device__ __forceinline__ bool mbar_test(uint32_t a, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // A thread whose phase is not complete sleeps in the hardware until it
 // completes or `kSuspendNs` pass: without the hint the time limit is short and
 // the waiting loops spin, taking issue slots from the warps that work.
