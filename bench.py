@@ -488,8 +488,11 @@ def main():
     for c in [ctx, *dctx.values()]:
         c.profile_enable(False)
 
-    # end-to-end through the public API with pinned host buffers
-    ctx.set_async(False)
+    # End to end through the public API with pinned host buffers: every call
+    # stages its host inputs (H2D) and copies its outputs back (D2H) on its
+    # context's stream; the calls are asynchronous (moe_set_async), the dense
+    # projections run on their own contexts' streams as in the device-timed
+    # step, and the step ends when the main stream has joined them.
     x_h = [x.cpu().pin_memory() for x in xs]
     xo_h = x_o.cpu().pin_memory()
     out_h = torch.empty((M, D)).pin_memory()
@@ -505,10 +508,22 @@ def main():
             x_d.copy_(x_h[li], non_blocking=True)
             epl.forward(descs[li], M, x_d, out, MB.F_POST_NORM, layers[li]["post_norm_w"])
             out_h.copy_(out, non_blocking=True)
-        else:
-            ctx.layer_forward(descs[li], M, x_h[li], out_h, MB.F_POST_NORM)
+            for name, (p, s, ci, co) in dense.items():
+                ctx.q4_matmul_batchN(M, p, s, xo_h if name == "o" else x_h[li], dout_h[name], ci, co)
+            return
+        main = torch.cuda.current_stream()
+        fork = torch.cuda.Event()
+        fork.record(main)
+        ctx.layer_forward(descs[li], M, x_h[li], out_h, MB.F_POST_NORM)
+        joins = []
         for name, (p, s, ci, co) in dense.items():
-            ctx.q4_matmul_batchN(M, p, s, xo_h if name == "o" else x_h[li], dout_h[name], ci, co)
+            dstream[name].wait_event(fork)
+            dctx[name].q4_matmul_batchN(M, p, s, xo_h if name == "o" else x_h[li], dout_h[name], ci, co)
+            ev = torch.cuda.Event()
+            ev.record(dstream[name])
+            joins.append(ev)
+        for ev in joins:
+            main.wait_event(ev)
 
     e2e_steps = max(1, min(args.steps, 500))
     for i in range(3):
