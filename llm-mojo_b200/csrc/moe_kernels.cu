@@ -536,13 +536,15 @@ __global__ void __launch_bounds__(128) k_topk(TopkArgs a) {
         float sc;
         if (a.part_n > 0) {  // router partial sums over K slices, in slice order
             sc = 0.f;
-            for (int c0 = 0; c0 < a.part_n; c0 += 8) {  // 8 loads in flight, then the ordered sum
-                float v[8];
+            // up to 32 loads in flight (one L2 round trip for d <= 4096), then
+            // the sum in slice order
+            for (int c0 = 0; c0 < a.part_n; c0 += 32) {
+                float v[32];
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
+                for (int j = 0; j < 32; ++j)
                     v[j] = c0 + j < a.part_n ? __ldg(a.part + ((int64_t)(c0 + j) * a.M + t) * E + e) : 0.f;
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
+                for (int j = 0; j < 32; ++j)
                     if (c0 + j < a.part_n) sc += v[j];
             }
             if (a.scores_out) a.scores_out[t * E + e] = sc;
