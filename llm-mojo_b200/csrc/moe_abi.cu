@@ -373,20 +373,21 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
                 bool prebucketed = false) {
     cudaStream_t s = ctx->stream;
     const int64_t P = M * K;
-    if (!prebucketed) {
+    const bool tc = use_tc(ctx, M, d, F, w);
+    if (!prebucketed) {  // the tensor-core path's token-tile prefix comes out of the same launch
         ProfScope ps(ctx, "bucket");
         int e_lo, e_hi;
         expert_range(ctx, E, &e_lo, &e_hi);
-        ctx->launches += moe::launch_bucket(bb.slot_expert, P, (int)K, (int)E, e_lo, e_hi, bb.b, s);
+        ctx->launches += moe::launch_bucket(bb.slot_expert, P, (int)K, (int)E, e_lo, e_hi, bb.b, s,
+                                            tc ? expert_token_tile(P, E) : 0, tc ? bb.tt_prefix : nullptr);
     }
     const int max_u = (int)std::min<int64_t>(E, P);
     const int max_t = (int)std::max<int64_t>(1, M);
 
     int ksplit = 1;
-    if (use_tc(ctx, M, d, F, w)) {
+    if (tc) {
         const int BN = expert_token_tile(P, E);
         if (!prebucketed) {
-            ctx->launches += moe::launch_tt_prefix(bb.b.meta, bb.b.seg_count, BN, bb.tt_prefix, s);
             ProfScope ps(ctx, "gather");
             ctx->launches += moe::launch_gather_f16(bb.x32, d, bb.b.pair_token, bb.b.meta, P, 0, bb.x16, s);
         }

@@ -163,7 +163,7 @@ int launch_dgemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);
 int launch_to_qlayout(const float* x, float* xq, int64_t rows, int K, int num_sms, cudaStream_t s);
 
 int launch_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo, int e_hi, const BucketOut& o,
-                  cudaStream_t s);
+                  cudaStream_t s, int BN = 0, int* tt_prefix = nullptr);
 int launch_gemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);
 int launch_gemv_wide(const uint8_t* W, const float* S, const float* X, float* out, int64_t rows, int K,
                      int ntok, int64_t out_stride, cudaStream_t s);

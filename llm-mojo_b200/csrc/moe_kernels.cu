@@ -889,8 +889,10 @@ __device__ __forceinline__ int block_excl_scan(int v, int* wsum, int* total) {
 
 // Pairs whose expert lies outside [e_lo, e_hi) are left out (expert
 // parallelism: this rank holds only those experts); their slots get no pair.
+// With tt_prefix, also the exclusive prefix of token tiles of BN tokens per
+// unique expert (the tensor-core work list), one launch fewer.
 __global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo,
-                                                 int e_hi, BucketOut o) {
+                                                 int e_hi, BucketOut o, int BN, int* tt_prefix) {
     pdl_wait();
     pdl_trigger();
     __shared__ int cnt[1024];
@@ -918,6 +920,12 @@ __global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t
         o.meta[0] = total_u;
         o.meta[1] = total_pairs;
     }
+    if (tt_prefix) {  // unique experts are numbered in thread (expert) order
+        int total_t = 0;
+        const int toff = block_excl_scan(c > 0 ? (c + BN - 1) / BN : 0, wsum, &total_t);
+        if (c > 0) tt_prefix[ui] = toff;
+        if (tid == 0) tt_prefix[total_u] = total_t;
+    }
     __syncthreads();
     for (int64_t p = tid; p < P; p += blockDim.x) {
         const int e = slot_expert[p];
@@ -933,8 +941,8 @@ __global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t
 }
 
 int launch_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo, int e_hi, const BucketOut& o,
-                  cudaStream_t s) {
-    launch_k(k_bucket, dim3(1), dim3(1024), 0, s, slot_expert, P, K, E, e_lo, e_hi, o);
+                  cudaStream_t s, int BN, int* tt_prefix) {
+    launch_k(k_bucket, dim3(1), dim3(1024), 0, s, slot_expert, P, K, E, e_lo, e_hi, o, BN, tt_prefix);
     return 1;
 }
 
