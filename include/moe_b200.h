@@ -93,7 +93,7 @@ enum moe_option {
     MOE_OPT_ROUTER_TC_MIN_TOKENS = 6, /* router on tensor cores from this many tokens (default 2048;
                                         below it the router runs in fp32 like the reference) */
     MOE_OPT_TC_STREAM = 7,         /* streaming tensor-core kernel for token tiles <= 64 and
-                                      K % 128 == 0: 0 never, 1 (default) expert GEMMs, 2 expert
+                                      K % 64 == 0: 0 never, 1 (default) expert GEMMs, 2 expert
                                       and dense GEMMs; else the general kernel */
     /* Expert parallelism: moe_layer_forward, moe_run_moe_coalesced_core and
        moe_run_diffusion_moe_experts_parallel evaluate only experts in
