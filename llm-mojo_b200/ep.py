@@ -61,3 +61,131 @@ class ExpertParallelLayer:
             d = out.shape[-1]
             self.ctx.rms_norm(out, post_norm_w, out, M, d)
         return out
+
+
+def expert_owner(e, world: int, num_experts: int):
+    """Rank owning expert id(s) `e` under expert_range (torch tensor of ids)."""
+    import torch
+    starts = torch.tensor([expert_range(r, world, num_experts)[0] for r in range(world)], device=e.device)
+    return torch.searchsorted(starts, e, right=True) - 1
+
+
+class AllToAllExpertParallelLayer:
+    """Expert parallelism with the tokens sharded over the ranks (the large-M
+    form: configs with thousands of routed tokens).  Each rank holds the
+    experts of expert_range(rank) and its own tokens; a layer step is:
+
+        route the local tokens -> send every routed (token, slot) row to the
+        rank that owns the slot's expert (all-to-all) -> evaluate the received
+        rows, one expert each -> send the results back (all-to-all) ->
+        per-token weighted sum over the token's slots, in slot order -> post-norm
+
+    The weighted sum runs at the token's home rank in slot order, as the
+    reference's per-token accumulation does (moe_kernels.mojo:775-779).
+
+    route_fn(x) -> (count [m], idx [m, K] global expert ids, w [m, K],
+    moe_in [m, d]) and experts_fn(rows [n, d], local_ids [n]) -> [n, d] (the
+    expert outputs, unweighted) are supplied by the caller: with the library
+    they are Context.route and Context.run_moe_coalesced_core over this
+    rank's weight slice (make_library_fns); the CPU tests pass the oracle.
+    """
+
+    def __init__(self, num_experts: int, route_fn, experts_fn, group=None, rms_norm_fn=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.E = num_experts
+        self.begin, self.end = expert_range(self.rank, self.world, num_experts)
+        self.route_fn = route_fn
+        self.experts_fn = experts_fn
+        self.rms_norm_fn = rms_norm_fn
+
+    def _exchange(self, send, send_counts, recv_counts):
+        import torch
+        recv = torch.empty((int(sum(recv_counts)),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
+        self.dist.all_to_all_single(recv, send.contiguous(), output_split_sizes=recv_counts,
+                                    input_split_sizes=send_counts, group=self.group)
+        return recv
+
+    def forward(self, x, post_norm_w=None):
+        """x: this rank's tokens [m, d] fp32 (m may be 0).  Returns [m, d]."""
+        import torch
+        count, idx, w, moe_in = self.route_fn(x)
+        m, K = idx.shape
+        d = moe_in.shape[1]
+        dev = moe_in.device
+        slot = torch.arange(K, device=dev).unsqueeze(0)
+        t_idx, k_idx = torch.nonzero(slot < count.unsqueeze(1), as_tuple=True)  # token order, slot order
+        e = idx[t_idx, k_idx].long()
+        dest = expert_owner(e, self.world, self.E)
+        dest_sorted, order = torch.sort(dest, stable=True)
+        send_counts = torch.bincount(dest_sorted, minlength=self.world)
+        recv_counts_t = torch.empty_like(send_counts)
+        self.dist.all_to_all_single(recv_counts_t, send_counts, group=self.group)
+        sc, rc = send_counts.tolist(), recv_counts_t.tolist()
+        starts = torch.tensor([expert_range(r, self.world, self.E)[0] for r in range(self.world)], device=dev)
+        rows = self._exchange(moe_in[t_idx[order]], sc, rc)
+        local_ids = self._exchange(e[order] - starts[dest_sorted], sc, rc)
+        y = self.experts_fn(rows, local_ids)
+        back = self._exchange(y, rc, sc)
+        y_pairs = torch.empty_like(back)
+        y_pairs[order] = back
+        out = torch.zeros((m, d), dtype=torch.float32, device=dev)
+        wp = w[t_idx, k_idx].to(torch.float32)
+        for k in range(K):  # slot order
+            sel = k_idx == k
+            if bool(sel.any()):
+                out.index_add_(0, t_idx[sel], y_pairs[sel] * wp[sel].unsqueeze(1))
+        if post_norm_w is not None:
+            if self.rms_norm_fn is not None:
+                self.rms_norm_fn(out, post_norm_w, out)
+            else:
+                out = out * torch.rsqrt((out * out).mean(1, keepdim=True) + 1e-6) * post_norm_w
+        return out
+
+
+def make_library_fns(ctx: "MB.Context", desc, layer: dict, rank: int, world: int):
+    """route_fn / experts_fn / rms_norm_fn for AllToAllExpertParallelLayer
+    over the library: routing with Context.route, the received rows through
+    Context.run_moe_coalesced_core (one active slot of weight 1 per row) with
+    the weights of this rank's experts, which the caller keeps resident."""
+    import torch
+    d, F, E, K = layer["d"], layer["F"], layer["E"], layer["top_k"]
+    lo, hi = expert_range(rank, world, E)
+    gu = d * F            # packed bytes of one expert's 2F x d gate/up rows
+    gs = 2 * F * d // 32  # its scales
+    dn = d * F // 2
+    ds = d * F // 32
+    gu_p = layer["gu_p"][lo * gu:hi * gu]
+    gu_s = layer["gu_s"][lo * gs:hi * gs]
+    dn_p = layer["dn_p"][lo * dn:hi * dn]
+    dn_s = layer["dn_s"][lo * ds:hi * ds]
+
+    def route_fn(x):
+        m = x.shape[0]
+        count = torch.empty(m, dtype=torch.int64, device=x.device)
+        idx = torch.empty((m, K), dtype=torch.int64, device=x.device)
+        w = torch.empty((m, K), dtype=torch.float32, device=x.device)
+        moe_in = torch.empty((m, d), dtype=torch.float32, device=x.device)
+        if m:
+            ctx.route(desc, m, x, count, idx, w, moe_in=moe_in)
+        return count, idx, w, moe_in
+
+    def experts_fn(rows, local_ids):
+        n = rows.shape[0]
+        out = torch.empty((n, d), dtype=torch.float32, device=rows.device)
+        if n:
+            cnt = torch.ones(n, dtype=torch.int64, device=rows.device)
+            wt = torch.ones((n, 1), dtype=torch.float32, device=rows.device)
+            ctx.run_moe_coalesced_core(n, gu_p, gu_s, dn_p, dn_s, rows.contiguous(), cnt,
+                                       local_ids.reshape(n, 1).contiguous(), wt, out, embed_dim=d,
+                                       expert_mlp_dim=F, num_experts=hi - lo, x_layout=MB.X_NATURAL, top_k=1)
+        return out
+
+    def rms_norm_fn(x, w, out):
+        if x.shape[0]:
+            ctx.rms_norm(x, w, out, x.shape[0], d)
+
+    return route_fn, experts_fn, rms_norm_fn

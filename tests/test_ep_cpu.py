@@ -96,3 +96,86 @@ def test_two_gloo_ranks_reproduce_the_full_layer():
         assert not isinstance(err, str), err
         assert err < 1e-6 and err_norm < 1e-5, (rank, err, err_norm)
     assert res[0][3] + res[1][3] > 0
+
+
+def _a2a_worker(rank, world, port, q, M):
+    """All-to-all expert parallelism on gloo ranks: tokens sharded over the
+    ranks, routed rows dispatched to the owners of their experts and the
+    results returned; route and expert evaluation by the oracle."""
+    try:
+        import torch
+        import torch.distributed as dist
+        import oracle as O
+        import datetime
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        d, F, E, K = 256, 64, 16, 4
+        L = O.make_layer(_layer(d, F, E, K, seed=21))
+        x_all = np.random.default_rng(22).standard_normal((M, d)).astype(np.float32)
+        t0, t1 = ep.row_range(rank, world, M)
+        x = x_all[t0:t1]
+        lo, hi = ep.expert_range(rank, world, E)
+
+        def route_fn(xt):
+            m = xt.shape[0]
+            if m == 0:
+                return (torch.zeros(0, dtype=torch.int64), torch.zeros((0, K), dtype=torch.int64),
+                        torch.zeros((0, K)), torch.zeros((0, d)))
+            r = O.route(L, xt.numpy())
+            return (torch.from_numpy(r["count"]), torch.from_numpy(r["idx"]), torch.from_numpy(r["w"]),
+                    torch.from_numpy(r["moe_in"]))
+
+        def experts_fn(rows, local_ids):
+            n = rows.shape[0]
+            if n == 0:
+                return torch.zeros((0, d))
+            idx = np.zeros((n, K), np.int64)
+            idx[:, 0] = local_ids.numpy() + lo
+            assert ((idx[:, 0] >= lo) & (idx[:, 0] < hi)).all()
+            wt = np.zeros((n, K), np.float32)
+            wt[:, 0] = 1.0
+            y = O.experts_forward(L, rows.numpy(), np.ones(n, np.int64), idx, wt, prec=O.F64)
+            return torch.from_numpy(y)
+
+        layer = ep.AllToAllExpertParallelLayer(E, route_fn, experts_fn)
+        ones = torch.ones(d)
+        out = layer.forward(torch.from_numpy(x), post_norm_w=ones).numpy()
+        ref, _, _, _ = O.layer_forward(L, x_all, post_norm=True, prec=O.F64)
+        err = float(np.max(np.abs(out - ref[t0:t1]))) if t1 > t0 else 0.0
+        dist.destroy_process_group()
+        q.put((rank, err, t1 - t0))
+    except Exception as e:  # reported to the parent
+        import traceback
+        q.put((rank, traceback.format_exc(), None))
+
+
+@pytest.mark.parametrize("world,M", [(2, 7), (3, 2)])
+def test_all_to_all_ranks_reproduce_the_full_layer(world, M):
+    """Uneven token shards (7 over 2 ranks; 2 over 3, one rank without
+    tokens): the dispatched, evaluated and combined output equals the
+    one-process layer."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_a2a_worker, args=(r, world, port, q, M)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err, m in res:
+        assert not isinstance(err, str), err
+        assert err < 1e-5, (rank, err)
+    assert sum(m for _, _, m in res) == M
+
+
+def test_expert_owner_matches_expert_range():
+    import torch
+    for world in (1, 2, 3, 8):
+        e = torch.arange(128)
+        own = ep.expert_owner(e, world, 128)
+        for r in range(world):
+            lo, hi = ep.expert_range(r, world, 128)
+            assert (own[lo:hi] == r).all()

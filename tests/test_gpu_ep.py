@@ -1,6 +1,7 @@
 """Expert parallelism on the GPU: the expert-range option of the library, the
-rms_norm entry point, and (with two or more GPUs) the NCCL all-reduce of
-partial outputs across ranks."""
+rms_norm entry point, and the two multi-rank forms over NCCL (all-reduce of
+partial outputs; all-to-all dispatch of routed rows), on one rank always and
+on two GPUs where the box has them."""
 import os
 import socket
 import subprocess
@@ -75,13 +76,14 @@ def _free_port():
     return port
 
 
-def test_two_gpu_expert_parallel_all_reduce():
+@pytest.mark.parametrize("nproc", [1, 2])
+def test_expert_parallel_ranks(nproc):
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < nproc:
+        pytest.skip(f"needs {nproc} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           f"--nproc-per-node={nproc}", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(HERE, "ep_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
