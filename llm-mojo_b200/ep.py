@@ -90,7 +90,7 @@ class AllToAllExpertParallelLayer:
     rank's weight slice (make_library_fns); the CPU tests pass the oracle.
     """
 
-    def __init__(self, num_experts: int, route_fn, experts_fn, group=None, rms_norm_fn=None):
+    def __init__(self, num_experts: int, route_fn, experts_fn, *, group=None, rms_norm_fn=None):
         import torch.distributed as dist
         self.dist = dist
         self.group = group

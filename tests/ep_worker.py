@@ -49,7 +49,8 @@ def main():
         # outputs have rms 1
         ok = ok and mx <= 5e-4 and rel <= 1e-4
     rank, world = dist.get_rank(), dist.get_world_size()
-    a2a = ep.AllToAllExpertParallelLayer(layer["E"], *ep.make_library_fns(ctx, desc, layer, rank, world))
+    route_fn, experts_fn, rms_norm_fn = ep.make_library_fns(ctx, desc, layer, rank, world)
+    a2a = ep.AllToAllExpertParallelLayer(layer["E"], route_fn, experts_fn, rms_norm_fn=rms_norm_fn)
     for M in (1, 64, 1000):
         x = synth.make_x(M, seed=70 + M)
         t0, t1 = ep.row_range(rank, world, M)

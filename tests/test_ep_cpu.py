@@ -179,3 +179,88 @@ def test_expert_owner_matches_expert_range():
         for r in range(world):
             lo, hi = ep.expert_range(r, world, 128)
             assert (own[lo:hi] == r).all()
+
+
+class _OracleCtx:
+    """Stands in for moe_b200.Context on CPU: the three calls make_library_fns
+    makes (route, run_moe_coalesced_core, rms_norm) evaluated by the oracle on
+    CPU tensors, with the library's argument meaning."""
+
+    def __init__(self, L):
+        self.L = L
+
+    def route(self, desc, M, x, count, idx, w, moe_in=None):
+        import oracle as O
+        import torch
+        r = O.route(self.L, x.numpy())
+        count.copy_(torch.from_numpy(r["count"]))
+        idx.copy_(torch.from_numpy(r["idx"]))
+        w.copy_(torch.from_numpy(r["w"]))
+        moe_in.copy_(torch.from_numpy(r["moe_in"]))
+
+    def run_moe_coalesced_core(self, n, gu_p, gu_s, dn_p, dn_s, rows, cnt, idx, wt, out, embed_dim,
+                               expert_mlp_dim, num_experts, x_layout, top_k):
+        import oracle as O
+        import torch
+        import moe_b200 as MB
+        assert x_layout == MB.X_NATURAL and top_k == 1
+        assert (idx >= 0).all() and (idx < num_experts).all()
+        sub = dict(d=embed_dim, F=expert_mlp_dim, E=num_experts, top_k=1,
+                   gu_p=np.ascontiguousarray(gu_p), gu_s=np.ascontiguousarray(gu_s),
+                   dn_p=np.ascontiguousarray(dn_p), dn_s=np.ascontiguousarray(dn_s))
+        for k in ("router_scale", "pre_norm_w", "post_norm_w"):
+            sub[k] = np.ones(embed_dim, np.float32)
+        sub["per_expert_scale"] = np.ones(num_experts, np.float32)
+        y = O.experts_forward(O.make_layer(sub), rows.numpy(), cnt.numpy(), idx.numpy(), wt.numpy(),
+                              prec=O.F64)
+        out.copy_(torch.from_numpy(y))
+
+    def rms_norm(self, x, w, out, M, d):
+        x64 = x.double()
+        out.copy_((x64 / (x64.pow(2).mean(1, keepdim=True) + 1e-6).sqrt() * w.double()).float())
+
+
+def _lib_worker(rank, world, port, q):
+    """make_library_fns' weight slices and calls, through the oracle stand-in."""
+    try:
+        import torch
+        import torch.distributed as dist
+        import oracle as O
+        import datetime
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        d, F, E, K, M = 256, 64, 16, 4, 9
+        w = _layer(d, F, E, K, seed=31)
+        L = O.make_layer(w)
+        x_all = np.random.default_rng(32).standard_normal((M, d)).astype(np.float32)
+        t0, t1 = ep.row_range(rank, world, M)
+        route_fn, experts_fn, rms_norm_fn = ep.make_library_fns(_OracleCtx(L), None, w, rank, world)
+        layer = ep.AllToAllExpertParallelLayer(E, route_fn, experts_fn, rms_norm_fn=rms_norm_fn)
+        out = layer.forward(torch.from_numpy(x_all[t0:t1].copy()), post_norm_w=torch.ones(d)).numpy()
+        ref, _, _, _ = O.layer_forward(L, x_all, post_norm=True, prec=O.F64)
+        err = float(np.max(np.abs(out - ref[t0:t1]))) if t1 > t0 else 0.0
+        dist.destroy_process_group()
+        q.put((rank, err, t1 - t0))
+    except Exception:  # reported to the parent
+        import traceback
+        q.put((rank, traceback.format_exc(), None))
+
+
+def test_all_to_all_library_functions_slice_the_weights():
+    """make_library_fns hands each rank's expert slice and local ids to the
+    coalesced core; with the oracle behind the calls, three ranks reproduce
+    the one-process layer."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_lib_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err, m in res:
+        assert not isinstance(err, str), err
+        assert err < 1e-5, (rank, err)

@@ -86,4 +86,4 @@ def test_expert_parallel_ranks(nproc):
            f"--nproc-per-node={nproc}", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(HERE, "ep_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
-    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[:3000]
