@@ -302,6 +302,91 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
                       void* out, int flags, int64_t* tok_active_count, int64_t* tok_active_idx,
                       float* tok_active_weights);
 
+/* ------------------------------------------ weights file, straight to HBM */
+/* The layer-blob file that convert_gemma4_moe.py:164-262 writes
+ * (gemma4_moe_weights_q4.bin): per layer, Q4_0 packed bytes of ten matrices
+ * in a fixed order, then their fp32 block scales in the same order, then
+ * twelve fp32 vectors, zero-padded to a multiple of 4096 bytes; layers follow
+ * each other with no header.  The reader's offsets are MoEConfig's
+ * get_layer_aligned_size / get_layer_offset / get_layer_weights
+ * (model_speculative_moe_batched.mojo:57-231).  The reference hard-codes the
+ * attention shapes (16 heads; head_dim 256 and 8 kv heads on sliding layers,
+ * 512 and 2 kv heads without v_proj on every sixth, global, layer); here they
+ * are fields of the configuration, with the reference's values as defaults. */
+typedef struct moe_model_config {
+    int64_t embed_dim;        /* 2816 */
+    int64_t standard_mlp_dim; /* 2112: the dense (shared) MLP */
+    int64_t expert_mlp_dim;   /* 704 */
+    int64_t num_experts;      /* 128 */
+    int64_t top_k;            /* 8 (copied into layer descriptors) */
+    int64_t num_layers;       /* 30 */
+    int64_t num_heads;        /* 16 */
+    int64_t head_dim_sliding, kv_heads_sliding; /* 256, 8 */
+    int64_t head_dim_global, kv_heads_global;   /* 512, 2 */
+    int64_t global_every;     /* 6: layer i is global when i % 6 == 5 (no v_proj) */
+} moe_model_config;
+
+/* The ten Q4_0 matrices of a layer, in file order. */
+enum moe_weight_matrix {
+    MOE_W_Q = 0, MOE_W_K, MOE_W_V, MOE_W_O, MOE_W_GATE, MOE_W_UP, MOE_W_DOWN, MOE_W_ROUTER,
+    MOE_W_EXPERTS_GATE_UP, MOE_W_EXPERTS_DOWN, MOE_W_COUNT
+};
+/* The twelve fp32 vectors of a layer, in file order. */
+enum moe_weight_vector {
+    MOE_V_INPUT_LAYERNORM = 0, MOE_V_POST_ATTENTION_LAYERNORM, MOE_V_PRE_FEEDFORWARD_LAYERNORM,
+    MOE_V_PRE_FEEDFORWARD_LAYERNORM_2, MOE_V_POST_FEEDFORWARD_LAYERNORM,
+    MOE_V_POST_FEEDFORWARD_LAYERNORM_1, MOE_V_POST_FEEDFORWARD_LAYERNORM_2, MOE_V_Q_NORM,
+    MOE_V_K_NORM, MOE_V_ROUTER_SCALE, MOE_V_ROUTER_PER_EXPERT_SCALE, MOE_V_LAYER_SCALAR,
+    MOE_V_COUNT
+};
+
+typedef struct moe_layer_layout {
+    int64_t layer_offset;  /* byte offset of the layer's blob in the file */
+    int64_t layer_bytes;   /* blob size, a multiple of 4096 */
+    int64_t payload_bytes; /* bytes before the zero padding */
+    int64_t is_global;
+    int64_t head_dim, kv_heads;
+    /* matrix m is rows[m] x cols[m] (cols = the inner dimension K; the expert
+       matrices stack all experts' rows: E*2F x d and E*d x F); rows 0 = absent */
+    int64_t rows[MOE_W_COUNT], cols[MOE_W_COUNT];
+    int64_t packed_offset[MOE_W_COUNT]; /* byte offsets within the blob */
+    int64_t scales_offset[MOE_W_COUNT];
+    int64_t vec_offset[MOE_V_COUNT];
+    int64_t vec_len[MOE_V_COUNT];       /* fp32 elements */
+} moe_layer_layout;
+
+/* Fills *cfg with the reference's MoEConfig defaults (Gemma-4 26B-A4B). */
+int moe_default_model_config(moe_model_config* cfg);
+/* Layout of layer `layer` (0 <= layer < num_layers).  MOE_E_SHAPE when a
+ * matrix's inner dimension is not a positive multiple of 32.  The
+ * router_per_expert_scale vector has num_experts elements, as the converter
+ * writes it (the reference reader reserves 128, the same for its model). */
+int moe_weights_layout(const moe_model_config* cfg, int64_t layer, moe_layer_layout* out);
+/* Size in bytes of the whole file (15311790080 for the defaults, the size
+ * model_speculative_moe_batched.mojo:1347 hard-codes). */
+int moe_weights_file_size(const moe_model_config* cfg, int64_t* bytes);
+/* The MoE layer descriptor of layer `layer` of a file image that starts at
+ * `weights_base` (device memory, or a registered host range), as
+ * get_layer_weights (model_speculative_moe_batched.mojo:121-231) hands the
+ * layer to run_moe_coalesced_subbatch: Q4_0 router, router_scale,
+ * router_per_expert_scale, pre_feedforward_layernorm_2 as pre-norm,
+ * post_feedforward_layernorm_2 as post-norm, the expert matrices;
+ * activation MOE_ACT_SIGMOID1702, r_scale_factor 1/sqrt(d), moe_top_p 1.
+ * Address arithmetic only: nothing is read. */
+int moe_layer_desc_from_weights(const moe_model_config* cfg, const void* weights_base,
+                                int64_t layer, moe_layer_desc* out);
+/* Reads bytes [file_offset, file_offset + bytes) of the file at `path` into
+ * device memory at `dst` (bytes < 0: to the end of the file), replacing the
+ * reference's read of the whole file into host RAM
+ * (model_speculative_moe_batched.mojo:1333-1380).  The file is read by
+ * several host threads into pinned staging buffers while earlier chunks
+ * copy to HBM on the context's stream.  Returns when the data is in place
+ * (also in asynchronous mode); *bytes_loaded (may be NULL) receives the
+ * count.  MOE_E_ARG: the file cannot be opened or read, or `dst` is not
+ * device memory; MOE_E_SHAPE: the range runs past the end of the file. */
+int moe_load_weights_file(moe_ctx* ctx, const char* path, int64_t file_offset, int64_t bytes,
+                          void* dst, int64_t* bytes_loaded);
+
 #ifdef __cplusplus
 }
 #endif

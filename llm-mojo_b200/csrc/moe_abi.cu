@@ -12,6 +12,8 @@
 #include <thread>
 #include <vector>
 
+#include <cuda.h>
+
 #include "../../include/moe_b200.h"
 #include "moe_internal.h"
 #include "moe_tc.h"
@@ -782,6 +784,45 @@ int moe_register_weights(moe_ctx* ctx, const void* host_base, size_t bytes) {
         return cuda_fail(ctx, e, "weight upload");
     }
     ctx->regs.push_back({h, bytes, d});
+    return MOE_OK;
+}
+
+int moe_load_weights_file(moe_ctx* ctx, const char* path, int64_t file_offset, int64_t bytes,
+                          void* dst, int64_t* bytes_loaded) {
+    TRY(begin(ctx));
+    if (bytes_loaded) *bytes_loaded = 0;
+    if (!path || !dst) return fail(ctx, MOE_E_ARG, "null pointer");
+    cudaPointerAttributes at;
+    cudaError_t e = cudaPointerGetAttributes(&at, dst);
+    if (e != cudaSuccess || at.type != cudaMemoryTypeDevice) {
+        cudaGetLastError();
+        return fail(ctx, MOE_E_ARG, "dst must be device memory");
+    }
+    // the copies must stay inside dst's allocation (driver call looked up
+    // through the runtime, so the library needs no link-time libcuda)
+    using RangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static RangeFn range_fn = nullptr;
+    if (!range_fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return fail(ctx, MOE_E_CUDA, "cuMemGetAddressRange not available");
+        range_fn = reinterpret_cast<RangeFn>(p);
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range_fn(&base, &size, (CUdeviceptr)dst) != CUDA_SUCCESS)
+        return fail(ctx, MOE_E_ARG, "dst is not inside a device allocation");
+    const int64_t capacity = (int64_t)(base + size - (CUdeviceptr)dst);
+    // work queued earlier on the stream (e.g. a kernel still reading the old
+    // contents of dst) runs before the copies, which are queued behind it
+    int64_t loaded = 0;
+    std::string err;
+    int s = moe::load_file_range(path, file_offset, bytes, static_cast<char*>(dst), capacity,
+                                 ctx->stream, err, &loaded);
+    if (s != MOE_OK) return fail(ctx, s, err);
+    if (bytes_loaded) *bytes_loaded = loaded;
     return MOE_OK;
 }
 

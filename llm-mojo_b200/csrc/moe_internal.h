@@ -5,7 +5,17 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace moe {
+
+// Reads [file_offset, file_offset + bytes) of `path` (bytes < 0: to the end)
+// into device memory `dst` of `dst_capacity` bytes through pinned staging
+// buffers and copies on `stream`; returns when the copies are complete.
+// MOE_E_ARG (open/read failure), MOE_E_SHAPE (range past the end of the file
+// or of the destination), MOE_E_NOMEM, MOE_E_CUDA; `err` gets the message.
+int load_file_range(const char* path, int64_t file_offset, int64_t bytes, char* dst,
+                    int64_t dst_capacity, cudaStream_t stream, std::string& err, int64_t* loaded);
 
 // Grouped Q4_0 GEMV over a device-side work list (see k_q4_gemv).
 struct GemvArgs {

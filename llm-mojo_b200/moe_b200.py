@@ -46,6 +46,8 @@ EXPORTS = [
     "moe_run_moe_experts_stage2", "moe_run_moe_coalesced_core",
     "moe_run_diffusion_moe_experts_parallel", "moe_route", "moe_layer_forward",
     "moe_q4_matmul_batchN_noalloc", "moe_rms_norm",
+    "moe_default_model_config", "moe_weights_layout", "moe_weights_file_size",
+    "moe_layer_desc_from_weights", "moe_load_weights_file",
 ]
 
 
@@ -84,6 +86,36 @@ class LayerDesc(C.Structure):
     ]
 
 
+W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_ROUTER, W_EXPERTS_GATE_UP, W_EXPERTS_DOWN = range(10)
+W_COUNT = 10
+WEIGHT_MATRICES = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj",
+                   "router", "experts_gate_up", "experts_down")
+(V_INPUT_LAYERNORM, V_POST_ATTENTION_LAYERNORM, V_PRE_FEEDFORWARD_LAYERNORM,
+ V_PRE_FEEDFORWARD_LAYERNORM_2, V_POST_FEEDFORWARD_LAYERNORM, V_POST_FEEDFORWARD_LAYERNORM_1,
+ V_POST_FEEDFORWARD_LAYERNORM_2, V_Q_NORM, V_K_NORM, V_ROUTER_SCALE, V_ROUTER_PER_EXPERT_SCALE,
+ V_LAYER_SCALAR) = range(12)
+V_COUNT = 12
+
+
+class ModelConfig(C.Structure):
+    """moe_model_config of include/moe_b200.h (MoEConfig,
+    model_speculative_moe_batched.mojo:41-63)."""
+    _fields_ = [(n, _i64) for n in (
+        "embed_dim", "standard_mlp_dim", "expert_mlp_dim", "num_experts", "top_k", "num_layers",
+        "num_heads", "head_dim_sliding", "kv_heads_sliding", "head_dim_global", "kv_heads_global",
+        "global_every")]
+
+
+class LayerLayout(C.Structure):
+    """moe_layer_layout of include/moe_b200.h: where each tensor of one layer
+    sits in the weights file (offsets within the layer's blob)."""
+    _fields_ = [("layer_offset", _i64), ("layer_bytes", _i64), ("payload_bytes", _i64),
+                ("is_global", _i64), ("head_dim", _i64), ("kv_heads", _i64),
+                ("rows", _i64 * W_COUNT), ("cols", _i64 * W_COUNT),
+                ("packed_offset", _i64 * W_COUNT), ("scales_offset", _i64 * W_COUNT),
+                ("vec_offset", _i64 * V_COUNT), ("vec_len", _i64 * V_COUNT)]
+
+
 def _declare(L):
     L.moe_ctx_create.argtypes = [_int, C.POINTER(_p)]
     L.moe_ctx_destroy.argtypes = [_p]
@@ -117,6 +149,11 @@ def _declare(L):
                                                          _i64, _i64, _i64, _int]
     L.moe_route.argtypes = [_p, C.POINTER(LayerDesc), _i64, _p, _int, _p, _p, _p, _p, _p, _p, _p]
     L.moe_layer_forward.argtypes = [_p, C.POINTER(LayerDesc), _i64, _p, _p, _int, _p, _p, _p]
+    L.moe_default_model_config.argtypes = [C.POINTER(ModelConfig)]
+    L.moe_weights_layout.argtypes = [C.POINTER(ModelConfig), _i64, C.POINTER(LayerLayout)]
+    L.moe_weights_file_size.argtypes = [C.POINTER(ModelConfig), C.POINTER(_i64)]
+    L.moe_layer_desc_from_weights.argtypes = [C.POINTER(ModelConfig), _p, _i64, C.POINTER(LayerDesc)]
+    L.moe_load_weights_file.argtypes = [_p, C.c_char_p, _i64, _i64, _p, C.POINTER(_i64)]
     for name in EXPORTS:
         if name not in ("moe_last_error", "moe_kernel_launches"):
             getattr(L, name).restype = _int
@@ -335,6 +372,16 @@ class Context:
                                       _addr(tok_active_idx), _addr(tok_active_weights),
                                       _addr(moe_in)))
 
+    def load_weights_file(self, path: str, dst, file_offset: int = 0, nbytes: int = -1) -> int:
+        """Reads bytes [file_offset, file_offset + nbytes) of the weights file
+        into the device buffer `dst` (nbytes -1: to the end of the file);
+        replaces the host-RAM load of model_speculative_moe_batched.mojo:1333-1380.
+        Returns the byte count."""
+        n = _i64(0)
+        self.check(self.lib.moe_load_weights_file(self.h, os.fsencode(path), file_offset, nbytes,
+                                                  _addr(dst), C.byref(n)))
+        return int(n.value)
+
     def layer_forward(self, desc: LayerDesc, M, x, out, flags=F_POST_NORM, tok_active_count=None,
                       tok_active_idx=None, tok_active_weights=None):
         """run_moe_coalesced_subbatch, model_speculative_moe_batched.mojo:1155-1204, any M."""
@@ -367,3 +414,62 @@ def make_desc(w: dict, act=ACT_SIGMOID1702, top_p=1.0, r_scale_factor=None, bias
     d.down_scales = _addr(w["dn_s"])
     d._keep = (w, bias)
     return d
+
+
+def _status(rc: int, what: str):
+    if rc != 0:
+        raise MoeError(rc, what)
+
+
+def default_model_config(**overrides) -> ModelConfig:
+    """MoEConfig's defaults (model_speculative_moe_batched.mojo:41-63), with
+    any field replaced by keyword."""
+    cfg = ModelConfig()
+    _status(load_library().moe_default_model_config(C.byref(cfg)), "moe_default_model_config")
+    for k, v in overrides.items():
+        if k not in dict(ModelConfig._fields_):
+            raise TypeError(f"unknown model config field {k}")
+        setattr(cfg, k, int(v))
+    return cfg
+
+
+def weights_layout(cfg: ModelConfig, layer: int) -> LayerLayout:
+    """Offsets of layer `layer`'s tensors in the weights file
+    (get_layer_offset / get_layer_weights, model_speculative_moe_batched.mojo:113-231)."""
+    out = LayerLayout()
+    _status(load_library().moe_weights_layout(C.byref(cfg), layer, C.byref(out)),
+            f"moe_weights_layout(layer={layer})")
+    return out
+
+
+def weights_file_size(cfg: ModelConfig) -> int:
+    n = _i64(0)
+    _status(load_library().moe_weights_file_size(C.byref(cfg), C.byref(n)), "moe_weights_file_size")
+    return int(n.value)
+
+
+def layer_desc_from_weights(cfg: ModelConfig, weights_base, layer: int) -> LayerDesc:
+    """The MoE layer descriptor of layer `layer` of a weights-file image at
+    `weights_base` (a device tensor or an address); keeps the image alive."""
+    d = LayerDesc()
+    _status(load_library().moe_layer_desc_from_weights(C.byref(cfg), _addr(weights_base), layer,
+                                                       C.byref(d)),
+            f"moe_layer_desc_from_weights(layer={layer})")
+    d._keep = weights_base
+    return d
+
+
+def load_weights_file(ctx: Context, path: str, cfg: ModelConfig | None = None, device=None):
+    """Loads the whole weights file into one device buffer and returns
+    (buffer, [LayerDesc per layer]): the B200 counterpart of the model's
+    start-up load (model_speculative_moe_batched.mojo:1333-1387).  The file
+    size must match the configuration."""
+    import torch
+    cfg = cfg if cfg is not None else default_model_config()
+    size = weights_file_size(cfg)
+    if os.path.getsize(path) != size:
+        raise MoeError(2, f"{path} holds {os.path.getsize(path)} bytes; the configuration needs {size}")
+    buf = torch.empty(size, dtype=torch.uint8, device=device if device is not None else f"cuda:{ctx.device}")
+    n = ctx.load_weights_file(path, buf)
+    assert n == size
+    return buf, [layer_desc_from_weights(cfg, buf, layer) for layer in range(cfg.num_layers)]
