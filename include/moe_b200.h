@@ -106,8 +106,10 @@ enum moe_option {
     MOE_OPT_FUSED_ROUTE = 10,      /* 1: moe_layer_forward routes batches of <= 16 tokens (Q4_0
                                       router, LOD routing) in one fused cluster launch; 0 (default):
                                       the separate norm / router / top-k / bucket / gather kernels */
-    MOE_OPT_DENSE_KSPLIT = 11      /* dense tensor-core GEMMs: split K into this many partial sums
+    MOE_OPT_DENSE_KSPLIT = 11,     /* dense tensor-core GEMMs: split K into this many partial sums
                                       (0, the default: enough work items for two per SM) */
+    MOE_OPT_EP_TIMEOUT_NS = 12     /* deadline of every host wait on the expert-parallel
+                                      communicator (set-up, collectives; default 30 s) */
 };
 enum moe_gemm_path {
     MOE_PATH_AUTO = 0, /* CUDA-core GEMV for few tokens, tensor cores above the threshold */
@@ -386,6 +388,34 @@ int moe_layer_desc_from_weights(const moe_model_config* cfg, const void* weights
  * device memory; MOE_E_SHAPE: the range runs past the end of the file. */
 int moe_load_weights_file(moe_ctx* ctx, const char* path, int64_t file_offset, int64_t bytes,
                           void* dst, int64_t* bytes_loaded);
+
+/* ------------------------------------------------ expert parallelism (NCCL) */
+/* No counterpart in the reference (a single process on one machine); the
+ * multi-GPU form of run_moe_coalesced_subbatch for a host that drives the
+ * library through this ABI alone.  One process (and context) per GPU. */
+#define MOE_EP_UNIQUE_ID_BYTES 128
+/* Creates the communicator id on one rank; the host passes the 128 bytes to
+ * every rank by its own means (a file, a socket, its launcher). */
+int moe_ep_get_unique_id(uint8_t* id);
+/* Joins the communicator of `nranks` ranks as `rank`.  Returns when all
+ * ranks joined, MOE_E_TIMEOUT (communicator aborted) when they have not
+ * within MOE_OPT_EP_TIMEOUT_NS, MOE_E_NCCL when NCCL cannot be loaded or
+ * fails, MOE_E_STATE when the context already has a communicator.  From then
+ * on moe_layer_forward evaluates the experts [rank*E/N, (rank+1)*E/N) only,
+ * sums the partial outputs of all ranks in place (NCCL all-reduce on the
+ * context's stream) and applies MOE_F_POST_NORM to the sum: every rank passes
+ * the same M tokens and receives the whole layer's output.  Every rank must
+ * make the same moe_layer_forward calls in the same order.  Output must be
+ * fp32 (MOE_F_FP16_OUT is refused), num_experts >= nranks, and the
+ * MOE_OPT_EXPERT_BEGIN/END options are ignored meanwhile.  Host waits on a
+ * call with a collective (completion of a synchronous call, moe_wait) give
+ * up after MOE_OPT_EP_TIMEOUT_NS or on an NCCL error: the communicator is
+ * then aborted and the call returns MOE_E_TIMEOUT / MOE_E_NCCL; the context
+ * stays usable without it. */
+int moe_ep_init(moe_ctx* ctx, const uint8_t* id, int rank, int nranks);
+/* Leaves the communicator (after completing enqueued work); the context
+ * evaluates all experts again.  MOE_OK also when there was none. */
+int moe_ep_finalize(moe_ctx* ctx);
 
 #ifdef __cplusplus
 }

@@ -77,6 +77,9 @@ struct moe_ctx {
     std::vector<std::string> prof_names;
     std::vector<double> prof_ms;
     std::vector<uint64_t> prof_cnt;
+    moe::FileStaging file_staging;       // moe_load_weights_file's pinned buffers
+    moe::EpComm ep;                      // moe_ep_init's communicator
+    uint64_t ep_timeout_ns = 30000000000ull;  // MOE_OPT_EP_TIMEOUT_NS
 };
 
 namespace {
@@ -244,7 +247,13 @@ int finish(moe_ctx* ctx) {
     ctx->pending.clear();
     MOE_CUDA(cudaEventRecord(ctx->done, ctx->stream));
     if (!ctx->async_mode) {
-        MOE_CUDA(cudaEventSynchronize(ctx->done));
+        if (ctx->ep.pending) {  // a collective: bounded wait that also watches NCCL
+            std::string err;
+            const int st = moe::ep_wait(ctx->ep, ctx->done, ctx->ep_timeout_ns, true, err);
+            if (st != MOE_OK) return fail(ctx, st, err);
+        } else {
+            MOE_CUDA(cudaEventSynchronize(ctx->done));
+        }
         return check_flag(ctx);
     }
     return MOE_OK;
@@ -613,6 +622,11 @@ int moe_ctx_create(int device, moe_ctx** out) {
 int moe_ctx_destroy(moe_ctx* ctx) {
     if (!ctx) return MOE_E_ARG;
     cudaSetDevice(ctx->device);
+    if (ctx->ep.comm) {  // complete (or abort) collectives before the stream wait below
+        std::string err;
+        cudaEventRecord(ctx->done, ctx->stream);
+        if (moe::ep_wait(ctx->ep, ctx->done, ctx->ep_timeout_ns, true, err) == MOE_OK) moe::ep_destroy(ctx->ep);
+    }
     cudaStreamSynchronize(ctx->stream);
     for (Reg& r : ctx->regs) cudaFree(r.dev);
     if (ctx->ws) cudaFree(ctx->ws);
@@ -623,6 +637,7 @@ int moe_ctx_destroy(moe_ctx* ctx) {
         cudaEventDestroy(r.b);
     }
     for (cudaEvent_t e : ctx->ev_pool) cudaEventDestroy(e);
+    ctx->file_staging.release();
     if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
     return MOE_OK;
@@ -657,6 +672,16 @@ int moe_set_async(moe_ctx* ctx, int async_mode) {
 int moe_wait(moe_ctx* ctx, uint64_t timeout_ns) {
     if (!ctx) return MOE_E_ARG;
     cudaSetDevice(ctx->device);
+    if (ctx->ep.pending) {
+        // enqueued collectives: the caller's deadline (or, without one, the
+        // communicator's), watching NCCL's asynchronous error meanwhile; only
+        // the communicator's own deadline aborts it
+        const bool own = timeout_ns == 0 || timeout_ns >= ctx->ep_timeout_ns;
+        std::string err;
+        const int st = moe::ep_wait(ctx->ep, ctx->done, own ? ctx->ep_timeout_ns : timeout_ns, own, err);
+        if (st != MOE_OK) return fail(ctx, st, err);
+        return check_flag(ctx);
+    }
     const auto t0 = std::chrono::steady_clock::now();
     for (;;) {
         cudaError_t e = cudaEventQuery(ctx->done);
@@ -706,6 +731,10 @@ int moe_set_option(moe_ctx* ctx, int option, int64_t value) {
         case MOE_OPT_EXPERT_END:
             if (value < 0) return fail(ctx, MOE_E_ARG, "bad expert index");
             ctx->expert_end = value;
+            return MOE_OK;
+        case MOE_OPT_EP_TIMEOUT_NS:
+            if (value <= 0) return fail(ctx, MOE_E_ARG, "bad timeout");
+            ctx->ep_timeout_ns = (uint64_t)value;
             return MOE_OK;
         case MOE_OPT_FUSED_ROUTE:
             ctx->fused_route = value != 0;
@@ -820,7 +849,7 @@ int moe_load_weights_file(moe_ctx* ctx, const char* path, int64_t file_offset, i
     int64_t loaded = 0;
     std::string err;
     int s = moe::load_file_range(path, file_offset, bytes, static_cast<char*>(dst), capacity,
-                                 ctx->stream, err, &loaded);
+                                 ctx->stream, ctx->file_staging, err, &loaded);
     if (s != MOE_OK) return fail(ctx, s, err);
     if (bytes_loaded) *bytes_loaded = loaded;
     return MOE_OK;
@@ -1416,6 +1445,26 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
     if (!x || !out) return fail(ctx, MOE_E_ARG, "null pointer");
     if (M <= 0) return fail(ctx, MOE_E_SHAPE, "M must be >= 1");
     const int64_t d = L->embed_dim, E = L->num_experts, K = L->top_k, F = L->expert_mlp_dim;
+    // expert parallelism (moe_ep_init): this rank's experts for the call
+    const bool ep = ctx->ep.comm != nullptr;
+    if (ep) {
+        if (flags & MOE_F_FP16_OUT)
+            return fail(ctx, MOE_E_ARG, "expert parallelism sums fp32 partial outputs: MOE_F_FP16_OUT not supported");
+        if (E < ctx->ep.nranks) return fail(ctx, MOE_E_SHAPE, "num_experts must be >= the number of ranks");
+    }
+    struct RangeScope {  // the option values come back on every exit
+        moe_ctx* c;
+        int64_t b, e;
+        RangeScope(moe_ctx* ctx_, bool on, int64_t E_) : c(ctx_), b(ctx_->expert_begin), e(ctx_->expert_end) {
+            if (!on) return;
+            c->expert_begin = (int64_t)c->ep.rank * E_ / c->ep.nranks;
+            c->expert_end = (int64_t)(c->ep.rank + 1) * E_ / c->ep.nranks;
+        }
+        ~RangeScope() {
+            c->expert_begin = b;
+            c->expert_end = e;
+        }
+    } range_scope(ctx, ep, E);
     const int64_t P = M * K;
     const size_t out_bytes = M * d * ((flags & MOE_F_FP16_OUT) ? 2 : 4);
     TRY(ws_reserve(ctx, layer_small_bytes(L) + expert_bufs_bytes(M, K, d, F, E) +
@@ -1481,11 +1530,57 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
         bb.x32q_ready = cc;
     }
     moe::CombineArgs c;
-    c.post_norm = (flags & MOE_F_POST_NORM) ? 1 : 0;
+    c.post_norm = (!ep && (flags & MOE_F_POST_NORM)) ? 1 : 0;
     c.post_w = ld.post_w;
     c.out_f16 = (flags & MOE_F_FP16_OUT) ? 1 : 0;
     TRY(run_experts(ctx, ld.w, M, K, d, F, E, L->activation, bb, &c, od, fused));
+    if (ep) {
+        // sum of the ranks' partial outputs, then the post-norm of the sum
+        std::string err;
+        const int st = moe::ep_all_reduce(ctx->ep, (float*)od, (size_t)(M * d), ctx->stream, ctx->ep_timeout_ns, err);
+        if (st != MOE_OK) return fail(ctx, st, err);
+        if (flags & MOE_F_POST_NORM) {
+            moe::PrepArgs pa;
+            pa.x = od;
+            pa.K = d;
+            pa.norm = 1;
+            pa.pre_w = ld.post_w;
+            pa.out = (float*)od;
+            ProfScope ps(ctx, "rms_norm");
+            ctx->launches += moe::launch_prep(pa, M, ctx->stream);
+        }
+    }
     return finish(ctx);
+}
+
+int moe_ep_get_unique_id(uint8_t* id) {
+    if (!id) return MOE_E_ARG;
+    std::string err;
+    const int st = moe::ep_unique_id(id, err);
+    if (st != MOE_OK) std::fprintf(stderr, "moe_ep_get_unique_id: %s\n", err.c_str());
+    return st;
+}
+
+int moe_ep_init(moe_ctx* ctx, const uint8_t* id, int rank, int nranks) {
+    TRY(begin(ctx));
+    if (!id) return fail(ctx, MOE_E_ARG, "null communicator id");
+    if (nranks < 1 || rank < 0 || rank >= nranks) return fail(ctx, MOE_E_ARG, "bad rank or rank count");
+    if (ctx->ep.comm) return fail(ctx, MOE_E_STATE, "the context already has a communicator");
+    std::string err;
+    const int st = moe::ep_init(ctx->ep, id, rank, nranks, ctx->ep_timeout_ns, err);
+    if (st != MOE_OK) return fail(ctx, st, err);
+    return MOE_OK;
+}
+
+int moe_ep_finalize(moe_ctx* ctx) {
+    TRY(begin(ctx));
+    if (!ctx->ep.comm) return MOE_OK;
+    std::string err;
+    MOE_CUDA(cudaEventRecord(ctx->done, ctx->stream));
+    const int st = moe::ep_wait(ctx->ep, ctx->done, ctx->ep_timeout_ns, true, err);
+    if (st != MOE_OK) return fail(ctx, st, err);
+    moe::ep_destroy(ctx->ep);
+    return MOE_OK;
 }
 
 }  // extern "C"

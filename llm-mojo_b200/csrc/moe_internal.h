@@ -6,16 +6,46 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 namespace moe {
 
+// NCCL communicator of a context (moe_ep.cu).  `pending`: a collective was
+// enqueued and its completion has not been observed yet.
+struct EpComm {
+    void* comm = nullptr;
+    int rank = 0, nranks = 0;
+    bool pending = false;
+};
+int ep_unique_id(uint8_t* out, std::string& err);
+// Joins the communicator; polls its set-up until `timeout_ns` (then aborts).
+int ep_init(EpComm& ep, const uint8_t* id, int rank, int nranks, uint64_t timeout_ns, std::string& err);
+// In-place fp32 sum over the ranks, enqueued on `s`.
+int ep_all_reduce(EpComm& ep, float* buf, size_t count, cudaStream_t s, uint64_t timeout_ns, std::string& err);
+// Waits for `done` (recorded after a collective), checking the communicator's
+// asynchronous error; aborts the communicator on an error, and after
+// `timeout_ns` when `abort_on_timeout`.
+int ep_wait(EpComm& ep, cudaEvent_t done, uint64_t timeout_ns, bool abort_on_timeout, std::string& err);
+void ep_abort(EpComm& ep);
+void ep_destroy(EpComm& ep);
+
+// Pinned staging buffers of the weights-file reader; a context keeps them
+// between loads and releases them when it is destroyed.
+struct FileStaging {
+    std::vector<char*> buf;
+    std::vector<cudaEvent_t> ev;
+    int64_t buf_bytes = 0;
+    void release();
+};
+
 // Reads [file_offset, file_offset + bytes) of `path` (bytes < 0: to the end)
-// into device memory `dst` of `dst_capacity` bytes through pinned staging
+// into device memory `dst` of `dst_capacity` bytes through the staging
 // buffers and copies on `stream`; returns when the copies are complete.
 // MOE_E_ARG (open/read failure), MOE_E_SHAPE (range past the end of the file
 // or of the destination), MOE_E_NOMEM, MOE_E_CUDA; `err` gets the message.
 int load_file_range(const char* path, int64_t file_offset, int64_t bytes, char* dst,
-                    int64_t dst_capacity, cudaStream_t stream, std::string& err, int64_t* loaded);
+                    int64_t dst_capacity, cudaStream_t stream, FileStaging& st, std::string& err,
+                    int64_t* loaded);
 
 // Grouped Q4_0 GEMV over a device-side work list (see k_q4_gemv).
 struct GemvArgs {

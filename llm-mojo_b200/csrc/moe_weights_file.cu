@@ -13,12 +13,14 @@
 //
 // Reader: the reference reads the 14.3 GB file into host RAM in 256 MB
 // chunks with one thread (:1366-1380) and the GPU then reads host memory.
-// Here the bytes go to HBM once: the file range is cut into chunks of
+// Here the bytes go to HBM once: the file range is cut into chunks of up to
 // kChunk bytes; each chunk is read by kThreads host threads (pread on
 // disjoint slices) into one of kBufs pinned buffers, and copied to the
 // device with cudaMemcpyAsync on the caller's stream while the next chunk
 // is being read.  A buffer is reused only after the event recorded behind
-// its previous copy has completed.
+// its previous copy has completed.  The pinned buffers belong to the
+// context and are kept between calls (pinning costs about as much as the
+// copies of a small file).
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <sys/stat.h>
@@ -115,10 +117,21 @@ int read_full(int fd, char* dst, int64_t n, int64_t pos) {
 
 namespace moe {
 
+void FileStaging::release() {
+    for (cudaEvent_t e : ev)
+        if (e) cudaEventDestroy(e);
+    for (char* b : buf)
+        if (b) cudaFreeHost(b);
+    ev.clear();
+    buf.clear();
+    buf_bytes = 0;
+}
+
 int load_file_range(const char* path, int64_t file_offset, int64_t bytes, char* dst,
-                    int64_t dst_capacity, cudaStream_t stream, std::string& err, int64_t* loaded) {
-    constexpr int64_t kChunk = 64ll << 20;  // bytes per staging buffer
-    constexpr int kBufs = 3;
+                    int64_t dst_capacity, cudaStream_t stream, FileStaging& st, std::string& err,
+                    int64_t* loaded) {
+    constexpr int64_t kChunk = 32ll << 20;  // largest staging buffer
+    constexpr int kBufs = 4;
     const int kThreads = std::max(1u, std::min(8u, std::thread::hardware_concurrency()));
     *loaded = 0;
     int fd = open(path, O_RDONLY | O_CLOEXEC);
@@ -126,13 +139,13 @@ int load_file_range(const char* path, int64_t file_offset, int64_t bytes, char* 
         err = std::string("cannot open ") + path + ": " + std::strerror(errno);
         return MOE_E_ARG;
     }
-    struct stat st;
-    if (fstat(fd, &st) != 0) {
+    struct stat sb;
+    if (fstat(fd, &sb) != 0) {
         err = std::string("cannot stat ") + path + ": " + std::strerror(errno);
         close(fd);
         return MOE_E_ARG;
     }
-    const int64_t size = st.st_size;
+    const int64_t size = sb.st_size;
     if (bytes < 0) bytes = size - file_offset;
     if (file_offset < 0 || bytes < 0 || file_offset + bytes > size) {
         err = std::string(path) + " holds " + std::to_string(size) + " bytes; requested [" +
@@ -151,34 +164,44 @@ int load_file_range(const char* path, int64_t file_offset, int64_t bytes, char* 
         return MOE_OK;
     }
     posix_fadvise(fd, file_offset, bytes, POSIX_FADV_SEQUENTIAL);
-    const int nbuf = (int)std::min<int64_t>(kBufs, (bytes + kChunk - 1) / kChunk);
-    const int64_t buf_bytes = std::min(kChunk, bytes);
-    std::vector<char*> buf(nbuf, nullptr);
-    std::vector<cudaEvent_t> ev(nbuf, nullptr);
-    std::vector<bool> in_flight(nbuf, false);
+    // staging: kBufs pinned buffers of up to kChunk bytes, grown on demand
+    const int64_t want = std::min(kChunk, (bytes + (1 << 20) - 1) >> 20 << 20);
     int status = MOE_OK;
     auto cuda_err = [&](cudaError_t e, const char* where) {
         err = std::string(where) + ": " + cudaGetErrorString(e);
         status = MOE_E_CUDA;
     };
-    for (int b = 0; b < nbuf && status == MOE_OK; ++b) {
-        cudaError_t e = cudaHostAlloc((void**)&buf[b], (size_t)buf_bytes, cudaHostAllocDefault);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            buf[b] = nullptr;
-            err = "pinned staging allocation failed";
-            status = MOE_E_NOMEM;
-            break;
+    if (st.buf_bytes < want) {
+        st.release();
+        st.buf.assign(kBufs, nullptr);
+        st.ev.assign(kBufs, nullptr);
+        for (int b = 0; b < kBufs && status == MOE_OK; ++b) {
+            cudaError_t e = cudaHostAlloc((void**)&st.buf[b], (size_t)want, cudaHostAllocDefault);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                st.buf[b] = nullptr;
+                err = "pinned staging allocation failed";
+                status = MOE_E_NOMEM;
+                break;
+            }
+            e = cudaEventCreateWithFlags(&st.ev[b], cudaEventDisableTiming);
+            if (e != cudaSuccess) cuda_err(e, "cudaEventCreateWithFlags");
         }
-        e = cudaEventCreateWithFlags(&ev[b], cudaEventDisableTiming);
-        if (e != cudaSuccess) cuda_err(e, "cudaEventCreateWithFlags");
+        if (status != MOE_OK) {
+            st.release();
+            close(fd);
+            return status;
+        }
+        st.buf_bytes = want;
     }
+    const int64_t chunk_bytes = st.buf_bytes;
+    std::vector<bool> in_flight(kBufs, false);
     int64_t done = 0;
     for (int64_t chunk = 0; status == MOE_OK && done < bytes; ++chunk) {
-        const int b = (int)(chunk % nbuf);
-        const int64_t n = std::min(kChunk, bytes - done);
+        const int b = (int)(chunk % kBufs);
+        const int64_t n = std::min(chunk_bytes, bytes - done);
         if (in_flight[b]) {
-            cudaError_t e = cudaEventSynchronize(ev[b]);
+            cudaError_t e = cudaEventSynchronize(st.ev[b]);
             if (e != cudaSuccess) {
                 cuda_err(e, "cudaEventSynchronize");
                 break;
@@ -192,7 +215,7 @@ int load_file_range(const char* path, int64_t file_offset, int64_t bytes, char* 
             const int64_t lo = t * slice, hi = std::min(n, lo + slice);
             if (lo >= hi) break;
             pool.emplace_back([&, t, lo, hi] {
-                rc[t] = read_full(fd, buf[b] + lo, hi - lo, file_offset + done + lo);
+                rc[t] = read_full(fd, st.buf[b] + lo, hi - lo, file_offset + done + lo);
             });
         }
         for (auto& th : pool) th.join();
@@ -204,12 +227,12 @@ int load_file_range(const char* path, int64_t file_offset, int64_t bytes, char* 
                 break;
             }
         if (status != MOE_OK) break;
-        cudaError_t e = cudaMemcpyAsync(dst + done, buf[b], (size_t)n, cudaMemcpyHostToDevice, stream);
+        cudaError_t e = cudaMemcpyAsync(dst + done, st.buf[b], (size_t)n, cudaMemcpyHostToDevice, stream);
         if (e != cudaSuccess) {
             cuda_err(e, "cudaMemcpyAsync");
             break;
         }
-        e = cudaEventRecord(ev[b], stream);
+        e = cudaEventRecord(st.ev[b], stream);
         if (e != cudaSuccess) {
             cuda_err(e, "cudaEventRecord");
             break;
@@ -217,17 +240,13 @@ int load_file_range(const char* path, int64_t file_offset, int64_t bytes, char* 
         in_flight[b] = true;
         done += n;
     }
-    // every copy that was issued completes before its buffer is released
-    for (int b = 0; b < nbuf; ++b) {
-        if (ev[b]) {
-            if (in_flight[b]) {
-                cudaError_t e = cudaEventSynchronize(ev[b]);
-                if (e != cudaSuccess && status == MOE_OK) cuda_err(e, "cudaEventSynchronize");
-            }
-            cudaEventDestroy(ev[b]);
+    // every copy that was issued completes before the call returns, so the
+    // buffers are idle between calls
+    for (int b = 0; b < kBufs; ++b)
+        if (in_flight[b]) {
+            cudaError_t e = cudaEventSynchronize(st.ev[b]);
+            if (e != cudaSuccess && status == MOE_OK) cuda_err(e, "cudaEventSynchronize");
         }
-        if (buf[b]) cudaFreeHost(buf[b]);
-    }
     close(fd);
     if (status == MOE_OK) *loaded = done;
     return status;

@@ -28,6 +28,8 @@ OPT_TC_STREAM = 7
 OPT_EXPERT_BEGIN, OPT_EXPERT_END = 8, 9
 OPT_FUSED_ROUTE = 10
 OPT_DENSE_KSPLIT = 11
+OPT_EP_TIMEOUT_NS = 12
+EP_UNIQUE_ID_BYTES = 128
 PATH_AUTO, PATH_GEMV, PATH_TC = 0, 1, 2
 
 STATUS = {0: "MOE_OK", 1: "MOE_E_ARG", 2: "MOE_E_SHAPE", 3: "MOE_E_UNREGISTERED",
@@ -48,6 +50,7 @@ EXPORTS = [
     "moe_q4_matmul_batchN_noalloc", "moe_rms_norm",
     "moe_default_model_config", "moe_weights_layout", "moe_weights_file_size",
     "moe_layer_desc_from_weights", "moe_load_weights_file",
+    "moe_ep_get_unique_id", "moe_ep_init", "moe_ep_finalize",
 ]
 
 
@@ -154,6 +157,9 @@ def _declare(L):
     L.moe_weights_file_size.argtypes = [C.POINTER(ModelConfig), C.POINTER(_i64)]
     L.moe_layer_desc_from_weights.argtypes = [C.POINTER(ModelConfig), _p, _i64, C.POINTER(LayerDesc)]
     L.moe_load_weights_file.argtypes = [_p, C.c_char_p, _i64, _i64, _p, C.POINTER(_i64)]
+    L.moe_ep_get_unique_id.argtypes = [_p]
+    L.moe_ep_init.argtypes = [_p, _p, _int, _int]
+    L.moe_ep_finalize.argtypes = [_p]
     for name in EXPORTS:
         if name not in ("moe_last_error", "moe_kernel_launches"):
             getattr(L, name).restype = _int
@@ -372,6 +378,18 @@ class Context:
                                       _addr(tok_active_idx), _addr(tok_active_weights),
                                       _addr(moe_in)))
 
+    def ep_init(self, unique_id: bytes, rank: int, nranks: int):
+        """Joins an NCCL communicator (moe_ep_init): from then on
+        layer_forward evaluates this rank's experts, sums the ranks' partial
+        outputs and applies the post-norm to the sum."""
+        if len(unique_id) != EP_UNIQUE_ID_BYTES:
+            raise ValueError("the communicator id has 128 bytes")
+        buf = C.create_string_buffer(bytes(unique_id), EP_UNIQUE_ID_BYTES)
+        self.check(self.lib.moe_ep_init(self.h, C.addressof(buf), rank, nranks))
+
+    def ep_finalize(self):
+        self.check(self.lib.moe_ep_finalize(self.h))
+
     def load_weights_file(self, path: str, dst, file_offset: int = 0, nbytes: int = -1) -> int:
         """Reads bytes [file_offset, file_offset + nbytes) of the weights file
         into the device buffer `dst` (nbytes -1: to the end of the file);
@@ -473,3 +491,11 @@ def load_weights_file(ctx: Context, path: str, cfg: ModelConfig | None = None, d
     n = ctx.load_weights_file(path, buf)
     assert n == size
     return buf, [layer_desc_from_weights(cfg, buf, layer) for layer in range(cfg.num_layers)]
+
+
+def ep_unique_id() -> bytes:
+    """A new NCCL communicator id (moe_ep_get_unique_id), to be passed to
+    every rank's Context.ep_init."""
+    buf = C.create_string_buffer(EP_UNIQUE_ID_BYTES)
+    _status(load_library().moe_ep_get_unique_id(C.addressof(buf)), "moe_ep_get_unique_id")
+    return buf.raw

@@ -3,7 +3,8 @@ tests/test_gpu_ep.py through torch.distributed.run, one process per GPU).
 
 Every rank builds the same seeded full-size layer and token batch.  The
 all-reduce form: each rank evaluates its expert range for all tokens and the
-partial outputs are all-reduced over NCCL.  The all-to-all form: each rank
+partial outputs are all-reduced over NCCL (torch.distributed, and the
+library's own communicator through moe_ep_init).  The all-to-all form: each rank
 keeps a shard of the tokens, routed rows travel to the ranks owning their
 experts and back.  Each rank compares the result with its own one-GPU
 evaluation of the whole layer.  Exit status 0 means the outputs agree within
@@ -77,6 +78,24 @@ def main():
         print(f"rank {rank} all-to-all M={M} rows {t0}:{t1}: max_abs={mx:.2e} rel_l2={rel:.2e} "
               f"(bar {bar_abs:.1e}, {bar_rel:.0e})", flush=True)
         ok = ok and mx <= bar_abs and rel <= bar_rel
+    # the library's own communicator (moe_ep_init): one call per layer
+    uid = [MB.ep_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    cnative = MB.Context(local)
+    cnative.set_stream(torch.cuda.current_stream().cuda_stream)
+    cnative.ep_init(uid[0], rank, world)
+    for M in (1, 16, 64):
+        x = synth.make_x(M, seed=90 + M)
+        out = torch.zeros((M, layer["d"]), device="cuda")
+        cnative.layer_forward(desc, M, x, out, MB.F_POST_NORM)
+        ref = torch.zeros_like(out)
+        ctx.layer_forward(desc, M, x, ref, MB.F_POST_NORM)
+        torch.cuda.synchronize()
+        mx, rel = errors(out.cpu().numpy(), ref.cpu().numpy())
+        print(f"rank {rank} native M={M}: max_abs={mx:.2e} rel_l2={rel:.2e}", flush=True)
+        ok = ok and mx <= 5e-4 and rel <= 1e-4
+    cnative.ep_finalize()
+    cnative.close()
     dist.barrier()
     dist.destroy_process_group()
     return 0 if ok else 1

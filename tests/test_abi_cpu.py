@@ -57,3 +57,16 @@ def test_null_context_is_rejected(lib):
     assert L.moe_set_async(None, 1) == 1
     assert L.moe_last_error(None) == b"null context"
     assert L.moe_kernel_launches(None) == 0
+
+
+def test_ep_entry_points_without_gpu(lib):
+    """Communicator ids come from NCCL on the host (no GPU involved); the
+    context-taking entry points refuse a null context."""
+    uid = moe_b200.ep_unique_id()
+    assert len(uid) == moe_b200.EP_UNIQUE_ID_BYTES and any(uid)
+    assert moe_b200.ep_unique_id() != uid
+    L = moe_b200.load_library()
+    assert L.moe_ep_get_unique_id(None) == 1
+    buf = C.create_string_buffer(128)
+    assert L.moe_ep_init(None, C.addressof(buf), 0, 1) == 1
+    assert L.moe_ep_finalize(None) == 1

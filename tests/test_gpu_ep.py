@@ -87,3 +87,84 @@ def test_expert_parallel_ranks(nproc):
            os.path.join(HERE, "ep_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[:3000]
+
+
+def test_native_ep_one_rank_equals_the_layer(ctx, full_layer):
+    """moe_ep_init with a single rank: the layer call takes the expert-
+    parallel path (local range = all experts, NCCL all-reduce, post-norm of
+    the sum) and agrees with the plain call; after moe_ep_finalize the
+    context is a plain one again."""
+    import torch
+    dev, _, _ = full_layer
+    d2 = dict(dev)
+    d2["post_norm_w"] = (1.0 + 0.1 * torch.randn(2816, generator=torch.Generator().manual_seed(7))).cuda()
+    desc = MB.make_desc(d2)
+    c2 = MB.Context(0)
+    try:
+        c2.ep_init(MB.ep_unique_id(), 0, 1)
+        with pytest.raises(MB.MoeError) as e:
+            c2.ep_init(MB.ep_unique_id(), 0, 1)
+        assert e.value.code == 8  # MOE_E_STATE: one communicator per context
+        for M in (1, 16, 64):
+            x = synth.make_x(M, seed=120 + M)
+            ref = torch.zeros((M, 2816), device="cuda")
+            ctx.layer_forward(desc, M, x, ref, MB.F_POST_NORM)
+            got = torch.zeros_like(ref)
+            c2.layer_forward(desc, M, x, got, MB.F_POST_NORM)
+            raw_ref = torch.zeros_like(ref)
+            ctx.layer_forward(desc, M, x, raw_ref, 0)
+            raw = torch.zeros_like(ref)
+            c2.layer_forward(desc, M, x, raw, 0)
+            torch.cuda.synchronize()
+            # same experts, same order: the partial sum is the whole sum
+            assert torch.equal(raw, raw_ref), f"M={M}"
+            # post-norm by the norm kernel instead of inside the combine
+            assert_close(got.cpu().numpy(), ref.cpu().numpy(), max_abs=1e-5, rel_l2=1e-6, what=f"ep1 M={M}")
+        with pytest.raises(MB.MoeError) as e:
+            x = synth.make_x(4, seed=1)
+            c2.layer_forward(desc, 4, x, torch.zeros((4, 2816), device="cuda"), MB.F_FP16_OUT)
+        assert e.value.code == 1
+        c2.ep_finalize()
+        x = synth.make_x(16, seed=3)
+        a, b = torch.zeros((16, 2816), device="cuda"), torch.zeros((16, 2816), device="cuda")
+        ctx.layer_forward(desc, 16, x, a, MB.F_POST_NORM)
+        c2.layer_forward(desc, 16, x, b, MB.F_POST_NORM)
+        torch.cuda.synchronize()
+        assert torch.equal(a, b)
+    finally:
+        c2.close()
+
+
+_MISSING_RANK = r"""
+import sys
+sys.path[:0] = sys.argv[1:]
+import numpy as np
+import moe_b200 as MB
+c = MB.Context(0)
+c.set_option(MB.OPT_EP_TIMEOUT_NS, 2_000_000_000)
+try:
+    c.ep_init(MB.ep_unique_id(), 0, 2)   # rank 1 never joins
+    print("joined?")
+    sys.exit(1)
+except MB.MoeError as e:
+    assert e.code == 6, e                # MOE_E_TIMEOUT, communicator aborted
+x = np.ones((2, 64), np.float32)
+out = np.zeros_like(x)
+c.rms_norm(x, np.ones(64, np.float32), out, 2, 64)   # the context still works
+assert np.allclose(out, 1.0, atol=1e-5)
+c.close()
+print("OK")
+"""
+
+
+def test_native_ep_missing_rank_times_out():
+    """A rank that never joins: moe_ep_init gives up after the communicator
+    deadline with MOE_E_TIMEOUT and the context stays usable.  Host-side
+    failure only (the bootstrap waits on sockets); run in a child process so
+    that nothing here can outlive its time limit."""
+    root = os.path.dirname(HERE)
+    paths = [os.path.join(root, "llm-mojo_b200"), HERE]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "10", "90", sys.executable, "-c", _MISSING_RANK, *paths],
+                       env=env, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
