@@ -269,8 +269,10 @@ def workload_config(args, M):
             "l2": f"weights of {args.layers} distinct layers cycled per step ({args.layers * 476} MB > 126 MB L2)",
             "post_norm": True,
             "parallelism": (f"ep{dist_setup()[0]}: 128/{dist_setup()[0]} experts per GPU, tokens replicated, "
-                            f"NCCL all-reduce of partial outputs; dense rows sharded"
-                            if dist_setup()[0] > 1 and getattr(args, "parallel", "ep") == "ep"
+                            f"NCCL all-reduce of partial outputs"
+                            f"{' inside the layer call (moe_ep_init)' if getattr(args, 'parallel', 'ep') == 'ep-native' else ''}"
+                            f"; dense rows sharded"
+                            if dist_setup()[0] > 1 and getattr(args, "parallel", "ep") in ("ep", "ep-native")
                             else f"replicas x{dist_setup()[0]}"),
             "gemm_path": getattr(args, "path", "auto"),
             "tc_kernel": getattr(args, "tc_kernel", "stream"),
@@ -295,9 +297,11 @@ def main():
                          "by default N > 1 launches eagerly")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"],
                     help="expert/dense GEMM path: CUDA-core GEMV, tcgen05, or automatic")
-    ap.add_argument("--parallel", default="ep", choices=["ep", "replicas"],
+    ap.add_argument("--parallel", default="ep", choices=["ep", "ep-native", "replicas"],
                     help="N > 1: expert parallel (128/N experts per GPU, tokens replicated, one NCCL "
-                         "all-reduce per layer; dense projections row-sharded) or independent replicas")
+                         "all-reduce per layer; dense projections row-sharded) with the all-reduce "
+                         "issued by torch.distributed (ep) or inside the library's layer call "
+                         "(ep-native, moe_ep_init), or independent replicas")
     ap.add_argument("--tc-kernel", default="stream", choices=["stream", "stream-all", "general"],
                     help="tensor-core kernel for token tiles <= 64: streaming for the expert GEMMs "
                          "(default), streaming also for dense projections, or general")
@@ -337,7 +341,12 @@ def main():
     ctx.set_gemm_path({"auto": MB.PATH_AUTO, "gemv": MB.PATH_GEMV, "tc": MB.PATH_TC}[args.path])
     ctx.set_option(MB.OPT_TC_STREAM, {"general": 0, "stream": 1, "stream-all": 2}[args.tc_kernel])
     M = wl["M"]
-    use_ep = ws > 1 and args.parallel == "ep"
+    use_ep = ws > 1 and args.parallel in ("ep", "ep-native")
+    native_ep = use_ep and args.parallel == "ep-native"
+    if native_ep:  # the library's own communicator: rank 0's id to every rank
+        uid = [MB.ep_unique_id() if rank == 0 else None]
+        pg.broadcast_object_list(uid, src=0)
+        ctx.ep_init(uid[0], rank, ws)
     # expert parallel: every rank holds the same layers and tokens and
     # evaluates its own expert range; replicas: independent data per rank
     seed_rank = 0 if use_ep else rank
@@ -381,7 +390,7 @@ def main():
 
     # routing per layer (unique experts of this rank -> algorithmic bytes)
     e_lo, e_hi = EP.expert_range(rank, ws, E) if use_ep else (0, E)
-    epl = EP.ExpertParallelLayer(ctx, E) if use_ep else None
+    epl = EP.ExpertParallelLayer(ctx, E) if use_ep and not native_ep else None
     uniq, pairs_l = [], []
     for li in range(args.layers):
         cnt = np.zeros(M, np.int64)
