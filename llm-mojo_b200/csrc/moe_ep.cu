@@ -86,8 +86,12 @@ std::string nccl_msg(const NcclApi* api, const char* what, ncclResult_t r) {
 }
 
 // Polls the communicator until its pending operation left ncclInProgress.
+// An enqueue usually settles within microseconds: the first 200 us poll
+// without sleeping, so that a layer call does not stall its host thread
+// (and, with eager launches, the GPU behind it) for a whole sleep.
 int settle(moe::EpComm& ep, const NcclApi* api, uint64_t deadline, const char* what, std::string& err) {
     ncclComm_t comm = static_cast<ncclComm_t>(ep.comm);
+    const uint64_t spin_until = now_ns() + 200000;
     for (;;) {
         ncclResult_t st = ncclInProgress;
         ncclResult_t r = api->async_error(comm, &st);
@@ -98,12 +102,16 @@ int settle(moe::EpComm& ep, const NcclApi* api, uint64_t deadline, const char* w
             moe::ep_abort(ep);
             return MOE_E_NCCL;
         }
-        if (now_ns() > deadline) {
+        const uint64_t t = now_ns();
+        if (t > deadline) {
             err = std::string(what) + ": no progress before the deadline (a rank missing?)";
             moe::ep_abort(ep);
             return MOE_E_TIMEOUT;
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (t < spin_until)
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
 
