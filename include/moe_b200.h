@@ -242,6 +242,42 @@ int moe_run_moe_coalesced_core(moe_ctx* ctx, int64_t sub_b,
                                float* batch_moe_out, int64_t embed_dim, int64_t expert_mlp_dim,
                                int64_t num_experts, int64_t top_k, int activation);
 
+/* run_moe_coalesced_stage1 (moe_kernels.mojo:784-1069) and
+ * run_moe_coalesced_stage2 (:1072-1318): the core in two calls, so that a
+ * caller can put other work between the gate/up half and the down half
+ * (model_speculative_moe_batched.mojo:3165-3234).  Together they give the
+ * same bits as moe_run_moe_coalesced_core on the same inputs.
+ * Stage 1 fills the reference's buckets: bucket_counts[E], bucket_toks[E*5]
+ * and bucket_weights[E*5] (token b and its weight at e*5 + c, in token then
+ * slot order), unique_experts / unique_base_slot (ascending expert ids and
+ * the prefix of their counts; *num_unique entries), and returns the count in
+ * *num_unique.  These arrays are read on the host, so the call completes
+ * before returning (also in asynchronous mode) as far as the routing
+ * arrays go.  1 <= sub_b <= 5, as in the reference (five bucket entries per
+ * expert).  The activations stay in device memory of the context, which
+ * keeps one stage-1 result at a time, identified by `act_deint_scratch`
+ * (its contents are not used); calls of other entry points in between do not
+ * disturb it.  Stage 2 takes the down weights, evaluates the down half of
+ * that result and writes the per-token weighted sums to batch_moe_out [sub_b
+ * x d]; the bucket arguments are accepted for signature parity and not read.
+ * MOE_E_STATE: no stage-1 result for that scratch pointer, or the options or
+ * the down weights' alignment changed the expert path between the calls. */
+int moe_run_moe_coalesced_stage1(moe_ctx* ctx, int64_t sub_b, const uint8_t* experts_gate_up_packed,
+                                 const float* experts_gate_up_scales, const float* batch_in,
+                                 int x_layout, const int64_t* tok_active_count,
+                                 const int64_t* tok_active_idx, const float* tok_active_weights,
+                                 int64_t* bucket_counts, int64_t* bucket_toks, float* bucket_weights,
+                                 int64_t* unique_experts, int64_t* unique_base_slot,
+                                 const float* act_deint_scratch, int64_t embed_dim,
+                                 int64_t expert_mlp_dim, int64_t num_experts, int64_t top_k,
+                                 int activation, int64_t* num_unique);
+int moe_run_moe_coalesced_stage2(moe_ctx* ctx, int64_t sub_b, int64_t num_unique,
+                                 const uint8_t* experts_down_packed, const float* experts_down_scales,
+                                 const int64_t* bucket_counts, const int64_t* bucket_toks,
+                                 const float* bucket_weights, const int64_t* unique_experts,
+                                 const int64_t* unique_base_slot, const float* act_deint_scratch,
+                                 float* batch_moe_out, int64_t embed_dim, int64_t expert_mlp_dim);
+
 /* run_diffusion_moe_experts_parallel (diffusion_kernels.mojo:236-253): fp16
  * canvas in/out (IEEE binary16 bits), a slot is active iff its weight > 0,
  * per-token fp32 combine then one rounding to fp16.  The reference's three

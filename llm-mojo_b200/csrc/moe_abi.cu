@@ -39,6 +39,25 @@ struct Status {
 
 }  // namespace
 
+namespace {
+// Internal buffers of an expert evaluation for M tokens x K slots.
+constexpr int64_t kMaxSplitY = 4;  // split-K partials of the down projection kept in y
+struct ExpertBufs {
+    int* slot_expert;
+    float* slot_weight;
+    moe::BucketOut b;
+    float* x32;   // [M][d] gate/up input, fp32 natural
+    float* xsum;  // [M][d/32] 1.5 * block sums of x32
+    float* x32q;  // [M][d]   CUDA-core path: x32 in the q layout
+    bool x32q_ready;  // x32q already written (by the router's prep)
+    float* act;   // [P][F]
+    float* y;     // [P][d]
+    __half* x16;  // [P][d]   tensor-core path: gathered gate/up input
+    __half* a16;  // [P][F]   tensor-core path: activations (down input)
+    int* tt_prefix;  // [E+1]
+};
+}  // namespace
+
 struct moe_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;
@@ -78,6 +97,20 @@ struct moe_ctx {
     std::vector<double> prof_ms;
     std::vector<uint64_t> prof_cnt;
     moe::FileStaging file_staging;       // moe_load_weights_file's pinned buffers
+    // moe_run_moe_coalesced_stage1 -> stage2: the first half's buffers live
+    // in their own device arena, so that calls in between cannot overwrite them
+    char* split_ws = nullptr;
+    size_t split_cap = 0;
+    struct Split {
+        bool active = false;
+        const void* key = nullptr;  // the caller's act_deint_scratch
+        int64_t sub_b = 0, top_k = 0, d = 0, F = 0, E = 0, num_unique = 0;
+        int act = 0;
+        const uint8_t* gu_p = nullptr;
+        const float* gu_s = nullptr;
+        bool tc = false, stream = false;
+        ExpertBufs bb;
+    } split;
     moe::EpComm ep;                      // moe_ep_init's communicator
     uint64_t ep_timeout_ns = 30000000000ull;  // MOE_OPT_EP_TIMEOUT_NS
 };
@@ -269,22 +302,6 @@ int check_q4_shape(moe_ctx* ctx, int64_t K, int64_t rows) {
     return MOE_OK;
 }
 
-// Internal buffers of an expert evaluation for M tokens x K slots.
-constexpr int64_t kMaxSplitY = 4;  // split-K partials of the down projection kept in y
-struct ExpertBufs {
-    int* slot_expert;
-    float* slot_weight;
-    moe::BucketOut b;
-    float* x32;   // [M][d] gate/up input, fp32 natural
-    float* xsum;  // [M][d/32] 1.5 * block sums of x32
-    float* x32q;  // [M][d]   CUDA-core path: x32 in the q layout
-    bool x32q_ready;  // x32q already written (by the router's prep)
-    float* act;   // [P][F]
-    float* y;     // [P][d]
-    __half* x16;  // [P][d]   tensor-core path: gathered gate/up input
-    __half* a16;  // [P][F]   tensor-core path: activations (down input)
-    int* tt_prefix;  // [E+1]
-};
 
 size_t expert_bufs_bytes(int64_t M, int64_t K, int64_t d, int64_t F, int64_t E) {
     const int64_t P = M * K;
@@ -293,28 +310,36 @@ size_t expert_bufs_bytes(int64_t M, int64_t K, int64_t d, int64_t F, int64_t E) 
            al(P * F * 2) + al((E + 1) * 4);
 }
 
+// Carves the buffers of one expert evaluation out of an arena; `take`
+// returns nullptr once the arena is exhausted (every later take does too).
+template <class Take>
+bool carve_expert_bufs(Take take, int64_t M, int64_t K, int64_t d, int64_t F, int64_t E, ExpertBufs* o) {
+    const int64_t P = M * K;
+    o->slot_expert = (int*)take(P * 4);
+    o->slot_weight = (float*)take(P * 4);
+    o->b.meta = (int*)take(16);
+    o->b.unique_expert = (int*)take(E * 4);
+    o->b.seg_start = (int*)take(E * 4);
+    o->b.seg_count = (int*)take(E * 4);
+    o->b.pair_token = (int*)take(P * 4);
+    o->b.pair_slot = (int*)take(P * 4);
+    o->b.slot_pair = (int*)take(P * 4);
+    o->x32 = (float*)take(M * d * 4);
+    o->xsum = (float*)take(M * d / 32 * 4);
+    o->x32q = (float*)take(M * d * 4);
+    o->x32q_ready = false;
+    o->act = (float*)take(P * F * 4);
+    o->y = (float*)take(P * d * 4 * kMaxSplitY);
+    o->x16 = (__half*)take(P * d * 2);
+    o->a16 = (__half*)take(P * F * 2);
+    o->tt_prefix = (int*)take((E + 1) * 4);
+    return o->tt_prefix != nullptr;
+}
+
 int take_expert_bufs(moe_ctx* ctx, int64_t M, int64_t K, int64_t d, int64_t F, int64_t E,
                      ExpertBufs* o) {
-    const int64_t P = M * K;
-    o->slot_expert = (int*)ws_take(ctx, P * 4);
-    o->slot_weight = (float*)ws_take(ctx, P * 4);
-    o->b.meta = (int*)ws_take(ctx, 16);
-    o->b.unique_expert = (int*)ws_take(ctx, E * 4);
-    o->b.seg_start = (int*)ws_take(ctx, E * 4);
-    o->b.seg_count = (int*)ws_take(ctx, E * 4);
-    o->b.pair_token = (int*)ws_take(ctx, P * 4);
-    o->b.pair_slot = (int*)ws_take(ctx, P * 4);
-    o->b.slot_pair = (int*)ws_take(ctx, P * 4);
-    o->x32 = (float*)ws_take(ctx, M * d * 4);
-    o->xsum = (float*)ws_take(ctx, M * d / 32 * 4);
-    o->x32q = (float*)ws_take(ctx, M * d * 4);
-    o->x32q_ready = false;
-    o->act = (float*)ws_take(ctx, P * F * 4);
-    o->y = (float*)ws_take(ctx, P * d * 4 * kMaxSplitY);
-    o->x16 = (__half*)ws_take(ctx, P * d * 2);
-    o->a16 = (__half*)ws_take(ctx, P * F * 2);
-    o->tt_prefix = (int*)ws_take(ctx, (E + 1) * 4);
-    if (!o->tt_prefix) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+    if (!carve_expert_bufs([&](size_t b) { return ws_take(ctx, b); }, M, K, d, F, E, o))
+        return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
     return MOE_OK;
 }
 
@@ -379,30 +404,29 @@ int expert_token_tile(int64_t P, int64_t E) {
 // bb.xsum must hold the gate/up input (prep_rows or the router's prep).
 // `prebucketed`: the fused routing kernel already wrote the buckets, the
 // token-tile prefix and (tensor-core path) the fp16 pair rows.
-int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int64_t d, int64_t F,
-                int64_t E, int act, ExpertBufs& bb, const moe::CombineArgs* comb_tmpl, void* out,
-                bool prebucketed = false) {
-    cudaStream_t s = ctx->stream;
+// Launch descriptors of one expert evaluation (gate/up + activation, then
+// down), fixed before anything is launched so that the two halves can run
+// as separate calls (moe_run_moe_coalesced_stage1/2) with the very kernels
+// and arguments of the one-call form.
+struct ExpertPlan {
+    bool tc = false;
+    moe::TcLaunch t1, t2;          // tensor-core path
+    moe::GemvArgs g1, g2;          // CUDA-core path (q-layout forms when `stream`)
+    bool stream = false;           // CUDA-core: the k_dgemv pair
+    int ksplit = 1;
+    int BN = 0;
+};
+
+void plan_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int64_t d, int64_t F,
+                  int64_t E, int act, const ExpertBufs& bb, ExpertPlan* p) {
     const int64_t P = M * K;
-    const bool tc = use_tc(ctx, M, d, F, w);
-    if (!prebucketed) {  // the tensor-core path's token-tile prefix comes out of the same launch
-        ProfScope ps(ctx, "bucket");
-        int e_lo, e_hi;
-        expert_range(ctx, E, &e_lo, &e_hi);
-        ctx->launches += moe::launch_bucket(bb.slot_expert, P, (int)K, (int)E, e_lo, e_hi, bb.b, s,
-                                            tc ? expert_token_tile(P, E) : 0, tc ? bb.tt_prefix : nullptr);
-    }
+    p->tc = use_tc(ctx, M, d, F, w);
     const int max_u = (int)std::min<int64_t>(E, P);
     const int max_t = (int)std::max<int64_t>(1, M);
-
-    int ksplit = 1;
-    if (tc) {
+    if (p->tc) {
         const int BN = expert_token_tile(P, E);
-        if (!prebucketed) {
-            ProfScope ps(ctx, "gather");
-            ctx->launches += moe::launch_gather_f16(bb.x32, d, bb.b.pair_token, bb.b.meta, P, 0, bb.x16, s);
-        }
-        moe::TcLaunch t1;
+        p->BN = BN;
+        moe::TcLaunch& t1 = p->t1;
         t1.a.Ws = w.gu_s;
         t1.a.K = (int)d;
         t1.a.R = 2 * F;
@@ -424,14 +448,8 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
         t1.max_items = (int64_t)(F / 64) * (max_u + (P + BN - 1) / BN);
         t1.a_in_smem = ctx->tc_a_in_smem;
         t1.stream = ctx->tc_stream >= 1;
-        int r;
-        {
-            ProfScope ps(ctx, "tc_gate_up");
-            r = moe::launch_tc_gemm(moe::TC_ACT, t1, ctx->num_sms, s);
-        }
-        if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core GEMM setup failed (gate/up)");
-        ctx->launches += r;
-        moe::TcLaunch t2 = t1;
+        moe::TcLaunch& t2 = p->t2;
+        t2 = t1;
         t2.a.Ws = w.dn_s;
         t2.a.K = (int)F;
         t2.a.R = d;
@@ -445,14 +463,9 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
         t2.a.ksplit = (int)std::min<int64_t>(choose_ksplit(ctx, ((d + 127) / 128) * max_u, F), kMaxSplitY);
         t2.a.split_stride = P * d;
         t2.max_items *= t2.a.ksplit;
-        ksplit = t2.a.ksplit;
-        {
-            ProfScope ps(ctx, "tc_down");
-            r = moe::launch_tc_gemm(moe::TC_PLAIN, t2, ctx->num_sms, s);
-        }
-        if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core GEMM setup failed (down)");
-        ctx->launches += r;
-    } else {
+        p->ksplit = t2.a.ksplit;
+        return;
+    }
     moe::GemvArgs g1;
     g1.Wp = w.gu_p;
     g1.Ws = w.gu_s;
@@ -493,29 +506,72 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
     q1.x_qlayout = 1;
     q1.out_qlayout = 1;
     q2.x_qlayout = 1;
-    const bool stream = moe::dgemv_supported(q1, moe::GEMV_ACT) && moe::dgemv_supported(q2, moe::GEMV_PLAIN);
-    if (stream && !bb.x32q_ready) {
+    p->stream = moe::dgemv_supported(q1, moe::GEMV_ACT) && moe::dgemv_supported(q2, moe::GEMV_PLAIN);
+    p->g1 = p->stream ? q1 : g1;
+    p->g2 = p->stream ? q2 : g2;
+}
+
+// Gate/up + activation: bucket the pairs (unless the caller's routing launch
+// did), gather the fp16 rows, run the first GEMM.
+int experts_stage1(moe_ctx* ctx, const ExpertPlan& p, ExpertBufs& bb, int64_t M, int64_t K, int64_t d,
+                   int64_t E, bool prebucketed) {
+    cudaStream_t s = ctx->stream;
+    const int64_t P = M * K;
+    if (!prebucketed) {  // the tensor-core path's token-tile prefix comes out of the same launch
+        ProfScope ps(ctx, "bucket");
+        int e_lo, e_hi;
+        expert_range(ctx, E, &e_lo, &e_hi);
+        ctx->launches += moe::launch_bucket(bb.slot_expert, P, (int)K, (int)E, e_lo, e_hi, bb.b, s,
+                                            p.tc ? p.BN : 0, p.tc ? bb.tt_prefix : nullptr);
+    }
+    if (p.tc) {
+        if (!prebucketed) {
+            ProfScope ps(ctx, "gather");
+            ctx->launches += moe::launch_gather_f16(bb.x32, d, bb.b.pair_token, bb.b.meta, P, 0, bb.x16, s);
+        }
+        int r;
+        {
+            ProfScope ps(ctx, "tc_gate_up");
+            r = moe::launch_tc_gemm(moe::TC_ACT, p.t1, ctx->num_sms, s);
+        }
+        if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core GEMM setup failed (gate/up)");
+        ctx->launches += r;
+        return MOE_OK;
+    }
+    if (p.stream && !bb.x32q_ready) {
         ProfScope ps(ctx, "qlayout");
         ctx->launches += moe::launch_to_qlayout(bb.x32, bb.x32q, M, (int)d, ctx->num_sms, s);
     }
-    {
-        ProfScope ps(ctx, "gemv_gate_up");
-        const int r = stream ? moe::launch_dgemv(moe::GEMV_ACT, q1, ctx->num_sms, s)
-                             : moe::launch_gemv(moe::GEMV_ACT, g1, ctx->num_sms, s);
-        if (r < 0) return fail(ctx, MOE_E_CUDA, "expert GEMV launch failed (gate/up)");
+    ProfScope ps(ctx, "gemv_gate_up");
+    const int r = p.stream ? moe::launch_dgemv(moe::GEMV_ACT, p.g1, ctx->num_sms, s)
+                           : moe::launch_gemv(moe::GEMV_ACT, p.g1, ctx->num_sms, s);
+    if (r < 0) return fail(ctx, MOE_E_CUDA, "expert GEMV launch failed (gate/up)");
+    ctx->launches += r;
+    return MOE_OK;
+}
+
+// Down GEMM, then the per-token weighted combine into `out`.
+int experts_stage2(moe_ctx* ctx, const ExpertPlan& p, ExpertBufs& bb, int64_t M, int64_t K, int64_t d,
+                   const moe::CombineArgs* comb_tmpl, void* out) {
+    cudaStream_t s = ctx->stream;
+    const int64_t P = M * K;
+    if (p.tc) {
+        int r;
+        {
+            ProfScope ps(ctx, "tc_down");
+            r = moe::launch_tc_gemm(moe::TC_PLAIN, p.t2, ctx->num_sms, s);
+        }
+        if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core GEMM setup failed (down)");
         ctx->launches += r;
-    }
-    {
+    } else {
         ProfScope ps(ctx, "gemv_down");
-        const int r = stream ? moe::launch_dgemv(moe::GEMV_PLAIN, q2, ctx->num_sms, s)
-                             : moe::launch_gemv(moe::GEMV_PLAIN, g2, ctx->num_sms, s);
+        const int r = p.stream ? moe::launch_dgemv(moe::GEMV_PLAIN, p.g2, ctx->num_sms, s)
+                               : moe::launch_gemv(moe::GEMV_PLAIN, p.g2, ctx->num_sms, s);
         if (r < 0) return fail(ctx, MOE_E_CUDA, "expert GEMV launch failed (down)");
         ctx->launches += r;
     }
-    }
-
     moe::CombineArgs c = *comb_tmpl;
-    c.ksplit = ksplit;
+    c.ksplit = p.ksplit;
     c.split_stride = P * d;
     c.y = bb.y;
     c.d = d;
@@ -528,6 +584,15 @@ int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int6
         ctx->launches += moe::launch_combine(c, M, s);
     }
     return MOE_OK;
+}
+
+int run_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, int64_t d, int64_t F,
+                int64_t E, int act, ExpertBufs& bb, const moe::CombineArgs* comb_tmpl, void* out,
+                bool prebucketed = false) {
+    ExpertPlan p;
+    plan_experts(ctx, w, M, K, d, F, E, act, bb, &p);
+    TRY(experts_stage1(ctx, p, bb, M, K, d, E, prebucketed));
+    return experts_stage2(ctx, p, bb, M, K, d, comb_tmpl, out);
 }
 
 // Workspace dense_q4 may take (fp16 copy of x and split-K partials).
@@ -630,6 +695,7 @@ int moe_ctx_destroy(moe_ctx* ctx) {
     cudaStreamSynchronize(ctx->stream);
     for (Reg& r : ctx->regs) cudaFree(r.dev);
     if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->split_ws) cudaFree(ctx->split_ws);
     if (ctx->err_flag) cudaFree(ctx->err_flag);
     if (ctx->done) cudaEventDestroy(ctx->done);
     for (auto& r : ctx->prof_pending) {
@@ -1199,6 +1265,199 @@ int moe_run_moe_coalesced_core(moe_ctx* ctx, int64_t sub_b, const uint8_t* gu_p,
     moe::CombineArgs c;
     TRY(prep_rows(ctx, xi, x_layout, 0, sub_b, d, bb.x32, bb.xsum));
     TRY(run_experts(ctx, w, sub_b, top_k, d, F, E, activation, bb, &c, out));
+    return finish(ctx);
+}
+
+// ---- run_moe_coalesced_stage1 / stage2: the core in two calls
+}  // extern "C"
+
+namespace {
+
+constexpr int64_t kBucketCap = 5;  // bucket entries per expert (moe_kernels.mojo:824)
+
+// Reads a small caller array (host or device memory) into `dst` after the
+// work queued on the context's stream.
+int get_small(moe_ctx* ctx, void* dst, const void* src, size_t bytes) {
+    MOE_CUDA(cudaStreamSynchronize(ctx->stream));
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, src) != cudaSuccess) {
+        cudaGetLastError();
+        at.type = cudaMemoryTypeUnregistered;
+    }
+    if (at.type == cudaMemoryTypeDevice) {
+        MOE_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+        MOE_CUDA(cudaStreamSynchronize(ctx->stream));
+    } else {
+        std::memcpy(dst, src, bytes);
+    }
+    return MOE_OK;
+}
+
+// Writes a small host-computed array to a caller buffer (host or device).
+int put_small(moe_ctx* ctx, void* dst, const void* src, size_t bytes) {
+    if (!bytes) return MOE_OK;
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, dst) != cudaSuccess) {
+        cudaGetLastError();
+        at.type = cudaMemoryTypeUnregistered;
+    }
+    if (at.type == cudaMemoryTypeDevice) {
+        MOE_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+        MOE_CUDA(cudaStreamSynchronize(ctx->stream));  // `src` is a host temporary
+    } else {
+        std::memcpy(dst, src, bytes);
+    }
+    return MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_run_moe_coalesced_stage1(moe_ctx* ctx, int64_t sub_b, const uint8_t* gu_p, const float* gu_s,
+                                 const float* batch_in, int x_layout, const int64_t* tok_count,
+                                 const int64_t* tok_idx, const float* tok_w, int64_t* bucket_counts,
+                                 int64_t* bucket_toks, float* bucket_weights, int64_t* unique_experts,
+                                 int64_t* unique_base_slot, const float* act_deint_scratch, int64_t d,
+                                 int64_t F, int64_t E, int64_t top_k, int activation, int64_t* num_unique) {
+    TRY(begin(ctx));
+    if (!gu_p || !gu_s || !batch_in || !tok_count || !tok_idx || !tok_w || !bucket_counts || !bucket_toks ||
+        !bucket_weights || !unique_experts || !unique_base_slot || !act_deint_scratch || !num_unique)
+        return fail(ctx, MOE_E_ARG, "null pointer");
+    TRY(check_q4_shape(ctx, d, 2 * F));
+    TRY(check_q4_shape(ctx, F, d));
+    if (sub_b < 1 || sub_b > kBucketCap)
+        return fail(ctx, MOE_E_SHAPE, "sub_b must be in [1, 5] (five bucket entries per expert)");
+    if (top_k <= 0 || top_k > 32) return fail(ctx, MOE_E_SHAPE, "top_k must be in [1, 32]");
+    if (E <= 0 || E > 1024) return fail(ctx, MOE_E_SHAPE, "num_experts must be in [1, 1024]");
+    if (x_layout < 0 || x_layout > 2 || activation < 0 || activation > 1)
+        return fail(ctx, MOE_E_ARG, "bad layout or activation");
+    ctx->split.active = false;
+    const int64_t P = sub_b * top_k;
+    // the reference's buckets (moe_kernels.mojo:815-835), built on the host:
+    // the call returns their unique-expert count
+    std::vector<int64_t> cnt(sub_b), idx(P), bc(E, 0), bt(E * kBucketCap, 0), ue, ub;
+    std::vector<float> wt(P), bw(E * kBucketCap, 0.f);
+    TRY(get_small(ctx, cnt.data(), tok_count, sub_b * 8));
+    TRY(get_small(ctx, idx.data(), tok_idx, P * 8));
+    TRY(get_small(ctx, wt.data(), tok_w, P * 4));
+    for (int64_t b = 0; b < sub_b; ++b) {
+        if (cnt[b] < 0 || cnt[b] > top_k) return fail(ctx, MOE_E_ARG, "active count out of range");
+        for (int64_t k = 0; k < cnt[b]; ++k) {
+            const int64_t e = idx[b * top_k + k];
+            if (e < 0 || e >= E) return fail(ctx, MOE_E_ARG, "expert index out of range in a routing array");
+            const int64_t c = bc[e];
+            if (c >= kBucketCap) return fail(ctx, MOE_E_ARG, "more than five entries for one expert");
+            bt[e * kBucketCap + c] = b;
+            bw[e * kBucketCap + c] = wt[b * top_k + k];
+            bc[e] = c + 1;
+        }
+    }
+    int64_t total = 0;
+    for (int64_t e = 0; e < E; ++e)
+        if (bc[e] > 0) {
+            ue.push_back(e);
+            ub.push_back(total);
+            total += bc[e];
+        }
+    const int64_t nu = (int64_t)ue.size();
+    TRY(put_small(ctx, bucket_counts, bc.data(), E * 8));
+    TRY(put_small(ctx, bucket_toks, bt.data(), E * kBucketCap * 8));
+    TRY(put_small(ctx, bucket_weights, bw.data(), E * kBucketCap * 4));
+    TRY(put_small(ctx, unique_experts, ue.data(), nu * 8));
+    TRY(put_small(ctx, unique_base_slot, ub.data(), nu * 8));
+    TRY(put_small(ctx, num_unique, &nu, 8));
+    // the device half: the core's kernels up to the activations, into the
+    // context's split arena
+    const size_t need = expert_bufs_bytes(sub_b, top_k, d, F, E) + 64 * kAlign;
+    if (ctx->split_cap < need) {
+        MOE_CUDA(cudaStreamSynchronize(ctx->stream));
+        if (ctx->split_ws) cudaFree(ctx->split_ws);
+        ctx->split_ws = nullptr;
+        ctx->split_cap = 0;
+        if (cudaMalloc(&ctx->split_ws, need) != cudaSuccess) {
+            cudaGetLastError();
+            ctx->split_ws = nullptr;
+            return fail(ctx, MOE_E_NOMEM, "device allocation for the stage-1 buffers failed");
+        }
+        ctx->split_cap = need;
+    }
+    size_t off = 0;
+    auto take = [&](size_t b) -> void* {
+        const size_t o = (off + kAlign - 1) / kAlign * kAlign;
+        if (o + b > ctx->split_cap) return nullptr;
+        off = o + b;
+        return ctx->split_ws + o;
+    };
+    ExpertBufs bb;
+    if (!carve_expert_bufs(take, sub_b, top_k, d, F, E, &bb)) return fail(ctx, MOE_E_NOMEM, "stage-1 arena exhausted");
+    TRY(ws_reserve(ctx, al(sub_b * d * 4) + al(sub_b * 8) + al(P * 8) + al(P * 4)));
+    void *gp, *gs, *xi, *tc, *ti, *tw;
+    TRY(dev_ptr(ctx, gu_p, 1, K_W, &gp));
+    TRY(dev_ptr(ctx, gu_s, 1, K_W, &gs));
+    TRY(dev_ptr(ctx, batch_in, sub_b * d * 4, K_IN, &xi));
+    TRY(dev_ptr(ctx, tok_count, sub_b * 8, K_IN, &tc));
+    TRY(dev_ptr(ctx, tok_idx, P * 8, K_IN, &ti));
+    TRY(dev_ptr(ctx, tok_w, P * 4, K_IN, &tw));
+    if (!al16(gp)) return fail(ctx, MOE_E_ARG, "packed weights must be 16-byte aligned");
+    ctx->launches += moe::launch_slots_from_lists(sub_b, (int)top_k, (const int64_t*)tc, 0, (const int64_t*)ti,
+                                                  (const float*)tw, bb.slot_expert, bb.slot_weight, (int)E,
+                                                  ctx->err_flag, ctx->stream);
+    TRY(prep_rows(ctx, xi, x_layout, 0, sub_b, d, bb.x32, bb.xsum));
+    ExpertWeights w{(const uint8_t*)gp, (const float*)gs, nullptr, nullptr};  // down weights: stage 2
+    ExpertPlan p;
+    plan_experts(ctx, w, sub_b, top_k, d, F, E, activation, bb, &p);
+    TRY(experts_stage1(ctx, p, bb, sub_b, top_k, d, E, false));
+    auto& sp = ctx->split;
+    sp.key = act_deint_scratch;
+    sp.sub_b = sub_b;
+    sp.top_k = top_k;
+    sp.d = d;
+    sp.F = F;
+    sp.E = E;
+    sp.num_unique = nu;
+    sp.act = activation;
+    sp.gu_p = w.gu_p;
+    sp.gu_s = w.gu_s;
+    sp.tc = p.tc;
+    sp.stream = p.stream;
+    sp.bb = bb;
+    TRY(finish(ctx));
+    sp.active = true;
+    return MOE_OK;
+}
+
+int moe_run_moe_coalesced_stage2(moe_ctx* ctx, int64_t sub_b, int64_t num_unique, const uint8_t* dn_p,
+                                 const float* dn_s, const int64_t* bucket_counts, const int64_t* bucket_toks,
+                                 const float* bucket_weights, const int64_t* unique_experts,
+                                 const int64_t* unique_base_slot, const float* act_deint_scratch,
+                                 float* batch_moe_out, int64_t d, int64_t F) {
+    TRY(begin(ctx));
+    (void)bucket_counts;  // the buckets stage 1 built stay on the device
+    (void)bucket_toks;
+    (void)bucket_weights;
+    (void)unique_experts;
+    (void)unique_base_slot;
+    if (!dn_p || !dn_s || !act_deint_scratch || !batch_moe_out) return fail(ctx, MOE_E_ARG, "null pointer");
+    auto& sp = ctx->split;
+    if (!sp.active || sp.key != act_deint_scratch)
+        return fail(ctx, MOE_E_STATE, "no stage-1 result for this act_deint_scratch on this context");
+    if (sub_b != sp.sub_b || num_unique != sp.num_unique || d != sp.d || F != sp.F)
+        return fail(ctx, MOE_E_ARG, "sub_b, num_unique or the dimensions differ from stage 1");
+    TRY(ws_reserve(ctx, al(sub_b * d * 4)));
+    void *dp, *ds, *out;
+    TRY(dev_ptr(ctx, dn_p, 1, K_W, &dp));
+    TRY(dev_ptr(ctx, dn_s, 1, K_W, &ds));
+    TRY(dev_ptr(ctx, batch_moe_out, sub_b * d * 4, K_OUT, &out));
+    if (!al16(dp)) return fail(ctx, MOE_E_ARG, "packed weights must be 16-byte aligned");
+    ExpertWeights w{sp.gu_p, sp.gu_s, (const uint8_t*)dp, (const float*)ds};
+    ExpertPlan p;
+    plan_experts(ctx, w, sp.sub_b, sp.top_k, sp.d, sp.F, sp.E, sp.act, sp.bb, &p);
+    if (p.tc != sp.tc || p.stream != sp.stream)
+        return fail(ctx, MOE_E_STATE, "the expert path changed between the stages (options or down-weight alignment)");
+    sp.active = false;  // consumed, whatever happens below
+    moe::CombineArgs c;
+    TRY(experts_stage2(ctx, p, sp.bb, sp.sub_b, sp.top_k, sp.d, &c, out));
     return finish(ctx);
 }
 

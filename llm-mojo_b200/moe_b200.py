@@ -51,6 +51,7 @@ EXPORTS = [
     "moe_default_model_config", "moe_weights_layout", "moe_weights_file_size",
     "moe_layer_desc_from_weights", "moe_load_weights_file",
     "moe_ep_get_unique_id", "moe_ep_init", "moe_ep_finalize",
+    "moe_run_moe_coalesced_stage1", "moe_run_moe_coalesced_stage2",
 ]
 
 
@@ -157,6 +158,9 @@ def _declare(L):
     L.moe_weights_file_size.argtypes = [C.POINTER(ModelConfig), C.POINTER(_i64)]
     L.moe_layer_desc_from_weights.argtypes = [C.POINTER(ModelConfig), _p, _i64, C.POINTER(LayerDesc)]
     L.moe_load_weights_file.argtypes = [_p, C.c_char_p, _i64, _i64, _p, C.POINTER(_i64)]
+    L.moe_run_moe_coalesced_stage1.argtypes = [_p, _i64, _p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _p, _p,
+                                               _p, _i64, _i64, _i64, _i64, _int, C.POINTER(_i64)]
+    L.moe_run_moe_coalesced_stage2.argtypes = [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64]
     L.moe_ep_get_unique_id.argtypes = [_p]
     L.moe_ep_init.argtypes = [_p, _p, _int, _int]
     L.moe_ep_finalize.argtypes = [_p]
@@ -344,6 +348,37 @@ class Context:
             _addr(experts_down_packed), _addr(experts_down_scales), _addr(batch_in_deint),
             x_layout, _addr(tok_active_count), _addr(tok_active_idx), _addr(tok_active_weights),
             _addr(batch_moe_out), embed_dim, expert_mlp_dim, num_experts, top_k, activation))
+
+    def run_moe_coalesced_stage1(self, sub_b, experts_gate_up_packed, experts_gate_up_scales,
+                                 batch_in_deint, tok_active_count, tok_active_idx,
+                                 tok_active_weights, bucket_counts, bucket_toks, bucket_weights,
+                                 unique_experts, unique_base_slot, gu_out_scratch, act_scratch,
+                                 act_deint_scratch, embed_dim=2816, expert_mlp_dim=704,
+                                 num_experts=128, num_tasks=8, x_layout=X_DEINT_HALVES, top_k=8,
+                                 activation=ACT_SIGMOID1702) -> int:
+        """moe_kernels.mojo:784-805; returns num_unique.  gu_out_scratch and
+        act_scratch are accepted for signature parity (the device keeps its
+        own); act_deint_scratch names the result for stage 2."""
+        n = _i64(0)
+        self.check(self.lib.moe_run_moe_coalesced_stage1(
+            self.h, sub_b, _addr(experts_gate_up_packed), _addr(experts_gate_up_scales),
+            _addr(batch_in_deint), x_layout, _addr(tok_active_count), _addr(tok_active_idx),
+            _addr(tok_active_weights), _addr(bucket_counts), _addr(bucket_toks),
+            _addr(bucket_weights), _addr(unique_experts), _addr(unique_base_slot),
+            _addr(act_deint_scratch), embed_dim, expert_mlp_dim, num_experts, top_k, activation,
+            C.byref(n)))
+        return int(n.value)
+
+    def run_moe_coalesced_stage2(self, sub_b, num_unique, experts_down_packed,
+                                 experts_down_scales, bucket_counts, bucket_toks, bucket_weights,
+                                 unique_experts, unique_base_slot, act_deint_scratch,
+                                 batch_moe_out, embed_dim=2816, expert_mlp_dim=704, num_tasks=8):
+        """moe_kernels.mojo:1072-1088."""
+        self.check(self.lib.moe_run_moe_coalesced_stage2(
+            self.h, sub_b, num_unique, _addr(experts_down_packed), _addr(experts_down_scales),
+            _addr(bucket_counts), _addr(bucket_toks), _addr(bucket_weights),
+            _addr(unique_experts), _addr(unique_base_slot), _addr(act_deint_scratch),
+            _addr(batch_moe_out), embed_dim, expert_mlp_dim))
 
     # ------------------------------------------- diffusion_kernels.mojo API
     def run_diffusion_moe_experts_parallel(self, experts_gate_up_packed, experts_gate_up_scales,
