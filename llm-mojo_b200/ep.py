@@ -83,14 +83,25 @@ class AllToAllExpertParallelLayer:
     The weighted sum runs at the token's home rank in slot order, as the
     reference's per-token accumulation does (moe_kernels.mojo:775-779).
 
+    With dedup=True a token travels once to each rank that owns any of its
+    experts, with that rank's slots (local expert ids and weights, in slot
+    order); the rank returns one weighted partial sum per token, and the home
+    rank adds the partial sums in rank order.  That moves min(K, ranks
+    touched) rows per token each way instead of K, and equals the slot-order
+    sum within fp32 reassociation (as the all-reduce form does).
+
     route_fn(x) -> (count [m], idx [m, K] global expert ids, w [m, K],
-    moe_in [m, d]) and experts_fn(rows [n, d], local_ids [n]) -> [n, d] (the
-    expert outputs, unweighted) are supplied by the caller: with the library
-    they are Context.route and Context.run_moe_coalesced_core over this
-    rank's weight slice (make_library_fns); the CPU tests pass the oracle.
+    moe_in [m, d]) and experts_fn are supplied by the caller: with the
+    library they are Context.route and Context.run_moe_coalesced_core over
+    this rank's weight slice (make_library_fns); the CPU tests pass the
+    oracle.  experts_fn(rows [n, d], local_ids [n]) -> [n, d] returns the
+    unweighted expert outputs (one expert per row); with dedup,
+    experts_fn(rows [n, d], local_idx [n, K], weights [n, K], count [n]) ->
+    [n, d] returns each row's weighted sum over its `count` leading slots.
     """
 
-    def __init__(self, num_experts: int, route_fn, experts_fn, *, group=None, rms_norm_fn=None):
+    def __init__(self, num_experts: int, route_fn, experts_fn, *, group=None, rms_norm_fn=None,
+                 dedup: bool = False):
         import torch.distributed as dist
         self.dist = dist
         self.group = group
@@ -101,6 +112,7 @@ class AllToAllExpertParallelLayer:
         self.route_fn = route_fn
         self.experts_fn = experts_fn
         self.rms_norm_fn = rms_norm_fn
+        self.dedup = dedup
 
     def _exchange(self, send, send_counts, recv_counts):
         import torch
@@ -109,10 +121,63 @@ class AllToAllExpertParallelLayer:
                                     input_split_sizes=send_counts, group=self.group)
         return recv
 
+    def _starts(self, dev):
+        import torch
+        return torch.tensor([expert_range(r, self.world, self.E)[0] for r in range(self.world)], device=dev)
+
+    def _exchange_counts(self, dest_sorted):
+        import torch
+        send_counts = torch.bincount(dest_sorted, minlength=self.world)
+        recv_counts = torch.empty_like(send_counts)
+        self.dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        return send_counts.tolist(), recv_counts.tolist()
+
+    def _forward_tokens(self, count, idx, w, moe_in):
+        """dedup: one row per (token, rank owning one of its experts)."""
+        import torch
+        m, K = idx.shape
+        d = moe_in.shape[1]
+        dev = moe_in.device
+        slot = torch.arange(K, device=dev).unsqueeze(0)
+        active = slot < count.unsqueeze(1)
+        owner = torch.where(active, expert_owner(idx.long().clamp(0, self.E - 1), self.world, self.E),
+                            torch.full_like(idx, -1, dtype=torch.long))
+        has = torch.zeros((m, self.world), dtype=torch.bool, device=dev)
+        t_a, k_a = torch.nonzero(active, as_tuple=True)
+        has[t_a, owner[t_a, k_a]] = True
+        t_idx, r_idx = torch.nonzero(has, as_tuple=True)  # token order, then rank
+        dest_sorted, order = torch.sort(r_idx, stable=True)
+        t_sorted = t_idx[order]
+        # this rank's slots of each (token, rank) row, compacted in slot order
+        mask = owner[t_sorted] == dest_sorted.unsqueeze(1)  # [n, K]
+        pos = torch.cumsum(mask.long(), 1) - 1
+        lcnt = mask.sum(1)
+        lidx = torch.zeros((len(t_sorted), K), dtype=torch.long, device=dev)
+        lw = torch.zeros((len(t_sorted), K), dtype=torch.float32, device=dev)
+        ri, ci = torch.nonzero(mask, as_tuple=True)
+        lidx[ri, pos[ri, ci]] = idx[t_sorted][ri, ci].long() - self._starts(dev)[dest_sorted][ri]
+        lw[ri, pos[ri, ci]] = w[t_sorted][ri, ci].to(torch.float32)
+        sc, rc = self._exchange_counts(dest_sorted)
+        rows = self._exchange(moe_in[t_sorted], sc, rc)
+        r_cnt = self._exchange(lcnt, sc, rc)
+        r_idx2 = self._exchange(lidx, sc, rc)
+        r_w = self._exchange(lw, sc, rc)
+        y = self.experts_fn(rows, r_idx2, r_w, r_cnt)
+        back = self._exchange(y, rc, sc)
+        out = torch.zeros((m, d), dtype=torch.float32, device=dev)
+        for r in range(self.world):  # rank order; each token at most once per rank
+            sel = dest_sorted == r
+            if bool(sel.any()):
+                out.index_add_(0, t_sorted[sel], back[sel])
+        return out
+
     def forward(self, x, post_norm_w=None):
         """x: this rank's tokens [m, d] fp32 (m may be 0).  Returns [m, d]."""
         import torch
         count, idx, w, moe_in = self.route_fn(x)
+        if self.dedup:
+            out = self._forward_tokens(count, idx, w, moe_in)
+            return self._post_norm(out, post_norm_w)
         m, K = idx.shape
         d = moe_in.shape[1]
         dev = moe_in.device
@@ -138,6 +203,10 @@ class AllToAllExpertParallelLayer:
             sel = k_idx == k
             if bool(sel.any()):
                 out.index_add_(0, t_idx[sel], y_pairs[sel] * wp[sel].unsqueeze(1))
+        return self._post_norm(out, post_norm_w)
+
+    def _post_norm(self, out, post_norm_w):
+        import torch
         if post_norm_w is not None:
             if self.rms_norm_fn is not None:
                 self.rms_norm_fn(out, post_norm_w, out)
@@ -173,15 +242,21 @@ def make_library_fns(ctx: "MB.Context", desc, layer: dict, rank: int, world: int
             ctx.route(desc, m, x, count, idx, w, moe_in=moe_in)
         return count, idx, w, moe_in
 
-    def experts_fn(rows, local_ids):
+    def experts_fn(rows, local_ids, weights=None, count=None):
         n = rows.shape[0]
         out = torch.empty((n, d), dtype=torch.float32, device=rows.device)
-        if n:
+        if not n:
+            return out
+        if local_ids.dim() == 1:  # one expert per row, weight 1
             cnt = torch.ones(n, dtype=torch.int64, device=rows.device)
             wt = torch.ones((n, 1), dtype=torch.float32, device=rows.device)
-            ctx.run_moe_coalesced_core(n, gu_p, gu_s, dn_p, dn_s, rows.contiguous(), cnt,
-                                       local_ids.reshape(n, 1).contiguous(), wt, out, embed_dim=d,
-                                       expert_mlp_dim=F, num_experts=hi - lo, x_layout=MB.X_NATURAL, top_k=1)
+            ids, k = local_ids.reshape(n, 1), 1
+        else:  # dedup: each row's leading `count` slots, weighted
+            cnt, wt, ids, k = count.to(torch.int64), weights, local_ids, local_ids.shape[1]
+        ctx.run_moe_coalesced_core(n, gu_p, gu_s, dn_p, dn_s, rows.contiguous(), cnt.contiguous(),
+                                   ids.to(torch.int64).contiguous(), wt.to(torch.float32).contiguous(), out,
+                                   embed_dim=d, expert_mlp_dim=F, num_experts=hi - lo,
+                                   x_layout=MB.X_NATURAL, top_k=k)
         return out
 
     def rms_norm_fn(x, w, out):

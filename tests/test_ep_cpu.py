@@ -98,7 +98,7 @@ def test_two_gloo_ranks_reproduce_the_full_layer():
     assert res[0][3] + res[1][3] > 0
 
 
-def _a2a_worker(rank, world, port, q, M):
+def _a2a_worker(rank, world, port, q, M, dedup=False):
     """All-to-all expert parallelism on gloo ranks: tokens sharded over the
     ranks, routed rows dispatched to the owners of their experts and the
     results returned; route and expert evaluation by the oracle."""
@@ -126,10 +126,18 @@ def _a2a_worker(rank, world, port, q, M):
             return (torch.from_numpy(r["count"]), torch.from_numpy(r["idx"]), torch.from_numpy(r["w"]),
                     torch.from_numpy(r["moe_in"]))
 
-        def experts_fn(rows, local_ids):
+        def experts_fn(rows, local_ids, weights=None, count=None):
             n = rows.shape[0]
             if n == 0:
                 return torch.zeros((0, d))
+            if dedup:  # each row's leading `count` slots, weighted
+                gidx = local_ids.numpy() + lo
+                c = count.numpy()
+                for r in range(n):
+                    assert ((gidx[r, :c[r]] >= lo) & (gidx[r, :c[r]] < hi)).all()
+                y = O.experts_forward(L, rows.numpy(), c.astype(np.int64), gidx.astype(np.int64),
+                                      weights.numpy().astype(np.float32), prec=O.F64)
+                return torch.from_numpy(y)
             idx = np.zeros((n, K), np.int64)
             idx[:, 0] = local_ids.numpy() + lo
             assert ((idx[:, 0] >= lo) & (idx[:, 0] < hi)).all()
@@ -138,7 +146,7 @@ def _a2a_worker(rank, world, port, q, M):
             y = O.experts_forward(L, rows.numpy(), np.ones(n, np.int64), idx, wt, prec=O.F64)
             return torch.from_numpy(y)
 
-        layer = ep.AllToAllExpertParallelLayer(E, route_fn, experts_fn)
+        layer = ep.AllToAllExpertParallelLayer(E, route_fn, experts_fn, dedup=dedup)
         ones = torch.ones(d)
         out = layer.forward(torch.from_numpy(x), post_norm_w=ones).numpy()
         ref, _, _, _ = O.layer_forward(L, x_all, post_norm=True, prec=O.F64)
@@ -150,15 +158,17 @@ def _a2a_worker(rank, world, port, q, M):
         q.put((rank, traceback.format_exc(), None))
 
 
+@pytest.mark.parametrize("dedup", [False, True], ids=["per-pair", "per-token"])
 @pytest.mark.parametrize("world,M", [(2, 7), (3, 2)])
-def test_all_to_all_ranks_reproduce_the_full_layer(world, M):
+def test_all_to_all_ranks_reproduce_the_full_layer(world, M, dedup):
     """Uneven token shards (7 over 2 ranks; 2 over 3, one rank without
     tokens): the dispatched, evaluated and combined output equals the
-    one-process layer."""
+    one-process layer, with one row per routed pair or (dedup) one row per
+    token and destination rank."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_a2a_worker, args=(r, world, port, q, M)) for r in range(world)]
+    procs = [ctx.Process(target=_a2a_worker, args=(r, world, port, q, M, dedup)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in procs]
@@ -203,9 +213,10 @@ class _OracleCtx:
         import oracle as O
         import torch
         import moe_b200 as MB
-        assert x_layout == MB.X_NATURAL and top_k == 1
-        assert (idx >= 0).all() and (idx < num_experts).all()
-        sub = dict(d=embed_dim, F=expert_mlp_dim, E=num_experts, top_k=1,
+        assert x_layout == MB.X_NATURAL and idx.shape == (n, top_k)
+        for r in range(n):
+            assert (idx[r, :cnt[r]] >= 0).all() and (idx[r, :cnt[r]] < num_experts).all()
+        sub = dict(d=embed_dim, F=expert_mlp_dim, E=num_experts, top_k=top_k,
                    gu_p=np.ascontiguousarray(gu_p), gu_s=np.ascontiguousarray(gu_s),
                    dn_p=np.ascontiguousarray(dn_p), dn_s=np.ascontiguousarray(dn_s))
         for k in ("router_scale", "pre_norm_w", "post_norm_w"):
@@ -220,7 +231,7 @@ class _OracleCtx:
         out.copy_((x64 / (x64.pow(2).mean(1, keepdim=True) + 1e-6).sqrt() * w.double()).float())
 
 
-def _lib_worker(rank, world, port, q):
+def _lib_worker(rank, world, port, q, dedup=False):
     """make_library_fns' weight slices and calls, through the oracle stand-in."""
     try:
         import torch
@@ -236,7 +247,7 @@ def _lib_worker(rank, world, port, q):
         x_all = np.random.default_rng(32).standard_normal((M, d)).astype(np.float32)
         t0, t1 = ep.row_range(rank, world, M)
         route_fn, experts_fn, rms_norm_fn = ep.make_library_fns(_OracleCtx(L), None, w, rank, world)
-        layer = ep.AllToAllExpertParallelLayer(E, route_fn, experts_fn, rms_norm_fn=rms_norm_fn)
+        layer = ep.AllToAllExpertParallelLayer(E, route_fn, experts_fn, rms_norm_fn=rms_norm_fn, dedup=dedup)
         out = layer.forward(torch.from_numpy(x_all[t0:t1].copy()), post_norm_w=torch.ones(d)).numpy()
         ref, _, _, _ = O.layer_forward(L, x_all, post_norm=True, prec=O.F64)
         err = float(np.max(np.abs(out - ref[t0:t1]))) if t1 > t0 else 0.0
@@ -247,14 +258,16 @@ def _lib_worker(rank, world, port, q):
         q.put((rank, traceback.format_exc(), None))
 
 
-def test_all_to_all_library_functions_slice_the_weights():
-    """make_library_fns hands each rank's expert slice and local ids to the
-    coalesced core; with the oracle behind the calls, three ranks reproduce
-    the one-process layer."""
+@pytest.mark.parametrize("dedup", [False, True], ids=["per-pair", "per-token"])
+def test_all_to_all_library_functions_slice_the_weights(dedup):
+    """make_library_fns hands each rank's expert slice and local ids (and,
+    per token, the local slot lists and weights) to the coalesced core; with
+    the oracle behind the calls, three ranks reproduce the one-process
+    layer."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_lib_worker, args=(r, 3, port, q)) for r in range(3)]
+    procs = [ctx.Process(target=_lib_worker, args=(r, 3, port, q, dedup)) for r in range(3)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in procs]
