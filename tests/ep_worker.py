@@ -78,6 +78,19 @@ def main():
         print(f"rank {rank} all-to-all M={M} rows {t0}:{t1}: max_abs={mx:.2e} rel_l2={rel:.2e} "
               f"(bar {bar_abs:.1e}, {bar_rel:.0e})", flush=True)
         ok = ok and mx <= bar_abs and rel <= bar_rel
+    # all-to-all, one row per token and destination rank (dedup): single rows
+    # take the same path as layer_forward's, so the tight bar holds at M=1 too
+    a2a_tok = ep.AllToAllExpertParallelLayer(layer["E"], route_fn, experts_fn, rms_norm_fn=rms_norm_fn, dedup=True)
+    for M in (1, 64, 1000):
+        x = synth.make_x(M, seed=170 + M)
+        t0, t1 = ep.row_range(rank, world, M)
+        out = a2a_tok.forward(x[t0:t1].contiguous(), post_norm_w=layer["post_norm_w"])
+        ref = torch.zeros((M, layer["d"]), device="cuda")
+        ctx.layer_forward(desc, M, x, ref, MB.F_POST_NORM)
+        torch.cuda.synchronize()
+        mx, rel = errors(out.cpu().numpy(), ref[t0:t1].cpu().numpy()) if t1 > t0 else (0.0, 0.0)
+        print(f"rank {rank} all-to-all dedup M={M} rows {t0}:{t1}: max_abs={mx:.2e} rel_l2={rel:.2e}", flush=True)
+        ok = ok and mx <= 5e-4 and rel <= 1e-4
     # the library's own communicator (moe_ep_init): one call per layer
     uid = [MB.ep_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
