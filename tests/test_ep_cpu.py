@@ -147,8 +147,19 @@ def _a2a_worker(rank, world, port, q, M, dedup=False):
             return torch.from_numpy(y)
 
         layer = ep.AllToAllExpertParallelLayer(E, route_fn, experts_fn, dedup=dedup)
+        sent = []  # rows of every exchange this rank sends
+        exchange = layer._exchange
+        layer._exchange = lambda send, sc, rc: (sent.append(int(sum(sc))), exchange(send, sc, rc))[1]
         ones = torch.ones(d)
         out = layer.forward(torch.from_numpy(x), post_norm_w=ones).numpy()
+        m = t1 - t0
+        pairs = int(O.route(L, x)["count"].sum()) if m else 0
+        rows = sent[0]  # the dispatch of the activation rows
+        assert rows <= pairs
+        if dedup:
+            assert rows <= m * world
+        else:
+            assert rows == pairs
         ref, _, _, _ = O.layer_forward(L, x_all, post_norm=True, prec=O.F64)
         err = float(np.max(np.abs(out - ref[t0:t1]))) if t1 > t0 else 0.0
         dist.destroy_process_group()
