@@ -262,6 +262,15 @@ def run_reference(args, ws, rank):
     return 0
 
 
+def dtype_desc(args, M):
+    """The arithmetic the GPU arm's expert GEMMs run (routing, norms and the
+    combine are fp32 on CUDA cores in every case)."""
+    path = getattr(args, "path", "auto")
+    if path == "gemv" or (path == "auto" and M < 2):
+        return "f32 (CUDA-core fp32 FMA throughout)"
+    return "f32 io and routing; fp16 x fp16 -> fp32 tcgen05 expert GEMMs"
+
+
 def workload_config(args, M):
     return {"workload": WORKLOAD_NAMES[args.workload],
             "tokens_per_step": M, "embed_dim": D, "expert_mlp_dim": F, "num_experts": E, "top_k": K,
@@ -611,7 +620,8 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "strong" if use_ep else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong" if use_ep else "weak", "vs_baseline": None, "dtype": dtype_desc(args, M),
+            "data": "synthetic",
             "config": dict(workload_config(args, M), **({"skew": skew} if skew else {})),
             "roofline": roof, "step_roofline": step_roof,
             "cpu_baseline": cpu,

@@ -165,16 +165,19 @@ int moe_q4_matmul_batchN(moe_ctx* ctx, int64_t batch_size, const uint8_t* W_pack
  * synchronise the device.  Same arguments and results as
  * moe_q4_matmul_batchN, except:
  *  - scratch (the fp16 copy of x_batch and split-K partial sums) lives in
- *    one static device array of 8 MiB per device, loaded with the library;
+ *    one static device array of 8 MiB per device.  moe_ctx_create commits
+ *    it when the first context on a device is created (it stays until the
+ *    process exits), so no call of this entry point loads or allocates it;
  *    batch_size * c_in * 2 must be <= 8 MiB (8388608 bytes), else the call
  *    returns MOE_E_SHAPE and does nothing.  The scratch needs no initial
  *    value: every byte a call reads was written earlier in that call;
+ *  - the split-K count is the one moe_q4_matmul_batchN picks (including
+ *    MOE_OPT_DENSE_KSPLIT), so the results are the same bits; only when
+ *    that many partial sums do not fit beside the fp16 copy is it lowered,
+ *    and the results then differ by fp32 reassociation;
  *  - every pointer must be device memory or inside a registered range
  *    (MOE_E_ARG otherwise: host buffers are not staged), and x_batch and
  *    W_packed 16-byte aligned;
- *  - the first call on a device looks up the scratch's address (once per
- *    device, with that device current); make that first call before any
- *    stream capture begins on the calling thread;
  *  - the scratch is shared by every context and stream on the device: two
  *    calls in flight at the same time on one device (different streams,
  *    contexts or threads) race on it.  Calls ordered on one stream do not. */
@@ -261,7 +264,12 @@ int moe_run_moe_coalesced_core(moe_ctx* ctx, int64_t sub_b,
  * that result and writes the per-token weighted sums to batch_moe_out [sub_b
  * x d]; the bucket arguments are accepted for signature parity and not read.
  * MOE_E_STATE: no stage-1 result for that scratch pointer, or the options or
- * the down weights' alignment changed the expert path between the calls. */
+ * the down weights' alignment changed the expert path between the calls.
+ * Summation order: stage 2 adds each token's expert outputs in the token's
+ * slot order (as run_moe_experts_stage2_8core does, moe_kernels.mojo:775-779);
+ * the reference's coalesced stage 2 zeroes the output and adds in ascending
+ * expert order (:1095-1318).  The two orders differ only by fp32
+ * reassociation of at most top_k terms per output element. */
 int moe_run_moe_coalesced_stage1(moe_ctx* ctx, int64_t sub_b, const uint8_t* experts_gate_up_packed,
                                  const float* experts_gate_up_scales, const float* batch_in,
                                  int x_layout, const int64_t* tok_active_count,

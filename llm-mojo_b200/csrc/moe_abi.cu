@@ -654,6 +654,10 @@ int dense_q4(moe_ctx* ctx, const uint8_t* w, const float* sc, const float* xd, f
     return MOE_OK;
 }
 
+// Device address of moe_q4_matmul_batchN_noalloc's static scratch on the
+// context's device (defined with the entry point at the end of this file).
+int noalloc_scratch(moe_ctx* ctx, void** out);
+
 }  // namespace
 
 // ======================================================================
@@ -680,6 +684,17 @@ int moe_ctx_create(int device, moe_ctx** out) {
         return MOE_E_CUDA;
     }
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+    // The no-alloc entry point's static scratch belongs to this file's device
+    // module, which has no kernel.  Under lazy module loading (the CUDA 12
+    // default) that module, and with it the 8 MiB array, is loaded the first
+    // time the array's address is looked up.  Looking it up here commits the
+    // memory when the first context on a device is created, so that no
+    // moe_q4_matmul_batchN_noalloc call ever triggers the load.
+    void* scratch = nullptr;
+    if (noalloc_scratch(ctx, &scratch) != MOE_OK) {
+        moe_ctx_destroy(ctx);
+        return MOE_E_NOMEM;
+    }
     *out = ctx;
     return MOE_OK;
 }
@@ -1965,8 +1980,11 @@ int moe_q4_matmul_batchN_noalloc(moe_ctx* ctx, int64_t batch, const uint8_t* W, 
     t.max_items = ((c_out + 127) / 128) * ((batch + BN - 1) / BN);
     t.a_in_smem = ctx->tc_a_in_smem;
     t.stream = ctx->tc_stream >= 2;
-    // split-K partials go after the activation copy, as many splits as fit
-    int ks = choose_ksplit(ctx, t.max_items, c_in);
+    // split-K partials go after the activation copy: the split count
+    // moe_q4_matmul_batchN would choose (so both give the same bits), lowered
+    // only when that many partial sums do not fit
+    int ks = ctx->dense_ksplit > 0 ? (int)std::min<int64_t>(ctx->dense_ksplit, std::max<int64_t>(1, c_in / 256))
+                                   : choose_ksplit(ctx, t.max_items, c_in);
     const size_t part_room = kNoAllocScratchBytes - x16_bytes;
     while (ks > 1 && (size_t)ks * batch * c_out * 4 > part_room) --ks;
     float* part = nullptr;

@@ -447,6 +447,8 @@ void orc_route(const orc_layer* L, int64_t M, const float* x, int use_set_cover,
             }
         }
         if (scores_out) memcpy(scores_out + t * E, sc, sizeof(float) * (size_t)E);
+        if (L->router_logit_bias)  /* synthetic skew only; the reference has no bias */
+            for (int64_t e = 0; e < E; ++e) sc[e] += L->router_logit_bias[e];
         orc_softmax(sc, E);
         orc_get_top_k(sc, E, K, ti + t * K, tv + t * K);
         if (moe_in) orc_rms_norm(xt, L->pre_norm_w, moe_in + t * d, d);

@@ -88,6 +88,11 @@ typedef struct {
     const float* post_norm_w;     /* [d] post_feedforward_layernorm_2 */
     const uint8_t* gu_p; const float* gu_s;           /* [E][2F x d] */
     const uint8_t* dn_p; const float* dn_s;           /* [E][d x F]  */
+    /* optional [E], added to the router logits before the softmax.  No
+     * counterpart in the reference (its router has no bias): the synthetic
+     * skew of the M=8192 prefill workload, a Zipf(1.1) bias, goes through
+     * the same place in the library (moe_layer_desc.router_logit_bias). */
+    const float* router_logit_bias;
 } orc_layer;
 
 void orc_route(const orc_layer* L, int64_t M, const float* x, int use_set_cover,

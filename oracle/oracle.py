@@ -53,6 +53,7 @@ class OrcLayer(C.Structure):
         ("router_scale", _p), ("per_expert_scale", _p),
         ("pre_norm_w", _p), ("post_norm_w", _p),
         ("gu_p", _p), ("gu_s", _p), ("dn_p", _p), ("dn_s", _p),
+        ("router_logit_bias", _p),
     ]
 
 
@@ -192,8 +193,11 @@ def experts_stage2(dn_p, dn_s, act_all, act_idx, act_w, d, F, prec=F64, nthreads
     return out
 
 
-def make_layer(w: dict, act=ACT_SIGMOID1702, top_p=1.0, r_scale_factor=None):
-    """Builds an OrcLayer from a dict of numpy arrays (see tests/synth.py)."""
+def make_layer(w: dict, act=ACT_SIGMOID1702, top_p=1.0, r_scale_factor=None, bias=None):
+    """Builds an OrcLayer from a dict of numpy arrays (see tests/synth.py).
+    `bias` (optional, [E] fp32) is added to the router logits before the
+    softmax: the synthetic skew of the prefill workload, not a reference
+    feature."""
     d, F, E, K = w["d"], w["F"], w["E"], w["top_k"]
     L = OrcLayer()
     L.d, L.F, L.E, L.top_k = d, F, E, K
@@ -209,7 +213,10 @@ def make_layer(w: dict, act=ACT_SIGMOID1702, top_p=1.0, r_scale_factor=None):
     L.post_norm_w = _ptr(w["post_norm_w"])
     L.gu_p, L.gu_s = _ptr(w["gu_p"]), _ptr(w["gu_s"])
     L.dn_p, L.dn_s = _ptr(w["dn_p"]), _ptr(w["dn_s"])
-    L._keep = w  # keep arrays alive
+    if bias is not None:
+        bias = np.ascontiguousarray(bias, np.float32)
+        L.router_logit_bias = _ptr(bias)
+    L._keep = (w, bias)  # keep arrays alive
     return L
 
 

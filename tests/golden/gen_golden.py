@@ -126,5 +126,12 @@ def main(ref_root: str) -> None:
     print("wrote", sorted(os.listdir(HERE)))
 
 
+def _ref_dir() -> str:
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLM_MOJO_REF")
+    if not ref:
+        sys.exit("usage: gen_golden.py /path/to/llm-mojo  (or set LLM_MOJO_REF)")
+    return ref
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLM_MOJO_REF", "/root/reference"))
+    main(_ref_dir())

@@ -108,4 +108,7 @@ def main(ref_root: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLM_MOJO_REF", "../llm-mojo"))
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLM_MOJO_REF")
+    if not ref:
+        sys.exit("usage: gen_weights_file_golden.py /path/to/llm-mojo  (or set LLM_MOJO_REF)")
+    main(ref)

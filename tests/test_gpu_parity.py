@@ -324,6 +324,36 @@ def test_async_enqueue_and_bounded_wait(ctx, full_layer):
     assert np.array_equal(out.cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("M", [1, 16])
+def test_device_wait_deadline_returns_timeout_and_context_recovers(ctx, full_layer, M):
+    """Every mbarrier wait of the expert kernels is bounded by
+    MOE_OPT_DEVICE_TIMEOUT_NS.  With a 1 us deadline the waits for weight
+    tiles that are still in flight run out: the kernel raises the error word,
+    drains its copies, frees its tensor memory and returns, and the call
+    returns MOE_E_TIMEOUT.  Then, with the default deadline back, the same
+    context gives oracle-correct output.  (M=1: the CUDA-core kernel pair,
+    M=16: the tensor-core streaming kernels.)"""
+    dev, host, L = full_layer
+    desc = MB.make_desc(dev)
+    x = synth.make_x(M, seed=41).cpu().numpy()
+    out = np.zeros((M, 2816), np.float32)
+    ctx.set_option(MB.OPT_DEVICE_TIMEOUT_NS, 1000)
+    try:
+        with pytest.raises(MB.MoeError) as ei:
+            ctx.layer_forward(desc, M, x, out, flags=0)
+        assert ei.value.code == 6, ei.value  # MOE_E_TIMEOUT
+        assert "deadline" in str(ei.value)
+    finally:
+        ctx.set_option(MB.OPT_DEVICE_TIMEOUT_NS, 4_000_000_000)
+    cnt = np.zeros(M, np.int64)
+    idx = np.zeros((M, 8), np.int64)
+    w = np.zeros((M, 8), np.float32)
+    ctx.layer_forward(desc, M, x, out, 0, cnt, idx, w)
+    r = O.route(L, x)
+    ref = O.experts_forward(L, r["moe_in"], cnt, idx, w, prec=O.F64)
+    assert_close(out, ref, what=f"after the timeout, M={M}")
+
+
 # ------------------------------------------------------------- error paths
 def test_unregistered_host_weights_are_rejected(ctx):
     W = np.zeros(64 * 32, np.uint8)

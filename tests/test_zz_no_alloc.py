@@ -70,6 +70,91 @@ def test_noalloc_matches_workspace_entry_point(nctx, batch, c_in, c_out):
         assert_close(got, ref_h, what=f"call {call} batch={batch} c_in={c_in} c_out={c_out}")
 
 
+def test_noalloc_vs_oracle(nctx):
+    """The variant against the CPU oracle itself, not only against the
+    workspace entry point (a fault both share would pass that comparison)."""
+    import torch
+    import oracle as O
+    batch, c_in, c_out = 16, 2816, 1024
+    rng = np.random.default_rng(21)
+    w = rng.normal(0, 0.02, c_out * c_in).astype(np.float32)
+    W, S, _ = O.quantize_q4_0(w)
+    x = rng.standard_normal((batch, c_in)).astype(np.float32)
+    Wd, Sd, xd = torch.from_numpy(W).cuda(), torch.from_numpy(S).cuda(), torch.from_numpy(x).cuda()
+    ref = O.q4_matmul(W, S, x, c_in, c_out, prec=O.F64)
+    for call in range(2):
+        out = torch.full((batch, c_out), float("nan"), device="cuda")
+        assert _call_noalloc(nctx, batch, Wd, Sd, xd, out, c_in, c_out) == 0, nctx.last_error()
+        torch.cuda.synchronize()
+        assert_close(out.cpu().numpy(), ref, what=f"call {call} vs oracle")
+
+
+def test_noalloc_honours_the_dense_ksplit_option(nctx):
+    """With MOE_OPT_DENSE_KSPLIT set, both entry points split K the same way
+    and give the same bits."""
+    import torch
+    import moe_b200 as MB
+    batch, c_in, c_out = 8, 2816, 2816
+    packed, scales = _q4_matrix(nctx, c_out, c_in, seed=31)
+    x = torch.randn(batch, c_in, device="cuda")
+    ref = torch.empty(batch, c_out, device="cuda")
+    out = torch.empty(batch, c_out, device="cuda")
+    nctx.set_option(MB.OPT_DENSE_KSPLIT, 3)
+    try:
+        assert nctx.lib.moe_q4_matmul_batchN(nctx.h, batch, C.c_void_p(packed.data_ptr()),
+                                             C.c_void_p(scales.data_ptr()), C.c_void_p(x.data_ptr()),
+                                             C.c_void_p(ref.data_ptr()), c_in, c_out) == 0, nctx.last_error()
+        assert _call_noalloc(nctx, batch, packed, scales, x, out, c_in, c_out) == 0, nctx.last_error()
+        torch.cuda.synchronize()
+    finally:
+        nctx.set_option(MB.OPT_DENSE_KSPLIT, 0)
+    assert torch.equal(out, ref)
+
+
+_FRESH = r"""
+import ctypes as C, sys, torch
+sys.path[:0] = [{pkg!r}]
+import moe_b200
+torch.cuda.init()
+c_in, c_out, batch = 2816, 2816, 16
+w = torch.randn(c_out * c_in, device="cuda") * 0.02
+packed = torch.empty(c_out * c_in // 2, dtype=torch.uint8, device="cuda")
+scales = torch.empty(c_out * c_in // 32, dtype=torch.float32, device="cuda")
+x = torch.randn(batch, c_in, device="cuda")
+out = torch.empty(batch, c_out, device="cuda")
+ctx = moe_b200.Context(0)
+ctx.quantize_fp32_to_q4_0(w, packed, scales, c_out * c_in)
+args = (ctx.h, batch, C.c_void_p(packed.data_ptr()), C.c_void_p(scales.data_ptr()),
+        C.c_void_p(x.data_ptr()), C.c_void_p(out.data_ptr()), c_in, c_out)
+# the workspace entry point first: it loads the kernels both entry points
+# launch and grows the context's workspace; neither is what is measured
+assert ctx.lib.moe_q4_matmul_batchN(*args) == 0, ctx.last_error()
+torch.cuda.synchronize()
+free0 = torch.cuda.mem_get_info()[0]
+for _ in range(2):
+    assert ctx.lib.moe_q4_matmul_batchN_noalloc(*args) == 0, ctx.last_error()
+torch.cuda.synchronize()
+free1 = torch.cuda.mem_get_info()[0]
+print("FREE", free0, free1)
+ctx.close()
+"""
+
+
+def test_first_noalloc_call_in_a_fresh_process_allocates_nothing():
+    """In a new process the first no-alloc call must not load the static
+    scratch (8 MiB) either: creating the context commits it."""
+    import os
+    import subprocess
+    import sys
+    pkg = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "llm-mojo_b200")
+    r = subprocess.run([sys.executable, "-c", _FRESH.format(pkg=pkg)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    line = [ln for ln in r.stdout.splitlines() if ln.startswith("FREE")][0]
+    free0, free1 = (int(v) for v in line.split()[1:])
+    assert free1 == free0, f"free device memory fell by {free0 - free1} bytes during the first no-alloc calls"
+
+
 def test_noalloc_allocates_nothing(nctx):
     import torch
     batch, c_in, c_out = 32, 2816, 2816
