@@ -301,6 +301,60 @@ int moe_run_diffusion_moe_experts_parallel(moe_ctx* ctx, const uint8_t* experts_
                                            int64_t embed_dim, int64_t expert_mlp_dim,
                                            int64_t top_k_experts, int activation);
 
+/* ------------------------------------- diffusion router-subspace FFN bypass */
+/* router_subspace_ffn_filter (diffusion_kernels.mojo:2253-2337).  For each
+ * canvas row b (canvas position o = active_canvas_idx[b], or b when it is
+ * NULL): when step >= 1, the token is accepted (eb_mask[o] != 0, or eb_mask
+ * NULL), top_k >= 2, its top-2 experts equal prev_top2[o] and the drift of
+ * its router logits r_curr[b] from r_prev[o] is small (sum (c-p)^2 <=
+ * tau_ffn^2 * sum p^2, or <= 1e-12 when sum p^2 <= 1e-12), the row is
+ * bypassed: its top_weights row (if given) is zeroed.  Otherwise b is
+ * appended to ffn_keep_b (ascending) and r_prev[o], prev_top2[o] take the
+ * current values.  *active_count receives the reference's return value (the
+ * number of kept rows); the call completes before returning, also in
+ * asynchronous mode.  The drift sums are formed in the reference's 8-lane
+ * order, so every decision is the reference's bit for bit.  r_curr [B x
+ * num_experts], r_prev [canvas x num_experts] fp32; top_idx [B x top_k],
+ * prev_top2 [canvas x 2] int64; eb_mask [canvas] uint8; ffn_keep_b [B].
+ * The canvas positions of the B rows must be distinct. */
+int moe_router_subspace_ffn_filter(moe_ctx* ctx, const float* r_curr, float* r_prev,
+                                   const int64_t* top_idx, int64_t* prev_top2,
+                                   const uint8_t* eb_mask, const int64_t* active_canvas_idx,
+                                   int64_t* ffn_keep_b, int64_t B, int64_t num_experts,
+                                   int64_t top_k, int64_t step, float tau_ffn,
+                                   float* top_weights, int64_t* active_count);
+
+/* sync_moe_subspace_cache (diffusion_kernels.mojo:2345-2381): rows of dim
+ * elements of elem_bytes bytes (2: the reference's default fp16; 4: fp32).
+ * Walking b in order with a cursor into ffn_keep_b[0, ffn_active_len), row b
+ * of moe_out is saved to moe_prev_cache[o] when it is the cursor's entry
+ * (evaluated), else restored from it (bypassed). */
+int moe_sync_moe_subspace_cache(moe_ctx* ctx, void* moe_out, void* moe_prev_cache,
+                                const int64_t* active_canvas_idx, const int64_t* ffn_keep_b,
+                                int64_t B, int64_t ffn_active_len, int64_t dim,
+                                int64_t elem_bytes);
+
+/* scatter_and_restore_ffn_subspace (diffusion_kernels.mojo:2386-2426): as
+ * the sync above, but an evaluated row comes from the compacted sub-batch
+ * output ffn_sub_out[cursor] and goes to both ffn_full_out[b] and
+ * ffn_prev_cache[o]; a bypassed row of ffn_full_out comes from the cache. */
+int moe_scatter_and_restore_ffn_subspace(moe_ctx* ctx, const void* ffn_sub_out,
+                                         void* ffn_prev_cache, void* ffn_full_out,
+                                         const int64_t* active_canvas_idx,
+                                         const int64_t* ffn_keep_b, int64_t B,
+                                         int64_t ffn_active_len, int64_t dim,
+                                         int64_t elem_bytes);
+
+/* Check of the bounded device-side waits (no counterpart in the reference).
+ * Every pipelined kernel of the library waits on shared-memory barriers
+ * with a deadline of MOE_OPT_DEVICE_TIMEOUT_NS; when one passes, the kernel
+ * stops, drains what it issued, raises the context's error word and the
+ * call returns MOE_E_TIMEOUT.  This call launches one block that waits on a
+ * barrier nothing completes, with the same wait code and the context's
+ * deadline, so it returns MOE_E_TIMEOUT after about that deadline when the
+ * mechanism works (never MOE_OK).  The context stays usable afterwards. */
+int moe_device_wait_check(moe_ctx* ctx);
+
 /* --------------------------------------------------------- whole layer */
 enum moe_layer_flags {
     MOE_F_POST_NORM = 1, /* apply rms_norm(moe_out, post_norm_w) (model_speculative_moe_batched.mojo:1144-1150) */

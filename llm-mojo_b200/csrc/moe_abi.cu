@@ -1517,6 +1517,142 @@ int moe_run_diffusion_moe_experts_parallel(moe_ctx* ctx, const uint8_t* gu_p, co
     return finish(ctx);
 }
 
+// ------------------------------------------- diffusion router-subspace bypass
+}  // extern "C"
+
+namespace {
+
+// Number of canvas rows the per-canvas arrays (indexed by
+// active_canvas_idx[b], else by b) must hold: max(B, max index + 1).
+int canvas_rows(moe_ctx* ctx, const int64_t* active_idx, int64_t B, int64_t* n) {
+    *n = B;
+    if (!active_idx) return MOE_OK;
+    std::vector<int64_t> h((size_t)B);
+    TRY(get_small(ctx, h.data(), active_idx, (size_t)B * 8));
+    for (int64_t v : h) {
+        if (v < 0) return fail(ctx, MOE_E_ARG, "negative entry in active_canvas_idx");
+        *n = std::max(*n, v + 1);
+    }
+    return MOE_OK;
+}
+
+// sync_moe_subspace_cache and scatter_and_restore_ffn_subspace: `sub` is
+// null for the former.
+int subspace_rows(moe_ctx* ctx, const void* sub, void* cache, void* out, const int64_t* active_idx,
+                  const int64_t* keep, int64_t B, int64_t len, int64_t dim, int64_t elem_bytes) {
+    TRY(begin(ctx));
+    if (!cache || !out || (len > 0 && !keep)) return fail(ctx, MOE_E_ARG, "null pointer");
+    if (elem_bytes != 2 && elem_bytes != 4) return fail(ctx, MOE_E_ARG, "elem_bytes must be 2 (fp16) or 4 (fp32)");
+    if (B <= 0 || dim <= 0) return MOE_OK;  // the reference returns at once
+    if (len < 0 || len > B) return fail(ctx, MOE_E_SHAPE, "ffn_active_len must be in [0, B]");
+    int64_t nc;
+    TRY(canvas_rows(ctx, active_idx, B, &nc));
+    const int64_t rb = dim * elem_bytes;
+    TRY(ws_reserve(ctx, al(B * 4) + al(B * 8) + al(len * 8) + al(len * rb) + al(B * rb) + al(nc * rb)));
+    void *m = ws_take(ctx, B * 4), *ai = nullptr, *kp = nullptr, *sp = nullptr, *cp, *op;
+    TRY(dev_ptr(ctx, active_idx, B * 8, K_IN, &ai));
+    if (len > 0) TRY(dev_ptr(ctx, keep, len * 8, K_IN, &kp));
+    if (sub && len > 0) TRY(dev_ptr(ctx, sub, len * rb, K_IN, &sp));
+    TRY(dev_ptr(ctx, cache, nc * rb, K_INOUT, &cp));
+    TRY(dev_ptr(ctx, out, B * rb, sub ? K_OUT : K_INOUT, &op));
+    moe::SubspaceRowsArgs a;
+    a.out = (uint8_t*)op;
+    a.cache = (uint8_t*)cp;
+    a.sub = sub ? (const uint8_t*)(sp ? sp : op) : nullptr;  // len 0: never read, but non-null selects the form
+    a.active_idx = (const int64_t*)ai;
+    a.map = (int*)m;
+    a.B = B;
+    a.row_bytes = rb;
+    ctx->launches += moe::launch_subspace_rows(a, (const int64_t*)kp, len, ctx->stream);
+    return finish(ctx);
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_router_subspace_ffn_filter(moe_ctx* ctx, const float* r_curr, float* r_prev, const int64_t* top_idx,
+                                   int64_t* prev_top2, const uint8_t* eb_mask, const int64_t* active_canvas_idx,
+                                   int64_t* ffn_keep_b, int64_t B, int64_t num_experts, int64_t top_k,
+                                   int64_t step, float tau_ffn, float* top_weights, int64_t* active_count) {
+    TRY(begin(ctx));
+    if (!active_count) return fail(ctx, MOE_E_ARG, "null pointer");
+    if (B <= 0) {  // the reference returns 0 at once
+        const int64_t zero = 0;
+        return put_small(ctx, active_count, &zero, 8);
+    }
+    if (!r_curr || !r_prev || !top_idx || !prev_top2 || !ffn_keep_b) return fail(ctx, MOE_E_ARG, "null pointer");
+    if (num_experts < 0 || top_k < 1 || num_experts > (1 << 20) || top_k > 1024)
+        return fail(ctx, MOE_E_SHAPE, "num_experts / top_k out of range");
+    int64_t nc;
+    TRY(canvas_rows(ctx, active_canvas_idx, B, &nc));
+    const int64_t E = num_experts, K = top_k;
+    TRY(ws_reserve(ctx, al(B * E * 4) + al(nc * E * 4) + al(B * K * 8) + al(nc * 16) + al(nc) + al(B * 8) * 2 +
+                            al(B * K * 4) + al(8)));
+    void *rc, *rp, *ti, *pt, *eb = nullptr, *ai = nullptr, *kb, *tw = nullptr;
+    TRY(dev_ptr(ctx, r_curr, B * E * 4, K_IN, &rc));
+    TRY(dev_ptr(ctx, r_prev, nc * E * 4, K_INOUT, &rp));
+    TRY(dev_ptr(ctx, top_idx, B * K * 8, K_IN, &ti));
+    TRY(dev_ptr(ctx, prev_top2, nc * 16, K_INOUT, &pt));
+    if (eb_mask) TRY(dev_ptr(ctx, eb_mask, nc, K_IN, &eb));
+    TRY(dev_ptr(ctx, active_canvas_idx, B * 8, K_IN, &ai));
+    TRY(dev_ptr(ctx, ffn_keep_b, B * 8, K_INOUT, &kb));
+    if (top_weights) TRY(dev_ptr(ctx, top_weights, B * K * 4, K_INOUT, &tw));
+    int64_t* cnt = (int64_t*)ws_take(ctx, 8);
+    moe::SubspaceFilterArgs a;
+    a.r_curr = (const float*)rc;
+    a.r_prev = (float*)rp;
+    a.top_idx = (const int64_t*)ti;
+    a.prev_top2 = (int64_t*)pt;
+    a.eb_mask = (const uint8_t*)eb;
+    a.active_idx = (const int64_t*)ai;
+    a.keep_out = (int64_t*)kb;
+    a.top_w = (float*)tw;
+    a.count_out = cnt;
+    a.B = B;
+    a.E = (int)E;
+    a.K = (int)K;
+    a.step = step;
+    a.tau = tau_ffn;
+    ctx->launches += moe::launch_subspace_filter(a, ctx->stream);
+    // the count is the reference's return value: the call completes here
+    const int async = ctx->async_mode;
+    ctx->async_mode = 0;
+    const int st = finish(ctx);
+    ctx->async_mode = async;
+    TRY(st);
+    int64_t n = 0;
+    MOE_CUDA(cudaMemcpy(&n, cnt, 8, cudaMemcpyDeviceToHost));
+    return put_small(ctx, active_count, &n, 8);
+}
+
+int moe_sync_moe_subspace_cache(moe_ctx* ctx, void* moe_out, void* moe_prev_cache,
+                                const int64_t* active_canvas_idx, const int64_t* ffn_keep_b, int64_t B,
+                                int64_t ffn_active_len, int64_t dim, int64_t elem_bytes) {
+    return subspace_rows(ctx, nullptr, moe_prev_cache, moe_out, active_canvas_idx, ffn_keep_b, B, ffn_active_len,
+                         dim, elem_bytes);
+}
+
+int moe_scatter_and_restore_ffn_subspace(moe_ctx* ctx, const void* ffn_sub_out, void* ffn_prev_cache,
+                                         void* ffn_full_out, const int64_t* active_canvas_idx,
+                                         const int64_t* ffn_keep_b, int64_t B, int64_t ffn_active_len, int64_t dim,
+                                         int64_t elem_bytes) {
+    if (ctx && !ffn_sub_out && ffn_active_len > 0) return fail(ctx, MOE_E_ARG, "null pointer");
+    static const char kNone = 0;  // a non-null marker when no sub-batch row exists
+    return subspace_rows(ctx, ffn_sub_out ? ffn_sub_out : &kNone, ffn_prev_cache, ffn_full_out, active_canvas_idx,
+                         ffn_keep_b, B, ffn_active_len, dim, elem_bytes);
+}
+
+int moe_device_wait_check(moe_ctx* ctx) {
+    TRY(begin(ctx));
+    ctx->launches += moe::launch_wait_check(ctx->err_flag, ctx->device_timeout_ns, ctx->stream);
+    const int async = ctx->async_mode;
+    ctx->async_mode = 0;
+    const int st = finish(ctx);
+    ctx->async_mode = async;
+    return st;
+}
+
 // ------------------------------------------------------------ layer level
 namespace {
 

@@ -218,4 +218,35 @@ int launch_apply_lod(const int64_t* top_idx, const float* top_val, const float* 
                      const int64_t* active_canvas_idx, int64_t unaccepted_top_k, cudaStream_t s);
 
 
+// Router-subspace FFN bypass of the diffusion engine (moe_subspace.cu).
+struct SubspaceFilterArgs {
+    const float* r_curr = nullptr;      // [B][E] router logits of this step
+    float* r_prev = nullptr;            // [canvas][E] logits at each token's last evaluation
+    const int64_t* top_idx = nullptr;   // [B][K]
+    int64_t* prev_top2 = nullptr;       // [canvas][2]
+    const uint8_t* eb_mask = nullptr;   // [canvas] accepted tokens (nullable: all)
+    const int64_t* active_idx = nullptr;  // [B] canvas position of row b (nullable: b)
+    int64_t* keep_out = nullptr;        // [B] evaluated rows, ascending
+    float* top_w = nullptr;             // [B][K] zeroed for bypassed rows (nullable)
+    int64_t* count_out = nullptr;       // number of evaluated rows
+    int64_t B = 0;
+    int E = 0, K = 0;
+    int64_t step = 0;
+    float tau = 0.05f;
+};
+struct SubspaceRowsArgs {
+    uint8_t* out = nullptr;              // [B] rows: moe_out (sync) or ffn_full_out (scatter)
+    uint8_t* cache = nullptr;            // [canvas] rows
+    const uint8_t* sub = nullptr;        // scatter: [ffn_active_len] compacted rows; sync: nullptr
+    const int64_t* active_idx = nullptr;  // [B] (nullable: b)
+    int* map = nullptr;                  // [B] workspace: row -> matched ffn_keep_b entry or -1
+    int64_t B = 0;
+    int64_t row_bytes = 0;
+};
+int launch_subspace_filter(const SubspaceFilterArgs& a, cudaStream_t s);
+int launch_subspace_rows(const SubspaceRowsArgs& a, const int64_t* keep, int64_t len, cudaStream_t s);
+// One CTA waiting on an mbarrier that nothing completes, bounded by
+// `timeout_ns` (the check behind moe_device_wait_check).
+int launch_wait_check(int* err_flag, uint64_t timeout_ns, cudaStream_t s);
+
 }  // namespace moe

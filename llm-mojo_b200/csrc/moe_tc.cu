@@ -150,6 +150,9 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
     pdl_wait();  // barrier init, TMEM allocation and tensor-map prefetch overlap the previous kernel
     pdl_trigger();
     Guard G{abort_flag, a.err_flag, globaltimer() + a.timeout_ns};
+    // draining work already in flight always ends: it gets at least 2 s,
+    // whatever the (possibly much shorter) deadline of the work itself
+    const uint64_t drain_ns = a.timeout_ns > 2000000000ull ? a.timeout_ns : 2000000000ull;
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
@@ -189,7 +192,7 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
                 }
             }
             // drain: every armed stage's bytes must have landed before exit
-            Guard Gd{abort_flag, a.err_flag, globaltimer() + a.timeout_ns};
+            Guard Gd{abort_flag, a.err_flag, globaltimer() + drain_ns};
             volatile int no_abort = 0;
             Gd.abort = &no_abort;
             for (int s = 0; s < SQ; ++s)
@@ -239,7 +242,7 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
             }
             if (issued) {  // all MMAs complete before TMEM is released
                 tc_commit(drain_bar);
-                Guard Gd{abort_flag, a.err_flag, globaltimer() + a.timeout_ns};
+                Guard Gd{abort_flag, a.err_flag, globaltimer() + drain_ns};
                 volatile int no_abort = 0;
                 Gd.abort = &no_abort;
                 mbar_wait(drain_bar, 0, Gd);

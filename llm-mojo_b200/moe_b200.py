@@ -52,6 +52,8 @@ EXPORTS = [
     "moe_layer_desc_from_weights", "moe_load_weights_file",
     "moe_ep_get_unique_id", "moe_ep_init", "moe_ep_finalize",
     "moe_run_moe_coalesced_stage1", "moe_run_moe_coalesced_stage2",
+    "moe_router_subspace_ffn_filter", "moe_sync_moe_subspace_cache",
+    "moe_scatter_and_restore_ffn_subspace", "moe_device_wait_check",
 ]
 
 
@@ -161,6 +163,11 @@ def _declare(L):
     L.moe_run_moe_coalesced_stage1.argtypes = [_p, _i64, _p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _p, _p,
                                                _p, _i64, _i64, _i64, _i64, _int, C.POINTER(_i64)]
     L.moe_run_moe_coalesced_stage2.argtypes = [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64]
+    L.moe_router_subspace_ffn_filter.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f,
+                                                 _p, C.POINTER(_i64)]
+    L.moe_sync_moe_subspace_cache.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64]
+    L.moe_scatter_and_restore_ffn_subspace.argtypes = [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64]
+    L.moe_device_wait_check.argtypes = [_p]
     L.moe_ep_get_unique_id.argtypes = [_p]
     L.moe_ep_init.argtypes = [_p, _p, _int, _int]
     L.moe_ep_finalize.argtypes = [_p]
@@ -393,6 +400,38 @@ class Context:
             _addr(experts_down_packed), _addr(experts_down_scales), _addr(canvas_moe_in),
             _addr(canvas_top_idx), _addr(canvas_top_weights), _addr(canvas_moe_out), B,
             embed_dim, expert_mlp_dim, top_k_experts, activation))
+
+    def router_subspace_ffn_filter(self, r_curr, r_prev, top_idx, prev_top2, eb_mask,
+                                   active_canvas_idx, ffn_keep_b, B, num_experts, top_k, step,
+                                   tau_ffn=0.05, top_weights=None) -> int:
+        """diffusion_kernels.mojo:2253-2337; returns the number of kept rows
+        (listed in ffn_keep_b); r_prev, prev_top2 and top_weights are updated."""
+        n = _i64(0)
+        self.check(self.lib.moe_router_subspace_ffn_filter(
+            self.h, _addr(r_curr), _addr(r_prev), _addr(top_idx), _addr(prev_top2), _addr(eb_mask),
+            _addr(active_canvas_idx), _addr(ffn_keep_b), B, num_experts, top_k, step, tau_ffn,
+            _addr(top_weights), C.byref(n)))
+        return int(n.value)
+
+    def sync_moe_subspace_cache(self, moe_out, moe_prev_cache, active_canvas_idx, ffn_keep_b, B,
+                                ffn_active_len, dim, elem_bytes=2):
+        """diffusion_kernels.mojo:2345-2381 (elem_bytes 2: fp16 rows, 4: fp32)."""
+        self.check(self.lib.moe_sync_moe_subspace_cache(
+            self.h, _addr(moe_out), _addr(moe_prev_cache), _addr(active_canvas_idx),
+            _addr(ffn_keep_b), B, ffn_active_len, dim, elem_bytes))
+
+    def scatter_and_restore_ffn_subspace(self, ffn_sub_out, ffn_prev_cache, ffn_full_out,
+                                         active_canvas_idx, ffn_keep_b, B, ffn_active_len, dim,
+                                         elem_bytes=2):
+        """diffusion_kernels.mojo:2386-2426 (elem_bytes 2: fp16 rows, 4: fp32)."""
+        self.check(self.lib.moe_scatter_and_restore_ffn_subspace(
+            self.h, _addr(ffn_sub_out), _addr(ffn_prev_cache), _addr(ffn_full_out),
+            _addr(active_canvas_idx), _addr(ffn_keep_b), B, ffn_active_len, dim, elem_bytes))
+
+    def device_wait_check(self):
+        """Runs the bounded-wait check (moe_device_wait_check): raises
+        MoeError with code 6 (MOE_E_TIMEOUT) when the wait gave up as designed."""
+        self.check(self.lib.moe_device_wait_check(self.h))
 
     def apply_moe_lod_and_set_cover(self, canvas_top_idx, canvas_top_val, router_per_expert_scale,
                                     canvas_top_weights, B, top_k_experts, active_top_k,

@@ -753,3 +753,100 @@ void orc_diffusion_experts(const uint8_t* gu_p, const float* gu_s, const uint8_t
         }
     free(y); free(slot); free(at); free(xin);
 }
+
+/* ------------------------------------------ diffusion router-subspace bypass
+ * router_subspace_ffn_filter (diffusion_kernels.mojo:2253-2337).  A token
+ * whose top-2 experts equal the ones it had when last evaluated, and whose
+ * router logits moved by at most tau_ffn relative to that evaluation, is
+ * bypassed (its routing weights zeroed); the others are listed in
+ * ffn_keep_b in ascending b and their r_prev / prev_top2 rows updated.
+ * The drift sums follow the reference's 8-lane SIMD loop: lane l takes the
+ * experts e = l (mod 8) with fused multiply-adds, the lanes are added as a
+ * halving tree (reduce8), and a tail of num_experts % 8 experts is added
+ * one by one (multiply, then add). */
+int64_t orc_router_subspace_ffn_filter(const float* r_curr, float* r_prev, const int64_t* top_idx,
+                                       int64_t* prev_top2, const uint8_t* eb_mask,
+                                       const int64_t* active_canvas_idx, int64_t* ffn_keep_b,
+                                       int64_t B, int64_t num_experts, int64_t top_k, int64_t step,
+                                       float tau_ffn, float* top_weights) {
+    if (B <= 0) return 0;
+    int64_t active = 0;
+    const float tau_sq = tau_ffn * tau_ffn;
+    for (int64_t b = 0; b < B; ++b) {
+        const int64_t ot = active_canvas_idx ? active_canvas_idx[b] : b;
+        const int accepted = eb_mask ? (eb_mask[ot] != 0) : 1;
+        int bypass = 0;
+        if (step >= 1 && accepted && top_k >= 2 && num_experts > 0) {
+            const int64_t e0 = top_idx[b * top_k], e1 = top_idx[b * top_k + 1];
+            const int64_t p0 = prev_top2[ot * 2], p1 = prev_top2[ot * 2 + 1];
+            if (p0 >= 0 && p1 >= 0 && e0 == p0 && e1 == p1) {
+                const float* cr = r_curr + b * num_experts;
+                const float* pr = r_prev + ot * num_experts;
+                float vd[8] = {0}, vn[8] = {0};
+                int64_t e = 0;
+                for (; e + 7 < num_experts; e += 8)
+                    for (int l = 0; l < 8; ++l) {
+                        const float d = cr[e + l] - pr[e + l];
+                        vd[l] = fmaf(d, d, vd[l]);
+                        vn[l] = fmaf(pr[e + l], pr[e + l], vn[l]);
+                    }
+                float diff_sq = reduce8(vd), norm_sq = reduce8(vn);
+                for (; e < num_experts; ++e) {
+                    const float d = cr[e] - pr[e];
+                    diff_sq += d * d;
+                    norm_sq += pr[e] * pr[e];
+                }
+                bypass = norm_sq > 1e-12f ? (diff_sq <= tau_sq * norm_sq) : (diff_sq <= 1e-12f);
+            }
+        }
+        if (bypass) {
+            if (top_weights)
+                for (int64_t s = 0; s < top_k; ++s) top_weights[b * top_k + s] = 0.0f;
+        } else {
+            ffn_keep_b[active++] = b;
+            if (top_k >= 1) prev_top2[ot * 2] = top_idx[b * top_k];
+            if (top_k >= 2) prev_top2[ot * 2 + 1] = top_idx[b * top_k + 1];
+            memcpy(r_prev + ot * num_experts, r_curr + b * num_experts, sizeof(float) * (size_t)num_experts);
+        }
+    }
+    return active;
+}
+
+/* sync_moe_subspace_cache (diffusion_kernels.mojo:2345-2381) and
+ * scatter_and_restore_ffn_subspace (:2386-2426), rows of `row_bytes` bytes
+ * (dim * sizeof(dtype)): walking b in order with a cursor into ffn_keep_b,
+ * an evaluated row is saved to the cache (and, for the scatter, taken from
+ * the compacted sub-batch output first); a bypassed row is restored from
+ * the cache. */
+void orc_sync_moe_subspace_cache(uint8_t* moe_out, uint8_t* cache, const int64_t* active_canvas_idx,
+                                 const int64_t* ffn_keep_b, int64_t B, int64_t ffn_active_len,
+                                 int64_t row_bytes) {
+    if (B <= 0 || row_bytes <= 0) return;
+    int64_t cur = 0;
+    for (int64_t b = 0; b < B; ++b) {
+        const int64_t ot = active_canvas_idx ? active_canvas_idx[b] : b;
+        if (cur < ffn_active_len && ffn_keep_b[cur] == b) {
+            memcpy(cache + ot * row_bytes, moe_out + b * row_bytes, (size_t)row_bytes);
+            ++cur;
+        } else {
+            memcpy(moe_out + b * row_bytes, cache + ot * row_bytes, (size_t)row_bytes);
+        }
+    }
+}
+
+void orc_scatter_and_restore_ffn_subspace(const uint8_t* sub_out, uint8_t* cache, uint8_t* full_out,
+                                          const int64_t* active_canvas_idx, const int64_t* ffn_keep_b,
+                                          int64_t B, int64_t ffn_active_len, int64_t row_bytes) {
+    if (B <= 0 || row_bytes <= 0) return;
+    int64_t cur = 0;
+    for (int64_t b = 0; b < B; ++b) {
+        const int64_t ot = active_canvas_idx ? active_canvas_idx[b] : b;
+        if (cur < ffn_active_len && ffn_keep_b[cur] == b) {
+            memcpy(full_out + b * row_bytes, sub_out + cur * row_bytes, (size_t)row_bytes);
+            memcpy(cache + ot * row_bytes, sub_out + cur * row_bytes, (size_t)row_bytes);
+            ++cur;
+        } else {
+            memcpy(full_out + b * row_bytes, cache + ot * row_bytes, (size_t)row_bytes);
+        }
+    }
+}

@@ -119,6 +119,22 @@ void orc_diffusion_experts(const uint8_t* gu_p, const float* gu_s, const uint8_t
                            int64_t B, int64_t d, int64_t F, int64_t top_k, int act,
                            int prec, int nthreads);
 
+/* Diffusion router-subspace bypass: router_subspace_ffn_filter
+ * (diffusion_kernels.mojo:2253-2337; returns the number of evaluated
+ * tokens), sync_moe_subspace_cache (:2345-2381) and
+ * scatter_and_restore_ffn_subspace (:2386-2426) over rows of row_bytes. */
+int64_t orc_router_subspace_ffn_filter(const float* r_curr, float* r_prev, const int64_t* top_idx,
+                                       int64_t* prev_top2, const uint8_t* eb_mask,
+                                       const int64_t* active_canvas_idx, int64_t* ffn_keep_b,
+                                       int64_t B, int64_t num_experts, int64_t top_k, int64_t step,
+                                       float tau_ffn, float* top_weights);
+void orc_sync_moe_subspace_cache(uint8_t* moe_out, uint8_t* cache, const int64_t* active_canvas_idx,
+                                 const int64_t* ffn_keep_b, int64_t B, int64_t ffn_active_len,
+                                 int64_t row_bytes);
+void orc_scatter_and_restore_ffn_subspace(const uint8_t* sub_out, uint8_t* cache, uint8_t* full_out,
+                                          const int64_t* active_canvas_idx, const int64_t* ffn_keep_b,
+                                          int64_t B, int64_t ffn_active_len, int64_t row_bytes);
+
 /* fp16 helpers (round to nearest even) */
 uint16_t orc_f32_to_f16(float f);
 float orc_f16_to_f32(uint16_t h);

@@ -77,6 +77,11 @@ def _declare(L):
     L.orc_layer_forward.argtypes = [C.POINTER(OrcLayer), _i64, _p, _p, _int, _int, _int, _p, _p, _p]
     L.orc_diffusion_experts.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
                                         _int, _int, _int]
+    L.orc_router_subspace_ffn_filter.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
+                                                 _f, _p]
+    L.orc_router_subspace_ffn_filter.restype = _i64
+    L.orc_sync_moe_subspace_cache.argtypes = [_p, _p, _p, _p, _i64, _i64, _i64]
+    L.orc_scatter_and_restore_ffn_subspace.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _i64]
 
 
 def _ptr(a):
@@ -270,3 +275,38 @@ def diffusion_experts(gu_p, gu_s, dn_p, dn_s, x_f16, top_idx, top_w, d, F, top_k
                                 _ptr(out.view(np.uint16)), B, d, F, top_k, act, prec,
                                 nthreads or nthreads_default())
     return out
+
+
+def router_subspace_ffn_filter(r_curr, r_prev, top_idx, prev_top2, B, num_experts, top_k, step,
+                               tau_ffn=0.05, eb_mask=None, active_canvas_idx=None, top_weights=None):
+    """diffusion_kernels.mojo:2253-2337.  r_prev, prev_top2 and top_weights
+    are updated in place; returns (ffn_keep_b[:count], count)."""
+    keep = np.zeros(max(B, 1), np.int64)
+    eb = None if eb_mask is None else np.ascontiguousarray(eb_mask, np.uint8)
+    ac = None if active_canvas_idx is None else np.ascontiguousarray(active_canvas_idx, np.int64)
+    n = lib().orc_router_subspace_ffn_filter(
+        _ptr(np.ascontiguousarray(r_curr, np.float32)), _ptr(r_prev),
+        _ptr(np.ascontiguousarray(top_idx, np.int64)), _ptr(prev_top2), _ptr(eb), _ptr(ac),
+        _ptr(keep), B, num_experts, top_k, step, tau_ffn, _ptr(top_weights))
+    return keep[:n], int(n)
+
+
+def sync_moe_subspace_cache(moe_out, cache, ffn_keep_b, B, ffn_active_len, active_canvas_idx=None):
+    """diffusion_kernels.mojo:2345-2381, in place on moe_out / cache (rows of
+    any dtype)."""
+    ac = None if active_canvas_idx is None else np.ascontiguousarray(active_canvas_idx, np.int64)
+    row_bytes = moe_out.nbytes // B
+    lib().orc_sync_moe_subspace_cache(_ptr(moe_out), _ptr(cache), _ptr(ac),
+                                      _ptr(np.ascontiguousarray(ffn_keep_b, np.int64)), B,
+                                      ffn_active_len, row_bytes)
+
+
+def scatter_and_restore_ffn_subspace(sub_out, cache, full_out, ffn_keep_b, B, ffn_active_len,
+                                     active_canvas_idx=None):
+    """diffusion_kernels.mojo:2386-2426, in place on cache / full_out."""
+    ac = None if active_canvas_idx is None else np.ascontiguousarray(active_canvas_idx, np.int64)
+    row_bytes = full_out.nbytes // B
+    lib().orc_scatter_and_restore_ffn_subspace(_ptr(np.ascontiguousarray(sub_out)), _ptr(cache),
+                                               _ptr(full_out), _ptr(ac),
+                                               _ptr(np.ascontiguousarray(ffn_keep_b, np.int64)), B,
+                                               ffn_active_len, row_bytes)

@@ -324,34 +324,37 @@ def test_async_enqueue_and_bounded_wait(ctx, full_layer):
     assert np.array_equal(out.cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("M", [1, 16])
-def test_device_wait_deadline_returns_timeout_and_context_recovers(ctx, full_layer, M):
-    """Every mbarrier wait of the expert kernels is bounded by
-    MOE_OPT_DEVICE_TIMEOUT_NS.  With a 1 us deadline the waits for weight
-    tiles that are still in flight run out: the kernel raises the error word,
-    drains its copies, frees its tensor memory and returns, and the call
-    returns MOE_E_TIMEOUT.  Then, with the default deadline back, the same
-    context gives oracle-correct output.  (M=1: the CUDA-core kernel pair,
-    M=16: the tensor-core streaming kernels.)"""
+def test_device_wait_deadline_returns_timeout_and_context_recovers(ctx, full_layer):
+    """The bounded device-side wait: moe_device_wait_check waits on a barrier
+    that nothing completes with the wait code and deadline the pipelined
+    expert kernels use (MOE_OPT_DEVICE_TIMEOUT_NS, here 2 ms).  It must give
+    up, raise the error word and return MOE_E_TIMEOUT; then the same context
+    gives oracle-correct layer output on both expert-kernel families (M=1:
+    CUDA-core pair, M=16: tensor-core streaming kernels)."""
+    import time
     dev, host, L = full_layer
     desc = MB.make_desc(dev)
-    x = synth.make_x(M, seed=41).cpu().numpy()
-    out = np.zeros((M, 2816), np.float32)
-    ctx.set_option(MB.OPT_DEVICE_TIMEOUT_NS, 1000)
+    ctx.set_option(MB.OPT_DEVICE_TIMEOUT_NS, 2_000_000)
     try:
+        t0 = time.perf_counter()
         with pytest.raises(MB.MoeError) as ei:
-            ctx.layer_forward(desc, M, x, out, flags=0)
+            ctx.device_wait_check()
+        dt = time.perf_counter() - t0
         assert ei.value.code == 6, ei.value  # MOE_E_TIMEOUT
         assert "deadline" in str(ei.value)
+        assert 0.002 <= dt < 2.0, dt
     finally:
         ctx.set_option(MB.OPT_DEVICE_TIMEOUT_NS, 4_000_000_000)
-    cnt = np.zeros(M, np.int64)
-    idx = np.zeros((M, 8), np.int64)
-    w = np.zeros((M, 8), np.float32)
-    ctx.layer_forward(desc, M, x, out, 0, cnt, idx, w)
-    r = O.route(L, x)
-    ref = O.experts_forward(L, r["moe_in"], cnt, idx, w, prec=O.F64)
-    assert_close(out, ref, what=f"after the timeout, M={M}")
+    for M in (1, 16):
+        x = synth.make_x(M, seed=41 + M).cpu().numpy()
+        out = np.zeros((M, 2816), np.float32)
+        cnt = np.zeros(M, np.int64)
+        idx = np.zeros((M, 8), np.int64)
+        w = np.zeros((M, 8), np.float32)
+        ctx.layer_forward(desc, M, x, out, 0, cnt, idx, w)
+        r = O.route(L, x)
+        ref = O.experts_forward(L, r["moe_in"], cnt, idx, w, prec=O.F64)
+        assert_close(out, ref, what=f"after the timeout, M={M}")
 
 
 # ------------------------------------------------------------- error paths

@@ -232,3 +232,63 @@ def test_layer_forward_post_norm_and_routing_consistency():
     raw = raw.astype(np.float64)
     exp = raw / np.sqrt((raw ** 2).mean(1, keepdims=True) + 1e-6)
     np.testing.assert_allclose(out, exp, rtol=1e-5, atol=1e-6)
+
+
+# ------------------------------------------- diffusion router-subspace bypass
+def _oracle_filter(r_curr, r_prev, top_idx, prev_top2, eb, act, keep, B, E, K, step, tau, top_w=None):
+    k, n = O.router_subspace_ffn_filter(r_curr, r_prev, top_idx, prev_top2, B, E, K, step, tau, eb, act,
+                                        top_w)
+    keep[:n] = k
+    return n
+
+
+def _oracle_scatter(sub, cache, full, act, keep, B, n, dim):
+    O.scatter_and_restore_ffn_subspace(sub, cache, full, keep, B, n, act)
+
+
+def test_subspace_bypass_known_answers():
+    """test_diffusion_suite.mojo:562-648 on the oracle."""
+    import subspace_cases
+    subspace_cases.known_answers(_oracle_filter, _oracle_scatter)
+
+
+def test_subspace_filter_zeroes_bypassed_weights_and_keeps_reference_points():
+    import subspace_cases
+    c = subspace_cases.random_filter_case(3)
+    r_prev0, pt0 = c["r_prev"].copy(), c["prev_top2"].copy()
+    tw = c["top_w"].copy()
+    keep, n = O.router_subspace_ffn_filter(c["r_curr"], c["r_prev"], c["top_idx"], c["prev_top2"], c["B"],
+                                           c["E"], c["K"], 1, c["tau"], c["eb"], c["act"], tw)
+    assert 0 < n < c["B"]  # the case sits on the boundary: both outcomes occur
+    kept = np.zeros(c["B"], bool)
+    kept[keep] = True
+    assert np.all(np.diff(keep) > 0)
+    assert np.all(tw[~kept] == 0) and np.array_equal(tw[kept], c["top_w"][kept])
+    o = c["act"]
+    assert np.array_equal(c["r_prev"][o[kept]], c["r_curr"][kept])
+    assert np.array_equal(c["r_prev"][o[~kept]], r_prev0[o[~kept]])
+    assert np.array_equal(c["prev_top2"][o[kept]], c["top_idx"][kept, :2])
+    assert np.array_equal(c["prev_top2"][o[~kept]], pt0[o[~kept]])
+    # step 0 evaluates everything
+    keep0, n0 = O.router_subspace_ffn_filter(c["r_curr"], r_prev0.copy(), c["top_idx"], pt0.copy(), c["B"],
+                                             c["E"], c["K"], 0, c["tau"], c["eb"], c["act"])
+    assert n0 == c["B"] and np.array_equal(keep0, np.arange(c["B"]))
+
+
+def test_subspace_sync_walk_stops_at_a_break_in_the_keep_list():
+    import subspace_cases
+    c = subspace_cases.random_rows_case(1, 40, 64, 16, np.float32)
+    out, cache = c["out"].copy(), c["cache"].copy()
+    O.sync_moe_subspace_cache(out, cache, c["keep"], 40, len(c["keep"]), c["act"])
+    # emulate the walk in Python
+    out2, cache2 = c["out"].copy(), c["cache"].copy()
+    cur = 0
+    for b in range(40):
+        o = c["act"][b]
+        if cur < len(c["keep"]) and c["keep"][cur] == b:
+            cache2[o] = out2[b]
+            cur += 1
+        else:
+            out2[b] = cache2[o]
+    assert cur < len(c["keep"])  # the break was hit
+    assert np.array_equal(out, out2) and np.array_equal(cache, cache2)
