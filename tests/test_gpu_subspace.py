@@ -11,6 +11,7 @@ import pytest
 
 import oracle as O
 import subspace_cases
+from tolerances import assert_close
 
 pytestmark = pytest.mark.gpu
 
@@ -108,7 +109,10 @@ def test_subspace_bypass_through_the_diffusion_layer(ctx, full_layer):
     filter -> experts on the canvas with the bypassed rows' weights zeroed ->
     sync of the output cache.  Step 0 evaluates every row and fills the
     cache; step 1 with unchanged logits bypasses every accepted row, whose
-    output then comes back from the cache: equal, bit for bit, to step 0's."""
+    output then comes back from the cache: equal, bit for bit, to step 0's.
+    The rows evaluated again (not accepted) agree with step 0 within the
+    parity bar: the expert GEMMs split each row's K range over accumulators
+    by the work list, which changes with the set of active rows."""
     import synth
     dev, host, L = full_layer
     B = 64
@@ -136,5 +140,7 @@ def test_subspace_bypass_through_the_diffusion_layer(ctx, full_layer):
                                                out, B, 2816, 704, 8)
         ctx.sync_moe_subspace_cache(out, cache, act, keep, B, n, 2816, elem_bytes=2)
         outs.append(out)
-    assert np.array_equal(outs[0], outs[1])
+    byp = eb == 1
+    assert np.array_equal(outs[0][byp], outs[1][byp])
+    assert_close(outs[1][~byp].astype(np.float32), outs[0][~byp].astype(np.float32), what="re-evaluated rows")
     assert np.abs(outs[0].astype(np.float32)).sum() > 0
