@@ -108,8 +108,28 @@ enum moe_option {
                                       the separate norm / router / top-k / bucket / gather kernels */
     MOE_OPT_DENSE_KSPLIT = 11,     /* dense tensor-core GEMMs: split K into this many partial sums
                                       (0, the default: enough work items for two per SM) */
-    MOE_OPT_EP_TIMEOUT_NS = 12     /* deadline of every host wait on the expert-parallel
+    MOE_OPT_EP_TIMEOUT_NS = 12,    /* deadline of every host wait on the expert-parallel
                                       communicator (set-up, collectives; default 30 s) */
+    MOE_OPT_EP_MODE = 13,          /* moe_ep_mode: how moe_layer_forward splits the layer over the
+                                      ranks of the context's communicator (default REPLICATED) */
+    MOE_OPT_EP_LOCAL_WEIGHTS = 14  /* 1: in the GATHER and ALL_TO_ALL modes the descriptor's expert
+                                      arrays hold only this rank's experts (expert rank*E/N + i at
+                                      index i); 0 (default): all E experts */
+};
+/* Expert-parallel forms of moe_layer_forward (no counterpart in the
+ * single-process reference; see moe_ep_init).  Rank r of N owns the experts
+ * [r*E/N, (r+1)*E/N); GATHER and ALL_TO_ALL need E % N == 0. */
+enum moe_ep_mode {
+    MOE_EP_REPLICATED = 0, /* every rank passes the same M tokens and receives the whole output:
+                              partial outputs are all-reduced (decode, M <= 64) */
+    MOE_EP_GATHER = 1,     /* every rank passes its own M tokens (M equal on all ranks): tokens are
+                              all-gathered, each rank evaluates its experts for all of them, and a
+                              reduce-scatter returns each rank its own rows (decode batches; no host
+                              synchronisation in the call) */
+    MOE_EP_ALL_TO_ALL = 2  /* every rank passes its own M >= 0 tokens: routed (token, expert) rows
+                              are sent, sorted by expert, to the expert's owner, evaluated there and
+                              sent back; the home rank adds each token's slots in slot order
+                              (prefill; the per-peer row counts are read on the host once per call) */
 };
 enum moe_gemm_path {
     MOE_PATH_AUTO = 0, /* CUDA-core GEMV for few tokens, tensor cores above the threshold */
@@ -499,12 +519,16 @@ int moe_ep_get_unique_id(uint8_t* id);
  * ranks joined, MOE_E_TIMEOUT (communicator aborted) when they have not
  * within MOE_OPT_EP_TIMEOUT_NS, MOE_E_NCCL when NCCL cannot be loaded or
  * fails, MOE_E_STATE when the context already has a communicator.  From then
- * on moe_layer_forward evaluates the experts [rank*E/N, (rank+1)*E/N) only,
+ * on moe_layer_forward evaluates the experts [rank*E/N, (rank+1)*E/N) only
+ * and combines the ranks' work as MOE_OPT_EP_MODE says: REPLICATED (default)
  * sums the partial outputs of all ranks in place (NCCL all-reduce on the
- * context's stream) and applies MOE_F_POST_NORM to the sum: every rank passes
- * the same M tokens and receives the whole layer's output.  Every rank must
- * make the same moe_layer_forward calls in the same order.  Output must be
- * fp32 (MOE_F_FP16_OUT is refused), num_experts >= nranks, and the
+ * context's stream) and applies MOE_F_POST_NORM to the sum, every rank
+ * passing the same M tokens and receiving the whole layer's output; GATHER
+ * and ALL_TO_ALL take each rank's own tokens and return their rows (see
+ * moe_ep_mode).  The routing outputs (tok_active_*) describe the rank's own
+ * tokens in GATHER and ALL_TO_ALL.  Every rank must make the same
+ * moe_layer_forward calls in the same order, with the same mode.  Output
+ * must be fp32 (MOE_F_FP16_OUT is refused), num_experts >= nranks, and the
  * MOE_OPT_EXPERT_BEGIN/END options are ignored meanwhile.  Host waits on a
  * call with a collective (completion of a synchronous call, moe_wait) give
  * up after MOE_OPT_EP_TIMEOUT_NS or on an NCCL error: the communicator is

@@ -113,6 +113,12 @@ struct moe_ctx {
     } split;
     moe::EpComm ep;                      // moe_ep_init's communicator
     uint64_t ep_timeout_ns = 30000000000ull;  // MOE_OPT_EP_TIMEOUT_NS
+    int ep_mode = MOE_EP_REPLICATED;     // MOE_OPT_EP_MODE
+    bool ep_local_weights = false;       // MOE_OPT_EP_LOCAL_WEIGHTS
+    char* ep_ws = nullptr;               // all-to-all: the rows a rank receives and evaluates
+    size_t ep_cap = 0;
+    int* ep_host_cnt = nullptr;          // all-to-all: pinned copy of the ranks' row counts
+    int ep_host_n = 0;
 };
 
 namespace {
@@ -711,6 +717,8 @@ int moe_ctx_destroy(moe_ctx* ctx) {
     for (Reg& r : ctx->regs) cudaFree(r.dev);
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->split_ws) cudaFree(ctx->split_ws);
+    if (ctx->ep_ws) cudaFree(ctx->ep_ws);
+    if (ctx->ep_host_cnt) cudaFreeHost(ctx->ep_host_cnt);
     if (ctx->err_flag) cudaFree(ctx->err_flag);
     if (ctx->done) cudaEventDestroy(ctx->done);
     for (auto& r : ctx->prof_pending) {
@@ -782,6 +790,13 @@ int moe_wait(moe_ctx* ctx, uint64_t timeout_ns) {
 int moe_set_option(moe_ctx* ctx, int option, int64_t value) {
     if (!ctx) return MOE_E_ARG;
     switch (option) {
+        case MOE_OPT_EP_MODE:
+            if (value < MOE_EP_REPLICATED || value > MOE_EP_ALL_TO_ALL) return fail(ctx, MOE_E_ARG, "bad EP mode");
+            ctx->ep_mode = (int)value;
+            return MOE_OK;
+        case MOE_OPT_EP_LOCAL_WEIGHTS:
+            ctx->ep_local_weights = value != 0;
+            return MOE_OK;
         case MOE_OPT_GEMM_PATH:
             if (value < MOE_PATH_AUTO || value > MOE_PATH_TC) return fail(ctx, MOE_E_ARG, "bad path");
             ctx->gemm_path = (int)value;
@@ -1388,6 +1403,8 @@ int moe_run_moe_coalesced_stage1(moe_ctx* ctx, int64_t sub_b, const uint8_t* gu_
     if (ctx->split_cap < need) {
         MOE_CUDA(cudaStreamSynchronize(ctx->stream));
         if (ctx->split_ws) cudaFree(ctx->split_ws);
+    if (ctx->ep_ws) cudaFree(ctx->ep_ws);
+    if (ctx->ep_host_cnt) cudaFreeHost(ctx->ep_host_cnt);
         ctx->split_ws = nullptr;
         ctx->split_cap = 0;
         if (cudaMalloc(&ctx->split_ws, need) != cudaSuccess) {
@@ -1690,8 +1707,11 @@ size_t layer_small_bytes(const moe_layer_desc* L) {
     return al(d * 4) * 3 + al(E * 4) * 2 + (L->router_f32 ? al(E * d * 4) : 0);
 }
 
-int layer_dev(moe_ctx* ctx, const moe_layer_desc* L, int flags, LayerDev* o) {
+// `E_w`: experts the descriptor's expert arrays hold (-1: num_experts; an
+// expert-parallel rank with MOE_OPT_EP_LOCAL_WEIGHTS holds only its own).
+int layer_dev(moe_ctx* ctx, const moe_layer_desc* L, int flags, LayerDev* o, int64_t E_w = -1) {
     const int64_t d = L->embed_dim, E = L->num_experts, F = L->expert_mlp_dim;
+    const int64_t Ew = E_w < 0 ? E : E_w;
     void* p;
     if (L->router_packed) {
         TRY(dev_ptr(ctx, L->router_packed, E * d / 2, K_W, &p));
@@ -1718,13 +1738,13 @@ int layer_dev(moe_ctx* ctx, const moe_layer_desc* L, int flags, LayerDev* o) {
         TRY(dev_ptr(ctx, L->post_norm_w, d * 4, K_IN, &p));
         o->post_w = (const float*)p;
     }
-    TRY(dev_ptr(ctx, L->gate_up_packed, E * 2 * F * d / 2, K_W, &p));
+    TRY(dev_ptr(ctx, L->gate_up_packed, Ew * 2 * F * d / 2, K_W, &p));
     o->w.gu_p = (const uint8_t*)p;
-    TRY(dev_ptr(ctx, L->gate_up_scales, E * 2 * F * d / 32 * 4, K_W, &p));
+    TRY(dev_ptr(ctx, L->gate_up_scales, Ew * 2 * F * d / 32 * 4, K_W, &p));
     o->w.gu_s = (const float*)p;
-    TRY(dev_ptr(ctx, L->down_packed, E * d * F / 2, K_W, &p));
+    TRY(dev_ptr(ctx, L->down_packed, Ew * d * F / 2, K_W, &p));
     o->w.dn_p = (const uint8_t*)p;
-    TRY(dev_ptr(ctx, L->down_scales, E * d * F / 32 * 4, K_W, &p));
+    TRY(dev_ptr(ctx, L->down_scales, Ew * d * F / 32 * 4, K_W, &p));
     o->w.dn_s = (const float*)p;
     if (!al16(o->w.gu_p) || !al16(o->w.dn_p)) return fail(ctx, MOE_E_ARG, "packed weights must be 16-byte aligned");
     return MOE_OK;
@@ -1817,6 +1837,242 @@ int route_dev(moe_ctx* ctx, const moe_layer_desc* L, const LayerDev& ld, int64_t
     return MOE_OK;
 }
 
+// ---------------------------------------------------------------- expert
+// parallelism: the gather and all-to-all forms of moe_layer_forward.
+
+// The local expert slice [e_lo, e_lo + El) of the descriptor's weights.
+ExpertWeights local_weights(moe_ctx* ctx, const ExpertWeights& w, int64_t e_lo, int64_t d, int64_t F) {
+    if (ctx->ep_local_weights) return w;
+    ExpertWeights o = w;
+    o.gu_p += e_lo * 2 * F * d / 2;
+    o.gu_s += e_lo * 2 * F * d / 32;
+    o.dn_p += e_lo * d * F / 2;
+    o.dn_s += e_lo * d * F / 32;
+    return o;
+}
+
+// The context's expert-range options are cleared for the call (the expert
+// kernels see the local slice as experts 0 .. El-1) and come back on exit.
+struct ClearRange {
+    moe_ctx* c;
+    int64_t b, e;
+    explicit ClearRange(moe_ctx* ctx_) : c(ctx_), b(ctx_->expert_begin), e(ctx_->expert_end) {
+        c->expert_begin = 0;
+        c->expert_end = 0;
+    }
+    ~ClearRange() {
+        c->expert_begin = b;
+        c->expert_end = e;
+    }
+};
+
+int post_norm_rows(moe_ctx* ctx, float* od, const float* post_w, int64_t M, int64_t d) {
+    moe::PrepArgs pa;
+    pa.x = od;
+    pa.K = d;
+    pa.norm = 1;
+    pa.pre_w = post_w;
+    pa.out = od;
+    ProfScope ps(ctx, "rms_norm");
+    ctx->launches += moe::launch_prep(pa, M, ctx->stream);
+    return MOE_OK;
+}
+
+// Gather form (decode): every rank passes its own M tokens (the same M on
+// every rank).  The tokens of all ranks are gathered, routed, and this
+// rank's experts evaluated for all of them; the partial outputs are summed
+// by a reduce-scatter that leaves each rank its own M rows, then the
+// post-norm.  No host synchronisation inside.
+int ep_gather_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const float* x, void* out, int flags,
+                      int64_t* tc, int64_t* ti, float* tw) {
+    const int N = ctx->ep.nranks, r = ctx->ep.rank;
+    const int64_t d = L->embed_dim, E = L->num_experts, K = L->top_k, F = L->expert_mlp_dim;
+    const int64_t El = E / N, e_lo = r * El, Mt = M * N, Pt = Mt * K;
+    cudaStream_t s = ctx->stream;
+    TRY(ws_reserve(ctx, layer_small_bytes(L) + expert_bufs_bytes(Mt, K, d, F, El) + route_bytes(Mt, d, E, K) +
+                            al(M * d * 4) * 2 + al(Mt * d * 4) * 2 + al(Mt * 8) + al(Pt * 8) + al(Pt * 4) +
+                            al(M * 8) + al(M * K * 8) + al(M * K * 4)));
+    LayerDev ld;
+    TRY(layer_dev(ctx, L, flags, &ld, ctx->ep_local_weights ? El : E));
+    void *xd, *od, *dtc = nullptr, *dti = nullptr, *dtw = nullptr;
+    TRY(dev_ptr(ctx, x, M * d * 4, K_IN, &xd));
+    TRY(dev_ptr(ctx, out, M * d * 4, K_OUT, &od));
+    if (tc) TRY(dev_ptr(ctx, tc, M * 8, K_OUT, &dtc));
+    if (ti) TRY(dev_ptr(ctx, ti, M * K * 8, K_OUT, &dti));
+    if (tw) TRY(dev_ptr(ctx, tw, M * K * 4, K_OUT, &dtw));
+    float* x_all = (float*)ws_take(ctx, Mt * d * 4);
+    float* part = (float*)ws_take(ctx, Mt * d * 4);
+    int64_t* tc_all = (int64_t*)ws_take(ctx, Mt * 8);
+    int64_t* ti_all = (int64_t*)ws_take(ctx, Pt * 8);
+    float* tw_all = (float*)ws_take(ctx, Pt * 4);
+    ExpertBufs bb;
+    TRY(take_expert_bufs(ctx, Mt, K, d, F, El, &bb));
+    if (!tw_all) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+    const ExpertWeights wl = local_weights(ctx, ld.w, e_lo, d, F);
+    std::string err;
+    int st = moe::ep_all_gather(ctx->ep, xd, x_all, (size_t)(M * d), true, s, ctx->ep_timeout_ns, err);
+    if (st != MOE_OK) return fail(ctx, st, err);
+    const bool cc = !use_tc(ctx, Mt, d, F, wl);
+    TRY(route_dev(ctx, L, ld, Mt, x_all, flags, bb.x32, bb.xsum, bb.slot_expert, bb.slot_weight, nullptr, nullptr,
+                  nullptr, tc_all, ti_all, tw_all, cc ? bb.x32q : nullptr));
+    bb.x32q_ready = cc;
+    ctx->launches += moe::launch_ep_localize(bb.slot_expert, Pt, (int)e_lo, (int)(e_lo + El), s);
+    // this rank's rows of the routing outputs
+    if (dtc) MOE_CUDA(cudaMemcpyAsync(dtc, tc_all + r * M, M * 8, cudaMemcpyDeviceToDevice, s));
+    if (dti) MOE_CUDA(cudaMemcpyAsync(dti, ti_all + r * M * K, M * K * 8, cudaMemcpyDeviceToDevice, s));
+    if (dtw) MOE_CUDA(cudaMemcpyAsync(dtw, tw_all + r * M * K, M * K * 4, cudaMemcpyDeviceToDevice, s));
+    moe::CombineArgs c;
+    {
+        ClearRange cr(ctx);
+        TRY(run_experts(ctx, wl, Mt, K, d, F, El, L->activation, bb, &c, part));
+    }
+    st = moe::ep_reduce_scatter(ctx->ep, part, (float*)od, (size_t)(M * d), s, ctx->ep_timeout_ns, err);
+    if (st != MOE_OK) return fail(ctx, st, err);
+    if (flags & MOE_F_POST_NORM) TRY(post_norm_rows(ctx, (float*)od, ld.post_w, M, d));
+    return finish(ctx);
+}
+
+// All-to-all form (prefill): every rank passes its own M tokens (M may
+// differ between ranks, 0 included).  Each rank routes its tokens; the
+// routed (token, expert) pairs, sorted by expert and so grouped by the rank
+// that owns the expert, travel as fp32 rows to that rank, which evaluates
+// them on its experts; the results travel back in the same order and the
+// home rank adds each token's slots in slot order and applies the post-norm.
+// The row counts are exchanged first and read on the host (one wait per
+// call) to size the exchange.
+int ep_a2a_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const float* x, void* out, int flags,
+                   int64_t* tc, int64_t* ti, float* tw) {
+    const int N = ctx->ep.nranks, r = ctx->ep.rank;
+    const int64_t d = L->embed_dim, E = L->num_experts, K = L->top_k, F = L->expert_mlp_dim;
+    const int64_t El = E / N, e_lo = r * El, Mh = std::max<int64_t>(M, 1), P = Mh * K;
+    cudaStream_t s = ctx->stream;
+    TRY(ws_reserve(ctx, layer_small_bytes(L) + expert_bufs_bytes(Mh, K, d, F, E) + route_bytes(Mh, d, E, K) +
+                            al(M * d * 4) * 2 + al(M * 8) + al(M * K * 8) + al(M * K * 4) + al(P * d * 4) * 2 +
+                            al(P * 4) + al(N * 4) + al((size_t)N * N * 4)));
+    LayerDev ld;
+    TRY(layer_dev(ctx, L, flags, &ld, ctx->ep_local_weights ? El : E));
+    void *xd = nullptr, *od = nullptr, *dtc = nullptr, *dti = nullptr, *dtw = nullptr;
+    if (M > 0) {
+        TRY(dev_ptr(ctx, x, M * d * 4, K_IN, &xd));
+        TRY(dev_ptr(ctx, out, M * d * 4, K_OUT, &od));
+        if (tc) TRY(dev_ptr(ctx, tc, M * 8, K_OUT, &dtc));
+        if (ti) TRY(dev_ptr(ctx, ti, M * K * 8, K_OUT, &dti));
+        if (tw) TRY(dev_ptr(ctx, tw, M * K * 4, K_OUT, &dtw));
+    }
+    ExpertBufs bb;
+    TRY(take_expert_bufs(ctx, Mh, K, d, F, E, &bb));
+    float* send_x = (float*)ws_take(ctx, P * d * 4);
+    float* y_back = (float*)ws_take(ctx, P * d * 4);
+    int* send_e = (int*)ws_take(ctx, P * 4);
+    int* send_cnt = (int*)ws_take(ctx, N * 4);
+    int* all_cnt = (int*)ws_take(ctx, (size_t)N * N * 4);
+    if (!all_cnt) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+    if (M > 0) {
+        TRY(route_dev(ctx, L, ld, M, (const float*)xd, flags, bb.x32, bb.xsum, bb.slot_expert, bb.slot_weight,
+                      nullptr, nullptr, nullptr, (int64_t*)dtc, (int64_t*)dti, (float*)dtw));
+        ProfScope ps(ctx, "ep_dispatch");
+        ctx->launches += moe::launch_bucket(bb.slot_expert, M * K, (int)K, (int)E, 0, (int)E, bb.b, s);
+        ctx->launches += moe::launch_ep_pack(bb.b, (int)El, N, send_e, send_cnt, s);
+        ctx->launches += moe::launch_gather_rows(bb.x32, bb.b.pair_token, bb.b.meta + 1, M * K, d, send_x, s);
+    } else {
+        MOE_CUDA(cudaMemsetAsync(send_cnt, 0, N * 4, s));
+    }
+    std::string err;
+    int st = moe::ep_all_gather(ctx->ep, send_cnt, all_cnt, (size_t)N, false, s, ctx->ep_timeout_ns, err);
+    if (st != MOE_OK) return fail(ctx, st, err);
+    if (ctx->ep_host_n < N * N) {
+        if (ctx->ep_host_cnt) cudaFreeHost(ctx->ep_host_cnt);
+        ctx->ep_host_cnt = nullptr;
+        ctx->ep_host_n = 0;
+        if (cudaMallocHost(&ctx->ep_host_cnt, (size_t)N * N * 4) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, MOE_E_NOMEM, "pinned count buffer");
+        }
+        ctx->ep_host_n = N * N;
+    }
+    MOE_CUDA(cudaMemcpyAsync(ctx->ep_host_cnt, all_cnt, (size_t)N * N * 4, cudaMemcpyDeviceToHost, s));
+    MOE_CUDA(cudaEventRecord(ctx->done, s));
+    st = moe::ep_wait(ctx->ep, ctx->done, ctx->ep_timeout_ns, true, err);
+    if (st != MOE_OK) return fail(ctx, st, err);
+    // row counts: this rank sends cnt[r][j] rows to j and receives cnt[j][r] from j
+    std::vector<int64_t> sc(N), rc(N), so(N + 1, 0), ro(N + 1, 0);
+    for (int j = 0; j < N; ++j) {
+        sc[j] = ctx->ep_host_cnt[r * N + j];
+        rc[j] = ctx->ep_host_cnt[j * N + r];
+        if (sc[j] < 0 || rc[j] < 0) return fail(ctx, MOE_E_STATE, "bad row count in the exchange");
+        so[j + 1] = so[j] + sc[j];
+        ro[j + 1] = ro[j] + rc[j];
+    }
+    const int64_t Pr = ro[N];
+    if (so[N] > (M > 0 ? M * K : 0)) return fail(ctx, MOE_E_STATE, "row counts disagree with the routing");
+    // receive side: its own arena, sized now that the counts are known (the
+    // stream is idle here)
+    const int64_t Prh = std::max<int64_t>(Pr, 1);
+    const size_t need = al(Prh * d * 4) * 2 + al(Prh * 4) + expert_bufs_bytes(Prh, 1, d, F, El) + 64 * kAlign;
+    if (need > ctx->ep_cap) {
+        if (ctx->ep_ws) cudaFree(ctx->ep_ws);
+        ctx->ep_ws = nullptr;
+        ctx->ep_cap = 0;
+        const size_t cap = std::max(need, need + need / 2);
+        if (cudaMalloc(&ctx->ep_ws, cap) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, MOE_E_NOMEM, "expert-parallel receive arena");
+        }
+        ctx->ep_cap = cap;
+    }
+    size_t off = 0;
+    auto take = [&](size_t b) -> void* {
+        size_t o = (off + kAlign - 1) / kAlign * kAlign;
+        if (o + b > ctx->ep_cap) return nullptr;
+        off = o + b;
+        return ctx->ep_ws + o;
+    };
+    float* recv_x = (float*)take(Prh * d * 4);
+    float* y2 = (float*)take(Prh * d * 4);
+    int* recv_e = (int*)take(Prh * 4);
+    ExpertBufs b2;
+    if (!carve_expert_bufs(take, Prh, 1, d, F, El, &b2) || !recv_e)
+        return fail(ctx, MOE_E_NOMEM, "expert-parallel receive arena exhausted");
+    std::vector<moe::EpXfer> xf;
+    for (int j = 0; j < N; ++j) {
+        xf.push_back({true, send_x + so[j] * d, (size_t)(sc[j] * d), true, j});
+        xf.push_back({true, send_e + so[j], (size_t)sc[j], false, j});
+        xf.push_back({false, recv_x + ro[j] * d, (size_t)(rc[j] * d), true, j});
+        xf.push_back({false, recv_e + ro[j], (size_t)rc[j], false, j});
+    }
+    st = moe::ep_exchange(ctx->ep, xf, s, ctx->ep_timeout_ns, err);
+    if (st != MOE_OK) return fail(ctx, st, err);
+    if (Pr > 0) {
+        const ExpertWeights wl = local_weights(ctx, ld.w, e_lo, d, F);
+        ctx->launches += moe::launch_ep_slots(recv_e, Pr, (int)El, b2.slot_expert, b2.slot_weight, ctx->err_flag, s);
+        TRY(prep_rows(ctx, recv_x, MOE_X_NATURAL, 0, Pr, d, b2.x32, b2.xsum));
+        moe::CombineArgs c0;  // one slot of weight 1 per row: the expert output itself
+        ClearRange cr(ctx);
+        TRY(run_experts(ctx, wl, Pr, 1, d, F, El, L->activation, b2, &c0, y2));
+    }
+    xf.clear();
+    for (int j = 0; j < N; ++j) {
+        xf.push_back({true, y2 + ro[j] * d, (size_t)(rc[j] * d), true, j});
+        xf.push_back({false, y_back + so[j] * d, (size_t)(sc[j] * d), true, j});
+    }
+    st = moe::ep_exchange(ctx->ep, xf, s, ctx->ep_timeout_ns, err);
+    if (st != MOE_OK) return fail(ctx, st, err);
+    if (M > 0) {
+        moe::CombineArgs c;
+        c.post_norm = (flags & MOE_F_POST_NORM) ? 1 : 0;
+        c.post_w = ld.post_w;
+        c.y = y_back;
+        c.d = d;
+        c.K = (int)K;
+        c.slot_pair = bb.b.slot_pair;
+        c.slot_weight = bb.slot_weight;
+        c.out = od;
+        ProfScope ps(ctx, "combine");
+        ctx->launches += moe::launch_combine(c, M, s);
+    }
+    return finish(ctx);
+}
+
 }  // namespace
 
 int moe_route(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const float* x, int flags,
@@ -1852,15 +2108,20 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
                       int flags, int64_t* tc, int64_t* ti, float* tw) {
     TRY(begin(ctx));
     TRY(check_desc(ctx, L));
-    if (!x || !out) return fail(ctx, MOE_E_ARG, "null pointer");
-    if (M <= 0) return fail(ctx, MOE_E_SHAPE, "M must be >= 1");
     const int64_t d = L->embed_dim, E = L->num_experts, K = L->top_k, F = L->expert_mlp_dim;
     // expert parallelism (moe_ep_init): this rank's experts for the call
     const bool ep = ctx->ep.comm != nullptr;
+    const bool a2a = ep && ctx->ep_mode == MOE_EP_ALL_TO_ALL;
+    if (M < 0 || (M == 0 && !a2a)) return fail(ctx, MOE_E_SHAPE, "M must be >= 1");
+    if (M > 0 && (!x || !out)) return fail(ctx, MOE_E_ARG, "null pointer");
     if (ep) {
         if (flags & MOE_F_FP16_OUT)
             return fail(ctx, MOE_E_ARG, "expert parallelism sums fp32 partial outputs: MOE_F_FP16_OUT not supported");
         if (E < ctx->ep.nranks) return fail(ctx, MOE_E_SHAPE, "num_experts must be >= the number of ranks");
+        if (ctx->ep_mode != MOE_EP_REPLICATED && E % ctx->ep.nranks != 0)
+            return fail(ctx, MOE_E_SHAPE, "the gather and all-to-all forms need num_experts divisible by the ranks");
+        if (ctx->ep_mode == MOE_EP_GATHER) return ep_gather_forward(ctx, L, M, x, out, flags, tc, ti, tw);
+        if (a2a) return ep_a2a_forward(ctx, L, M, x, out, flags, tc, ti, tw);
     }
     struct RangeScope {  // the option values come back on every exit
         moe_ctx* c;

@@ -25,6 +25,7 @@
 #include <string>
 #include <thread>
 #include <type_traits>
+#include <vector>
 
 #include "moe_b200.h"
 #include "moe_internal.h"
@@ -35,6 +36,12 @@ struct NcclApi {
     decltype(&ncclGetUniqueId) get_unique_id = nullptr;
     decltype(&ncclCommInitRankConfig) init_rank_config = nullptr;
     decltype(&ncclAllReduce) all_reduce = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
+    decltype(&ncclReduceScatter) reduce_scatter = nullptr;
+    decltype(&ncclSend) send = nullptr;
+    decltype(&ncclRecv) recv = nullptr;
+    decltype(&ncclGroupStart) group_start = nullptr;
+    decltype(&ncclGroupEnd) group_end = nullptr;
     decltype(&ncclCommDestroy) destroy = nullptr;
     decltype(&ncclCommAbort) abort = nullptr;
     decltype(&ncclCommGetAsyncError) async_error = nullptr;
@@ -62,6 +69,12 @@ const NcclApi* nccl(std::string& err) {
         get(api.get_unique_id, "ncclGetUniqueId");
         get(api.init_rank_config, "ncclCommInitRankConfig");
         get(api.all_reduce, "ncclAllReduce");
+        get(api.all_gather, "ncclAllGather");
+        get(api.reduce_scatter, "ncclReduceScatter");
+        get(api.send, "ncclSend");
+        get(api.recv, "ncclRecv");
+        get(api.group_start, "ncclGroupStart");
+        get(api.group_end, "ncclGroupEnd");
         get(api.destroy, "ncclCommDestroy");
         get(api.abort, "ncclCommAbort");
         get(api.async_error, "ncclCommGetAsyncError");
@@ -172,6 +185,73 @@ int ep_all_reduce(EpComm& ep, float* buf, size_t count, cudaStream_t s, uint64_t
     }
     ep.pending = true;
     return MOE_OK;
+}
+
+namespace {
+// Common tail of an enqueue: an error aborts the communicator, an enqueue
+// still in progress is polled to completion, and the context is marked as
+// having a collective in flight.
+int enqueued(EpComm& ep, const NcclApi* api, ncclResult_t r, const char* what, uint64_t timeout_ns, std::string& err) {
+    if (r != ncclSuccess && r != ncclInProgress) {
+        err = nccl_msg(api, what, r);
+        ep_abort(ep);
+        return MOE_E_NCCL;
+    }
+    if (r == ncclInProgress) {
+        const int s2 = settle(ep, api, now_ns() + timeout_ns, what, err);
+        if (s2 != MOE_OK) return s2;
+    }
+    ep.pending = true;
+    return MOE_OK;
+}
+}  // namespace
+
+int ep_all_gather(EpComm& ep, const void* send, void* recv, size_t count, bool is_float, cudaStream_t s,
+                  uint64_t timeout_ns, std::string& err) {
+    const NcclApi* api = nccl(err);
+    if (!api || !ep.comm) {
+        if (api) err = "no expert-parallel communicator";
+        return MOE_E_STATE;
+    }
+    const ncclResult_t r = api->all_gather(send, recv, count, is_float ? ncclFloat32 : ncclInt32,
+                                           static_cast<ncclComm_t>(ep.comm), s);
+    return enqueued(ep, api, r, "ncclAllGather", timeout_ns, err);
+}
+
+int ep_reduce_scatter(EpComm& ep, const float* send, float* recv, size_t count, cudaStream_t s, uint64_t timeout_ns,
+                      std::string& err) {
+    const NcclApi* api = nccl(err);
+    if (!api || !ep.comm) {
+        if (api) err = "no expert-parallel communicator";
+        return MOE_E_STATE;
+    }
+    const ncclResult_t r =
+        api->reduce_scatter(send, recv, count, ncclFloat32, ncclSum, static_cast<ncclComm_t>(ep.comm), s);
+    return enqueued(ep, api, r, "ncclReduceScatter", timeout_ns, err);
+}
+
+int ep_exchange(EpComm& ep, const std::vector<EpXfer>& xfers, cudaStream_t s, uint64_t timeout_ns, std::string& err) {
+    const NcclApi* api = nccl(err);
+    if (!api || !ep.comm) {
+        if (api) err = "no expert-parallel communicator";
+        return MOE_E_STATE;
+    }
+    ncclComm_t comm = static_cast<ncclComm_t>(ep.comm);
+    ncclResult_t r = api->group_start();
+    if (r != ncclSuccess) return enqueued(ep, api, r, "ncclGroupStart", timeout_ns, err);
+    for (const EpXfer& x : xfers) {
+        if (x.count == 0) continue;
+        const ncclDataType_t dt = x.is_float ? ncclFloat32 : ncclInt32;
+        r = x.send ? api->send(x.buf, x.count, dt, x.peer, comm, s) : api->recv(x.buf, x.count, dt, x.peer, comm, s);
+        if (r != ncclSuccess && r != ncclInProgress) break;
+    }
+    const ncclResult_t r2 = api->group_end();
+    if (r != ncclSuccess && r != ncclInProgress) {
+        err = nccl_msg(api, "ncclSend/ncclRecv", r);
+        ep_abort(ep);
+        return MOE_E_NCCL;
+    }
+    return enqueued(ep, api, r2, "ncclGroupEnd (send/recv)", timeout_ns, err);
 }
 
 int ep_wait(EpComm& ep, cudaEvent_t done, uint64_t timeout_ns, bool abort_on_timeout, std::string& err) {

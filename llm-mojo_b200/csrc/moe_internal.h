@@ -22,6 +22,23 @@ int ep_unique_id(uint8_t* out, std::string& err);
 int ep_init(EpComm& ep, const uint8_t* id, int rank, int nranks, uint64_t timeout_ns, std::string& err);
 // In-place fp32 sum over the ranks, enqueued on `s`.
 int ep_all_reduce(EpComm& ep, float* buf, size_t count, cudaStream_t s, uint64_t timeout_ns, std::string& err);
+// Gathers `count` elements (fp32 or int32) of every rank into `recv`, rank order.
+int ep_all_gather(EpComm& ep, const void* send, void* recv, size_t count, bool is_float, cudaStream_t s,
+                  uint64_t timeout_ns, std::string& err);
+// Sums `send` [nranks * count] over the ranks; this rank receives its `count` slice.
+int ep_reduce_scatter(EpComm& ep, const float* send, float* recv, size_t count, cudaStream_t s, uint64_t timeout_ns,
+                      std::string& err);
+// One point-to-point transfer of a grouped exchange.
+struct EpXfer {
+    bool send;
+    void* buf;
+    size_t count;   // elements
+    bool is_float;  // fp32, else int32
+    int peer;
+};
+// All transfers in one NCCL group (an all-to-all-v when every rank lists
+// one send and one receive per peer).
+int ep_exchange(EpComm& ep, const std::vector<EpXfer>& xfers, cudaStream_t s, uint64_t timeout_ns, std::string& err);
 // Waits for `done` (recorded after a collective), checking the communicator's
 // asynchronous error; aborts the communicator on an error, and after
 // `timeout_ns` when `abort_on_timeout`.
@@ -248,5 +265,21 @@ int launch_subspace_rows(const SubspaceRowsArgs& a, const int64_t* keep, int64_t
 // One CTA waiting on an mbarrier that nothing completes, bounded by
 // `timeout_ns` (the check behind moe_device_wait_check).
 int launch_wait_check(int* err_flag, uint64_t timeout_ns, cudaStream_t s);
+
+// Expert-parallel helpers (moe_kernels.cu).
+// slot_expert: global expert ids -> ids local to [e_lo, e_hi) (others -1).
+int launch_ep_localize(int* slot_expert, int64_t P, int e_lo, int e_hi, cudaStream_t s);
+// From the buckets of a token shard (global expert ids): the destination
+// rank of every sorted pair's expert (experts_per_rank apiece), the pair's
+// expert id local to that rank, and the row count per destination.
+int launch_ep_pack(const BucketOut& b, int experts_per_rank, int nranks, int* send_local_e, int* send_cnt,
+                   cudaStream_t s);
+// dst[p] = src[map[p]] for the rows p < *n_rows (device count), fp32 rows of d.
+int launch_gather_rows(const float* src, const int* map, const int* n_rows, int64_t max_rows, int64_t d, float* dst,
+                       cudaStream_t s);
+// A slot table for rows that each carry one pair: slot_expert[i] =
+// local_e[i], slot_weight[i] = 1; ids outside [0, E) raise err_flag 1.
+int launch_ep_slots(const int* local_e, int64_t P, int E, int* slot_expert, float* slot_weight, int* err_flag,
+                    cudaStream_t s);
 
 }  // namespace moe

@@ -9,6 +9,8 @@
 // with warp shuffles.
 #include <float.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "moe_internal.h"
 
@@ -1269,6 +1271,88 @@ int launch_apply_lod(const int64_t* top_idx, const float* top_val, const float* 
     launch_k(k_apply_lod, dim3((unsigned)((B + 127) / 128)), dim3(128), 0, s, top_idx, top_val, pes, top_w, B, K,
                                                              eff_k, unacc, eb_mask,
                                                              active_canvas_idx);
+    return 1;
+}
+
+}  // namespace moe
+
+namespace moe {
+
+// ------------------------------------------------------- expert parallelism
+__global__ void k_ep_localize(int* se, int64_t P, int e_lo, int e_hi) {
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < P; p += (int64_t)gridDim.x * blockDim.x) {
+        const int e = se[p];
+        se[p] = (e >= e_lo && e < e_hi) ? e - e_lo : -1;
+    }
+}
+
+int launch_ep_localize(int* slot_expert, int64_t P, int e_lo, int e_hi, cudaStream_t s) {
+    if (P <= 0) return 0;
+    const int grid = (int)std::min<int64_t>((P + 255) / 256, 1184);
+    launch_k(k_ep_localize, dim3(grid), dim3(256), 0, s, slot_expert, P, e_lo, e_hi);
+    return 1;
+}
+
+// One warp per unique expert: its pairs go to rank e / epr as local id e % epr.
+__global__ void __launch_bounds__(1024) k_ep_pack(BucketOut b, int epr, int nranks, int* local_e, int* cnt) {
+    pdl_wait();
+    pdl_trigger();
+    for (int j = threadIdx.x; j < nranks; j += blockDim.x) cnt[j] = 0;
+    __syncthreads();
+    const int U = b.meta[0];
+    const int lane = threadIdx.x & 31;
+    for (int u = threadIdx.x >> 5; u < U; u += blockDim.x >> 5) {
+        const int e = b.unique_expert[u], dest = e / epr, n = b.seg_count[u], s0 = b.seg_start[u];
+        for (int i = lane; i < n; i += 32) local_e[s0 + i] = e - dest * epr;
+        if (lane == 0) atomicAdd(&cnt[dest], n);
+    }
+}
+
+int launch_ep_pack(const BucketOut& b, int experts_per_rank, int nranks, int* send_local_e, int* send_cnt,
+                   cudaStream_t s) {
+    launch_k(k_ep_pack, dim3(1), dim3(1024), 0, s, b, experts_per_rank, nranks, send_local_e, send_cnt);
+    return 1;
+}
+
+__global__ void __launch_bounds__(256) k_gather_rows(const float* src, const int* map, const int* n_rows,
+                                                     int64_t max_rows, int64_t d, float* dst) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t n = min((int64_t)*n_rows, max_rows), d4 = d / 4;
+    for (int64_t r = blockIdx.x; r < n; r += gridDim.x) {
+        const float4* a = reinterpret_cast<const float4*>(src + (int64_t)map[r] * d);
+        float4* o = reinterpret_cast<float4*>(dst + r * d);
+        for (int64_t j = threadIdx.x; j < d4; j += blockDim.x) o[j] = __ldg(a + j);
+    }
+}
+
+int launch_gather_rows(const float* src, const int* map, const int* n_rows, int64_t max_rows, int64_t d, float* dst,
+                       cudaStream_t s) {
+    if (max_rows <= 0) return 0;
+    const int grid = (int)std::min<int64_t>(max_rows, 1184);
+    launch_k(k_gather_rows, dim3(grid), dim3(256), 0, s, src, map, n_rows, max_rows, d, dst);
+    return 1;
+}
+
+__global__ void k_ep_slots(const int* le, int64_t P, int E, int* se, float* sw, int* err) {
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < P; p += (int64_t)gridDim.x * blockDim.x) {
+        const int e = le[p];
+        const bool ok = e >= 0 && e < E;
+        if (!ok) atomicExch(err, 1);
+        se[p] = ok ? e : -1;
+        sw[p] = 1.0f;
+    }
+}
+
+int launch_ep_slots(const int* local_e, int64_t P, int E, int* slot_expert, float* slot_weight, int* err_flag,
+                    cudaStream_t s) {
+    if (P <= 0) return 0;
+    const int grid = (int)std::min<int64_t>((P + 255) / 256, 1184);
+    launch_k(k_ep_slots, dim3(grid), dim3(256), 0, s, local_e, P, E, slot_expert, slot_weight, err_flag);
     return 1;
 }
 

@@ -14,7 +14,7 @@ import os
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path[:0] = [os.path.join(HERE, "..", "llm-mojo_b200"), HERE]
+sys.path[:0] = [os.path.join(HERE, "..", "llm-mojo_b200"), os.path.join(HERE, "..", "oracle"), HERE]
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
@@ -107,6 +107,66 @@ def main():
         mx, rel = errors(out.cpu().numpy(), ref.cpu().numpy())
         print(f"rank {rank} native M={M}: max_abs={mx:.2e} rel_l2={rel:.2e}", flush=True)
         ok = ok and mx <= 5e-4 and rel <= 1e-4
+    # the library's token forms: gather (decode) and all-to-all (prefill),
+    # each rank holding only its experts' weights (slices of the full layer)
+    E, d = layer["E"], layer["d"]
+    El, e_lo = E // world, rank * (E // world)
+    F2 = 2 * layer["F"]
+    local = dict(layer)
+    local["gu_p"] = layer["gu_p"][e_lo * F2 * d // 2:(e_lo + El) * F2 * d // 2]
+    local["gu_s"] = layer["gu_s"][e_lo * F2 * d // 32:(e_lo + El) * F2 * d // 32]
+    local["dn_p"] = layer["dn_p"][e_lo * d * layer["F"] // 2:(e_lo + El) * d * layer["F"] // 2]
+    local["dn_s"] = layer["dn_s"][e_lo * d * layer["F"] // 32:(e_lo + El) * d * layer["F"] // 32]
+    ldesc = MB.make_desc(local)
+    cnative.set_option(MB.OPT_EP_LOCAL_WEIGHTS, 1)
+    for mode, sizes in ((MB.EP_GATHER, (1, 16, 64)), (MB.EP_ALL_TO_ALL, (1, 64, 1000))):
+        cnative.set_option(MB.OPT_EP_MODE, mode)
+        for M in sizes:
+            Mt = M * world if mode == MB.EP_GATHER else M
+            x = synth.make_x(Mt, seed=210 + Mt)
+            t0, t1 = (rank * M, (rank + 1) * M) if mode == MB.EP_GATHER else ep.row_range(rank, world, Mt)
+            mine = x[t0:t1].contiguous()
+            out = torch.zeros((t1 - t0, d), device="cuda")
+            cnt = torch.zeros(t1 - t0, dtype=torch.int64, device="cuda")
+            cnative.layer_forward(ldesc, t1 - t0, mine if t1 > t0 else None, out if t1 > t0 else None,
+                                  MB.F_POST_NORM, cnt if t1 > t0 else None)
+            ref = torch.zeros((Mt, d), device="cuda")
+            rcnt = torch.zeros(Mt, dtype=torch.int64, device="cuda")
+            ctx.layer_forward(desc, Mt, x, ref, MB.F_POST_NORM, rcnt)
+            torch.cuda.synchronize()
+            bar_abs, bar_rel = 5e-4, 1e-4
+            if t1 > t0:
+                mx, rel = errors(out.cpu().numpy(), ref[t0:t1].cpu().numpy())
+                same_cnt = torch.equal(cnt, rcnt[t0:t1])
+                if Mt == 1:  # one token: fp32 CUDA-core reference against fp16 dispatched rows
+                    raw = torch.zeros_like(ref)
+                    ctx.layer_forward(desc, Mt, x, raw, 0)
+                    bar_abs = 2e-3 * float((1.0 / torch.sqrt(raw.double().pow(2).mean(1) + 1e-6)).max())
+                    bar_rel = 1e-3
+            else:
+                mx, rel, same_cnt = 0.0, 0.0, True
+            print(f"rank {rank} native {'gather' if mode == MB.EP_GATHER else 'all-to-all'} M={Mt} rows "
+                  f"{t0}:{t1}: max_abs={mx:.2e} rel_l2={rel:.2e} counts_equal={same_cnt}", flush=True)
+            ok = ok and mx <= bar_abs and rel <= bar_rel and same_cnt
+    # the all-to-all form against the oracle itself on a sample of this
+    # rank's tokens (the M=1000 batch): pre-norm outputs, routing from the
+    # oracle
+    import oracle as O
+    cnative.set_option(MB.OPT_EP_MODE, MB.EP_ALL_TO_ALL)
+    x = synth.make_x(1000, seed=909)
+    t0, t1 = ep.row_range(rank, world, 1000)
+    out = torch.zeros((t1 - t0, d), device="cuda")
+    cnative.layer_forward(ldesc, t1 - t0, x[t0:t1].contiguous(), out, 0)
+    torch.cuda.synchronize()
+    host = synth.to_host(layer)
+    L = O.make_layer(host)
+    pick = np.arange(t0, t1)[:: max(1, (t1 - t0) // 48)]
+    r = O.route(L, x[pick].cpu().numpy())
+    oref = O.experts_forward(L, r["moe_in"], r["count"], r["idx"], r["w"], prec=O.F64)
+    mx, rel = errors(out[pick - t0].cpu().numpy(), oref)
+    print(f"rank {rank} native all-to-all vs oracle ({len(pick)} tokens): max_abs={mx:.2e} rel_l2={rel:.2e}",
+          flush=True)
+    ok = ok and mx <= 2e-3 and rel <= 1e-3
     cnative.ep_finalize()
     cnative.close()
     dist.barrier()

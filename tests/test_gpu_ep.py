@@ -135,6 +135,54 @@ def test_native_ep_one_rank_equals_the_layer(ctx, full_layer):
         c2.close()
 
 
+@pytest.mark.parametrize("mode", ["gather", "all_to_all"])
+def test_native_ep_token_forms_one_rank(ctx, full_layer, mode):
+    """The gather and all-to-all forms on a one-rank communicator (the
+    exchange goes to the rank itself) against the plain layer call, the
+    routing outputs bit-exact, outputs within fp32 reordering; the
+    all-to-all form also with no token at all (M = 0), which must still
+    take part in the exchange, and with the local-weights option (the
+    descriptor's expert arrays are the rank's slice: here all experts)."""
+    import torch
+    dev, _, _ = full_layer
+    d2 = dict(dev)
+    d2["post_norm_w"] = (1.0 + 0.1 * torch.randn(2816, generator=torch.Generator().manual_seed(9))).cuda()
+    desc = MB.make_desc(d2)
+    c2 = MB.Context(0)
+    try:
+        c2.ep_init(MB.ep_unique_id(), 0, 1)
+        c2.set_option(MB.OPT_EP_MODE, MB.EP_GATHER if mode == "gather" else MB.EP_ALL_TO_ALL)
+        for local in (0, 1):
+            c2.set_option(MB.OPT_EP_LOCAL_WEIGHTS, local)
+            for M in (1, 16, 300):
+                x = synth.make_x(M, seed=140 + M)
+                ref = torch.zeros((M, 2816), device="cuda")
+                rc, ri, rw = (torch.zeros(M, dtype=torch.int64, device="cuda"),
+                              torch.zeros((M, 8), dtype=torch.int64, device="cuda"),
+                              torch.zeros((M, 8), device="cuda"))
+                ctx.layer_forward(desc, M, x, ref, MB.F_POST_NORM, rc, ri, rw)
+                got = torch.zeros_like(ref)
+                gc, gi, gw = torch.zeros_like(rc), torch.zeros_like(ri), torch.zeros_like(rw)
+                c2.layer_forward(desc, M, x, got, MB.F_POST_NORM, gc, gi, gw)
+                torch.cuda.synchronize()
+                assert torch.equal(gc, rc) and torch.equal(gi, ri) and torch.equal(gw, rw), f"{mode} M={M}"
+                bar = (5e-4, 1e-4)
+                if mode == "all_to_all" and M == 1:
+                    # the plain call takes the fp32 CUDA-core kernels for one
+                    # token, the eight dispatched rows the fp16 tensor-core
+                    # path: the north-star bar carried through the post-norm
+                    raw = torch.zeros_like(ref)
+                    ctx.layer_forward(desc, M, x, raw, 0)
+                    inv_rms = float((1.0 / torch.sqrt(raw.double().pow(2).mean(1) + 1e-6)).max())
+                    bar = (2e-3 * inv_rms, 1e-3)
+                assert_close(got.cpu().numpy(), ref.cpu().numpy(), max_abs=bar[0], rel_l2=bar[1],
+                             what=f"ep1 {mode} M={M} local={local}")
+        if mode == "all_to_all":
+            c2.layer_forward(desc, 0, None, None, MB.F_POST_NORM)
+    finally:
+        c2.close()
+
+
 _MISSING_RANK = r"""
 import sys
 sys.path[:0] = sys.argv[1:]
