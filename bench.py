@@ -42,20 +42,23 @@ DN_BYTES = D * F // 2 + D * F // 32 * 4           # 1,239,040 per expert
 ROUTER_BYTES = E * D // 2 + E * D // 32 * 4       # 225,280
 DENSE = [("q", D, 4096), ("k", D, 1024), ("v", D, 1024), ("o", 4096, D)]
 # tokens per step, distinct layers cycled (default), skewed routing, step count (default)
+# tokens per step, distinct layers, whether a step runs the whole stack of
+# layers, skewed routing, default step count, the N > 1 form
 WORKLOADS = {
     "decode16": dict(M=16, layers=4),
     "decode1": dict(M=1, layers=4),
     "block256": dict(M=256, layers=4),
-    "decode64": dict(M=64, layers=30),
-    "prefill8k": dict(M=8192, layers=2, skew=True, steps=50),
+    "decode64": dict(M=64, layers=30, stack=True, steps=100),
+    "prefill8k": dict(M=8192, layers=30, stack=True, skew=True, steps=5, a2a=True),
 }
 WORKLOAD_NAMES = {
     "decode16": "cfg2: M=16 decode MoE layer + dense q/k/v/o",
     "decode1": "cfg1: M=1 decode MoE layer",
     "block256": "cfg3: M=256 block through the MoE layer",
-    "decode64": "cfg4: M=64 decode, one layer step of a 30-layer stack (independent seeded layers)",
-    "prefill8k": "cfg5: M=8192 (4 x 2048) through the MoE layer, Zipf(1.1)-skewed router",
+    "decode64": "cfg4: M=64 decode through the 30-layer stack (independent seeded layers); a step is all 30 layers",
+    "prefill8k": "cfg5: M=8192 (4 x 2048) through the 30-layer stack, Zipf(1.1)-skewed router; a step is all 30 layers",
 }
+SUB_WORKLOADS = ("decode1", "block256", "decode64", "prefill8k")
 METRIC = "moe_layer_tokens_per_s"
 
 
@@ -224,6 +227,7 @@ def run_reference(args, ws, rank):
     if rank != 0:
         return 0
     M = WORKLOADS[args.workload]["M"]
+    n_lay = args.layers if WORKLOADS[args.workload].get("stack") else 1
     nthreads = os.cpu_count() or 1
     w, dense = host_layer(seed=0)
     # bounded sample: at most ~120 s for the K timed steps
@@ -246,12 +250,14 @@ def run_reference(args, ws, rank):
     for _ in range(args.steps):
         cpu_step(L, use_dense, x, x_o, nthreads)
     dt = time.perf_counter() - t0
-    value = m * args.steps / dt
+    value = m * args.steps / dt / n_lay
     sample = f"{m} of {M} tokens per step, {args.steps} steps, 1 layer (+dense q/k/v/o)" if M == 16 \
         else f"{m} of {M} tokens per step, {args.steps} steps, 1 layer"
+    if n_lay > 1:
+        sample += f"; rate divided by {n_lay} for the {n_lay}-layer step"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps * n_lay,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": workload_config(args, M),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
@@ -271,71 +277,80 @@ def dtype_desc(args, M):
     return "f32 io and routing; fp16 x fp16 -> fp32 tcgen05 expert GEMMs"
 
 
-def workload_config(args, M):
+def workload_config(args, M, par="replicas", ws=1):
+    wl = WORKLOADS[args.workload]
+    stack = bool(wl.get("stack"))
+    n_mb = args.layers * 476
+    par_desc = {
+        "replicas": f"replicas x{ws}",
+        "ep": f"ep{ws}: 128/{ws} experts per GPU, tokens replicated, torch.distributed NCCL all-reduce of "
+              f"partial outputs; dense rows sharded",
+        "ep-native": f"ep{ws}: 128/{ws} experts per GPU, tokens replicated, NCCL all-reduce inside the layer "
+                     f"call (moe_ep_init); dense rows sharded",
+        "ep-gather": f"ep{ws}: 128/{ws} experts per GPU (weight slices), {M} own tokens per GPU; the layer "
+                     f"call all-gathers the tokens and reduce-scatters the partial outputs (NCCL)",
+        "ep-a2a": f"ep{ws}: 128/{ws} experts per GPU (weight slices), the {M} tokens sharded over the GPUs; "
+                  f"the layer call sends routed rows to the expert owners and back (NCCL send/recv)",
+    }[par]
     return {"workload": WORKLOAD_NAMES[args.workload],
             "tokens_per_step": M, "embed_dim": D, "expert_mlp_dim": F, "num_experts": E, "top_k": K,
-            "layers_cycled": args.layers,
-            "l2": f"weights of {args.layers} distinct layers cycled per step ({args.layers * 476} MB > 126 MB L2)",
-            "post_norm": True,
-            "parallelism": (f"ep{dist_setup()[0]}: 128/{dist_setup()[0]} experts per GPU, tokens replicated, "
-                            f"NCCL all-reduce of partial outputs"
-                            f"{' inside the layer call (moe_ep_init)' if getattr(args, 'parallel', 'ep') == 'ep-native' else ''}"
-                            f"; dense rows sharded"
-                            if dist_setup()[0] > 1 and getattr(args, "parallel", "ep") in ("ep", "ep-native")
-                            else f"replicas x{dist_setup()[0]}"),
+            "layers": args.layers, "layers_per_step": args.layers if stack else 1,
+            "l2": f"weights of {args.layers} distinct layers ({n_mb} MB > 126 MB L2) "
+                  f"{'run back to back in every step' if stack else 'cycled step by step'}",
+            "post_norm": True, "parallelism": par_desc,
             "gemm_path": getattr(args, "path", "auto"),
             "tc_kernel": getattr(args, "tc_kernel", "stream"),
-            "dense_projections": "own contexts and streams, concurrent with the MoE layer",
+            "dense_projections": "own contexts and streams, concurrent with the MoE layer" if M == 16 else "none",
             "cuda_graph": not getattr(args, "no_graph", False)}
 
 
 # ----------------------------------------------------------------- GPU leg
-def main():
+PAR_HELP = ("N > 1: ep-gather (default for decode: each rank its own tokens, 128/N experts per rank, the "
+            "library all-gathers the tokens and reduce-scatters the partial outputs inside the layer call), "
+            "ep-a2a (default for prefill8k: each rank a shard of the tokens, routed rows to the expert owners "
+            "and back over NCCL inside the layer call), ep / ep-native (tokens replicated, NCCL all-reduce of "
+            "partial outputs by torch.distributed / inside the library), or replicas")
+
+
+def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (workload default)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode16", choices=sorted(WORKLOADS))
-    ap.add_argument("--layers", type=int, default=None, help="distinct layers cycled (workload default)")
+    ap.add_argument("--layers", type=int, default=None, help="distinct layers (workload default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="N = 1, default workload: skip the other configurations' sub-lines")
     ap.add_argument("--no-graph", action="store_true", help="launch every step from the host")
     ap.add_argument("--graph", action="store_true",
-                    help="with N > 1, capture steps (NCCL all-reduce included) in CUDA graphs; "
+                    help="with N > 1, capture steps (collectives included) in CUDA graphs; "
                          "by default N > 1 launches eagerly")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"],
                     help="expert/dense GEMM path: CUDA-core GEMV, tcgen05, or automatic")
-    ap.add_argument("--parallel", default="ep", choices=["ep", "ep-native", "replicas"],
-                    help="N > 1: expert parallel (128/N experts per GPU, tokens replicated, one NCCL "
-                         "all-reduce per layer; dense projections row-sharded) with the all-reduce "
-                         "issued by torch.distributed (ep) or inside the library's layer call "
-                         "(ep-native, moe_ep_init), or independent replicas")
+    ap.add_argument("--parallel", default=None,
+                    choices=["ep-gather", "ep-a2a", "ep", "ep-native", "replicas"], help=PAR_HELP)
+    ap.add_argument("--fused-route", type=int, default=None, choices=[0, 1, 2],
+                    help="routing of small batches: separate kernels (0), one cluster (1), one cooperative "
+                         "grid launch (2); default: the library's")
     ap.add_argument("--tc-kernel", default="stream", choices=["stream", "stream-all", "general"],
                     help="tensor-core kernel for token tiles <= 64: streaming for the expert GEMMs "
                          "(default), streaming also for dense projections, or general")
-    args = ap.parse_args()
+    return ap.parse_args(argv)
+
+
+def main():
+    args = parse_args()
     args.warmup = max(args.warmup, 3)
-    wl = WORKLOADS[args.workload]
-    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and not args.graph:
-        # replaying graphs that hold the NCCL all-reduce was slower than eager
-        # launches at 8 ranks (825 us per step replayed, 462 us per step for
-        # eager calls even with host copies), so N > 1 runs eagerly
-        args.no_graph = True
-    if args.layers is None:
-        args.layers = wl["layers"]
-    if args.steps is None:
-        args.steps = wl.get("steps", 2000)
     ws, rank, local = dist_setup()
+    explicit_steps, explicit_layers = args.steps, args.layers
+    fill_defaults(args, ws)
     if args.impl == "reference":
         return run_reference(args, ws, rank)
 
-    import numpy as np
     import torch
-    import ep as EP
-    import moe_b200 as MB
-    import synth
-
     torch.cuda.set_device(local)
     pg = None
     if ws > 1:
@@ -344,51 +359,136 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
         pg = dist
+    line = measure(args, pg, ws, rank, local)
+    if ws == 1 and args.workload == "decode16" and not args.no_workloads:
+        # the other configurations, each measured the same way in this run
+        subs = {}
+        for name in SUB_WORKLOADS:
+            sa = parse_args([])
+            sa.workload, sa.warmup, sa.path, sa.tc_kernel = name, 3, args.path, args.tc_kernel
+            sa.fused_route = args.fused_route
+            sa.no_cpu_baseline = args.no_cpu_baseline
+            sa.cpu_budget_s = min(args.cpu_budget_s, 4.0)
+            fill_defaults(sa, ws)
+            sub = measure(sa, None, 1, 0, local)
+            subs[name] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "steps", "warmup", "dtype",
+                                              "config", "roofline", "step_roofline", "cpu_baseline", "e2e",
+                                              "gpu_launches", "clocks") if k in sub}
+        line["workloads"] = subs
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        torch.cuda.synchronize()
+        pg.destroy_process_group()
+    return 0
+
+
+def fill_defaults(args, ws):
+    wl = WORKLOADS[args.workload]
+    if args.parallel is None:
+        args.parallel = ("ep-a2a" if wl.get("a2a") else "ep-gather") if ws > 1 else "replicas"
+    if ws > 1 and not args.graph:
+        # replaying graphs that hold NCCL calls was slower than eager launches
+        # at 8 ranks (825 us per step replayed against 462 us eager for the
+        # all-reduce form), so N > 1 runs eagerly
+        args.no_graph = True
+    if args.parallel == "ep-a2a":
+        args.no_graph = True  # the all-to-all form reads its row counts on the host
+    if args.layers is None:
+        args.layers = wl["layers"]
+    if args.steps is None:
+        args.steps = wl.get("steps", 2000)
+
+
+def measure(args, pg, ws, rank, local):
+    import numpy as np
+    import torch
+    import ep as EP
+    import moe_b200 as MB
+    import synth
+
+    wl = WORKLOADS[args.workload]
+    stack = bool(wl.get("stack"))
     ctx = MB.Context(local)
     stream = torch.cuda.current_stream()
     ctx.set_stream(stream.cuda_stream)
     ctx.set_gemm_path({"auto": MB.PATH_AUTO, "gemv": MB.PATH_GEMV, "tc": MB.PATH_TC}[args.path])
     ctx.set_option(MB.OPT_TC_STREAM, {"general": 0, "stream": 1, "stream-all": 2}[args.tc_kernel])
-    M = wl["M"]
-    use_ep = ws > 1 and args.parallel in ("ep", "ep-native")
-    native_ep = use_ep and args.parallel == "ep-native"
-    if native_ep:  # the library's own communicator: rank 0's id to every rank
+    if args.fused_route is not None:
+        ctx.set_option(MB.OPT_FUSED_ROUTE, args.fused_route)
+    M_total = wl["M"]
+    par = args.parallel if ws > 1 else "replicas"
+    lib_ep = par in ("ep-native", "ep-gather", "ep-a2a")
+    shared_layers = par != "replicas"       # every rank holds (a slice of) the same layers
+    if par == "ep-a2a":  # a shard of the workload's tokens per rank (strong scaling)
+        t0_, t1_ = EP.row_range(rank, ws, M_total)
+        M = t1_ - t0_
+    else:
+        M = M_total
+    if lib_ep:  # the library's own communicator: rank 0's id to every rank
         uid = [MB.ep_unique_id() if rank == 0 else None]
         pg.broadcast_object_list(uid, src=0)
         ctx.ep_init(uid[0], rank, ws)
-    # expert parallel: every rank holds the same layers and tokens and
-    # evaluates its own expert range; replicas: independent data per rank
-    seed_rank = 0 if use_ep else rank
+        ctx.set_option(MB.OPT_EP_MODE, {"ep-native": MB.EP_REPLICATED, "ep-gather": MB.EP_GATHER,
+                                        "ep-a2a": MB.EP_ALL_TO_ALL}[par])
+    seed_rank = 0 if shared_layers else rank
+    # own batches per rank (gather form, replicas); the all-to-all form shards
+    # one global batch; the replicated forms share one batch
+    tok_seed = rank if par in ("ep-gather", "replicas") else 0
+    e_lo, e_hi = EP.expert_range(rank, ws, E) if par != "replicas" else (0, E)
 
     layers, descs = [], []
     for li in range(args.layers):
         lw = synth.make_layer(ctx, seed=1000 * seed_rank + li)
         layers.append(lw)
-        descs.append(MB.make_desc(lw))
     skew = None
+    bias = None
     if wl.get("skew"):
-        x_cal = synth.make_x(M, seed=499)
-        alpha, ratio, bias = calibrate_skew(ctx, MB, synth, layers[0], x_cal, M)
-        descs = [MB.make_desc(lw, bias=bias) for lw in layers]
+        x_cal = synth.make_x(M_total, seed=499)
+        alpha, ratio, bias = calibrate_skew(ctx, MB, synth, layers[0], x_cal, M_total)
         skew = {"zipf_s": 1.1, "alpha": alpha, "max_over_mean_load": ratio}
+    full_descs = [MB.make_desc(lw, bias=bias) for lw in layers]
+    if par in ("ep-gather", "ep-a2a"):
+        # each rank hands the library only its experts' weights
+        ctx.set_option(MB.OPT_EP_LOCAL_WEIGHTS, 1)
+        El = e_hi - e_lo
+        for lw in layers:
+            loc = dict(lw)
+            loc["gu_p"] = lw["gu_p"][e_lo * 2 * F * D // 2:e_hi * 2 * F * D // 2]
+            loc["gu_s"] = lw["gu_s"][e_lo * 2 * F * D // 32:e_hi * 2 * F * D // 32]
+            loc["dn_p"] = lw["dn_p"][e_lo * D * F // 2:e_hi * D * F // 2]
+            loc["dn_s"] = lw["dn_s"][e_lo * D * F // 32:e_hi * D * F // 32]
+            descs.append(MB.make_desc(loc, bias=bias))
+        assert El * ws == E
+    else:
+        descs = full_descs
     gen = torch.Generator(device="cuda")
-    gen.manual_seed(77 + seed_rank)
+    gen.manual_seed(77 + tok_seed)
     dense = {}
-    if M == 16:
+    if M_total == 16:
         for name, ci, co in DENSE:
             wt = torch.randn(ci * co, generator=gen, device="cuda") * 0.02
             p, s = synth.quantize(ctx, wt)
-            if use_ep:  # row-sharded: this rank's slice of the output features
+            if par in ("ep", "ep-native"):  # row-sharded: this rank's slice of the output features
                 r0, r1 = EP.row_range(rank, ws, co)
                 p, s, co = p[r0 * ci // 2:r1 * ci // 2], s[r0 * ci // 32:r1 * ci // 32], r1 - r0
             dense[name] = (p, s, ci, co)
-    xs = [synth.make_x(M, seed=500 + 10 * seed_rank + li) for li in range(args.layers)]
-    x_o = torch.randn((M, 4096), generator=gen, device="cuda")
-    out = torch.empty((M, D), device="cuda")
+    n_x = 1 if stack else args.layers
+
+    def make_tokens(r):
+        xs_r = []
+        for li in range(n_x):
+            xf = synth.make_x(M_total, seed=500 + 10 * r + li)
+            if par == "ep-a2a":
+                xf = xf[t0_:t1_].contiguous()
+            xs_r.append(xf)
+        return xs_r
+    xs = make_tokens(tok_seed)
+    x_o = torch.randn((max(M, 1), 4096), generator=gen, device="cuda")
+    out = torch.empty((max(M, 1), D), device="cuda")
+    out2 = torch.empty((max(M, 1), D), device="cuda")
     dense_out = {n: torch.empty((M, co), device="cuda") for n, (_, _, _, co) in dense.items()}
-    # The dense projections do not depend on the MoE layer or on each other in
-    # this workload, so each gets its own context and stream: they run beside
-    # the MoE layer (fork / join with events, captured into the same graph).
     dctx, dstream = {}, {}
     for name in dense:
         dctx[name] = MB.Context(local)
@@ -397,36 +497,56 @@ def main():
         dctx[name].set_gemm_path({"auto": MB.PATH_AUTO, "gemv": MB.PATH_GEMV, "tc": MB.PATH_TC}[args.path])
         dctx[name].set_option(MB.OPT_TC_STREAM, {"general": 0, "stream": 1, "stream-all": 2}[args.tc_kernel])
 
-    # routing per layer (unique experts of this rank -> algorithmic bytes)
-    e_lo, e_hi = EP.expert_range(rank, ws, E) if use_ep else (0, E)
-    epl = EP.ExpertParallelLayer(ctx, E) if use_ep and not native_ep else None
+    # routing of the tokens this rank's experts see, per layer (unique experts
+    # -> algorithmic bytes), on a plain context over the full layer
+    rctx = MB.Context(local)
+    rctx.set_stream(stream.cuda_stream)
     uniq, pairs_l = [], []
     for li in range(args.layers):
-        cnt = np.zeros(M, np.int64)
-        idx = np.zeros((M, K), np.int64)
-        w = np.zeros((M, K), np.float32)
-        ctx.layer_forward(descs[li], M, xs[li], out, MB.F_POST_NORM, cnt, idx, w)
-        uniq.append(len({int(idx[t, k]) for t in range(M) for k in range(cnt[t])
-                         if e_lo <= int(idx[t, k]) < e_hi}))
-        pairs = int(cnt.sum())
-        pairs_l.append(pairs)
+        if par == "ep-gather":
+            xr = torch.cat([make_tokens(r)[li % n_x] for r in range(ws)])
+        elif par == "ep-a2a":
+            xr = synth.make_x(M_total, seed=500 + (li % n_x))
+        else:
+            xr = xs[li % n_x]
+        Mr = xr.shape[0]
+        cnt = np.zeros(Mr, np.int64)
+        idx = np.zeros((Mr, K), np.int64)
+        w = np.zeros((Mr, K), np.float32)
+        tmp = torch.empty((Mr, D), device="cuda")
+        rctx.route(full_descs[li], Mr, xr, cnt, idx, w)
+        act = idx[np.arange(K)[None, :] < cnt[:, None]]
+        uniq.append(int(np.unique(act[(act >= e_lo) & (act < e_hi)]).size))
+        pairs_l.append(int(((act >= e_lo) & (act < e_hi)).sum()))
+        del tmp
+    rctx.close()
+    epl = EP.ExpertParallelLayer(ctx, E) if par == "ep" else None
 
-    def moe_step(li, x, o):
+    def moe_layer(li, x, o):
         if epl is not None:
             epl.forward(descs[li], M, x, o, MB.F_POST_NORM, layers[li]["post_norm_w"])
-        else:
+        elif M > 0:
             ctx.layer_forward(descs[li], M, x, o, MB.F_POST_NORM)
+        else:  # an empty token shard still takes part in the exchange
+            ctx.layer_forward(descs[li], 0, None, None, MB.F_POST_NORM)
 
     def step(i):
-        li = i % args.layers
         main = torch.cuda.current_stream()
         fork = torch.cuda.Event()
         fork.record(main)
-        moe_step(li, xs[li], out)
+        if stack:  # the whole stack: every layer's output is the next layer's input
+            h = xs[0]
+            for li in range(args.layers):
+                o = (out, out2)[li % 2]
+                moe_layer(li, h, o)
+                h = o
+        else:
+            li = i % args.layers
+            moe_layer(li, xs[li], out)
         joins = []
         for name, (p, s, ci, co) in dense.items():
             dstream[name].wait_event(fork)
-            dctx[name].q4_matmul_batchN(M, p, s, x_o if name == "o" else xs[li], dense_out[name], ci, co)
+            dctx[name].q4_matmul_batchN(M, p, s, x_o if name == "o" else xs[i % n_x], dense_out[name], ci, co)
             ev = torch.cuda.Event()
             ev.record(dstream[name])
             joins.append(ev)
@@ -443,28 +563,29 @@ def main():
         step(i)
     torch.cuda.synchronize()
 
-    # One CUDA graph per layer holding a whole step (the library's calls are
-    # asynchronous and allocation-free once warm), replayed step by step.
+    # One CUDA graph per distinct step (the library's calls are asynchronous
+    # and allocation-free once warm), replayed step by step.
+    n_graphs = 1 if stack else args.layers
     graphs, launches_per_step = [], None
     if not args.no_graph:
         cap = torch.cuda.Stream()
         ctx.set_stream(cap.cuda_stream)
         n_cap = all_launches()
-        for li in range(args.layers):
+        for gi in range(n_graphs):
             graphs.append(torch.cuda.CUDAGraph())
             with torch.cuda.graph(graphs[-1], stream=cap):
-                step(li)
-        launches_per_step = (all_launches() - n_cap) / args.layers
+                step(gi)
+        launches_per_step = (all_launches() - n_cap) / n_graphs
         if pg:
-            launches_per_step += 1  # the NCCL all-reduce kernel is not counted by the library
+            launches_per_step += 2 * (args.layers if stack else 1)  # NCCL kernels are not counted by the library
         ctx.set_stream(stream.cuda_stream)
         for i in range(args.warmup):
-            graphs[i % args.layers].replay()
+            graphs[i % n_graphs].replay()
         torch.cuda.synchronize()
 
     def run_step(i):
         if graphs:
-            graphs[i % args.layers].replay()
+            graphs[i % n_graphs].replay()
         else:
             step(i)
 
@@ -488,8 +609,10 @@ def main():
         pg.barrier()
     torch.cuda.synchronize()
     ms_per_step = ms / args.steps
-    # expert parallel: all ranks serve the same M tokens; replicas: M each
-    tokens_per_step = M if use_ep else ws * M
+    # tokens of the whole job per step: expert-parallel forms with replicated
+    # tokens serve M; own-token forms serve M per rank (the all-to-all form's
+    # shards add up to the workload's M)
+    tokens_per_step = {"ep": M_total, "ep-native": M_total, "ep-a2a": M_total}.get(par, ws * M_total)
     value = tokens_per_step * args.steps / (ms / 1e3)
 
     # profiled pass over the same steps: per-kernel device time
@@ -505,38 +628,50 @@ def main():
             prof[k] = (t0 + t_ms, n0_ + n_l)
     for c in [ctx, *dctx.values()]:
         c.profile_enable(False)
+    if pg:
+        pg.barrier()
 
     # End to end through the public API with pinned host buffers: every call
     # stages its host inputs (H2D) and copies its outputs back (D2H) on its
     # context's stream; the calls are asynchronous (moe_set_async), the dense
     # projections run on their own contexts' streams as in the device-timed
-    # step, and the step ends when the main stream has joined them.
+    # step, and the step ends when the main stream has joined them.  A stack
+    # keeps its activations on the device between layers.
     x_h = [x.cpu().pin_memory() for x in xs]
     xo_h = x_o.cpu().pin_memory()
-    out_h = torch.empty((M, D)).pin_memory()
+    out_h = torch.empty((max(M, 1), D)).pin_memory()
     dout_h = {n: torch.empty((M, co)).pin_memory() for n, (_, _, _, co) in dense.items()}
     h2d = M * D * 4 + sum((M * (4096 if n == "o" else D) * 4) for n in dense)
     d2h = M * D * 4 + sum(M * co * 4 for (_, _, _, co) in dense.values())
-
-    x_d = torch.empty((M, D), device="cuda")
+    x_d = torch.empty((max(M, 1), D), device="cuda")
+    h_d = torch.empty((max(M, 1), D), device="cuda")
 
     def step_e2e(i):
-        li = i % args.layers
-        if epl is not None:  # the collective needs device buffers: copy in, reduce, copy out
-            x_d.copy_(x_h[li], non_blocking=True)
-            epl.forward(descs[li], M, x_d, out, MB.F_POST_NORM, layers[li]["post_norm_w"])
-            out_h.copy_(out, non_blocking=True)
-            for name, (p, s, ci, co) in dense.items():
-                ctx.q4_matmul_batchN(M, p, s, xo_h if name == "o" else x_h[li], dout_h[name], ci, co)
-            return
         main = torch.cuda.current_stream()
         fork = torch.cuda.Event()
         fork.record(main)
-        ctx.layer_forward(descs[li], M, x_h[li], out_h, MB.F_POST_NORM)
+        xh = x_h[i % n_x]
+        if epl is not None:  # the torch collective needs device buffers
+            x_d[:M].copy_(xh, non_blocking=True)
+            moe_layer(i % args.layers, x_d[:M], out)
+            out_h[:M].copy_(out[:M], non_blocking=True)
+        elif stack and M > 0:  # host in, 30 layers on the device, host out
+            bufs = (h_d[:M], x_d[:M])
+            ctx.layer_forward(descs[0], M, xh, bufs[0], MB.F_POST_NORM)
+            for li in range(1, args.layers - 1):
+                moe_layer(li, bufs[(li - 1) % 2], bufs[li % 2])
+            ctx.layer_forward(descs[args.layers - 1], M, bufs[(args.layers - 2) % 2], out_h[:M], MB.F_POST_NORM)
+        elif stack:
+            for li in range(args.layers):
+                moe_layer(li, None, None)
+        elif M > 0:
+            ctx.layer_forward(descs[i % args.layers], M, xh, out_h[:M], MB.F_POST_NORM)
+        else:
+            moe_layer(i % args.layers, None, None)
         joins = []
         for name, (p, s, ci, co) in dense.items():
             dstream[name].wait_event(fork)
-            dctx[name].q4_matmul_batchN(M, p, s, xo_h if name == "o" else x_h[li], dout_h[name], ci, co)
+            dctx[name].q4_matmul_batchN(M, p, s, xo_h if name == "o" else xh, dout_h[name], ci, co)
             ev = torch.cuda.Event()
             ev.record(dstream[name])
             joins.append(ev)
@@ -566,18 +701,16 @@ def main():
     hbm, tf_burst, tf_sust, src = peaks()
     pairs_mean = sum(pairs_l) / len(pairs_l)
     u_mean = sum(uniq) / len(uniq)
+    Mx = M_total * ws if par == "ep-gather" else M_total  # tokens a rank's experts see
     # the dominant kernel of the MoE path (the dense projections run on their
     # own streams beside it, and their summed time is not one kernel's)
-    dom = max((kv for kv in prof.items() if kv[0] in ("gemv_gate_up", "gemv_down", "tc_gate_up", "tc_down")),
-              key=lambda kv: kv[1][0])[0] if prof else None
+    cand = [kv for kv in prof.items() if kv[0] in ("gemv_gate_up", "gemv_down", "tc_gate_up", "tc_down")]
+    dom = max(cand, key=lambda kv: kv[1][0])[0] if cand else None
     alg = {
-        "gemv_gate_up": u_mean * GU_BYTES + M * D * 4 + M * K * F * 4,
-        "gemv_down": u_mean * DN_BYTES + M * K * F * 4 + M * K * D * 4,
-        "tc_gate_up": u_mean * GU_BYTES + M * K * D * 2 + M * K * F * 2,
-        "tc_down": u_mean * DN_BYTES + M * K * F * 2 + M * K * D * 4,
-        "q4_matmul": sum(q4_bytes(ci, co) + M * (ci + co) * 4 for (_, _, ci, co) in dense.values()) / max(1, len(dense)),
-        "router": ROUTER_BYTES + M * D * 4 + M * E * 4,
-        "prep": 4 * M * D * 4,
+        "gemv_gate_up": u_mean * GU_BYTES + Mx * D * 4 + pairs_mean * F * 4,
+        "gemv_down": u_mean * DN_BYTES + pairs_mean * F * 4 + pairs_mean * D * 4,
+        "tc_gate_up": u_mean * GU_BYTES + pairs_mean * D * 2 + pairs_mean * F * 2,
+        "tc_down": u_mean * DN_BYTES + pairs_mean * F * 2 + pairs_mean * D * 4,
     }
     roof = None
     if wl.get("skew") and dom in ("tc_gate_up", "tc_down") and prof[dom][1] > 0:
@@ -593,18 +726,19 @@ def main():
         achieved = alg[dom] / (avg_ms / 1e3) / 1e9
         traffic = None
         tp = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tp):
+        if os.path.exists(tp) and ws == 1:
             with open(tp) as f:
                 traffic = json.load(f).get(args.workload, {}).get(dom)
         roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "traffic": traffic,
                 "alg_bytes_per_launch": alg[dom], "avg_launch_ms": avg_ms,
                 "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({'of measured' if src == 'measured' else 'of fallback'})"}
-    step_bytes = u_mean * (GU_BYTES + DN_BYTES) + ROUTER_BYTES + 2 * M * D * 4 + \
+    n_lay = args.layers if stack else 1
+    step_bytes = n_lay * (u_mean * (GU_BYTES + DN_BYTES) + ROUTER_BYTES + 2 * M * D * 4) + \
         sum(q4_bytes(ci, co) for (_, _, ci, co) in dense.values())
     step_roof = {"alg_bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (ms_per_step / 1e3) / 1e9,
                  "frac_of_hbm": step_bytes / (ms_per_step / 1e3) / 1e9 / hbm,
-                 "unique_experts_per_step": u_mean, "pairs_per_step": pairs,
+                 "unique_experts_per_layer": u_mean, "pairs_per_layer": pairs_mean, "layers_per_step": n_lay,
                  "kernel_ms_per_step": {k: v[0] / args.steps for k, v in prof.items()}}
 
     cpu = None
@@ -612,24 +746,26 @@ def main():
         host = synth.to_host(layers[0])
         hd = {n: (p.cpu().numpy(), s.cpu().numpy(), ci, co) for n, (p, s, ci, co) in dense.items()}
         nth = os.cpu_count() or 1
-        v, n, dt = cpu_time(host, hd, M, args.cpu_budget_s, 200, nth)
-        cpu = {"value": v, "unit": "tokens/s", "cores": nth, "kind": "port",
-               "sample": f"{n} full steps of {M} tokens (layer 0{', + dense q/k/v/o' if hd else ''}) in {dt:.1f} s"}
+        m_cpu = min(M_total, 512)
+        v, n, dt = cpu_time(host, hd, m_cpu, args.cpu_budget_s, 200, nth)
+        v = v / n_lay
+        tag = f"{n} steps of {m_cpu}{' of ' + str(M_total) if m_cpu < M_total else ''} tokens through layer 0"
+        tag += ", + dense q/k/v/o" if hd else ""
+        tag += f" in {dt:.1f} s" + (f"; rate divided by {n_lay} for the {n_lay}-layer step" if n_lay > 1 else "")
+        cpu = {"value": v, "unit": "tokens/s", "cores": nth, "kind": "port", "sample": tag}
 
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "strong" if use_ep else "weak", "vs_baseline": None, "dtype": dtype_desc(args, M),
-            "data": "synthetic",
-            "config": dict(workload_config(args, M), **({"skew": skew} if skew else {})),
-            "roofline": roof, "step_roofline": step_roof,
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-            "gpu_launches": launches, "clocks": clk.summary(),
-        }
-        print(json.dumps(line), flush=True)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong" if par in ("ep", "ep-native", "ep-a2a") else "weak", "vs_baseline": None,
+        "dtype": dtype_desc(args, M_total), "data": "synthetic",
+        "config": dict(workload_config(args, M_total, par, ws), **({"skew": skew} if skew else {})),
+        "roofline": roof, "step_roofline": step_roof,
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+        "gpu_launches": launches, "clocks": clk.summary(),
+    }
     # graphs that hold NCCL calls must be gone before the process group is
     graphs.clear()
     import gc
@@ -637,12 +773,13 @@ def main():
     torch.cuda.synchronize()
     for c in dctx.values():
         c.close()
+    if lib_ep:
+        ctx.ep_finalize()
     ctx.close()
-    if pg:
-        pg.barrier()
-        torch.cuda.synchronize()
-        pg.destroy_process_group()
-    return 0
+    del layers, descs, full_descs, xs
+    gc.collect()
+    torch.cuda.empty_cache()
+    return line
 
 
 if __name__ == "__main__":

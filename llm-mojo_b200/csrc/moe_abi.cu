@@ -82,7 +82,7 @@ struct moe_ctx {
     int tc_stream = 1;                   // MOE_OPT_TC_STREAM
     int64_t expert_begin = 0;            // MOE_OPT_EXPERT_BEGIN
     int64_t expert_end = 0;              // MOE_OPT_EXPERT_END (0: all experts)
-    bool fused_route = false;            // MOE_OPT_FUSED_ROUTE
+    int fused_route = 0;                 // MOE_OPT_FUSED_ROUTE
     int dense_ksplit = 0;                // MOE_OPT_DENSE_KSPLIT (0: automatic)
     uint64_t device_timeout_ns = 4000000000ull;
     // profiling (moe_profile_enable)
@@ -833,7 +833,8 @@ int moe_set_option(moe_ctx* ctx, int option, int64_t value) {
             ctx->ep_timeout_ns = (uint64_t)value;
             return MOE_OK;
         case MOE_OPT_FUSED_ROUTE:
-            ctx->fused_route = value != 0;
+            if (value < 0 || value > 2) return fail(ctx, MOE_E_ARG, "bad fused-routing mode");
+            ctx->fused_route = (int)value;
             return MOE_OK;
         case MOE_OPT_DENSE_KSPLIT:
             if (value < 0 || value > 64) return fail(ctx, MOE_E_ARG, "MOE_OPT_DENSE_KSPLIT is 0..64");
@@ -2152,10 +2153,69 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
     ExpertBufs bb;
     TRY(take_expert_bufs(ctx, M, K, d, F, E, &bb));
     int C = 0;
-    const bool fused = ctx->fused_route && ld.rp && !(flags & MOE_F_SET_COVER) &&
-                       M < ctx->router_tc_min_tokens && al16(xd) &&
-                       moe::route_fused_supported((int)M, (int)E, (int)K, (int)d, &C);
-    if (fused) {
+    const bool coop = ctx->fused_route == 2 && ld.rp && !(flags & MOE_F_SET_COVER) &&
+                      M < ctx->router_tc_min_tokens && al16(xd) &&
+                      moe::route_coop_supported((int)M, (int)E, (int)d, ctx->num_sms);
+    const bool fused = coop || (ctx->fused_route == 1 && ld.rp && !(flags & MOE_F_SET_COVER) &&
+                                M < ctx->router_tc_min_tokens && al16(xd) &&
+                                moe::route_fused_supported((int)M, (int)E, (int)K, (int)d, &C));
+    if (coop) {
+        // the whole routing chain in one cooperative grid launch
+        const bool tc_path = use_tc(ctx, M, d, F, ld.w);
+        const int nsl = (int)(d / 128);
+        int* ti32 = (int*)ws_take(ctx, P * 4);
+        float* tv = (float*)ws_take(ctx, P * 4);
+        float* scaled = (float*)ws_take(ctx, M * d * 4);
+        float* part = (float*)ws_take(ctx, (size_t)nsl * M * E * 4);
+        unsigned* bar = (unsigned*)ws_take(ctx, 4);
+        if (!bar) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+        moe::RouteCoopArgs ra;
+        ra.pa.x = xd;
+        ra.pa.K = d;
+        ra.pa.norm = 1;
+        ra.pa.pre_w = ld.pre_w;
+        ra.pa.router_scale = ld.router_scale;
+        ra.pa.rsf = L->r_scale_factor;
+        ra.pa.out = bb.x32;
+        ra.pa.out_sum = bb.xsum;
+        ra.pa.out_q = tc_path ? nullptr : bb.x32q;
+        ra.pa.scaled = scaled;
+        ra.rp = ld.rp;
+        ra.rs = ld.rs;
+        ra.ta.part = part;
+        ra.ta.part_out = part;
+        ra.ta.part_n = nsl;
+        ra.ta.M = (int)M;
+        ra.ta.bias = ld.bias;
+        ra.ta.E = (int)E;
+        ra.ta.K = (int)K;
+        ra.ta.pes = ld.pes;
+        ra.ta.top_p = L->moe_top_p;
+        ra.ta.lod = 1;
+        ra.ta.ti32 = ti32;
+        ra.ta.tv = tv;
+        ra.ta.slot_expert = bb.slot_expert;
+        ra.ta.slot_weight = bb.slot_weight;
+        ra.ta.tok_count = (int64_t*)dtc;
+        ra.ta.tok_idx = (int64_t*)dti;
+        ra.ta.tok_w = (float*)dtw;
+        ra.b = bb.b;
+        expert_range(ctx, E, &ra.e_lo, &ra.e_hi);
+        ra.BN = tc_path ? expert_token_tile(P, E) : 0;
+        ra.tt_prefix = tc_path ? bb.tt_prefix : nullptr;
+        ra.x16 = tc_path ? bb.x16 : nullptr;
+        ra.bar = bar;
+        ra.err_flag = ctx->err_flag;
+        ra.timeout_ns = ctx->device_timeout_ns;
+        int r;
+        {
+            ProfScope ps(ctx, "route_coop");
+            r = moe::launch_route_coop(ra, ctx->num_sms, ctx->stream);
+        }
+        if (r < 0) return fail(ctx, MOE_E_CUDA, "cooperative routing launch failed");
+        ctx->launches += r;
+        bb.x32q_ready = !tc_path;
+    } else if (fused) {
         const bool tc_path = use_tc(ctx, M, d, F, ld.w);
         moe::RouteFusedArgs ra;
         ra.x = (const float*)xd;

@@ -385,16 +385,17 @@ int launch_gemv_wide(const uint8_t* W, const float* S, const float* X, float* ou
 // of a warp read the same activations (broadcast).  part[c][t][e] is summed
 // over c, in c order, by k_topk.
 constexpr int RS = 128;  // K slice per CTA (4 Q4 blocks)
-__global__ void __launch_bounds__(512) k_router_part(const uint8_t* __restrict__ W, const float* __restrict__ S,
-                                                     const float* __restrict__ X, int M, int K, int E,
-                                                     float* __restrict__ part) {
-    pdl_wait();
-    pdl_trigger();
-    __shared__ __align__(16) float xs[16][RS];
-    const int c = blockIdx.x, k0 = c * RS, tid = threadIdx.x;
+// J: tokens per thread group (4 groups of 128 threads): M <= 4 * J.  `xs`
+// holds RS floats per token in shared memory.
+template <int J>
+__device__ __forceinline__ void router_slice(const uint8_t* __restrict__ W, const float* __restrict__ S,
+                                             const float* __restrict__ X, int M, int K, int E,
+                                             float* __restrict__ part, int c, float* xs) {
+    const int k0 = c * RS, tid = threadIdx.x;
     for (int i = tid; i < M * RS / 4; i += blockDim.x) {
         const int t = (i * 4) / RS, k = (i * 4) % RS;
-        reinterpret_cast<float4*>(&xs[t][0])[k / 4] = __ldg(reinterpret_cast<const float4*>(X + (int64_t)t * K + k0 + k));
+        reinterpret_cast<float4*>(xs + t * RS)[k / 4] =
+            __ldg(reinterpret_cast<const float4*>(X + (int64_t)t * K + k0 + k));
     }
     __syncthreads();
     const int tg = tid >> 7, TG = blockDim.x >> 7;
@@ -408,7 +409,9 @@ __global__ void __launch_bounds__(512) k_router_part(const uint8_t* __restrict__
             q[b] = ldg_stream(W + (int64_t)e * (K / 2) + k0 / 2 + b * 16);
             sc[b] = ldg_stream_f(S + (int64_t)e * (K / 32) + k0 / 32 + b);
         }
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float acc[J];
+#pragma unroll
+        for (int j = 0; j < J; ++j) acc[j] = 0.f;
 #pragma unroll
         for (int b = 0; b < RS / 32; ++b) {
             const uint32_t w4[4] = {q[b].x, q[b].y, q[b].z, q[b].w};
@@ -419,10 +422,10 @@ __global__ void __launch_bounds__(512) k_router_part(const uint8_t* __restrict__
                 for (int n = 0; n < 8; ++n)  // element 8w+n: nibble n of word w
                     wv[8 * w + n] = (float)((int)((w4[w] >> (4 * n)) & 15u) - 8);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < J; ++j) {
                 const int t = tg + TG * j;
                 if (t < M) {
-                    const float4* xp = reinterpret_cast<const float4*>(&xs[t][b * 32]);
+                    const float4* xp = reinterpret_cast<const float4*>(xs + t * RS + b * 32);
                     float d = 0.f;
 #pragma unroll
                     for (int v = 0; v < 8; ++v) {
@@ -437,11 +440,20 @@ __global__ void __launch_bounds__(512) k_router_part(const uint8_t* __restrict__
             }
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < J; ++j) {
             const int t = tg + TG * j;
             if (t < M) part[((int64_t)c * M + t) * E + e] = acc[j];
         }
     }
+}
+
+__global__ void __launch_bounds__(512) k_router_part(const uint8_t* __restrict__ W, const float* __restrict__ S,
+                                                     const float* __restrict__ X, int M, int K, int E,
+                                                     float* __restrict__ part) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ __align__(16) float xs[16 * RS];
+    router_slice<4>(W, S, X, M, K, E, part, blockIdx.x, xs);
 }
 
 bool router_part_supported(int M, int K) { return M >= 1 && M <= 16 && K % RS == 0; }
@@ -457,13 +469,9 @@ int launch_router_part(const uint8_t* W, const float* S, const float* X, int M, 
 // rms norms (model_speculative_moe_batched.mojo:857-879): out = x * inv *
 // pre_w and scaled = x * inv * router_scale * r_scale_factor; and the
 // per-32-block sums (x1.5) the XS GEMV needs.
-__global__ void __launch_bounds__(512) k_prep(PrepArgs a) {
-    pdl_wait();
-    pdl_trigger();
-    extern __shared__ float4 smem4[];
-    float* xs = reinterpret_cast<float*>(smem4);
-    __shared__ float red[33];
-    const int64_t K = a.K, t = blockIdx.x;
+// Row t of the prep; `xs` holds K floats of shared memory, `red` 33.
+__device__ __forceinline__ void prep_row(const PrepArgs& a, int64_t t, float* xs, float* red) {
+    const int64_t K = a.K;
     float ss = 0.f;
     if (a.x_layout == 0 && !a.x_f16 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0) {
         // natural fp32 rows: float4 loads, several in flight per thread
@@ -510,6 +518,14 @@ __global__ void __launch_bounds__(512) k_prep(PrepArgs a) {
     }
 }
 
+__global__ void __launch_bounds__(512) k_prep(PrepArgs a) {
+    pdl_wait();
+    pdl_trigger();
+    extern __shared__ float4 smem4[];
+    __shared__ float red[33];
+    prep_row(a, blockIdx.x, reinterpret_cast<float*>(smem4), red);
+}
+
 int launch_prep(const PrepArgs& a, int64_t M, cudaStream_t s) {
     if (M <= 0) return 0;
     const size_t smem = (size_t)a.K * sizeof(float);
@@ -523,16 +539,10 @@ int launch_prep(const PrepArgs& a, int64_t M, cudaStream_t s) {
 // batched.mojo:921-933), top-k with insertion semantics (:936-953; equal
 // values keep the lower index first) and, when a.lod,
 // compute_moe_lod_weights (moe_kernels.mojo:445-490).
-__global__ void __launch_bounds__(128) k_topk(TopkArgs a) {
-    pdl_wait();
-    pdl_trigger();
-    extern __shared__ float4 smem4[];
-    float* pr = reinterpret_cast<float*>(smem4);  // [E]
-    __shared__ float red[33];
-    __shared__ float tval[32];
-    __shared__ int tidx[32];
+// Token t: `pr` holds E floats of shared memory, `red` 33, tval / tidx 32.
+__device__ __forceinline__ void topk_row(const TopkArgs& a, int64_t t, float* pr, float* red, float* tval,
+                                         int* tidx) {
     const int E = a.E, K = a.K;
-    const int64_t t = blockIdx.x;
     float m = -INFINITY;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         float sc;
@@ -637,6 +647,16 @@ __global__ void __launch_bounds__(128) k_topk(TopkArgs a) {
         if (a.tok_w) a.tok_w[t * K + k] = on ? ow[k] : 0.f;
     }
     if (a.tok_count) a.tok_count[t] = cnt;
+}
+
+__global__ void __launch_bounds__(128) k_topk(TopkArgs a) {
+    pdl_wait();
+    pdl_trigger();
+    extern __shared__ float4 smem4[];
+    __shared__ float red[33];
+    __shared__ float tval[32];
+    __shared__ int tidx[32];
+    topk_row(a, blockIdx.x, reinterpret_cast<float*>(smem4), red, tval, tidx);
 }
 
 int launch_topk(const TopkArgs& a, int64_t M, cudaStream_t s) {
@@ -893,13 +913,11 @@ __device__ __forceinline__ int block_excl_scan(int v, int* wsum, int* total) {
 // parallelism: this rank holds only those experts); their slots get no pair.
 // With tt_prefix, also the exclusive prefix of token tiles of BN tokens per
 // unique expert (the tensor-core work list), one launch fewer.
-__global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo,
-                                                 int e_hi, BucketOut o, int BN, int* tt_prefix) {
-    pdl_wait();
-    pdl_trigger();
-    __shared__ int cnt[1024];
-    __shared__ int cur[1024];
-    __shared__ int wsum[32];
+// The bucketing by one CTA of at least E threads; cnt / cur hold blockDim
+// ints of shared memory, wsum 32.
+__device__ __forceinline__ void bucket_block(const int* slot_expert, int64_t P, int K, int E, int e_lo, int e_hi,
+                                             const BucketOut& o, int BN, int* tt_prefix, int* cnt, int* cur,
+                                             int* wsum) {
     const int tid = threadIdx.x;
     cnt[tid] = 0;
     __syncthreads();
@@ -940,6 +958,16 @@ __global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t
             o.slot_pair[p] = -1;
         }
     }
+}
+
+__global__ void __launch_bounds__(1024) k_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo,
+                                                 int e_hi, BucketOut o, int BN, int* tt_prefix) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ int cnt[1024];
+    __shared__ int cur[1024];
+    __shared__ int wsum[32];
+    bucket_block(slot_expert, P, K, E, e_lo, e_hi, o, BN, tt_prefix, cnt, cur, wsum);
 }
 
 int launch_bucket(const int* slot_expert, int64_t P, int K, int E, int e_lo, int e_hi, const BucketOut& o,
@@ -1354,6 +1382,144 @@ int launch_ep_slots(const int* local_e, int64_t P, int E, int* slot_expert, floa
     const int grid = (int)std::min<int64_t>((P + 255) / 256, 1184);
     launch_k(k_ep_slots, dim3(grid), dim3(256), 0, s, local_e, P, E, slot_expert, slot_weight, err_flag);
     return 1;
+}
+
+}  // namespace moe
+
+namespace moe {
+
+// ------------------------------------------- routing chain as one grid launch
+// The routing chain of a decode batch (k_prep -> k_router_part -> k_topk ->
+// k_bucket -> fp16 gather) as one cooperative launch of G CTAs: the phases
+// run the very device functions of the separate kernels, separated by grid
+// barriers (a counter the host zeroes before the launch; every CTA adds one
+// per barrier and waits, with a globaltimer deadline, for G * (phase + 1)).
+// A CTA that gives up at a barrier raises the error word and leaves; the
+// others then give up at the next barrier.  Nothing is launched between the
+// phases, so the chain pays one launch instead of five.
+namespace {
+
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool grid_barrier(unsigned* bar, unsigned target, uint64_t deadline, int* err,
+                                             int* ok_s) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(bar, 1u);
+        int ok = 1;
+        for (uint32_t it = 0;; ++it) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+            if (v >= target) break;
+            if ((it & 31u) == 31u && gtimer() > deadline) {
+                atomicExch(err, 2);
+                ok = 0;
+                break;
+            }
+            __nanosleep(32);
+        }
+        __threadfence();
+        *ok_s = ok;
+    }
+    __syncthreads();
+    return *ok_s != 0;
+}
+
+template <int J>
+__global__ void __launch_bounds__(512, 1) k_route_coop(RouteCoopArgs a) {
+    extern __shared__ float4 sm4[];
+    float* sm = reinterpret_cast<float*>(sm4);
+    __shared__ float red[33];
+    __shared__ float tval[32];
+    __shared__ int tidx[32];
+    __shared__ int wsum[32];
+    __shared__ int ok_s;
+    const unsigned G = gridDim.x;
+    const uint64_t deadline = gtimer() + a.timeout_ns;
+    const int M = a.ta.M, d = (int)a.pa.K;
+    // 1. norms: router input and expert input per token
+    for (int t = blockIdx.x; t < M; t += G) {
+        prep_row(a.pa, t, sm, red);
+        __syncthreads();
+    }
+    if (!grid_barrier(a.bar, G, deadline, a.err_flag, &ok_s)) return;
+    // 2. router partial sums per 128-wide K slice
+    for (int c = blockIdx.x; c < d / RS; c += G) {
+        router_slice<J>(a.rp, a.rs, a.pa.scaled, M, d, a.ta.E, a.ta.part_out, c, sm);
+        __syncthreads();
+    }
+    if (!grid_barrier(a.bar, 2 * G, deadline, a.err_flag, &ok_s)) return;
+    // 3. softmax, top-k, LOD weights per token
+    for (int t = blockIdx.x; t < M; t += G) {
+        topk_row(a.ta, t, sm, red, tval, tidx);
+        __syncthreads();
+    }
+    if (!grid_barrier(a.bar, 3 * G, deadline, a.err_flag, &ok_s)) return;
+    // 4. bucketing of the (token, slot) pairs (one CTA)
+    if (blockIdx.x == 0) {
+        int* cnt = reinterpret_cast<int*>(sm);
+        bucket_block(a.ta.slot_expert, (int64_t)M * a.ta.K, a.ta.K, a.ta.E, a.e_lo, a.e_hi, a.b, a.BN,
+                     a.tt_prefix, cnt, cnt + blockDim.x, wsum);
+    }
+    if (!a.x16) return;
+    if (!grid_barrier(a.bar, 4 * G, deadline, a.err_flag, &ok_s)) return;
+    // 5. fp16 rows of the pairs in bucket order, every 8-group of K in
+    //    [0,4,1,5,2,6,3,7] order (the tensor-core kernels' operand order)
+    const int P = a.b.meta[1];
+    for (int p = blockIdx.x; p < P; p += G) {
+        const float4* x4 = reinterpret_cast<const float4*>(a.pa.out + (int64_t)a.b.pair_token[p] * d);
+        uint4* o = reinterpret_cast<uint4*>(a.x16 + (int64_t)p * d);
+        for (int g = threadIdx.x; g < d / 8; g += blockDim.x) {
+            const float4 u = __ldg(x4 + 2 * g), v = __ldg(x4 + 2 * g + 1);
+            const __half2 h0 = __floats2half2_rn(u.x, v.x);
+            const __half2 h1 = __floats2half2_rn(u.y, v.y);
+            const __half2 h2 = __floats2half2_rn(u.z, v.z);
+            const __half2 h3 = __floats2half2_rn(u.w, v.w);
+            o[g] = make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                              *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+        }
+    }
+}
+
+}  // namespace
+
+bool route_coop_supported(int M, int E, int d, int num_sms) {
+    return M >= 1 && M <= 64 && E >= 1 && E <= 512 && d % RS == 0 && d <= 12288 && d / RS <= 4 * num_sms;
+}
+
+int launch_route_coop(const RouteCoopArgs& a, int num_sms, cudaStream_t s) {
+    const int M = a.ta.M, d = (int)a.pa.K, E = a.ta.E;
+    if (!route_coop_supported(M, E, d, num_sms)) return -1;
+    int G = std::max(d / RS, M);
+    G = std::max(G, 32);
+    G = std::min(G, num_sms);
+    const size_t smem = std::max<size_t>(std::max<size_t>((size_t)d * 4, (size_t)M * RS * 4),
+                                         std::max<size_t>((size_t)E * 4, 2 * 512 * 4));
+    if (cudaMemsetAsync(a.bar, 0, sizeof(unsigned), s) != cudaSuccess) return -1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(512);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    if (M <= 16) {
+        if (smem > 48 * 1024) cudaFuncSetAttribute(k_route_coop<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        e = cudaLaunchKernelEx(&cfg, k_route_coop<4>, a);
+    } else {
+        if (smem > 48 * 1024) cudaFuncSetAttribute(k_route_coop<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        e = cudaLaunchKernelEx(&cfg, k_route_coop<16>, a);
+    }
+    return e == cudaSuccess ? 1 : -1;
 }
 
 }  // namespace moe
