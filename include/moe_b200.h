@@ -106,8 +106,10 @@ enum moe_option {
     MOE_OPT_FUSED_ROUTE = 10,      /* moe_layer_forward's routing of small batches (Q4_0 router, LOD
                                       routing): 0 the separate norm / router / top-k / bucket /
                                       gather kernels; 1 one thread-block cluster (<= 16 tokens);
-                                      2 one cooperative grid launch running the separate kernels'
-                                      code between grid barriers (<= 64 tokens, <= 512 experts) */
+                                      2 one launch for the norms, the router, top-k / LOD and the
+                                      buckets (its last CTA routes every token), then the fp16
+                                      gather; routing bit-identical to 0 (<= 64 tokens, <= 512
+                                      experts) */
     MOE_OPT_DENSE_KSPLIT = 11,     /* dense tensor-core GEMMs: split K into this many partial sums
                                       (0, the default: enough work items for two per SM) */
     MOE_OPT_EP_TIMEOUT_NS = 12,    /* deadline of every host wait on the expert-parallel

@@ -70,6 +70,7 @@ struct moe_ctx {
     size_t ws_off = 0;
     size_t ws_res = 0;
     int* err_flag = nullptr;
+    unsigned* route_ticket = nullptr;    // the one-launch routing's last-CTA ticket (zero between launches)
     uint64_t launches = 0;
     int num_sms = 148;
     std::vector<CopyBack> pending;
@@ -684,7 +685,9 @@ int moe_ctx_create(int device, moe_ctx** out) {
         cudaStreamCreateWithFlags(&ctx->stream, cudaStreamDefault) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->done, cudaEventDisableTiming) != cudaSuccess ||
         cudaMalloc(&ctx->err_flag, sizeof(int)) != cudaSuccess ||
-        cudaMemset(ctx->err_flag, 0, sizeof(int)) != cudaSuccess) {
+        cudaMemset(ctx->err_flag, 0, sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&ctx->route_ticket, sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(ctx->route_ticket, 0, sizeof(unsigned)) != cudaSuccess) {
         cudaGetLastError();
         delete ctx;
         return MOE_E_CUDA;
@@ -720,6 +723,7 @@ int moe_ctx_destroy(moe_ctx* ctx) {
     if (ctx->ep_ws) cudaFree(ctx->ep_ws);
     if (ctx->ep_host_cnt) cudaFreeHost(ctx->ep_host_cnt);
     if (ctx->err_flag) cudaFree(ctx->err_flag);
+    if (ctx->route_ticket) cudaFree(ctx->route_ticket);
     if (ctx->done) cudaEventDestroy(ctx->done);
     for (auto& r : ctx->prof_pending) {
         cudaEventDestroy(r.a);
@@ -2153,23 +2157,20 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
     ExpertBufs bb;
     TRY(take_expert_bufs(ctx, M, K, d, F, E, &bb));
     int C = 0;
-    const bool coop = ctx->fused_route == 2 && ld.rp && !(flags & MOE_F_SET_COVER) &&
-                      M < ctx->router_tc_min_tokens && al16(xd) &&
-                      moe::route_coop_supported((int)M, (int)E, (int)d, ctx->num_sms);
-    const bool fused = coop || (ctx->fused_route == 1 && ld.rp && !(flags & MOE_F_SET_COVER) &&
-                                M < ctx->router_tc_min_tokens && al16(xd) &&
-                                moe::route_fused_supported((int)M, (int)E, (int)K, (int)d, &C));
-    if (coop) {
-        // the whole routing chain in one cooperative grid launch
+    const bool rt = ctx->fused_route == 2 && ld.rp && !(flags & MOE_F_SET_COVER) &&
+                    M < ctx->router_tc_min_tokens && al16(xd) && moe::route_rt_supported((int)M, (int)E, (int)K, (int)d);
+    const bool fused = rt || (ctx->fused_route == 1 && ld.rp && !(flags & MOE_F_SET_COVER) &&
+                              M < ctx->router_tc_min_tokens && al16(xd) &&
+                              moe::route_fused_supported((int)M, (int)E, (int)K, (int)d, &C));
+    if (rt) {
+        // norms, router, top-k / LOD and buckets in one launch, then the gather
         const bool tc_path = use_tc(ctx, M, d, F, ld.w);
         const int nsl = (int)(d / 128);
         int* ti32 = (int*)ws_take(ctx, P * 4);
         float* tv = (float*)ws_take(ctx, P * 4);
-        float* scaled = (float*)ws_take(ctx, M * d * 4);
         float* part = (float*)ws_take(ctx, (size_t)nsl * M * E * 4);
-        unsigned* bar = (unsigned*)ws_take(ctx, 4);
-        if (!bar) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
-        moe::RouteCoopArgs ra;
+        if (!part) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
+        moe::RouteRtArgs ra;
         ra.pa.x = xd;
         ra.pa.K = d;
         ra.pa.norm = 1;
@@ -2179,7 +2180,6 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
         ra.pa.out = bb.x32;
         ra.pa.out_sum = bb.xsum;
         ra.pa.out_q = tc_path ? nullptr : bb.x32q;
-        ra.pa.scaled = scaled;
         ra.rp = ld.rp;
         ra.rs = ld.rs;
         ra.ta.part = part;
@@ -2203,17 +2203,18 @@ int moe_layer_forward(moe_ctx* ctx, const moe_layer_desc* L, int64_t M, const fl
         expert_range(ctx, E, &ra.e_lo, &ra.e_hi);
         ra.BN = tc_path ? expert_token_tile(P, E) : 0;
         ra.tt_prefix = tc_path ? bb.tt_prefix : nullptr;
-        ra.x16 = tc_path ? bb.x16 : nullptr;
-        ra.bar = bar;
-        ra.err_flag = ctx->err_flag;
-        ra.timeout_ns = ctx->device_timeout_ns;
+        ra.ticket = ctx->route_ticket;
         int r;
         {
-            ProfScope ps(ctx, "route_coop");
-            r = moe::launch_route_coop(ra, ctx->num_sms, ctx->stream);
+            ProfScope ps(ctx, "route");
+            r = moe::launch_route_rt(ra, ctx->stream);
         }
-        if (r < 0) return fail(ctx, MOE_E_CUDA, "cooperative routing launch failed");
+        if (r < 0) return fail(ctx, MOE_E_CUDA, "routing launch failed");
         ctx->launches += r;
+        if (tc_path) {
+            ProfScope ps(ctx, "gather");
+            ctx->launches += moe::launch_gather_f16(bb.x32, d, bb.b.pair_token, bb.b.meta, P, 0, bb.x16, ctx->stream);
+        }
         bb.x32q_ready = !tc_path;
     } else if (fused) {
         const bool tc_path = use_tc(ctx, M, d, F, ld.w);

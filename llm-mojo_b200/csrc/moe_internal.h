@@ -207,25 +207,23 @@ struct RouteFusedArgs {
 };
 bool route_fused_supported(int M, int E, int K, int d, int* C_out);
 
-// The routing chain (prep, router partial sums, top-k + LOD, bucketing and
-// the fp16 gather) as one cooperative grid launch (moe_kernels.cu).
-struct RouteCoopArgs {
-    PrepArgs pa;                 // norms of the M rows (scaled, out, out_sum, out_q)
+// The routing of a small batch in one launch (moe_kernels.cu): the norms,
+// the K-slice router partial sums, and, in the router CTA that finishes
+// last, softmax / top-k / LOD for every token and the bucketing.  The fp16
+// gather of the pair rows is left to launch_gather_f16.
+struct RouteRtArgs {
+    PrepArgs pa;                 // norms of the M rows: x, K, pre_w, router_scale, rsf, out, out_sum, out_q
     const uint8_t* rp = nullptr; // Q4_0 router
     const float* rs = nullptr;
-    TopkArgs ta;                 // part = part_out (the router partial sums), part_n = d / 128
+    TopkArgs ta;                 // part = part_out (router partial sums), part_n = d / 128
     BucketOut b;
     int e_lo = 0, e_hi = 0;      // local expert range of the buckets
     int BN = 0;                  // token tile of the tensor-core prefix (0: none)
     int* tt_prefix = nullptr;
-    __half* x16 = nullptr;       // fp16 pair rows (nullptr: not gathered)
-    unsigned* bar = nullptr;     // grid barrier counter (zeroed by the launcher)
-    int* err_flag = nullptr;
-    uint64_t timeout_ns = 0;
+    unsigned* ticket = nullptr;  // zero between launches (the last CTA resets it)
 };
-bool route_coop_supported(int M, int E, int d, int num_sms);
-// Returns 1 (kernels launched) or -1 (unsupported shape or launch failure).
-int launch_route_coop(const RouteCoopArgs& a, int num_sms, cudaStream_t s);
+bool route_rt_supported(int M, int E, int K, int d);
+int launch_route_rt(const RouteRtArgs& a, cudaStream_t s);
 int launch_route_fused(const RouteFusedArgs& a, cudaStream_t s);
 
 // Router logits of <= 16 tokens as per-K-slice partial sums (moe_kernels.cu).

@@ -388,16 +388,9 @@ constexpr int RS = 128;  // K slice per CTA (4 Q4 blocks)
 // J: tokens per thread group (4 groups of 128 threads): M <= 4 * J.  `xs`
 // holds RS floats per token in shared memory.
 template <int J>
-__device__ __forceinline__ void router_slice(const uint8_t* __restrict__ W, const float* __restrict__ S,
-                                             const float* __restrict__ X, int M, int K, int E,
-                                             float* __restrict__ part, int c, float* xs) {
+__device__ __forceinline__ void router_slice_dot(const uint8_t* __restrict__ W, const float* __restrict__ S, int M,
+                                                 int K, int E, float* __restrict__ part, int c, const float* xs) {
     const int k0 = c * RS, tid = threadIdx.x;
-    for (int i = tid; i < M * RS / 4; i += blockDim.x) {
-        const int t = (i * 4) / RS, k = (i * 4) % RS;
-        reinterpret_cast<float4*>(xs + t * RS)[k / 4] =
-            __ldg(reinterpret_cast<const float4*>(X + (int64_t)t * K + k0 + k));
-    }
-    __syncthreads();
     const int tg = tid >> 7, TG = blockDim.x >> 7;
     for (int e0 = 0; e0 < E; e0 += 128) {
         const int e = e0 + (tid & 127);
@@ -447,6 +440,20 @@ __device__ __forceinline__ void router_slice(const uint8_t* __restrict__ W, cons
     }
 }
 
+template <int J>
+__device__ __forceinline__ void router_slice(const uint8_t* __restrict__ W, const float* __restrict__ S,
+                                             const float* __restrict__ X, int M, int K, int E,
+                                             float* __restrict__ part, int c, float* xs) {
+    const int k0 = c * RS, tid = threadIdx.x;
+    for (int i = tid; i < M * RS / 4; i += blockDim.x) {
+        const int t = (i * 4) / RS, k = (i * 4) % RS;
+        reinterpret_cast<float4*>(xs + t * RS)[k / 4] =
+            __ldg(reinterpret_cast<const float4*>(X + (int64_t)t * K + k0 + k));
+    }
+    __syncthreads();
+    router_slice_dot<J>(W, S, M, K, E, part, c, xs);
+}
+
 __global__ void __launch_bounds__(512) k_router_part(const uint8_t* __restrict__ W, const float* __restrict__ S,
                                                      const float* __restrict__ X, int M, int K, int E,
                                                      float* __restrict__ part) {
@@ -469,6 +476,12 @@ int launch_router_part(const uint8_t* W, const float* S, const float* X, int M, 
 // rms norms (model_speculative_moe_batched.mojo:857-879): out = x * inv *
 // pre_w and scaled = x * inv * router_scale * r_scale_factor; and the
 // per-32-block sums (x1.5) the XS GEMV needs.
+// One step of a thread's sum of squares over float4 elements (shared by
+// every kernel that forms the rms of a row, so that they agree bit for bit).
+__device__ __forceinline__ float ss_step(float ss, const float4 v) {
+    return ss + (v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+}
+
 // Row t of the prep; `xs` holds K floats of shared memory, `red` 33.
 __device__ __forceinline__ void prep_row(const PrepArgs& a, int64_t t, float* xs, float* red) {
     const int64_t K = a.K;
@@ -480,7 +493,7 @@ __device__ __forceinline__ void prep_row(const PrepArgs& a, int64_t t, float* xs
         for (int64_t j = threadIdx.x; j < K / 4; j += blockDim.x) {
             const float4 v = __ldg(x4 + j);
             reinterpret_cast<float4*>(xs)[j] = v;
-            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            ss = ss_step(ss, v);
         }
     } else {
 #pragma unroll 4
@@ -539,6 +552,8 @@ int launch_prep(const PrepArgs& a, int64_t M, cudaStream_t s) {
 // batched.mojo:921-933), top-k with insertion semantics (:936-953; equal
 // values keep the lower index first) and, when a.lod,
 // compute_moe_lod_weights (moe_kernels.mojo:445-490).
+__device__ __forceinline__ void topk_finish(const TopkArgs& a, int64_t t, const float* tval, const int* tidx);
+
 // Token t: `pr` holds E floats of shared memory, `red` 33, tval / tidx 32.
 __device__ __forceinline__ void topk_row(const TopkArgs& a, int64_t t, float* pr, float* red, float* tval,
                                          int* tidx) {
@@ -601,6 +616,14 @@ __device__ __forceinline__ void topk_row(const TopkArgs& a, int64_t t, float* pr
     }
     __syncthreads();
     if (threadIdx.x != 0) return;
+    topk_finish(a, t, tval, tidx);
+}
+
+// Outputs of token t from its top-k values and ids (one thread): the top-k
+// arrays, then (a.lod) compute_moe_lod_weights (moe_kernels.mojo:445-490)
+// into the slot table and the reference's per-token lists.
+__device__ __forceinline__ void topk_finish(const TopkArgs& a, int64_t t, const float* tval, const int* tidx) {
+    const int K = a.K;
     for (int k = 0; k < K; ++k) {
         if (a.top_idx) a.top_idx[t * K + k] = tidx[k];
         if (a.top_val) a.top_val[t * K + k] = tval[k];
@@ -1386,140 +1409,208 @@ int launch_ep_slots(const int* local_e, int64_t P, int E, int* slot_expert, floa
 
 }  // namespace moe
 
+
 namespace moe {
 
-// ------------------------------------------- routing chain as one grid launch
-// The routing chain of a decode batch (k_prep -> k_router_part -> k_topk ->
-// k_bucket -> fp16 gather) as one cooperative launch of G CTAs: the phases
-// run the very device functions of the separate kernels, separated by grid
-// barriers (a counter the host zeroes before the launch; every CTA adds one
-// per barrier and waits, with a globaltimer deadline, for G * (phase + 1)).
-// A CTA that gives up at a barrier raises the error word and leaves; the
-// others then give up at the next barrier.  Nothing is launched between the
-// phases, so the chain pays one launch instead of five.
+// ------------------------------------------ routing of a small batch, 2 launches
+// k_route_rt, one launch of (d/128 router CTAs) + (M prep CTAs):
+//  - prep CTA t writes the expert input of token t (prep_row: moe_in, its
+//    block sums, the q layout of the CUDA-core kernels);
+//  - router CTA c forms the rms of every token with prep_row's arithmetic
+//    (per-thread sums of squares, then block_sum's reduction order), scales
+//    its 128-wide K slice as prep_row does (x * inv * router_scale * rsf),
+//    and writes the slice's router partial sums as k_router_part does;
+//  - the router CTA that finishes last (a ticket taken after a threadfence,
+//    as in the classic threadfence reduction: no CTA waits for another) adds
+//    the partials of every token in slice order, runs softmax, top-k and the
+//    LOD weights with one warp per token, reproducing k_topk's 128-thread
+//    sums exactly, then buckets the pairs (bucket_block) and resets the
+//    ticket.
+// The routing outputs are therefore bit-identical to the separate kernels'.
+// The fp16 gather of the pair rows follows as its own launch.
 namespace {
 
-__device__ __forceinline__ uint64_t gtimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ bool grid_barrier(unsigned* bar, unsigned target, uint64_t deadline, int* err,
-                                             int* ok_s) {
+// block_sum of R values per thread at once: warp xor trees, then the warps'
+// sums as block_sum adds them.  red holds R * 33 floats.
+template <int R>
+__device__ __forceinline__ void block_sum_rows(float (&v)[R], int nrows, float* red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = warp_sum(v[r]);
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(bar, 1u);
-        int ok = 1;
-        for (uint32_t it = 0;; ++it) {
-            unsigned v;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
-            if (v >= target) break;
-            if ((it & 31u) == 31u && gtimer() > deadline) {
-                atomicExch(err, 2);
-                ok = 0;
-                break;
-            }
-            __nanosleep(32);
-        }
-        __threadfence();
-        *ok_s = ok;
+    if (lane == 0)
+        for (int r = 0; r < nrows; ++r) red[r * 33 + wid] = v[r];
+    __syncthreads();
+    for (int r = wid; r < nrows; r += nw) {
+        float t = lane < nw ? red[r * 33 + lane] : 0.f;
+        t = warp_sum(t);
+        if (lane == 0) red[r * 33 + 32] = t;
     }
     __syncthreads();
-    return *ok_s != 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = r < nrows ? red[r * 33 + 32] : 0.f;
+}
+
+// Softmax, top-k and LOD of token t by one warp, with the arithmetic of
+// topk_row run by 128 threads: virtual thread v = 32 w + lane (w = 0..3)
+// owns experts v, v + 128, ...; the sums are that thread's sequential sums,
+// each warp's xor tree, then the tree of the four warp sums, (S0 + S2) +
+// (S1 + S3).  pr holds E floats, tval / tidx 32 (this warp's).
+__device__ __forceinline__ void topk_warp(const TopkArgs& a, int t, float* pr, float* tval, int* tidx) {
+    const int lane = threadIdx.x & 31, E = a.E, K = a.K;
+    float m = -INFINITY;
+    for (int e = lane; e < E; e += 32) {
+        float sc = 0.f;
+        for (int c = 0; c < a.part_n; ++c) sc += __ldcg(a.part + ((int64_t)c * a.M + t) * E + e);
+        if (a.scores_out) a.scores_out[(int64_t)t * E + e] = sc;
+        const float v = sc + (a.bias ? a.bias[e] : 0.f);
+        pr[e] = v;
+        m = fmaxf(m, v);
+    }
+    m = warp_max(m);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int e0 = 0; e0 < E; e0 += 128)
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const int e = e0 + 32 * w + lane;
+            if (e < E) {
+                const float v = expf(pr[e] - m);
+                pr[e] = v;
+                acc[w] += v;
+            }
+        }
+#pragma unroll
+    for (int w = 0; w < 4; ++w) acc[w] = warp_sum(acc[w]);
+    const float se = (acc[0] + acc[2]) + (acc[1] + acc[3]);
+    const float den = se + 1e-10f;
+    __syncwarp();
+    for (int e = lane; e < E; e += 32) {
+        pr[e] = pr[e] / den;
+        if (a.probs_out) a.probs_out[(int64_t)t * E + e] = pr[e];
+    }
+    __syncwarp();
+    // top-k: k rounds of the largest remaining probability, the lower index
+    // first on equal values (the rank order of topk_row); NaNs never enter,
+    // and a chosen entry is set to NaN in pr (it is not read again)
+    for (int k = 0; k < K; ++k) {
+        float bv = 0.f;
+        int be = -1;
+        for (int e = lane; e < E; e += 32) {
+            const float p = pr[e];
+            if (p != p) continue;
+            if (be < 0 || p > bv) {
+                bv = p;
+                be = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (oe >= 0 && (be < 0 || ov > bv || (ov == bv && oe < be))) {
+                bv = ov;
+                be = oe;
+            }
+        }
+        if (lane == 0) {
+            tval[k] = be >= 0 ? bv : -999999.0f;
+            tidx[k] = be;
+        }
+        if (be >= 0 && lane == (be & 31)) pr[be] = __int_as_float(0x7fc00000);
+        __syncwarp();
+    }
+    __syncwarp();
+    if (lane == 0) topk_finish(a, t, tval, tidx);
 }
 
 template <int J>
-__global__ void __launch_bounds__(512, 1) k_route_coop(RouteCoopArgs a) {
+__global__ void __launch_bounds__(512, 1) k_route_rt(RouteRtArgs a) {
     extern __shared__ float4 sm4[];
     float* sm = reinterpret_cast<float*>(sm4);
     __shared__ float red[33];
-    __shared__ float tval[32];
-    __shared__ int tidx[32];
-    __shared__ int wsum[32];
-    __shared__ int ok_s;
-    const unsigned G = gridDim.x;
-    const uint64_t deadline = gtimer() + a.timeout_ns;
-    const int M = a.ta.M, d = (int)a.pa.K;
-    // 1. norms: router input and expert input per token
-    for (int t = blockIdx.x; t < M; t += G) {
-        prep_row(a.pa, t, sm, red);
-        __syncthreads();
+    __shared__ int is_last;
+    pdl_wait();
+    pdl_trigger();
+    const int M = a.ta.M, d = (int)a.pa.K, E = a.ta.E, nsl = d / RS;
+    if ((int)blockIdx.x >= nsl) {  // expert input of one token
+        prep_row(a.pa, blockIdx.x - nsl, sm, red);
+        return;
     }
-    if (!grid_barrier(a.bar, G, deadline, a.err_flag, &ok_s)) return;
-    // 2. router partial sums per 128-wide K slice
-    for (int c = blockIdx.x; c < d / RS; c += G) {
-        router_slice<J>(a.rp, a.rs, a.pa.scaled, M, d, a.ta.E, a.ta.part_out, c, sm);
-        __syncthreads();
-    }
-    if (!grid_barrier(a.bar, 2 * G, deadline, a.err_flag, &ok_s)) return;
-    // 3. softmax, top-k, LOD weights per token
-    for (int t = blockIdx.x; t < M; t += G) {
-        topk_row(a.ta, t, sm, red, tval, tidx);
-        __syncthreads();
-    }
-    if (!grid_barrier(a.bar, 3 * G, deadline, a.err_flag, &ok_s)) return;
-    // 4. bucketing of the (token, slot) pairs (one CTA)
-    if (blockIdx.x == 0) {
-        int* cnt = reinterpret_cast<int*>(sm);
-        bucket_block(a.ta.slot_expert, (int64_t)M * a.ta.K, a.ta.K, a.ta.E, a.e_lo, a.e_hi, a.b, a.BN,
-                     a.tt_prefix, cnt, cnt + blockDim.x, wsum);
-    }
-    if (!a.x16) return;
-    if (!grid_barrier(a.bar, 4 * G, deadline, a.err_flag, &ok_s)) return;
-    // 5. fp16 rows of the pairs in bucket order, every 8-group of K in
-    //    [0,4,1,5,2,6,3,7] order (the tensor-core kernels' operand order)
-    const int P = a.b.meta[1];
-    for (int p = blockIdx.x; p < P; p += G) {
-        const float4* x4 = reinterpret_cast<const float4*>(a.pa.out + (int64_t)a.b.pair_token[p] * d);
-        uint4* o = reinterpret_cast<uint4*>(a.x16 + (int64_t)p * d);
-        for (int g = threadIdx.x; g < d / 8; g += blockDim.x) {
-            const float4 u = __ldg(x4 + 2 * g), v = __ldg(x4 + 2 * g + 1);
-            const __half2 h0 = __floats2half2_rn(u.x, v.x);
-            const __half2 h1 = __floats2half2_rn(u.y, v.y);
-            const __half2 h2 = __floats2half2_rn(u.z, v.z);
-            const __half2 h3 = __floats2half2_rn(u.w, v.w);
-            o[g] = make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
-                              *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+    const int c = blockIdx.x, k0 = c * RS;
+    // rms of every token: prep_row's per-thread sums, block_sum's order
+    float* red_rows = sm;                 // [16][33] per pass
+    float* inv_s = sm + 16 * 33;          // [M]
+    float* xs = inv_s + 64;               // [M][RS] scaled slice
+    const float4* x4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.pa.x));
+    for (int t0 = 0; t0 < M; t0 += 16) {
+        const int nr = min(16, M - t0);
+        float ss[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            ss[r] = 0.f;
+            if (r < nr) {
+                const float4* row = x4 + (int64_t)(t0 + r) * (d / 4);
+#pragma unroll 4
+                for (int j = threadIdx.x; j < d / 4; j += blockDim.x) ss[r] = ss_step(ss[r], __ldg(row + j));
+            }
         }
+        block_sum_rows<16>(ss, nr, red_rows);
+        if (threadIdx.x < nr) inv_s[t0 + threadIdx.x] = 1.0f / sqrtf(ss[threadIdx.x] / (float)d + 1e-6f);
+        __syncthreads();
     }
+    // this CTA's slice of the router input, as prep_row writes `scaled`
+    const float* xin = reinterpret_cast<const float*>(a.pa.x);
+    for (int i = threadIdx.x; i < M * RS; i += blockDim.x) {
+        const int t = i / RS, k = i % RS;
+        const float v = __ldg(xin + (int64_t)t * d + k0 + k);
+        xs[t * RS + k] = v * inv_s[t] * __ldg(a.pa.router_scale + k0 + k) * a.pa.rsf;
+    }
+    __syncthreads();
+    router_slice_dot<J>(a.rp, a.rs, M, d, E, a.ta.part_out, c, xs);
+    // the last router CTA to finish routes every token
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        is_last = atomicAdd(a.ticket, 1u) == (unsigned)(nsl - 1);
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const int warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    float* pr = sm + warp * E;                       // [nwarp][E]
+    float* tv_s = sm + nwarp * E + warp * 32;        // [nwarp][32]
+    int* ti_s = reinterpret_cast<int*>(sm + nwarp * E + nwarp * 32) + warp * 32;
+    for (int t = warp; t < M; t += nwarp) topk_warp(a.ta, t, pr, tv_s, ti_s);
+    __syncthreads();
+    __threadfence_block();
+    int* cnt = reinterpret_cast<int*>(sm);
+    __shared__ int wsum[32];
+    bucket_block(a.ta.slot_expert, (int64_t)M * a.ta.K, a.ta.K, E, a.e_lo, a.e_hi, a.b, a.BN, a.tt_prefix, cnt,
+                 cnt + blockDim.x, wsum);
+    if (threadIdx.x == 0) atomicExch(a.ticket, 0u);
 }
 
 }  // namespace
 
-bool route_coop_supported(int M, int E, int d, int num_sms) {
-    return M >= 1 && M <= 64 && E >= 1 && E <= 512 && d % RS == 0 && d <= 12288 && d / RS <= 4 * num_sms;
+bool route_rt_supported(int M, int E, int K, int d) {
+    return M >= 1 && M <= 64 && E >= 1 && E <= 512 && K >= 1 && K <= 32 && d % RS == 0 && d <= 12288 &&
+           d / RS >= 1;
 }
 
-int launch_route_coop(const RouteCoopArgs& a, int num_sms, cudaStream_t s) {
+int launch_route_rt(const RouteRtArgs& a, cudaStream_t s) {
     const int M = a.ta.M, d = (int)a.pa.K, E = a.ta.E;
-    if (!route_coop_supported(M, E, d, num_sms)) return -1;
-    int G = std::max(d / RS, M);
-    G = std::max(G, 32);
-    G = std::min(G, num_sms);
-    const size_t smem = std::max<size_t>(std::max<size_t>((size_t)d * 4, (size_t)M * RS * 4),
-                                         std::max<size_t>((size_t)E * 4, 2 * 512 * 4));
-    if (cudaMemsetAsync(a.bar, 0, sizeof(unsigned), s) != cudaSuccess) return -1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(G);
-    cfg.blockDim = dim3(512);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e;
-    if (M <= 16) {
-        if (smem > 48 * 1024) cudaFuncSetAttribute(k_route_coop<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        e = cudaLaunchKernelEx(&cfg, k_route_coop<4>, a);
-    } else {
-        if (smem > 48 * 1024) cudaFuncSetAttribute(k_route_coop<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        e = cudaLaunchKernelEx(&cfg, k_route_coop<16>, a);
-    }
-    return e == cudaSuccess ? 1 : -1;
+    if (!route_rt_supported(M, E, a.ta.K, d)) return -1;
+    const int nsl = d / RS;
+    size_t smem = (size_t)d * 4;                                             // prep CTAs
+    smem = std::max(smem, (size_t)(16 * 33 + 64 + M * RS) * 4);              // router CTAs
+    smem = std::max(smem, (size_t)(16 * E + 16 * 64) * 4);                   // top-k (16 warps)
+    smem = std::max(smem, (size_t)2 * 512 * 4);                              // bucketing
+    auto kern = M <= 16 ? k_route_rt<4> : k_route_rt<16>;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return -1;
+    launch_k(kern, dim3(nsl + M), dim3(512), smem, s, a);
+    return 1;
 }
 
 }  // namespace moe

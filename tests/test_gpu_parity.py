@@ -429,13 +429,14 @@ def test_fused_routing_matches_separate_kernels(ctx, full_layer, M):
 
 
 @pytest.mark.parametrize("M", [1, 5, 16, 33, 64])
-def test_cooperative_routing_matches_separate_kernels(ctx, full_layer, M):
-    """The cooperative grid launch (MOE_OPT_FUSED_ROUTE=2) runs the separate
-    routing kernels' code between grid barriers: up to 16 tokens (where the
-    separate chain also takes the K-slice router) routing outputs equal, bit
-    for bit, on the whole layer and on an expert range, outputs within fp32
-    reassociation (the pairs of an expert may land in other tile positions);
-    at every size, routing and outputs against the oracle."""
+def test_one_launch_routing_matches_separate_kernels(ctx, full_layer, M):
+    """The routing in one launch (MOE_OPT_FUSED_ROUTE=2; its last CTA routes
+    every token) reproduces the separate kernels' arithmetic: up to 16
+    tokens (where the separate chain also takes the K-slice router) routing
+    outputs equal, bit for bit, on the whole layer and on an expert range,
+    outputs within fp32 reassociation (the pairs of an expert may land in
+    other tile positions); at every size, routing and outputs against the
+    oracle."""
     dev, host, L = full_layer
     desc = MB.make_desc(dev)
     x = synth.make_x(M, seed=320 + M).cpu().numpy()
@@ -443,27 +444,27 @@ def test_cooperative_routing_matches_separate_kernels(ctx, full_layer, M):
     for mode in (2, 0):
         ctx.set_option(MB.OPT_FUSED_ROUTE, mode)
         try:
-            for lo, hi in ((0, 0), (32, 96)):
+            for lo, hi, fl in ((0, 0, MB.F_POST_NORM), (32, 96, 0), (0, 0, 0)):
                 ctx.set_expert_range(lo, hi)
                 out = np.zeros((M, 2816), np.float32)
                 cnt = np.zeros(M, np.int64)
                 idx = np.zeros((M, 8), np.int64)
                 w = np.zeros((M, 8), np.float32)
-                ctx.layer_forward(desc, M, x, out, MB.F_POST_NORM if hi == 0 else 0, cnt, idx, w)
+                ctx.layer_forward(desc, M, x, out, fl, cnt, idx, w)
                 res.append((out, cnt, idx, w))
         finally:
             ctx.set_expert_range(0, 0)
             ctx.set_option(MB.OPT_FUSED_ROUTE, 0)
     if M <= 16:
-        for a, b in ((res[0], res[2]), (res[1], res[3])):
+        for a, b in zip(res[:3], res[3:]):
             assert np.array_equal(a[1], b[1]) and np.array_equal(a[2], b[2])
             assert np.array_equal(a[3].view(np.uint32), b[3].view(np.uint32))
-            assert_close(a[0], b[0], max_abs=1e-4, rel_l2=1e-5, what=f"cooperative vs separate M={M}")
+            assert_close(a[0], b[0], max_abs=1e-4, rel_l2=1e-5, what=f"one-launch vs separate M={M}")
     r = O.route(L, x)
-    ties = _check_routing(res[1][1], res[1][2], res[1][3], r, _softmax_rows(r["scores"]), 8)
+    ties = _check_routing(res[2][1], res[2][2], res[2][3], r, _softmax_rows(r["scores"]), 8)
     keep = np.array([t for t in range(M) if t not in ties])
     moe_ref = O.experts_forward(L, r["moe_in"], r["count"], r["idx"], r["w"], prec=O.F64)
-    assert_close(res[1][0][keep], moe_ref[keep], what=f"cooperative routing layer M={M}")
+    assert_close(res[2][0][keep], moe_ref[keep], what=f"one-launch routing layer M={M}")
 
 
 @pytest.mark.parametrize("M", [1, 3, 16])
