@@ -47,22 +47,26 @@ namespace {
 
 constexpr int QW = 8;                    // compute warps
 constexpr int RW = 4;                    // weight rows per compute warp
-constexpr int QT = 4;                    // tokens per pass
+constexpr int QT = 4;                    // tokens per pass (at most)
 constexpr int IROWS = QW * RW;           // weight rows per item (ACT: half gate, half up)
 constexpr int NXS = 2;                   // activation pass slots
-constexpr int MAX_SLOTS = 4;             // weight item slots (as many as fit, at least 2)
+constexpr int MAX_SLOTS = 6;             // weight item slots (as many as fit, at least 2)
 constexpr int QTHREADS = (QW + 1) * 32;  // + the copy warp
 
 struct QLay {
-    int xbytes;      // one pass: QT rows of K floats
+    int qt;          // tokens per pass: min(QT, most tokens any expert has)
+    int xbytes;      // one pass: qt rows of K floats
     int qbytes;      // IROWS rows x K/2 bytes
     int slot_bytes;  // packed rows, then their scales; 128-aligned
     int nslot;
     int off_slot, off_bar, total;
 };
-__host__ __device__ inline QLay qlay(int K) {
+// Passes only as wide as the batch can fill: a one-token batch leaves the
+// activation slots small and the weight ring deeper.
+__host__ __device__ inline QLay qlay(int K, int max_tokens) {
     QLay L;
-    L.xbytes = QT * K * 4;
+    L.qt = max_tokens < 1 ? 1 : (max_tokens < QT ? max_tokens : QT);
+    L.xbytes = L.qt * K * 4;
     L.qbytes = IROWS * (K / 2);
     L.slot_bytes = (L.qbytes + IROWS * (K / 32) * 4 + 127) & ~127;
     const int budget = 225 * 1024 - NXS * L.xbytes - 256;
@@ -221,7 +225,7 @@ template <int MODE>
 __global__ void __launch_bounds__(QTHREADS, 1) k_dgemv(GemvArgs a) {
     extern __shared__ __align__(128) uint8_t qsm[];
     const int K = a.K, nb = K >> 5;
-    const QLay L = qlay(K);
+    const QLay L = qlay(K, a.max_tokens);
     const uint32_t bar0 = tc::smem_u32(qsm + L.off_bar);
     auto full = [&](int s) { return bar0 + 8u * s; };
     auto empty = [&](int s) { return bar0 + 8u * (MAX_SLOTS + s); };
@@ -284,12 +288,12 @@ __global__ void __launch_bounds__(QTHREADS, 1) k_dgemv(GemvArgs a) {
                 par = (par & ~(1u << slot)) | (ph << slot);
                 // the item's activation passes, each once per run of items that share it
                 const int n = a.seg_count[u], s0 = a.seg_start[u];
-                for (int t0 = 0; t0 < n; t0 += QT) {
+                for (int t0 = 0; t0 < n; t0 += L.qt) {
                     if (u == xs_u && t0 == xs_t0) continue;
                     const int xsl = (int)(xk % NXS);
                     const uint32_t xph = (xk / NXS) & 1u;
                     if (!(ok = tc::mbar_wait(xempty(xsl), xph ^ 1u, G))) break;
-                    const int nt = min(QT, n - t0);
+                    const int nt = min(L.qt, n - t0);
                     tc::mbar_expect_tx(xfull(xsl), (uint32_t)nt * K * 4);
                     for (int t = 0; t < nt; ++t) {
                         const int p = s0 + t0 + t;
@@ -348,7 +352,7 @@ __global__ void __launch_bounds__(QTHREADS, 1) k_dgemv(GemvArgs a) {
                 rv[i] = row[i] < R;
             }
         }
-        for (int t0 = 0; ok && t0 < n; t0 += QT) {
+        for (int t0 = 0; ok && t0 < n; t0 += L.qt) {
             if (u != xs_u || t0 != xs_t0) {  // next activation pass
                 if (xsl >= 0) {
                     __syncwarp();
@@ -361,7 +365,7 @@ __global__ void __launch_bounds__(QTHREADS, 1) k_dgemv(GemvArgs a) {
                 ++xk;
             }
             const float4* xs = reinterpret_cast<const float4*>(qsm + xsl * L.xbytes);
-            const int nt = min(QT, n - t0);
+            const int nt = min(L.qt, n - t0);
             auto emit = [&](int t, const float (&v)[RW]) {
                 const int p = s0 + t0 + t;
                 if (MODE == GEMV_ACT) {
@@ -417,7 +421,7 @@ bool dgemv_supported(const GemvArgs& a, int mode) {
     const int64_t item = mode == GEMV_ACT ? QRows<GEMV_ACT>::ITEM : QRows<GEMV_PLAIN>::ITEM;
     if (tile % item != 0 || (a.rows_per_expert * nb) % 4 != 0 || (mode == GEMV_ACT && (a.F * nb) % 4 != 0))
         return false;
-    if (qlay(a.K).nslot < 2) return false;
+    if (qlay(a.K, a.max_tokens).nslot < 2) return false;
     return (reinterpret_cast<uintptr_t>(a.Wp) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.Ws) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(a.X) & 15) == 0;
 }
@@ -429,7 +433,7 @@ int launch_dgemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s) {
     const int64_t cap = num_sms;
     const int grid = (int)(items < cap ? items : cap);
     if (grid <= 0) return 0;
-    const int smem = qlay(a.K).total;
+    const int smem = qlay(a.K, a.max_tokens).total;
     if (mode == GEMV_ACT) {
         if (cudaFuncSetAttribute(k_dgemv<GEMV_ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
             cudaSuccess)

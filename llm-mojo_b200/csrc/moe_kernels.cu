@@ -1456,14 +1456,13 @@ __device__ __forceinline__ void block_sum_rows(float (&v)[R], int nrows, float* 
 // owns experts v, v + 128, ...; the sums are that thread's sequential sums,
 // each warp's xor tree, then the tree of the four warp sums, (S0 + S2) +
 // (S1 + S3).  pr holds E floats, tval / tidx 32 (this warp's).
-__device__ __forceinline__ void topk_warp(const TopkArgs& a, int t, float* pr, float* tval, int* tidx) {
+// `lg` holds the token's logits (the partials summed in slice order).
+__device__ __forceinline__ void topk_warp(const TopkArgs& a, int t, const float* lg, float* pr, float* tval,
+                                          int* tidx) {
     const int lane = threadIdx.x & 31, E = a.E, K = a.K;
     float m = -INFINITY;
     for (int e = lane; e < E; e += 32) {
-        float sc = 0.f;
-        for (int c = 0; c < a.part_n; ++c) sc += __ldcg(a.part + ((int64_t)c * a.M + t) * E + e);
-        if (a.scores_out) a.scores_out[(int64_t)t * E + e] = sc;
-        const float v = sc + (a.bias ? a.bias[e] : 0.f);
+        const float v = lg[e] + (a.bias ? a.bias[e] : 0.f);
         pr[e] = v;
         m = fmaxf(m, v);
     }
@@ -1546,13 +1545,16 @@ __global__ void __launch_bounds__(512, 1) k_route_rt(RouteRtArgs a) {
         const int nr = min(16, M - t0);
         float ss[16];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            ss[r] = 0.f;
-            if (r < nr) {
-                const float4* row = x4 + (int64_t)(t0 + r) * (d / 4);
-#pragma unroll 4
-                for (int j = threadIdx.x; j < d / 4; j += blockDim.x) ss[r] = ss_step(ss[r], __ldg(row + j));
-            }
+        for (int r = 0; r < 16; ++r) ss[r] = 0.f;
+        // each row's elements in prep_row's order; the rows' loads in flight together
+        for (int j = threadIdx.x; j < d / 4; j += blockDim.x) {
+            float4 v[16];
+#pragma unroll
+            for (int r = 0; r < 16; ++r)
+                if (r < nr) v[r] = __ldg(x4 + (int64_t)(t0 + r) * (d / 4) + j);
+#pragma unroll
+            for (int r = 0; r < 16; ++r)
+                if (r < nr) ss[r] = ss_step(ss[r], v[r]);
         }
         block_sum_rows<16>(ss, nr, red_rows);
         if (threadIdx.x < nr) inv_s[t0 + threadIdx.x] = 1.0f / sqrtf(ss[threadIdx.x] / (float)d + 1e-6f);
@@ -1576,11 +1578,37 @@ __global__ void __launch_bounds__(512, 1) k_route_rt(RouteRtArgs a) {
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    // logits of every token: the partials of each 4 experts summed in slice
+    // order by one thread, every slice's load in flight at once
+    float* lg = sm;                                  // [M][E]
+    const int E4 = E / 4, nsum = M * E4;
+    for (int i = threadIdx.x; i < nsum; i += blockDim.x) {
+        const int t = i / E4, e4 = i - t * E4;
+        float4 sc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c0 = 0; c0 < nsl; c0 += 12) {
+            float4 v[12];
+#pragma unroll
+            for (int j = 0; j < 12; ++j)
+                if (c0 + j < nsl)
+                    v[j] = __ldcg(reinterpret_cast<const float4*>(a.ta.part + ((int64_t)(c0 + j) * M + t) * E) + e4);
+#pragma unroll
+            for (int j = 0; j < 12; ++j)
+                if (c0 + j < nsl) {
+                    sc.x += v[j].x;
+                    sc.y += v[j].y;
+                    sc.z += v[j].z;
+                    sc.w += v[j].w;
+                }
+        }
+        reinterpret_cast<float4*>(lg + t * E)[e4] = sc;
+        if (a.ta.scores_out) reinterpret_cast<float4*>(a.ta.scores_out + (int64_t)t * E)[e4] = sc;
+    }
+    __syncthreads();
     const int warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
-    float* pr = sm + warp * E;                       // [nwarp][E]
-    float* tv_s = sm + nwarp * E + warp * 32;        // [nwarp][32]
-    int* ti_s = reinterpret_cast<int*>(sm + nwarp * E + nwarp * 32) + warp * 32;
-    for (int t = warp; t < M; t += nwarp) topk_warp(a.ta, t, pr, tv_s, ti_s);
+    float* pr = lg + M * E + warp * E;                       // [nwarp][E]
+    float* tv_s = lg + M * E + nwarp * E + warp * 32;        // [nwarp][32]
+    int* ti_s = reinterpret_cast<int*>(lg + M * E + nwarp * E + nwarp * 32) + warp * 32;
+    for (int t = warp; t < M; t += nwarp) topk_warp(a.ta, t, lg + t * E, pr, tv_s, ti_s);
     __syncthreads();
     __threadfence_block();
     int* cnt = reinterpret_cast<int*>(sm);
@@ -1593,8 +1621,8 @@ __global__ void __launch_bounds__(512, 1) k_route_rt(RouteRtArgs a) {
 }  // namespace
 
 bool route_rt_supported(int M, int E, int K, int d) {
-    return M >= 1 && M <= 64 && E >= 1 && E <= 512 && K >= 1 && K <= 32 && d % RS == 0 && d <= 12288 &&
-           d / RS >= 1;
+    return M >= 1 && M <= 64 && E >= 4 && E <= 512 && E % 4 == 0 && K >= 1 && K <= 32 && d % RS == 0 &&
+           d <= 12288 && d / RS >= 1;
 }
 
 int launch_route_rt(const RouteRtArgs& a, cudaStream_t s) {
@@ -1603,7 +1631,7 @@ int launch_route_rt(const RouteRtArgs& a, cudaStream_t s) {
     const int nsl = d / RS;
     size_t smem = (size_t)d * 4;                                             // prep CTAs
     smem = std::max(smem, (size_t)(16 * 33 + 64 + M * RS) * 4);              // router CTAs
-    smem = std::max(smem, (size_t)(16 * E + 16 * 64) * 4);                   // top-k (16 warps)
+    smem = std::max(smem, (size_t)(M * E + 16 * E + 16 * 64) * 4);           // logits + top-k (16 warps)
     smem = std::max(smem, (size_t)2 * 512 * 4);                              // bucketing
     auto kern = M <= 16 ? k_route_rt<4> : k_route_rt<16>;
     if (smem > 48 * 1024 &&
