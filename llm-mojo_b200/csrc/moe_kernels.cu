@@ -16,6 +16,13 @@
 
 namespace moe {
 
+// Asks L2 for [p, p + bytes) (128-byte lines spread over the block's threads).
+__device__ __forceinline__ void prefetch_l2(const void* p, int64_t bytes) {
+    const char* c = static_cast<const char*>(p);
+    for (int64_t o = (int64_t)threadIdx.x * 128; o < bytes; o += (int64_t)blockDim.x * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(c + o));
+}
+
 // Dot products of one Q4_0 block (16 bytes = 32 weights) with the
 // matching 32 activations of T rows, one 32-bit word (8 weights) at a time.
 // XS = true: weights as 1 + n/16 (shift + LOP3 per weight, see nib_1p); the
@@ -457,6 +464,10 @@ __device__ __forceinline__ void router_slice(const uint8_t* __restrict__ W, cons
 __global__ void __launch_bounds__(512) k_router_part(const uint8_t* __restrict__ W, const float* __restrict__ S,
                                                      const float* __restrict__ X, int M, int K, int E,
                                                      float* __restrict__ part) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {  // weights: ahead of the dependency wait
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(W + (int64_t)e * (K / 2) + blockIdx.x * RS / 2));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(S + (int64_t)e * (K / 32) + blockIdx.x * RS / 32));
+    }
     pdl_wait();
     pdl_trigger();
     __shared__ __align__(16) float xs[16 * RS];
@@ -532,6 +543,8 @@ __device__ __forceinline__ void prep_row(const PrepArgs& a, int64_t t, float* xs
 }
 
 __global__ void __launch_bounds__(512) k_prep(PrepArgs a) {
+    if (a.norm) prefetch_l2(a.pre_w, a.K * 4);  // weights: ahead of the dependency wait
+    if (a.scaled) prefetch_l2(a.router_scale, a.K * 4);
     pdl_wait();
     pdl_trigger();
     extern __shared__ float4 smem4[];
@@ -552,12 +565,14 @@ int launch_prep(const PrepArgs& a, int64_t M, cudaStream_t s) {
 // batched.mojo:921-933), top-k with insertion semantics (:936-953; equal
 // values keep the lower index first) and, when a.lod,
 // compute_moe_lod_weights (moe_kernels.mojo:445-490).
-__device__ __forceinline__ void topk_finish(const TopkArgs& a, int64_t t, const float* tval, const int* tidx);
+__device__ __forceinline__ void topk_finish(const TopkArgs& a, int64_t t, const float* tval, const int* tidx,
+                                            const float* pes);
 
 // Token t: `pr` holds E floats of shared memory, `red` 33, tval / tidx 32.
 __device__ __forceinline__ void topk_row(const TopkArgs& a, int64_t t, float* pr, float* red, float* tval,
-                                         int* tidx) {
+                                         int* tidx, float* pes_s) {
     const int E = a.E, K = a.K;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) pes_s[e] = __ldg(a.pes + e);
     float m = -INFINITY;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         float sc;
@@ -616,13 +631,17 @@ __device__ __forceinline__ void topk_row(const TopkArgs& a, int64_t t, float* pr
     }
     __syncthreads();
     if (threadIdx.x != 0) return;
-    topk_finish(a, t, tval, tidx);
+    topk_finish(a, t, tval, tidx, pes_s);
 }
 
 // Outputs of token t from its top-k values and ids (one thread): the top-k
 // arrays, then (a.lod) compute_moe_lod_weights (moe_kernels.mojo:445-490)
 // into the slot table and the reference's per-token lists.
-__device__ __forceinline__ void topk_finish(const TopkArgs& a, int64_t t, const float* tval, const int* tidx) {
+// `pes` is per_expert_scale, staged in shared memory by the caller: the LOD
+// loop below reads it slot by slot, and from global memory each read would
+// be a dependent round trip.
+__device__ __forceinline__ void topk_finish(const TopkArgs& a, int64_t t, const float* tval, const int* tidx,
+                                            const float* pes) {
     const int K = a.K;
     for (int k = 0; k < K; ++k) {
         if (a.top_idx) a.top_idx[t * K + k] = tidx[k];
@@ -644,7 +663,7 @@ __device__ __forceinline__ void topk_finish(const TopkArgs& a, int64_t t, const 
             if ((np_ >= 0.05f || k == 0) && tidx[k] >= 0) {
                 const int e = tidx[k];
                 oi[cnt] = e;
-                ow[cnt] = np_ * a.pes[e];
+                ow[cnt] = np_ * pes[e];
                 ++cnt;
             }
         }
@@ -660,7 +679,7 @@ __device__ __forceinline__ void topk_finish(const TopkArgs& a, int64_t t, const 
             ++cnt;
         }
         const float rn = 1.0f / (cum + 1e-10f);
-        for (int k = 0; k < cnt; ++k) ow[k] = (ow[k] * rn) * a.pes[oi[k]];
+        for (int k = 0; k < cnt; ++k) ow[k] = (ow[k] * rn) * pes[oi[k]];
     }
     for (int k = 0; k < K; ++k) {
         const bool on = k < cnt;
@@ -679,12 +698,13 @@ __global__ void __launch_bounds__(128) k_topk(TopkArgs a) {
     __shared__ float red[33];
     __shared__ float tval[32];
     __shared__ int tidx[32];
-    topk_row(a, blockIdx.x, reinterpret_cast<float*>(smem4), red, tval, tidx);
+    topk_row(a, blockIdx.x, reinterpret_cast<float*>(smem4), red, tval, tidx,
+             reinterpret_cast<float*>(smem4) + a.E);
 }
 
 int launch_topk(const TopkArgs& a, int64_t M, cudaStream_t s) {
     if (M <= 0) return 0;
-    const size_t smem = (size_t)a.E * sizeof(float);
+    const size_t smem = (size_t)a.E * 2 * sizeof(float);
     launch_k(k_topk, dim3((unsigned)M), dim3(128), smem, s, a);
     return 1;
 }
@@ -1079,6 +1099,12 @@ __global__ void __launch_bounds__(512) k_combine(CombineArgs a) {
 // cluster-rank order.
 constexpr int CW_CL = 4;
 __global__ void __launch_bounds__(256) k_combine_cl(CombineArgs a) {
+    if (a.post_norm) {  // the norm weights of this CTA's part of the row, ahead of the dependency wait
+        const int64_t per = a.d / CW_CL;
+        const char* w = reinterpret_cast<const char*>(a.post_w + cl_rank() * per);
+        for (int64_t o = (int64_t)threadIdx.x * 128; o < per * 4; o += (int64_t)blockDim.x * 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(w + o));
+    }
     pdl_wait();
     pdl_trigger();
     __shared__ float red[33];
@@ -1458,7 +1484,7 @@ __device__ __forceinline__ void block_sum_rows(float (&v)[R], int nrows, float* 
 // (S1 + S3).  pr holds E floats, tval / tidx 32 (this warp's).
 // `lg` holds the token's logits (the partials summed in slice order).
 __device__ __forceinline__ void topk_warp(const TopkArgs& a, int t, const float* lg, float* pr, float* tval,
-                                          int* tidx) {
+                                          int* tidx, const float* pes) {
     const int lane = threadIdx.x & 31, E = a.E, K = a.K;
     float m = -INFINITY;
     for (int e = lane; e < E; e += 32) {
@@ -1519,7 +1545,7 @@ __device__ __forceinline__ void topk_warp(const TopkArgs& a, int t, const float*
         __syncwarp();
     }
     __syncwarp();
-    if (lane == 0) topk_finish(a, t, tval, tidx);
+    if (lane == 0) topk_finish(a, t, tval, tidx, pes);
 }
 
 template <int J>
@@ -1528,14 +1554,26 @@ __global__ void __launch_bounds__(512, 1) k_route_rt(RouteRtArgs a) {
     float* sm = reinterpret_cast<float*>(sm4);
     __shared__ float red[33];
     __shared__ int is_last;
-    pdl_wait();
-    pdl_trigger();
     const int M = a.ta.M, d = (int)a.pa.K, E = a.ta.E, nsl = d / RS;
+    // Weights are no product of the previous kernel: their L2 prefetch is
+    // issued before the dependency wait and overlaps that kernel's tail.
     if ((int)blockIdx.x >= nsl) {  // expert input of one token
+        prefetch_l2(a.pa.pre_w, d * 4);
+        prefetch_l2(a.pa.router_scale, d * 4);
+        pdl_wait();
+        pdl_trigger();
         prep_row(a.pa, blockIdx.x - nsl, sm, red);
         return;
     }
     const int c = blockIdx.x, k0 = c * RS;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {  // this slice's router rows and scales
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.rp + (int64_t)e * (d / 2) + k0 / 2));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.rs + (int64_t)e * (d / 32) + k0 / 32));
+    }
+    if (threadIdx.x < RS / 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(a.pa.router_scale + k0 + 32 * threadIdx.x));
+    if (threadIdx.x == 0 && a.ta.pes) asm volatile("prefetch.global.L2 [%0];" ::"l"(a.ta.pes));
+    pdl_wait();
+    pdl_trigger();
     // rms of every token: prep_row's per-thread sums, block_sum's order
     float* red_rows = sm;                 // [16][33] per pass
     float* inv_s = sm + 16 * 33;          // [M]
@@ -1608,7 +1646,10 @@ __global__ void __launch_bounds__(512, 1) k_route_rt(RouteRtArgs a) {
     float* pr = lg + M * E + warp * E;                       // [nwarp][E]
     float* tv_s = lg + M * E + nwarp * E + warp * 32;        // [nwarp][32]
     int* ti_s = reinterpret_cast<int*>(lg + M * E + nwarp * E + nwarp * 32) + warp * 32;
-    for (int t = warp; t < M; t += nwarp) topk_warp(a.ta, t, lg + t * E, pr, tv_s, ti_s);
+    float* pes_s = lg + M * E + nwarp * E + 2 * nwarp * 32;  // [E]
+    for (int e = threadIdx.x; e < E; e += blockDim.x) pes_s[e] = __ldg(a.ta.pes + e);
+    __syncthreads();
+    for (int t = warp; t < M; t += nwarp) topk_warp(a.ta, t, lg + t * E, pr, tv_s, ti_s, pes_s);
     __syncthreads();
     __threadfence_block();
     int* cnt = reinterpret_cast<int*>(sm);
@@ -1631,7 +1672,7 @@ int launch_route_rt(const RouteRtArgs& a, cudaStream_t s) {
     const int nsl = d / RS;
     size_t smem = (size_t)d * 4;                                             // prep CTAs
     smem = std::max(smem, (size_t)(16 * 33 + 64 + M * RS) * 4);              // router CTAs
-    smem = std::max(smem, (size_t)(M * E + 16 * E + 16 * 64) * 4);           // logits + top-k (16 warps)
+    smem = std::max(smem, (size_t)(M * E + 16 * E + 16 * 64 + E) * 4);       // logits + top-k (16 warps)
     smem = std::max(smem, (size_t)2 * 512 * 4);                              // bucketing
     auto kern = M <= 16 ? k_route_rt<4> : k_route_rt<16>;
     if (smem > 48 * 1024 &&
