@@ -116,9 +116,13 @@ enum moe_option {
                                       communicator (set-up, collectives; default 30 s) */
     MOE_OPT_EP_MODE = 13,          /* moe_ep_mode: how moe_layer_forward splits the layer over the
                                       ranks of the context's communicator (default REPLICATED) */
-    MOE_OPT_EP_LOCAL_WEIGHTS = 14  /* 1: in the GATHER and ALL_TO_ALL modes the descriptor's expert
+    MOE_OPT_EP_LOCAL_WEIGHTS = 14, /* 1: in the GATHER and ALL_TO_ALL modes the descriptor's expert
                                       arrays hold only this rank's experts (expert rank*E/N + i at
                                       index i); 0 (default): all E experts */
+    MOE_OPT_GEMV_ONE_TOKEN = 15    /* CUDA-core expert path when every expert has at most one token
+                                      (one-token batches): 1 (default) one warp per weight row,
+                                      rows streamed from HBM; 0 the ring-buffered GEMV.  Same
+                                      results either way */
 };
 /* Expert-parallel forms of moe_layer_forward (no counterpart in the
  * single-process reference; see moe_ep_init).  Rank r of N owns the experts

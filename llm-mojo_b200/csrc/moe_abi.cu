@@ -84,6 +84,7 @@ struct moe_ctx {
     int64_t expert_begin = 0;            // MOE_OPT_EXPERT_BEGIN
     int64_t expert_end = 0;              // MOE_OPT_EXPERT_END (0: all experts)
     int fused_route = 0;                 // MOE_OPT_FUSED_ROUTE
+    bool gemv1 = true;                   // MOE_OPT_GEMV_ONE_TOKEN
     int dense_ksplit = 0;                // MOE_OPT_DENSE_KSPLIT (0: automatic)
     uint64_t device_timeout_ns = 4000000000ull;
     // profiling (moe_profile_enable)
@@ -420,6 +421,7 @@ struct ExpertPlan {
     moe::TcLaunch t1, t2;          // tensor-core path
     moe::GemvArgs g1, g2;          // CUDA-core path (q-layout forms when `stream`)
     bool stream = false;           // CUDA-core: the k_dgemv pair
+    bool one = false;              // CUDA-core, one token per expert: the k_gemv1 pair
     int ksplit = 1;
     int BN = 0;
 };
@@ -514,6 +516,8 @@ void plan_experts(moe_ctx* ctx, const ExpertWeights& w, int64_t M, int64_t K, in
     q1.out_qlayout = 1;
     q2.x_qlayout = 1;
     p->stream = moe::dgemv_supported(q1, moe::GEMV_ACT) && moe::dgemv_supported(q2, moe::GEMV_PLAIN);
+    // one token per expert (a one-token batch): one warp per row, no ring
+    p->one = ctx->gemv1 && p->stream && moe::gemv1_supported(q1) && moe::gemv1_supported(q2);
     p->g1 = p->stream ? q1 : g1;
     p->g2 = p->stream ? q2 : g2;
 }
@@ -550,8 +554,9 @@ int experts_stage1(moe_ctx* ctx, const ExpertPlan& p, ExpertBufs& bb, int64_t M,
         ctx->launches += moe::launch_to_qlayout(bb.x32, bb.x32q, M, (int)d, ctx->num_sms, s);
     }
     ProfScope ps(ctx, "gemv_gate_up");
-    const int r = p.stream ? moe::launch_dgemv(moe::GEMV_ACT, p.g1, ctx->num_sms, s)
-                           : moe::launch_gemv(moe::GEMV_ACT, p.g1, ctx->num_sms, s);
+    const int r = p.one      ? moe::launch_gemv1(moe::GEMV_ACT, p.g1, ctx->num_sms, s)
+                  : p.stream ? moe::launch_dgemv(moe::GEMV_ACT, p.g1, ctx->num_sms, s)
+                             : moe::launch_gemv(moe::GEMV_ACT, p.g1, ctx->num_sms, s);
     if (r < 0) return fail(ctx, MOE_E_CUDA, "expert GEMV launch failed (gate/up)");
     ctx->launches += r;
     return MOE_OK;
@@ -572,8 +577,9 @@ int experts_stage2(moe_ctx* ctx, const ExpertPlan& p, ExpertBufs& bb, int64_t M,
         ctx->launches += r;
     } else {
         ProfScope ps(ctx, "gemv_down");
-        const int r = p.stream ? moe::launch_dgemv(moe::GEMV_PLAIN, p.g2, ctx->num_sms, s)
-                               : moe::launch_gemv(moe::GEMV_PLAIN, p.g2, ctx->num_sms, s);
+        const int r = p.one      ? moe::launch_gemv1(moe::GEMV_PLAIN, p.g2, ctx->num_sms, s)
+                      : p.stream ? moe::launch_dgemv(moe::GEMV_PLAIN, p.g2, ctx->num_sms, s)
+                                 : moe::launch_gemv(moe::GEMV_PLAIN, p.g2, ctx->num_sms, s);
         if (r < 0) return fail(ctx, MOE_E_CUDA, "expert GEMV launch failed (down)");
         ctx->launches += r;
     }
@@ -797,6 +803,9 @@ int moe_set_option(moe_ctx* ctx, int option, int64_t value) {
         case MOE_OPT_EP_MODE:
             if (value < MOE_EP_REPLICATED || value > MOE_EP_ALL_TO_ALL) return fail(ctx, MOE_E_ARG, "bad EP mode");
             ctx->ep_mode = (int)value;
+            return MOE_OK;
+        case MOE_OPT_GEMV_ONE_TOKEN:
+            ctx->gemv1 = value != 0;
             return MOE_OK;
         case MOE_OPT_EP_LOCAL_WEIGHTS:
             ctx->ep_local_weights = value != 0;

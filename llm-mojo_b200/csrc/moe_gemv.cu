@@ -412,6 +412,153 @@ __global__ void __launch_bounds__(QTHREADS, 1) k_dgemv(GemvArgs a) {
     }
 }
 
+// ------------------------------------------------------------ one token
+// k_gemv1: the expert GEMV when every expert has at most one token (a
+// one-token batch).  One warp per output row (ACT: per activation row, i.e.
+// gate row j and up row F + j), no shared-memory staging: each lane streams
+// its 16-byte chunks of the row straight from HBM (all of them requested
+// before the first is used) and reads the token's q-layout activations
+// through L1 (every warp of the expert reads the same row).  Without a ring
+// or a copy warp the kernel needs few registers, so many warps per SM hide
+// the latency that bounds k_dgemv at one token.  The per-chunk arithmetic,
+// the order of the chunk sums in a lane and the warp reduction are
+// rows_dot's, so the results equal k_dgemv's bit for bit.
+namespace {
+
+constexpr int G1_WARPS = 8;  // warps per CTA
+constexpr int G1_MAXIT = 4;  // chunks per lane held in flight (K <= 4096)
+
+template <int MODE, int IT>  // IT: chunks per lane, ceil(K / 32 / 32)
+__global__ void __launch_bounds__(G1_WARPS * 32) k_gemv1(GemvArgs a) {
+    pdl_wait();
+    pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    const int K = a.K, nc = K >> 5, ku = K >> 2;
+    const int64_t R = a.rows_per_expert;
+    const int64_t rows_tile = (MODE == GEMV_ACT) ? a.F : R;
+    const int64_t U = a.meta[0];
+    const int64_t ntask = U * rows_tile;
+    const unsigned long long m01 = pkf(-8388616.0f, -8388736.0f);
+    const unsigned long long m23 = pkf(-8390656.0f, -8421376.0f);
+    uint32_t mk[4] = {0xFu, 0xF0u, 0xF00u, 0xF000u}, magic = 0x4B000000u;
+    asm volatile("" : "+r"(mk[0]), "+r"(mk[1]), "+r"(mk[2]), "+r"(mk[3]), "+r"(magic));
+    constexpr int NR = (MODE == GEMV_ACT) ? 2 : 1;  // rows per task
+    for (int64_t task = (int64_t)blockIdx.x * G1_WARPS + (threadIdx.x >> 5); task < ntask;
+         task += (int64_t)gridDim.x * G1_WARPS) {
+        const int u = (int)(task / rows_tile);
+        const int64_t j = task - (int64_t)u * rows_tile;
+        const int64_t ebase = (int64_t)a.unique_expert[u] * R;
+        const int p = a.seg_start[u];  // the expert's one pair
+        int64_t row[NR];
+        row[0] = j;
+        if (MODE == GEMV_ACT) row[NR - 1] = (int64_t)a.F + j;
+        // every chunk of the task's rows in flight before the first is used
+        uint4 q[NR][IT];
+        float sc[NR][IT];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            const uint8_t* wr = a.Wp + (ebase + row[r]) * (K / 2);
+            const float* sr = a.Ws + (ebase + row[r]) * nc;
+#pragma unroll
+            for (int it = 0; it < IT; ++it) {
+                const int c = lane + 32 * it;
+                const bool live = c < nc;
+                q[r][it] = live ? ldg_stream(wr + (int64_t)c * 16) : make_uint4(0, 0, 0, 0);
+                sc[r][it] = live ? ldg_stream_f(sr + c) : 0.f;
+            }
+        }
+        const int64_t xr = a.pair_row ? a.pair_row[p] : p;
+        const float4* xs = reinterpret_cast<const float4*>(a.X + xr * K);
+        float res[NR];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) res[r] = 0.f;
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int c = lane + 32 * it;
+            const bool live = c < nc;
+            const float4* xc = xs + (live ? (c << 3) : 0);
+            const int sw = live ? (c & 7) : 0;
+            unsigned long long acc[NR];
+#pragma unroll
+            for (int r = 0; r < NR; ++r) acc[r] = 0ull;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float4 f = __ldg(xc + ((2 * w + h) ^ sw));  // pre-scaled activations
+                    const unsigned long long x01 = pkf(f.x, f.y), x23 = pkf(f.z, f.w);
+#pragma unroll
+                    for (int r = 0; r < NR; ++r) {
+                        const uint4 qq = q[r][it];
+                        const uint32_t word = w == 0 ? qq.x : w == 1 ? qq.y : w == 2 ? qq.z : qq.w;
+                        const uint32_t uu = h ? (word >> 16) : word;
+                        const unsigned long long v01 =
+                            fadd2(pk2(tc::and_or(uu, mk[0], magic), tc::and_or(uu, mk[1], magic)), m01);
+                        const unsigned long long v23 =
+                            fadd2(pk2(tc::and_or(uu, mk[2], magic), tc::and_or(uu, mk[3], magic)), m23);
+                        acc[r] = ffma2(v01, x01, acc[r]);
+                        acc[r] = ffma2(v23, x23, acc[r]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                const float2 a2 = upk(acc[r]);
+                res[r] = fmaf(sc[r][it], a2.x + a2.y, res[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < NR; ++r) res[r] = warp_sum(res[r]);
+        if (lane == 0) {
+            if (MODE == GEMV_ACT) {
+                if (a.gu_out) {
+                    a.gu_out[(int64_t)p * a.gu_stride + row[0]] = res[0];
+                    a.gu_out[(int64_t)p * a.gu_stride + row[NR - 1]] = res[NR - 1];
+                }
+                const float y = act_fn(res[0], res[NR - 1], a.act);
+                if (a.out_qlayout)
+                    a.out[(int64_t)p * a.out_stride + qpos(j)] = y * qscale(j);
+                else
+                    a.out[(int64_t)p * a.out_stride + j] = y;
+            } else {
+                const int64_t orow = a.out_row ? a.out_row[p] : p;
+                a.out[orow * a.out_stride + j] = res[0];
+            }
+        }
+    }
+}
+
+}  // namespace
+
+bool gemv1_supported(const GemvArgs& a) {
+    return a.dense_tokens == 0 && a.max_tokens == 1 && a.x_qlayout && a.K % 32 == 0 && a.K <= 32 * 32 * G1_MAXIT &&
+           (reinterpret_cast<uintptr_t>(a.Wp) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.Ws) & 3) == 0 &&
+           (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && (a.K / 2) % 16 == 0;
+}
+
+int launch_gemv1(int mode, const GemvArgs& a, int num_sms, cudaStream_t s) {
+    const int64_t rows_tile = mode == GEMV_ACT ? a.F : a.rows_per_expert;
+    const int64_t tasks = rows_tile * a.max_unique;
+    int64_t grid = (tasks + G1_WARPS - 1) / G1_WARPS;
+    if (grid > (int64_t)num_sms * 8) grid = (int64_t)num_sms * 8;  // the CTAs stride over the rest
+    if (grid <= 0) return 0;
+    const int it = (a.K / 32 + 31) / 32;
+    const dim3 g((unsigned)grid), b(G1_WARPS * 32);
+    auto go = [&](auto kern) { launch_k(kern, g, b, 0, s, a); };
+    if (mode == GEMV_ACT) {
+        if (it == 1) go(k_gemv1<GEMV_ACT, 1>);
+        else if (it == 2) go(k_gemv1<GEMV_ACT, 2>);
+        else if (it == 3) go(k_gemv1<GEMV_ACT, 3>);
+        else go(k_gemv1<GEMV_ACT, 4>);
+    } else {
+        if (it == 1) go(k_gemv1<GEMV_PLAIN, 1>);
+        else if (it == 2) go(k_gemv1<GEMV_PLAIN, 2>);
+        else if (it == 3) go(k_gemv1<GEMV_PLAIN, 3>);
+        else go(k_gemv1<GEMV_PLAIN, 4>);
+    }
+    return 1;
+}
+
 // Whole blocks of rows only (every bulk copy a multiple of 16 bytes at a
 // 16-byte aligned address), activations in the q layout, two item slots fit.
 bool dgemv_supported(const GemvArgs& a, int mode) {

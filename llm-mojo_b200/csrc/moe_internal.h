@@ -235,6 +235,10 @@ int launch_router_part(const uint8_t* W, const float* S, const float* X, int M, 
 // work lists only (dense_tokens == 0).
 bool dgemv_supported(const GemvArgs& a, int mode);
 int launch_dgemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);
+// One-token form (every expert has at most one token): one warp per row,
+// chunks streamed straight from HBM (moe_gemv.cu); same results as k_dgemv.
+bool gemv1_supported(const GemvArgs& a);
+int launch_gemv1(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);
 // rows x K fp32 -> the q layout k_dgemv reads (pre-scaled, swizzled per row)
 int launch_to_qlayout(const float* x, float* xq, int64_t rows, int K, int num_sms, cudaStream_t s);
 

@@ -467,6 +467,53 @@ def test_one_launch_routing_matches_separate_kernels(ctx, full_layer, M):
     assert_close(res[2][0][keep], moe_ref[keep], what=f"one-launch routing layer M={M}")
 
 
+def test_one_token_gemv_equals_ring_gemv_and_oracle(ctx, full_layer):
+    """One-token batches take the one-warp-per-row GEMV (MOE_OPT_GEMV_ONE_TOKEN,
+    default on); it repeats the ring GEMV's arithmetic, so the outputs are the
+    same bits, and both meet the oracle.  Also through the expert-stage entry
+    points (one token, eight slots) and with gate/up values returned."""
+    dev, host, L = full_layer
+    desc = MB.make_desc(dev)
+    outs = []
+    for one in (1, 0):
+        ctx.set_option(MB.OPT_GEMV_ONE_TOKEN, one)
+        try:
+            res = []
+            for seed in (61, 62, 63):
+                x = synth.make_x(1, seed=seed).cpu().numpy()
+                out = np.zeros((1, 2816), np.float32)
+                cnt = np.zeros(1, np.int64)
+                idx = np.zeros((1, 8), np.int64)
+                w = np.zeros((1, 8), np.float32)
+                ctx.layer_forward(desc, 1, x, out, 0, cnt, idx, w)
+                res.append((x, out, cnt, idx, w))
+            outs.append(res)
+        finally:
+            ctx.set_option(MB.OPT_GEMV_ONE_TOKEN, 1)
+    for a, b in zip(*outs):
+        assert np.array_equal(a[1].view(np.uint32), b[1].view(np.uint32))
+    for x, out, cnt, idx, w in outs[0]:
+        r = O.route(L, x)
+        ref = O.experts_forward(L, r["moe_in"], cnt, idx, w, prec=O.F64)
+        mx, rel = assert_close(out, ref, what="one-token GEMV layer")
+        assert rel <= 1e-5  # fp32 path
+    # stage entry points: one token, eight experts, raw gate/up values too
+    t = torch()
+    gp, gs, dp, ds, x = _pattern(8, 2816, 704)
+    devp = [t.from_numpy(v).cuda() for v in (gp, gs)]
+    idx = np.array([7, 2, 5, 0, 1, 6, 3, 4], np.int64)
+    ctx.set_gemm_path(MB.PATH_GEMV)
+    try:
+        gu = np.zeros((8, 1408), np.float32)
+        act = np.zeros((8, 704), np.float32)
+        ctx.run_moe_experts_stage1_8core(devp[0], devp[1], x, None, idx, 8, gu, act, 2816, 704)
+    finally:
+        ctx.set_gemm_path(MB.PATH_AUTO)
+    ogu, oact = O.experts_stage1(gp, gs, x, idx, 2816, 704, prec=O.F64)
+    assert_close(gu, ogu, what="stage1 gate_up (one token)")
+    assert_close(act, oact, what="stage1 act (one token)")
+
+
 @pytest.mark.parametrize("M", [1, 3, 16])
 def test_gemv_path_layer_vs_oracle(ctx, full_layer, M):
     """CUDA-core expert GEMV (MOE_PATH_GEMV): fp32 arithmetic, checked against
