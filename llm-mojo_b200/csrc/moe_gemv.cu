@@ -425,50 +425,63 @@ __global__ void __launch_bounds__(QTHREADS, 1) k_dgemv(GemvArgs a) {
 // rows_dot's, so the results equal k_dgemv's bit for bit.
 namespace {
 
-constexpr int G1_WARPS = 8;  // warps per CTA
-constexpr int G1_MAXIT = 4;  // chunks per lane held in flight (K <= 4096)
+constexpr int G1_WARPS = 8;     // warps per CTA
+constexpr int G1_MAXIT = 4;     // chunks per lane and row (K <= 4096)
+constexpr int G1_MAXU = 1024;   // experts staged in shared memory
 
-template <int MODE, int IT>  // IT: chunks per lane, ceil(K / 32 / 32)
+// UR: row units per task (ACT: activation rows, each a gate and an up row;
+// PLAIN: rows), IT: 16-byte chunks per lane and row (ceil(K / 1024)).
+template <int MODE, int UR, int IT>
 __global__ void __launch_bounds__(G1_WARPS * 32) k_gemv1(GemvArgs a) {
+    __shared__ int s_base[G1_MAXU];  // expert id of unique expert u
+    __shared__ int s_pair[G1_MAXU];
+    __shared__ int s_xrow[G1_MAXU];
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
-    const int K = a.K, nc = K >> 5, ku = K >> 2;
-    const int64_t R = a.rows_per_expert;
-    const int64_t rows_tile = (MODE == GEMV_ACT) ? a.F : R;
-    const int64_t U = a.meta[0];
-    const int64_t ntask = U * rows_tile;
+    const int K = a.K, nc = K >> 5;
+    const int R = (int)a.rows_per_expert;
+    const int rows_tile = (MODE == GEMV_ACT) ? a.F : R;
+    const int U = a.meta[0];
+    // the experts' indices once per CTA: no dependent index loads per task
+    for (int u = threadIdx.x; u < U; u += blockDim.x) {
+        const int p = a.seg_start[u];
+        s_base[u] = a.unique_expert[u];
+        s_pair[u] = p;
+        s_xrow[u] = a.pair_row ? a.pair_row[p] : p;
+    }
+    __syncthreads();
     const unsigned long long m01 = pkf(-8388616.0f, -8388736.0f);
     const unsigned long long m23 = pkf(-8390656.0f, -8421376.0f);
     uint32_t mk[4] = {0xFu, 0xF0u, 0xF00u, 0xF000u}, magic = 0x4B000000u;
     asm volatile("" : "+r"(mk[0]), "+r"(mk[1]), "+r"(mk[2]), "+r"(mk[3]), "+r"(magic));
-    constexpr int NR = (MODE == GEMV_ACT) ? 2 : 1;  // rows per task
-    for (int64_t task = (int64_t)blockIdx.x * G1_WARPS + (threadIdx.x >> 5); task < ntask;
-         task += (int64_t)gridDim.x * G1_WARPS) {
-        const int u = (int)(task / rows_tile);
-        const int64_t j = task - (int64_t)u * rows_tile;
-        const int64_t ebase = (int64_t)a.unique_expert[u] * R;
-        const int p = a.seg_start[u];  // the expert's one pair
-        int64_t row[NR];
-        row[0] = j;
-        if (MODE == GEMV_ACT) row[NR - 1] = (int64_t)a.F + j;
+    constexpr int NR = (MODE == GEMV_ACT) ? 2 * UR : UR;  // weight rows per task
+    const int tasks_per_expert = (rows_tile + UR - 1) / UR;
+    const int ntask = U * tasks_per_expert;
+    for (int task = blockIdx.x * G1_WARPS + (threadIdx.x >> 5); task < ntask; task += gridDim.x * G1_WARPS) {
+        const int u = task / tasks_per_expert;
+        const int j0 = (task - u * tasks_per_expert) * UR;
+        const int64_t ebase = (int64_t)s_base[u] * R;
+        const int p = s_pair[u];
         // every chunk of the task's rows in flight before the first is used
         uint4 q[NR][IT];
         float sc[NR][IT];
 #pragma unroll
         for (int r = 0; r < NR; ++r) {
-            const uint8_t* wr = a.Wp + (ebase + row[r]) * (K / 2);
-            const float* sr = a.Ws + (ebase + row[r]) * nc;
+            const int ju = j0 + (MODE == GEMV_ACT ? r / 2 : r);
+            const int64_t row = (MODE == GEMV_ACT && (r & 1)) ? (int64_t)a.F + ju : ju;
+            const bool rv = ju < rows_tile;
+            const uint8_t* wr = a.Wp + (ebase + row) * (K / 2);
+            const float* sr = a.Ws + (ebase + row) * nc;
 #pragma unroll
             for (int it = 0; it < IT; ++it) {
                 const int c = lane + 32 * it;
-                const bool live = c < nc;
+                const bool live = rv && c < nc;
                 q[r][it] = live ? ldg_stream(wr + (int64_t)c * 16) : make_uint4(0, 0, 0, 0);
                 sc[r][it] = live ? ldg_stream_f(sr + c) : 0.f;
             }
         }
-        const int64_t xr = a.pair_row ? a.pair_row[p] : p;
-        const float4* xs = reinterpret_cast<const float4*>(a.X + xr * K);
+        const float4* xs = reinterpret_cast<const float4*>(a.X + (int64_t)s_xrow[u] * K);
         float res[NR];
 #pragma unroll
         for (int r = 0; r < NR; ++r) res[r] = 0.f;
@@ -510,19 +523,25 @@ __global__ void __launch_bounds__(G1_WARPS * 32) k_gemv1(GemvArgs a) {
 #pragma unroll
         for (int r = 0; r < NR; ++r) res[r] = warp_sum(res[r]);
         if (lane == 0) {
-            if (MODE == GEMV_ACT) {
-                if (a.gu_out) {
-                    a.gu_out[(int64_t)p * a.gu_stride + row[0]] = res[0];
-                    a.gu_out[(int64_t)p * a.gu_stride + row[NR - 1]] = res[NR - 1];
+#pragma unroll
+            for (int uu = 0; uu < UR; ++uu) {
+                const int j = j0 + uu;
+                if (j >= rows_tile) break;
+                if (MODE == GEMV_ACT) {
+                    const float g = res[2 * uu], up = res[2 * uu + 1];
+                    if (a.gu_out) {
+                        a.gu_out[(int64_t)p * a.gu_stride + j] = g;
+                        a.gu_out[(int64_t)p * a.gu_stride + a.F + j] = up;
+                    }
+                    const float y = act_fn(g, up, a.act);
+                    if (a.out_qlayout)
+                        a.out[(int64_t)p * a.out_stride + qpos(j)] = y * qscale(j);
+                    else
+                        a.out[(int64_t)p * a.out_stride + j] = y;
+                } else {
+                    const int64_t orow = a.out_row ? a.out_row[p] : p;
+                    a.out[orow * a.out_stride + j] = res[uu];
                 }
-                const float y = act_fn(res[0], res[NR - 1], a.act);
-                if (a.out_qlayout)
-                    a.out[(int64_t)p * a.out_stride + qpos(j)] = y * qscale(j);
-                else
-                    a.out[(int64_t)p * a.out_stride + j] = y;
-            } else {
-                const int64_t orow = a.out_row ? a.out_row[p] : p;
-                a.out[orow * a.out_stride + j] = res[0];
             }
         }
     }
@@ -532,29 +551,33 @@ __global__ void __launch_bounds__(G1_WARPS * 32) k_gemv1(GemvArgs a) {
 
 bool gemv1_supported(const GemvArgs& a) {
     return a.dense_tokens == 0 && a.max_tokens == 1 && a.x_qlayout && a.K % 32 == 0 && a.K <= 32 * 32 * G1_MAXIT &&
+           a.max_unique <= G1_MAXU && a.rows_per_expert < (1LL << 30) &&
            (reinterpret_cast<uintptr_t>(a.Wp) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.Ws) & 3) == 0 &&
            (reinterpret_cast<uintptr_t>(a.X) & 15) == 0 && (a.K / 2) % 16 == 0;
 }
 
 int launch_gemv1(int mode, const GemvArgs& a, int num_sms, cudaStream_t s) {
+    // rows per task: enough 16-byte chunks in flight per warp (about 8 per
+    // lane) to cover the HBM latency with the warps an SM holds
+    const int it = (a.K / 32 + 31) / 32;
+    const int ur = mode == GEMV_ACT ? (it >= 3 ? 2 : 4) : (it >= 3 ? 2 : (it == 2 ? 4 : 8));
     const int64_t rows_tile = mode == GEMV_ACT ? a.F : a.rows_per_expert;
-    const int64_t tasks = rows_tile * a.max_unique;
+    const int64_t tasks = (rows_tile + ur - 1) / ur * a.max_unique;
     int64_t grid = (tasks + G1_WARPS - 1) / G1_WARPS;
     if (grid > (int64_t)num_sms * 8) grid = (int64_t)num_sms * 8;  // the CTAs stride over the rest
     if (grid <= 0) return 0;
-    const int it = (a.K / 32 + 31) / 32;
     const dim3 g((unsigned)grid), b(G1_WARPS * 32);
     auto go = [&](auto kern) { launch_k(kern, g, b, 0, s, a); };
     if (mode == GEMV_ACT) {
-        if (it == 1) go(k_gemv1<GEMV_ACT, 1>);
-        else if (it == 2) go(k_gemv1<GEMV_ACT, 2>);
-        else if (it == 3) go(k_gemv1<GEMV_ACT, 3>);
-        else go(k_gemv1<GEMV_ACT, 4>);
+        if (it == 1) go(k_gemv1<GEMV_ACT, 4, 1>);
+        else if (it == 2) go(k_gemv1<GEMV_ACT, 4, 2>);
+        else if (it == 3) go(k_gemv1<GEMV_ACT, 2, 3>);
+        else go(k_gemv1<GEMV_ACT, 2, 4>);
     } else {
-        if (it == 1) go(k_gemv1<GEMV_PLAIN, 1>);
-        else if (it == 2) go(k_gemv1<GEMV_PLAIN, 2>);
-        else if (it == 3) go(k_gemv1<GEMV_PLAIN, 3>);
-        else go(k_gemv1<GEMV_PLAIN, 4>);
+        if (it == 1) go(k_gemv1<GEMV_PLAIN, 8, 1>);
+        else if (it == 2) go(k_gemv1<GEMV_PLAIN, 4, 2>);
+        else if (it == 3) go(k_gemv1<GEMV_PLAIN, 2, 3>);
+        else go(k_gemv1<GEMV_PLAIN, 2, 4>);
     }
     return 1;
 }
