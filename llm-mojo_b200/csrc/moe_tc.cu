@@ -217,18 +217,19 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
                     if (!(ok = mbar_wait(a_full(as), ap, G))) break;
                     if (!(ok = mbar_wait(b_full(bs), bp, G))) break;
                     tc_fence_after();
-                    const uint32_t sb = smem_u32(smem + L::OFF_B + bs * L::B_BYTES);
+                    // descriptors built once per k-tile: a K step of 16 fp16 is 32 bytes,
+                    // i.e. 2 in the descriptor's 16-byte address field
+                    const uint64_t bdesc = sw128_desc(smem_u32(smem + L::OFF_B + bs * L::B_BYTES));
                     if (A_TMEM) {
                         const uint32_t ta = tmem_base + ACOL + (uint32_t)(as * 32);
 #pragma unroll
                         for (int k = 0; k < KT / 16; ++k)
-                            tc_mma_ts(d_tmem, ta + 8u * k, sw128_desc(sb + 32u * k), IDESC, (kt != kb) || k);
+                            tc_mma_ts(d_tmem, ta + 8u * k, bdesc + 2u * k, IDESC, (kt != kb) || k);
                     } else {
-                        const uint32_t sa = smem_u32(smem + L::OFF_A + as * L::A_BYTES);
+                        const uint64_t adesc = sw128_desc(smem_u32(smem + L::OFF_A + as * L::A_BYTES));
 #pragma unroll
                         for (int k = 0; k < KT / 16; ++k)
-                            tc_mma(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), IDESC,
-                                   (kt != kb) || k);
+                            tc_mma(d_tmem, adesc + 2u * k, bdesc + 2u * k, IDESC, (kt != kb) || k);
                     }
                     issued = true;
                     tc_commit(a_empty(as));
@@ -309,16 +310,19 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
                                   hv);
                         tc_fence_before();
                     } else {
+                        // the same fp16 arithmetic as the tensor-memory variant:
+                        // (0x6400 | n) is 1024 + n, minus 1032, times the fp16 scale
+                        // (one LOP3, one HSUB2, one HMUL2 per pair)
                         uint8_t* arow = smem + L::OFF_A + as * L::A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
+                        const __half2 sc = __float2half2_rn(s);
+                        const __half2 off = __float2half2_rn(1032.0f);
 #pragma unroll
                         for (int w = 0; w < 4; ++w) {
                             uint32_t hh[4];
 #pragma unroll
                             for (int p = 0; p < 4; ++p) {
-                                const uint32_t v = (wv[w] >> (4 * p)) & 0x000F000Fu;
-                                const float lo = (__uint_as_float(0x4B000000u | (v & 0xFFFFu)) - 8388616.0f) * s;
-                                const float hi = (__uint_as_float(0x4B000000u | (v >> 16)) - 8388616.0f) * s;
-                                const __half2 x = __floats2half2_rn(lo, hi);
+                                const uint32_t v = ((wv[w] >> (4 * p)) & 0x000F000Fu) | 0x64006400u;
+                                const __half2 x = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&v), off), sc);
                                 hh[p] = *reinterpret_cast<const uint32_t*>(&x);
                             }
                             const int cw = 4 * h + w;  // 16-byte chunk of the 128-byte row
