@@ -617,7 +617,7 @@ size_t dense_bytes(int64_t batch, int64_t c_in, int64_t c_out) {
 // (x fp32, 16-byte aligned).  Tensor cores (split-K, deterministic reduce)
 // from dense_tc_min_tokens tokens on, else the token-chunked fp32 GEMV.
 int dense_q4(moe_ctx* ctx, const uint8_t* w, const float* sc, const float* xd, float* od, int64_t c_in,
-             int64_t c_out, int64_t batch, const char* prof_name) {
+             int64_t c_out, int64_t batch, const char* prof_name, bool exact_a = false) {
     const bool tc = ctx->gemm_path != MOE_PATH_GEMV && moe::tc_supported(c_in, c_out, 0, 0) &&
                     al8(sc) && (ctx->gemm_path == MOE_PATH_TC || batch >= ctx->dense_tc_min_tokens);
     if (tc) {
@@ -630,6 +630,7 @@ int dense_q4(moe_ctx* ctx, const uint8_t* w, const float* sc, const float* xd, f
         t.a.dense_tokens = (int)batch;
         t.a.y_out = od;
         t.a.y_stride = c_out;
+        t.a.exact_a = exact_a ? 1 : 0;
         t.a.err_flag = ctx->err_flag;
         t.a.timeout_ns = ctx->device_timeout_ns;
         t.Wp = w;
@@ -1804,7 +1805,7 @@ int route_dev(moe_ctx* ctx, const moe_layer_desc* L, const LayerDev& ld, int64_t
     float* part = nullptr;
     int part_n = 0;
     if (ld.rp && M >= ctx->router_tc_min_tokens && ctx->gemm_path != MOE_PATH_GEMV) {
-        TRY(dense_q4(ctx, ld.rp, ld.rs, scaled, scores, d, E, M, "router"));
+        TRY(dense_q4(ctx, ld.rp, ld.rs, scaled, scores, d, E, M, "router", true));
     } else if (ld.rp && moe::router_part_supported((int)M, (int)d)) {
         // few tokens: fp32 partial sums over 128-wide K slices, added by k_topk
         part_n = (int)(d / 128);

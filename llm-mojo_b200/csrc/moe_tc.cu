@@ -313,16 +313,26 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
                         // the same fp16 arithmetic as the tensor-memory variant:
                         // (0x6400 | n) is 1024 + n, minus 1032, times the fp16 scale
                         // (one LOP3, one HSUB2, one HMUL2 per pair)
+                        // (a.exact_a: the router's logits, which decide the routing, keep
+                        // fp32 arithmetic and one rounding of (n - 8) * scale)
                         uint8_t* arow = smem + L::OFF_A + as * L::A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
                         const __half2 sc = __float2half2_rn(s);
                         const __half2 off = __float2half2_rn(1032.0f);
+                        const bool exact = a.exact_a != 0;
 #pragma unroll
                         for (int w = 0; w < 4; ++w) {
                             uint32_t hh[4];
 #pragma unroll
                             for (int p = 0; p < 4; ++p) {
                                 const uint32_t v = ((wv[w] >> (4 * p)) & 0x000F000Fu) | 0x64006400u;
-                                const __half2 x = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&v), off), sc);
+                                __half2 x;
+                                if (exact) {
+                                    const float lo = (__uint_as_float(0x4B000000u | (v & 0xFu)) - 8388616.0f) * s;
+                                    const float hi = (__uint_as_float(0x4B000000u | ((v >> 16) & 0xFu)) - 8388616.0f) * s;
+                                    x = __floats2half2_rn(lo, hi);
+                                } else {
+                                    x = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&v), off), sc);
+                                }
                                 hh[p] = *reinterpret_cast<const uint32_t*>(&x);
                             }
                             const int cw = 4 * h + w;  // 16-byte chunk of the 128-byte row

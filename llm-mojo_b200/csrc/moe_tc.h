@@ -27,6 +27,8 @@ struct TcArgs {
     const int* out_row = nullptr;   // PLAIN: output row of pair p (nullptr: p)
     int ksplit = 1;                 // PLAIN: K split into this many partial sums
     int64_t split_stride = 0;       // PLAIN: floats between the partial-sum buffers
+    int exact_a = 0;                // 1: dequantise in fp32 and round once to fp16 (shared-memory A
+                                    // path; the router's logits); 0: fp16 arithmetic as in TMEM
     int* err_flag = nullptr;        // set to 2 when a bounded wait expires
     uint64_t timeout_ns = 4000000000ull;
 };
