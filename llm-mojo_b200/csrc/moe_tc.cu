@@ -70,7 +70,8 @@ struct Smem {
     static constexpr int OFF_BAR = OFF_Q + SQ * Q_BYTES;
     static constexpr int N_BAR = 2 * SQ + 2 * SA + 2 * SB + 4 + 1;
     static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
-    static constexpr int TOTAL = OFF_MISC + 16 + 1024;    // + alignment slack
+    static constexpr int OFF_WL = OFF_MISC + 16;          // the work list (stage_worklist)
+    static constexpr int TOTAL = OFF_WL + WL_SMEM + 1024; // + alignment slack
 };
 
 __host__ __device__ constexpr uint32_t pow2_cols(int n) {
@@ -91,7 +92,10 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
     constexpr int SQ = L::SQ;
     constexpr int SB = L::SB;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned by pointer arithmetic on the __shared__ array: through
+    // an integer cast the compiler loses the address space and every read of
+    // the rings becomes a generic load (the L1TEX path, long-scoreboard waits)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
     const uint32_t bar0 = smem_u32(bars);
     auto q_full = [&](int s) { return bar0 + 8u * s; };
@@ -149,6 +153,7 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
     const uint32_t tmem_base = *tmem_slot;
     pdl_wait();  // barrier init, TMEM allocation and tensor-map prefetch overlap the previous kernel
     pdl_trigger();
+    const WorkList wl = stage_worklist(a, reinterpret_cast<int*>(smem + L::OFF_WL));
     Guard G{abort_flag, a.err_flag, globaltimer() + a.timeout_ns};
     // draining work already in flight always ends: it gets at least 2 s,
     // whatever the (possibly much shorter) deadline of the work itself
@@ -163,7 +168,7 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
             uint32_t q_par[SQ], b_par[SB];
             Item it;
             bool ok = true;
-            for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
+            for (int64_t item = blockIdx.x; ok && decode_item(wl, item, row_tiles, BN, it); item += gridDim.x) {
                 int row_a, row_b;  // first weight rows of the two 64-row halves
                 if (MODE == TC_ACT) {
                     row_a = (int)((int64_t)it.e * a.R + it.rt * 64);
@@ -208,7 +213,7 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
             constexpr uint32_t IDESC = f16_idesc(128, BN);
             Item it;
             bool ok = true, issued = false;
-            for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
+            for (int64_t item = blockIdx.x; ok && decode_item(wl, item, row_tiles, BN, it); item += gridDim.x) {
                 if (!(ok = mbar_wait(acc_empty(ab), accp ^ 1, G))) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(ab * BN);
@@ -260,7 +265,7 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
         uint32_t qp = 0, ap = 0;
         Item it;
         bool ok = true;
-        for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
+        for (int64_t item = blockIdx.x; ok && decode_item(wl, item, row_tiles, BN, it); item += gridDim.x) {
             int64_t grow;  // global weight row of this thread
             int sr;        // its row in the Q4 stage (gate box rows 0-63, up box 64-127)
             if (MODE == TC_ACT) {
@@ -359,7 +364,7 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
         uint32_t accp = 0;
         Item it;
         bool ok = true;
-        for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
+        for (int64_t item = blockIdx.x; ok && decode_item(wl, item, row_tiles, BN, it); item += gridDim.x) {
             ok = mbar_wait(acc_full(ab), accp, G);
             tc_fence_after();
             const int nv = min(BN, it.n - it.tt * BN);

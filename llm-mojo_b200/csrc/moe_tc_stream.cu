@@ -83,7 +83,8 @@ struct StLayout {
     // item-scale mode (K % 128 == 64): the scale area holds two item buffers
     static constexpr int ISCALE_BYTES = SQ * ST_S / 2;
     static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
-    static constexpr int TOTAL = OFF_MISC + 16 + 1024;  // + alignment slack
+    static constexpr int OFF_WL = OFF_MISC + 16;        // the work list (stage_worklist)
+    static constexpr int TOTAL = OFF_WL + WL_SMEM + 1024;  // + alignment slack
 };
 
 // Whole-warp wait: every lane waits, and the warp leaves together (a lane
@@ -102,22 +103,6 @@ __device__ __forceinline__ bool mbar_wait_warp1(uint32_t a, uint32_t parity, con
     if ((threadIdx.x & 31) == 0) ok = mbar_wait(a, parity, g) ? 1 : 0;
     __syncwarp();
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
-}
-
-// Wait with back-off for roles that are far from the critical path.
-__device__ __forceinline__ bool mbar_wait_sleep(uint32_t a, uint32_t parity, const Guard& g) {
-    for (uint32_t it = 0;; ++it) {
-        if (mbar_try(a, parity)) return true;
-        if (it >= 2) __nanosleep(256);
-        if ((it & 31u) == 31u) {
-            if (*g.abort) return false;
-            if (globaltimer() > g.deadline) {
-                *g.abort = 1;
-                atomicExch(g.err, 2);
-                return false;
-            }
-        }
-    }
 }
 
 // fp16 pair (lo = element p, hi = element p + 4 of the word's 8-group) of
@@ -144,7 +129,10 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
     constexpr int SA = L::SA;
     constexpr int SAG = L::SAG;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned by pointer arithmetic on the __shared__ array: through
+    // an integer cast the compiler loses the address space and every read of
+    // the rings becomes a generic load (the L1TEX path, long-scoreboard waits)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t bar0 = smem_u32(smem + L::OFF_BAR);
     auto q_full = [&](int s) { return bar0 + 8u * s; };
     auto q_empty = [&](int s) { return bar0 + 8u * (SQ + s); };
@@ -223,6 +211,7 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
     const uint32_t tmem_base = *tmem_slot;
     pdl_wait();  // barrier init, TMEM allocation and tensor-map prefetch overlap the previous kernel
     pdl_trigger();
+    const WorkList wl = stage_worklist(a, reinterpret_cast<int*>(smem + L::OFF_WL));
     Guard G{abort_flag, a.err_flag, globaltimer() + a.timeout_ns};
 
     if (warp == 0) {
@@ -238,7 +227,7 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
             uint32_t ii = 0;       // items of this CTA so far
             Item it;
             bool ok = true;
-            for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x, ++ii) {
+            for (int64_t item = blockIdx.x; ok && decode_item(wl, item, row_tiles, BN, it); item += gridDim.x, ++ii) {
                 int row_a, row_b;
                 box_rows(it, row_a, row_b);
                 const int tok_row = it.s0 + it.tt * BN;
@@ -269,11 +258,15 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
                     const uint32_t qd = smem_u32(smem + L::OFF_Q + qs * ST_Q);
                     const uint32_t sd = smem_u32(smem + L::OFF_S + qs * ST_S);
                     mbar_expect_tx(q_full(qs), ST_Q + (iscale ? 0 : ST_S));
-                    tma_load_2d(qd, &qmap, q_full(qs), s * (ST_K / 2), row_a);
-                    tma_load_2d(qd + ST_Q / 2, &qmap, q_full(qs), s * (ST_K / 2), row_b);
-                    if (!iscale) {
-                        tma_load_2d(sd, &smap, q_full(qs), s * (ST_K / 32), row_a);
-                        tma_load_2d(sd + ST_S / 2, &smap, q_full(qs), s * (ST_K / 32), row_b);
+                    // one copy for the 128 rows' bytes and one for their scales: in ACT
+                    // mode the maps see the weights as [2E][F][.] (gate and up halves),
+                    // a box takes 64 rows of the gate half and the same 64 of the up half
+                    if (MODE == TC_ACT) {
+                        tma_load_3d(qd, &qmap, q_full(qs), s * (ST_K / 2), it.rt * 64, 2 * it.e);
+                        if (!iscale) tma_load_3d(sd, &smap, q_full(qs), s * (ST_K / 32), it.rt * 64, 2 * it.e);
+                    } else {
+                        tma_load_2d(qd, &qmap, q_full(qs), s * (ST_K / 2), row_a);
+                        if (!iscale) tma_load_2d(sd, &smap, q_full(qs), s * (ST_K / 32), row_a);
                     }
                     q_armed |= 1u << qs;
                     q_par = (q_par & ~(1u << qs)) | (qp << qs);
@@ -309,7 +302,7 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
             constexpr uint32_t IDESC = f16_idesc(128, BN);
             Item it;
             bool ok = true, issued = false;
-            for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
+            for (int64_t item = blockIdx.x; ok && decode_item(wl, item, row_tiles, BN, it); item += gridDim.x) {
                 if (!(ok = mbar_wait(acc_empty(ab), accp ^ 1u, G))) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)((ab * NG + me) * BN);
@@ -323,7 +316,7 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
                     // descriptors as constant offsets of one base: computed per MMA,
                     // they held the issuer ~190 cycles per tcgen05.mma instead of ~55.
                     const uint64_t bdesc = sw128_desc(smem_u32(smem + L::OFF_B + qs * L::B_BYTES));
-#pragma unroll
+#pragma unroll 1
                     for (int h = 0; h < 2; ++h) {
                         const uint32_t la = 2u * (st / NG) + (uint32_t)h;  // place in this issuer's ring
                         const int as = me * SAG + (int)(la % SAG);
@@ -377,7 +370,7 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
         uint32_t st = 0, ii = 0;
         Item it;
         bool ok = true;
-        for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x, ++ii) {
+        for (int64_t item = blockIdx.x; ok && decode_item(wl, item, row_tiles, BN, it); item += gridDim.x, ++ii) {
             const int ns = s_end(it) - s_begin(it);
             const float* iscl = nullptr;  // item-scale mode: this row's scales
             if (iscale) {
@@ -412,27 +405,40 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
                 for (int c = 0; c < 8; ++c) wq[c] = *reinterpret_cast<const uint4*>(qrow + ((c ^ swz) << 4));
                 __syncwarp();
                 if (lane == 0) mbar_arrive(q_empty(qs));
-#pragma unroll
+                // The two 128-K halves run as a loop, not unrolled: one copy of
+                // the dequant code keeps the hot loop small for the instruction
+                // cache, which three dequant warps and the issuers share per SM
+                // sub-partition.  The second half's chunks move into wq[0..3].
+#pragma unroll 1
                 for (int h = 0; h < 2; ++h) {
-                    // Two 32-column quarters: the first quarter's TMEM store runs
-                    // while the second is computed, one wait for both.  The math of
-                    // the first quarter comes before the wait for the A slot.
-                    auto deq_quarter = [&](int c0, uint32_t (&hv)[32]) {
+                    // Four 16-column chunks through two 16-register buffers: a
+                    // chunk's TMEM store runs while the next is computed (the
+                    // store reads its registers when it issues; one wait before
+                    // the hand-off covers all four), and the small live set lets
+                    // the compiler build each store's consecutive registers in
+                    // place (with two 32-register blocks it spent ~55 moves per
+                    // half).  The first chunk's math comes before the wait for
+                    // the A slot.
+                    auto deq_chunk = [&](int c, uint32_t (&hv)[16]) {  // chunk = Q4 block 8s + 4h + c
+                        const uint4 wv = wq[c];
+                        const __half2 sc = __float2half2_rn(scl[c]);
+                        const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-                        for (int cc = 0; cc < 2; ++cc) {
-                            const int c = c0 + cc;  // chunk = Q4 block 8s + c
-                            const uint4 wv = wq[c];
-                            const __half2 sc = __float2half2_rn(scl[c]);
-                            const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-                            for (int w = 0; w < 4; ++w) {
-                                hv[16 * cc + 4 * w + 0] = deq_pair<0>(w4[w], sc);
-                                hv[16 * cc + 4 * w + 1] = deq_pair<1>(w4[w], sc);
-                                hv[16 * cc + 4 * w + 2] = deq_pair<2>(w4[w], sc);
-                                hv[16 * cc + 4 * w + 3] = deq_pair<3>(w4[w], sc);
-                            }
+                        for (int w = 0; w < 4; ++w) {
+                            hv[4 * w + 0] = deq_pair<0>(w4[w], sc);
+                            hv[4 * w + 1] = deq_pair<1>(w4[w], sc);
+                            hv[4 * w + 2] = deq_pair<2>(w4[w], sc);
+                            hv[4 * w + 3] = deq_pair<3>(w4[w], sc);
                         }
                     };
+                    auto st16 = [&](uint32_t col, const uint32_t (&hv)[16]) {
+                        asm volatile(
+                            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tl + col),
+                            "r"(hv[0]), "r"(hv[1]), "r"(hv[2]), "r"(hv[3]), "r"(hv[4]), "r"(hv[5]), "r"(hv[6]), "r"(hv[7]),
+                            "r"(hv[8]), "r"(hv[9]), "r"(hv[10]), "r"(hv[11]), "r"(hv[12]), "r"(hv[13]), "r"(hv[14]), "r"(hv[15])
+                            : "memory");
+                    };
+                    auto st_wait = [&]() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); };
                     const uint32_t la = 2u * (gs / NG) + (uint32_t)h;  // place in this group's ring
                     const int as = grp * SAG + (int)(la % SAG);
                     const uint32_t apar = ((la / SAG) & 1u) ^ 1u;
@@ -440,34 +446,32 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
                     // ahead of the math hides its latency; the bounded wait only
                     // when it was not
                     const uint32_t early = (lane == 0) ? (mbar_test(a_empty(as), apar) ? 1u : 0u) : 0u;
-                    uint32_t hA[32], hB[32];
-                    deq_quarter(4 * h, hA);
+                    uint32_t b0[16], b1[16];
+                    deq_chunk(0, b0);
                     if (__shfl_sync(0xffffffffu, early, 0) == 0u) {
                         if (!(ok = mbar_wait_warp1(a_empty(as), apar, G))) break;
                     } else {
                         __syncwarp();
                     }
                     tc_fence_after();
-                    asm volatile(
-                        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(tl + (uint32_t)(as * 64)),
-                        "r"(hA[0]), "r"(hA[1]), "r"(hA[2]), "r"(hA[3]), "r"(hA[4]), "r"(hA[5]), "r"(hA[6]), "r"(hA[7]),
-                        "r"(hA[8]), "r"(hA[9]), "r"(hA[10]), "r"(hA[11]), "r"(hA[12]), "r"(hA[13]), "r"(hA[14]), "r"(hA[15]),
-                        "r"(hA[16]), "r"(hA[17]), "r"(hA[18]), "r"(hA[19]), "r"(hA[20]), "r"(hA[21]), "r"(hA[22]), "r"(hA[23]),
-                        "r"(hA[24]), "r"(hA[25]), "r"(hA[26]), "r"(hA[27]), "r"(hA[28]), "r"(hA[29]), "r"(hA[30]), "r"(hA[31])
-                        : "memory");
-                    deq_quarter(4 * h + 2, hB);
-                    // the wait covers both stores: the MMAs may read the slot after it
-                    asm volatile(
-                        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
-                        "tcgen05.wait::st.sync.aligned;" ::"r"(tl + (uint32_t)(as * 64 + 32)),
-                        "r"(hB[0]), "r"(hB[1]), "r"(hB[2]), "r"(hB[3]), "r"(hB[4]), "r"(hB[5]), "r"(hB[6]), "r"(hB[7]),
-                        "r"(hB[8]), "r"(hB[9]), "r"(hB[10]), "r"(hB[11]), "r"(hB[12]), "r"(hB[13]), "r"(hB[14]), "r"(hB[15]),
-                        "r"(hB[16]), "r"(hB[17]), "r"(hB[18]), "r"(hB[19]), "r"(hB[20]), "r"(hB[21]), "r"(hB[22]), "r"(hB[23]),
-                        "r"(hB[24]), "r"(hB[25]), "r"(hB[26]), "r"(hB[27]), "r"(hB[28]), "r"(hB[29]), "r"(hB[30]), "r"(hB[31])
-                        : "memory");
+                    const uint32_t c0 = (uint32_t)(as * 64);
+                    st16(c0, b0);
+                    deq_chunk(1, b1);
+                    st16(c0 + 16, b1);
+                    deq_chunk(2, b0);
+                    st16(c0 + 32, b0);
+                    deq_chunk(3, b1);
+                    // the wait covers every store: the MMAs may read the slot after it
+                    st16(c0 + 48, b1);
+                    st_wait();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(a_full(as));
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        wq[c] = wq[c + 4];
+                        scl[c] = scl[c + 4];
+                    }
                 }
                 if (!ok) break;
             }
@@ -488,8 +492,13 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
         uint32_t accp = 0;
         Item it;
         bool ok = true;
-        for (int64_t item = blockIdx.x; ok && decode_item(a, item, row_tiles, BN, it); item += gridDim.x) {
-            ok = __all_sync(0xffffffffu, mbar_wait_sleep(acc_full(ab), accp, G)) != 0;
+        for (int64_t item = blockIdx.x; ok && decode_item(wl, item, row_tiles, BN, it); item += gridDim.x) {
+            // lane 0 waits (suspended in hardware, no issue slots), the tcgen05
+            // fence after the warp's sync orders the accumulator loads.  A
+            // __nanosleep back-off loop here cost ~0.9 M instructions per
+            // launch: the sleep may end at once, and the four warps share
+            // their SM sub-partitions with the dequant warps.
+            ok = mbar_wait_warp1(acc_full(ab), accp, G);
             if (!ok) break;
             tc_fence_after();
             const int nv = min(BN, it.n - it.tt * BN);
@@ -555,10 +564,39 @@ namespace {
 
 template <int MODE, int BN>
 int launch_st(const TcLaunch& L, int num_sms, cudaStream_t s) {
+    // Q4 rows [rows][K/2] bytes and scales [rows][K/32] fp32, one stage (256 K)
+    // of 128 rows per copy: ACT as [2E][F][.] (box: 64 rows of a gate half and
+    // of the matching up half), PLAIN as [rows][.] (box: 128 rows).  When the
+    // scale row stride is not a multiple of 16 bytes (K % 128 == 64) no map
+    // can describe the scales and the kernel copies each item's scale rows in
+    // one piece instead.
     CUtensorMap qmap, bmap;
-    if (!tc_make_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.Wp, (uint64_t)L.a.K / 2, (uint64_t)L.total_rows,
-                     (uint64_t)L.a.K / 2, tc::ST_K / 2, 64, CU_TENSOR_MAP_SWIZZLE_128B))
-        return -1;
+    const int iscale = (L.a.K % 128) != 0;
+    CUtensorMap smap;
+    const uint64_t kq = (uint64_t)L.a.K / 2, ks = (uint64_t)L.a.K / 32;
+    if (MODE == TC_ACT) {
+        const uint64_t halves = (uint64_t)L.total_rows / (uint64_t)L.a.F;
+        const uint64_t qd[3] = {kq, (uint64_t)L.a.F, halves};
+        const uint64_t qst[2] = {kq, kq * (uint64_t)L.a.F};
+        const uint32_t qb[3] = {tc::ST_K / 2, 64, 2};
+        if (!tc_make_map_nd(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.Wp, 3, qd, qst, qb, CU_TENSOR_MAP_SWIZZLE_128B))
+            return -1;
+        smap = qmap;
+        const uint64_t sdm[3] = {ks, (uint64_t)L.a.F, halves};
+        const uint64_t sst[2] = {ks * 4, ks * 4 * (uint64_t)L.a.F};
+        const uint32_t sb[3] = {tc::ST_K / 32, 64, 2};
+        if (!iscale && !tc_make_map_nd(&smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, L.a.Ws, 3, sdm, sst, sb,
+                                       CU_TENSOR_MAP_SWIZZLE_NONE))
+            return -1;
+    } else {
+        if (!tc_make_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.Wp, kq, (uint64_t)L.total_rows, kq, tc::ST_K / 2,
+                         128, CU_TENSOR_MAP_SWIZZLE_128B))
+            return -1;
+        smap = qmap;
+        if (!iscale && !tc_make_map(&smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, L.a.Ws, ks, (uint64_t)L.total_rows,
+                                    ks * 4, tc::ST_K / 32, 128, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return -1;
+    }
     // activations as [K/64 chunks][rows][64 fp16]: one box per stage lands as
     // four UMMA K-major SWIZZLE_128B tiles of BN rows x 64 K (128-byte rows,
     // so the TMA moves whole 128-byte lines)
@@ -566,15 +604,6 @@ int launch_st(const TcLaunch& L, int num_sms, cudaStream_t s) {
     const uint64_t bstr[2] = {(uint64_t)L.a.K * 2, 128};
     const uint32_t bbox[3] = {64, (uint32_t)BN, tc::ST_K / 64};
     if (!tc_make_map_nd(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L.B, 3, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B))
-        return -1;
-    // scales [rows][K/32] fp32: 8 blocks (one stage) of 64 rows per box; when
-    // the row stride is not a multiple of 16 bytes (K % 128 == 64) the kernel
-    // copies each item's scale rows in one piece instead
-    const int iscale = (L.a.K % 128) != 0;
-    CUtensorMap smap = qmap;
-    if (!iscale && !tc_make_map(&smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, L.a.Ws, (uint64_t)L.a.K / 32,
-                                (uint64_t)L.total_rows, (uint64_t)L.a.K / 32 * 4, tc::ST_K / 32, 64,
-                                CU_TENSOR_MAP_SWIZZLE_NONE))
         return -1;
     if (iscale) {
         const int64_t nb = L.a.K / 32;

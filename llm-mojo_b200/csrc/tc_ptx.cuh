@@ -231,10 +231,63 @@ struct Item {
     int u, e, rt, tt, n, s0, ks;
 };
 
-// Every role of a kernel decodes every work item, so the arithmetic is 32-bit
-// (work lists stay far below 2^31 items): 64-bit division by a run-time value
-// is a long instruction sequence.
-__device__ __forceinline__ bool decode_item(const TcArgs& a, int64_t item64, int row_tiles, int BN,
+// The grouped GEMMs' work list: the arrays the bucketing kernels wrote
+// (unique experts, their token segments, the token-tile prefix), in shared
+// memory once per CTA when they fit.  Every role of a kernel decodes every
+// work item; from global memory each decode is a chain of about ten dependent
+// L2 round trips (the binary search over the prefix), which cost the stream
+// kernel's dequant warps about 14 % of their time.
+constexpr int WL_CAP = 256;                       // experts staged in shared memory
+constexpr int WL_SMEM = (4 * WL_CAP + 1) * 4;     // bytes
+struct WorkList {
+    const int* tt_prefix = nullptr;
+    const int* unique_expert = nullptr;
+    const int* seg_start = nullptr;
+    const int* seg_count = nullptr;
+    int U = 0;
+    int dense_tokens = 0;
+    int ksplit = 1;
+};
+
+// Every thread of the CTA calls this after griddepcontrol.wait (the lists are
+// the previous kernels' output); it ends with __syncthreads.
+__device__ __forceinline__ WorkList stage_worklist(const TcArgs& a, int* s_wl) {
+    WorkList w;
+    w.dense_tokens = a.dense_tokens;
+    w.ksplit = a.ksplit;
+    if (a.dense_tokens > 0) return w;
+    const int U = a.meta[0];
+    w.U = U;
+    if (U <= WL_CAP) {
+        int* sp = s_wl;
+        int* se = s_wl + WL_CAP + 1;
+        int* ss = se + WL_CAP;
+        int* sc = ss + WL_CAP;
+        for (int i = threadIdx.x; i <= U; i += blockDim.x) {
+            sp[i] = a.tt_prefix[i];
+            if (i < U) {
+                se[i] = a.unique_expert[i];
+                ss[i] = a.seg_start[i];
+                sc[i] = a.seg_count[i];
+            }
+        }
+        __syncthreads();
+        w.tt_prefix = sp;
+        w.unique_expert = se;
+        w.seg_start = ss;
+        w.seg_count = sc;
+    } else {
+        w.tt_prefix = a.tt_prefix;
+        w.unique_expert = a.unique_expert;
+        w.seg_start = a.seg_start;
+        w.seg_count = a.seg_count;
+    }
+    return w;
+}
+
+// 32-bit arithmetic (work lists stay far below 2^31 items): 64-bit division
+// by a run-time value is a long instruction sequence.
+__device__ __forceinline__ bool decode_item(const WorkList& a, int64_t item64, int row_tiles, int BN,
                                             Item& it) {
     if (item64 >= 0x7FFFFFFF) return false;
     int item = (int)item64;
@@ -255,7 +308,7 @@ __device__ __forceinline__ bool decode_item(const TcArgs& a, int64_t item64, int
         it.s0 = 0;
         return true;
     }
-    const int U = a.meta[0];
+    const int U = a.U;
     const int total = row_tiles * a.tt_prefix[U];
     if (item >= total) return false;
     int lo = 0, hi = U - 1;  // last u with row_tiles * tt_prefix[u] <= item
