@@ -107,12 +107,19 @@ def calibrate_skew(ctx, MB, synth, layer, x, M, target=5.0):
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """nvidia-smi clocks/throttle sampling during the timed region.
+
+    nvidia-smi needs a few hundred ms to start, so it is started ahead of the
+    timed region and its rows carry their arrival time; begin()/end() mark the
+    region on the host (from the start event to the final synchronize).  A
+    region shorter than the sampling interval keeps the row nearest to it,
+    taken while the warm-up steps ran."""
 
     def __init__(self, index: int):
         self.index = index
         self.rows = []
         self.proc = None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -121,20 +128,29 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            deadline = time.monotonic() + 3.0
+            while not self.rows and time.monotonic() < deadline and self.proc.poll() is None:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+            self.rows.append((time.monotonic(), [c.strip() for c in line.split(",")]))
+
+    def begin(self):
+        self.t0 = time.monotonic()
+
+    def end(self):
+        self.t1 = time.monotonic()
+        time.sleep(0.03)  # the row sampled at the end of the region
 
     def __exit__(self, *a):
         if self.proc:
-            time.sleep(0.06)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -143,9 +159,19 @@ class ClockSampler:
             self.t.join(timeout=2)
 
     def summary(self):
+        rows = self.rows
+        if self.t0 is not None and self.t1 is not None:
+            inside = [r for t, r in rows if self.t0 <= t <= self.t1]
+            if not inside and rows:
+                # shorter than the interval: the row nearest to the region
+                t_mid = 0.5 * (self.t0 + self.t1)
+                inside = [min(rows, key=lambda tr: abs(tr[0] - t_mid))[1]]
+            rows_used = inside
+        else:
+            rows_used = [r for _, r in rows]
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
+        for r in rows_used:
             try:
                 sm.append(float(r[1]))
                 mx = float(r[2])
@@ -154,8 +180,11 @@ class ClockSampler:
                         reasons.add(n)
             except (ValueError, IndexError):
                 continue
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+               "reasons": sorted(reasons), "samples": len(sm)}
+        if self.t0 is not None and self.t1 is not None:
+            out["window_ms"] = round((self.t1 - self.t0) * 1e3, 1)
+        return out
 
 
 def dist_setup():
@@ -388,10 +417,11 @@ def fill_defaults(args, ws):
     wl = WORKLOADS[args.workload]
     if args.parallel is None:
         args.parallel = ("ep-a2a" if wl.get("a2a") else "ep-gather") if ws > 1 else "replicas"
-    if ws > 1 and not args.graph:
+    if ws > 1 and not args.graph and args.parallel not in ("ep-gather",):
         # replaying graphs that hold NCCL calls was slower than eager launches
-        # at 8 ranks (825 us per step replayed against 462 us eager for the
-        # all-reduce form), so N > 1 runs eagerly
+        # at 8 ranks for the replicated all-reduce form (825 us per step
+        # replayed against 462 us eager); the gather form is faster replayed
+        # (229 against 497 us at 8 ranks, 199 against 231 at 2)
         args.no_graph = True
     if args.parallel == "ep-a2a":
         args.no_graph = True  # the all-to-all form reads its row counts on the host
@@ -559,12 +589,17 @@ def measure(args, pg, ws, rank, local):
     ctx.set_async(True)
     for c in dctx.values():
         c.set_async(True)
+    # the clock sampler starts now, so that it runs by the timed region
+    clk = ClockSampler(local).__enter__()
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
 
     # One CUDA graph per distinct step (the library's calls are asynchronous
-    # and allocation-free once warm), replayed step by step.
+    # and allocation-free once warm), replayed step by step.  With several
+    # ranks the expert-parallel forms replay graphs too: at 8 ranks the gather
+    # form took 229 us per step replayed against 497 us launched eagerly (its
+    # NCCL calls are captured in the graph).
     n_graphs = 1 if stack else args.layers
     graphs, launches_per_step = [], None
     if not args.no_graph:
@@ -594,12 +629,16 @@ def measure(args, pg, ws, rank, local):
     torch.cuda.synchronize()
     n0 = all_launches()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    try:
+        clk.begin()
         ev0.record(stream)
         for i in range(args.steps):
             run_step(i)
         ev1.record(stream)
         torch.cuda.synchronize()
+        clk.end()
+    finally:
+        clk.__exit__(None, None, None)
     launches = all_launches() - n0 if not graphs else int(round(launches_per_step * args.steps))
     ms = ev0.elapsed_time(ev1)
     if pg:

@@ -85,7 +85,10 @@ __host__ __device__ constexpr uint32_t tmem_cols(int BN, bool A_TMEM) {
 }
 
 // -------------------------------------------------------------- kernel
-template <int MODE, int BN, bool A_TMEM>
+// EXACT (shared-memory A only; the router's logits): fp32 dequant, one
+// rounding of (n - 8) * scale.  A template parameter, so that the fp16 path's
+// hot loop carries no second copy of the arithmetic.
+template <int MODE, int BN, bool A_TMEM, bool EXACT>
 __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap bmap, TcArgs a) {
     using L = Smem<BN, A_TMEM>;
@@ -280,19 +283,22 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
             const bool row_ok = (MODE == TC_ACT) || (it.rt * 128 + t < a.R);
             const float* srow = a.Ws + grow * nb + h;  // scale of block 2*kt + h
             const int kb = k_begin(it), ke = k_end(it);
-            constexpr int PF = 8;  // scale prefetch distance in k-tiles
+            // the scales PF k-tiles ahead in a shift register; the k-tile loop
+            // is not unrolled (one copy of the body for the instruction cache)
+            constexpr int PF = 8;
             float sreg[PF];
 #pragma unroll
             for (int j = 0; j < PF; ++j) sreg[j] = (row_ok && kb + j < ke) ? __ldg(srow + 2 * (kb + j)) : 0.f;
-            for (int kt0 = kb; kt0 < ke && ok; kt0 += PF) {
+#pragma unroll 1
+            for (int kt = kb; kt < ke && ok; ++kt) {
+                {
+                    const float s = sreg[0];
 #pragma unroll
-                for (int j = 0; j < PF; ++j) {
-                    const int kt = kt0 + j;
-                    if (kt >= ke) break;
-                    const float s = sreg[j];
-                    if (row_ok && kt + PF < ke) sreg[j] = __ldg(srow + 2 * (kt + PF));
+                    for (int j = 0; j < PF - 1; ++j) sreg[j] = sreg[j + 1];
+                    sreg[PF - 1] = (row_ok && kt + PF < ke) ? __ldg(srow + 2 * (kt + PF)) : 0.f;
                     if (!(ok = mbar_wait(q_full(qs), qp, G))) break;
-                    if (!(ok = mbar_wait(a_empty(as), ap ^ 1, G))) break;
+                    // the A slot guards no data these lanes read: lane 0 waits
+                    if (!(ok = mbar_wait_warp1(a_empty(as), ap ^ 1, G))) break;
                     const int sw = ((sr >> 2) & 1) << 4;  // SWIZZLE_32B: chunk ^= row bit 2
                     const uint4 c = *reinterpret_cast<const uint4*>(smem + L::OFF_Q + qs * L::Q_BYTES + sr * 32 +
                                                                      ((h << 4) ^ sw));
@@ -323,7 +329,6 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
                         uint8_t* arow = smem + L::OFF_A + as * L::A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
                         const __half2 sc = __float2half2_rn(s);
                         const __half2 off = __float2half2_rn(1032.0f);
-                        const bool exact = a.exact_a != 0;
 #pragma unroll
                         for (int w = 0; w < 4; ++w) {
                             uint32_t hh[4];
@@ -331,7 +336,7 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
                             for (int p = 0; p < 4; ++p) {
                                 const uint32_t v = ((wv[w] >> (4 * p)) & 0x000F000Fu) | 0x64006400u;
                                 __half2 x;
-                                if (exact) {
+                                if (EXACT) {
                                     const float lo = (__uint_as_float(0x4B000000u | (v & 0xFu)) - 8388616.0f) * s;
                                     const float hi = (__uint_as_float(0x4B000000u | ((v >> 16) & 0xFu)) - 8388616.0f) * s;
                                     x = __floats2half2_rn(lo, hi);
@@ -365,7 +370,7 @@ __global__ void __launch_bounds__(THREADS, A_TMEM ? 2 : 1)
         Item it;
         bool ok = true;
         for (int64_t item = blockIdx.x; ok && decode_item(wl, item, row_tiles, BN, it); item += gridDim.x) {
-            ok = mbar_wait(acc_full(ab), accp, G);
+            ok = mbar_wait_warp1(acc_full(ab), accp, G);  // lane 0 waits; the fence orders the TMEM loads
             tc_fence_after();
             const int nv = min(BN, it.n - it.tt * BN);
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
@@ -518,7 +523,7 @@ bool tc_make_map_nd(CUtensorMap* m, CUtensorMapDataType dt, const void* base, in
 
 namespace {
 
-template <int MODE, int BN, bool A_TMEM>
+template <int MODE, int BN, bool A_TMEM, bool EXACT = false>
 int launch_t(const TcLaunch& L, int num_sms, cudaStream_t s) {
     CUtensorMap qmap, bmap;
     if (!tc_make_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, L.Wp, (uint64_t)L.a.K / 2, (uint64_t)L.total_rows,
@@ -528,7 +533,7 @@ int launch_t(const TcLaunch& L, int num_sms, cudaStream_t s) {
                   (uint64_t)L.a.K * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B))
         return -1;
     const int smem = tc::Smem<BN, A_TMEM>::TOTAL;
-    auto kern = tc::k_tc_gemm<MODE, BN, A_TMEM>;
+    auto kern = tc::k_tc_gemm<MODE, BN, A_TMEM, EXACT>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -1;
     int per_sm = (227 * 1024) / smem;
     const int by_tmem = 512 / (int)tc::tmem_cols(BN, A_TMEM);
@@ -549,6 +554,16 @@ int launch_t(const TcLaunch& L, int num_sms, cudaStream_t s) {
 
 template <int MODE>
 int launch_mode(const TcLaunch& L, int num_sms, cudaStream_t s) {
+    if (MODE == TC_PLAIN && L.a.exact_a && (L.a_in_smem || L.BN >= 128)) {
+        switch (L.BN) {  // the router's dense GEMM: shared-memory A, fp32 dequant
+            case 16: return launch_t<MODE, 16, false, true>(L, num_sms, s);
+            case 32: return launch_t<MODE, 32, false, true>(L, num_sms, s);
+            case 64: return launch_t<MODE, 64, false, true>(L, num_sms, s);
+            case 128: return launch_t<MODE, 128, false, true>(L, num_sms, s);
+            case 256: return launch_t<MODE, 256, false, true>(L, num_sms, s);
+            default: return -1;
+        }
+    }
     if (L.a_in_smem) {
         switch (L.BN) {
             case 16: return launch_t<MODE, 16, false>(L, num_sms, s);

@@ -87,24 +87,6 @@ struct StLayout {
     static constexpr int TOTAL = OFF_WL + WL_SMEM + 1024;  // + alignment slack
 };
 
-// Whole-warp wait: every lane waits, and the warp leaves together (a lane
-// that saw the deadline makes all of them give up), so .sync.aligned
-// instructions after it always run with the full warp.
-__device__ __forceinline__ bool mbar_wait_warp(uint32_t a, uint32_t parity, const Guard& g) {
-    const bool ok = mbar_wait(a, parity, g);
-    return __all_sync(0xffffffffu, ok) != 0;
-}
-// Whole-warp wait where lane 0 alone polls: for barriers that guard no data
-// the lanes read afterwards (a TMEM slot freed by MMAs; the tcgen05 fence
-// after it orders the warp's stores).  32 lanes polling one barrier cost a
-// few hundred cycles per wait.
-__device__ __forceinline__ bool mbar_wait_warp1(uint32_t a, uint32_t parity, const Guard& g) {
-    int ok = 1;
-    if ((threadIdx.x & 31) == 0) ok = mbar_wait(a, parity, g) ? 1 : 0;
-    __syncwarp();
-    return __shfl_sync(0xffffffffu, ok, 0) != 0;
-}
-
 // fp16 pair (lo = element p, hi = element p + 4 of the word's 8-group) of
 // (nibble - 8) * scale; P selects the nibble pair 0..3 of the 32-bit word.
 template <int P>

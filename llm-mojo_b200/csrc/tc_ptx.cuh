@@ -89,6 +89,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, const Gua
     }
 }
 
+// Whole-warp wait: every lane waits, and the warp leaves together (a lane
+// that saw the deadline makes all of them give up), so .sync.aligned
+// instructions after it always run with the full warp.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t a, uint32_t parity, const Guard& g) {
+    const bool ok = mbar_wait(a, parity, g);
+    return __all_sync(0xffffffffu, ok) != 0;
+}
+// Whole-warp wait where lane 0 alone polls: for barriers that guard no data
+// the lanes read afterwards (a TMEM slot freed by MMAs; the tcgen05 fence
+// after it orders the warp's stores).  32 lanes polling one barrier cost a
+// few hundred cycles per wait.
+__device__ __forceinline__ bool mbar_wait_warp1(uint32_t a, uint32_t parity, const Guard& g) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(a, parity, g) ? 1 : 0;
+    __syncwarp();
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t mbar,
                                             int32_t x, int32_t y) {
     asm volatile(
