@@ -119,10 +119,15 @@ enum moe_option {
     MOE_OPT_EP_LOCAL_WEIGHTS = 14, /* 1: in the GATHER and ALL_TO_ALL modes the descriptor's expert
                                       arrays hold only this rank's experts (expert rank*E/N + i at
                                       index i); 0 (default): all E experts */
-    MOE_OPT_GEMV_ONE_TOKEN = 15    /* CUDA-core expert path when every expert has at most one token
+    MOE_OPT_GEMV_ONE_TOKEN = 15,   /* CUDA-core expert path when every expert has at most one token
                                       (one-token batches): 1 (default) one warp per weight row,
                                       rows streamed from HBM; 0 the ring-buffered GEMV.  Same
                                       results either way */
+    MOE_OPT_DENSE_ONE_LAUNCH = 16  /* moe_q4_matmul_batchN on tensor cores for 1..16 tokens
+                                      (c_in % 256 == 0, c_out % 128 == 0): 1 (default) one kernel
+                                      that converts the tokens to fp16 itself and adds its split-K
+                                      partial sums in split order (the last CTA of a row tile);
+                                      0 the fp16 gather, the general GEMM and a reduction kernel */
 };
 /* Expert-parallel forms of moe_layer_forward (no counterpart in the
  * single-process reference; see moe_ep_init).  Rank r of N owns the experts

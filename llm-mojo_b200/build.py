@@ -18,7 +18,7 @@ LIB = os.path.join(HERE, "libmoe_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 SOURCES = ["moe_abi.cu", "moe_kernels.cu", "moe_tc.cu", "moe_tc_stream.cu", "moe_route.cu", "moe_gemv.cu",
-           "moe_weights_file.cu", "moe_ep.cu", "moe_subspace.cu"]
+           "moe_weights_file.cu", "moe_ep.cu", "moe_subspace.cu", "moe_dense.cu"]
 OBJDIR = os.path.join(HERE, "_build")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",

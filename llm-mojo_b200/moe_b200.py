@@ -29,7 +29,7 @@ OPT_EXPERT_BEGIN, OPT_EXPERT_END = 8, 9
 OPT_FUSED_ROUTE = 10
 OPT_DENSE_KSPLIT = 11
 OPT_EP_TIMEOUT_NS = 12
-OPT_EP_MODE, OPT_EP_LOCAL_WEIGHTS, OPT_GEMV_ONE_TOKEN = 13, 14, 15
+OPT_EP_MODE, OPT_EP_LOCAL_WEIGHTS, OPT_GEMV_ONE_TOKEN, OPT_DENSE_ONE_LAUNCH = 13, 14, 15, 16
 EP_REPLICATED, EP_GATHER, EP_ALL_TO_ALL = 0, 1, 2
 EP_UNIQUE_ID_BYTES = 128
 PATH_AUTO, PATH_GEMV, PATH_TC = 0, 1, 2

@@ -51,6 +51,41 @@ def test_tc_dense_q4_matmul(tc, c_in, c_out, batch):
     assert_close(out, ref, max_abs=2e-3 * max(1.0, rms), what=f"tc dense {c_in}x{c_out}x{batch}")
 
 
+@pytest.mark.parametrize("c_in,c_out,batch", [(2816, 4096, 16), (2816, 1024, 1), (4096, 2816, 7),
+                                              (256, 128, 3), (512, 384, 16), (2816, 128, 16)])
+def test_dense_one_launch(ctx, c_in, c_out, batch):
+    """The one-launch projection (MOE_OPT_DENSE_ONE_LAUNCH, up to 16 tokens)
+    against the oracle and against the three-kernel path, with its default
+    split of K and with one stage per CTA; each call twice in a row (the
+    last-CTA tickets must be back at zero)."""
+    import torch
+    rng = np.random.default_rng(c_in * 3 + c_out + batch)
+    W, S, _ = O.quantize_q4_0(rng.normal(0, 0.02, c_out * c_in).astype(np.float32))
+    x = rng.standard_normal((batch, c_in)).astype(np.float32)
+    Wd, Sd, xd = torch.from_numpy(W).cuda(), torch.from_numpy(S).cuda(), torch.from_numpy(x).cuda()
+    ref = O.q4_matmul(W, S, x, c_in, c_out, prec=O.F64)
+    rms = float(np.sqrt((ref.astype(np.float64) ** 2).mean()))
+    ctx.set_gemm_path(MB.PATH_TC)
+    outs = {}
+    try:
+        for one, ks in ((1, 0), (1, c_in // 256), (0, 0)):
+            ctx.set_option(MB.OPT_DENSE_ONE_LAUNCH, one)
+            ctx.set_option(MB.OPT_DENSE_KSPLIT, ks)
+            for rep in range(2):
+                o = torch.full((batch, c_out), float("nan"), device="cuda")
+                ctx.q4_matmul_batchN(batch, Wd, Sd, xd, o, c_in, c_out)
+                torch.cuda.synchronize()
+                outs[(one, ks, rep)] = o.cpu().numpy()
+                assert_close(outs[(one, ks, rep)], ref, max_abs=2e-3 * max(1.0, rms),
+                             what=f"dense one={one} ks={ks} {c_in}x{c_out}x{batch}")
+            # a fixed order of the split sums: the same bits on every call
+            assert np.array_equal(outs[(one, ks, 0)], outs[(one, ks, 1)])
+    finally:
+        ctx.set_option(MB.OPT_DENSE_ONE_LAUNCH, 1)
+        ctx.set_option(MB.OPT_DENSE_KSPLIT, 0)
+        ctx.set_gemm_path(MB.PATH_AUTO)
+
+
 @pytest.mark.parametrize("M", [16, 64])
 def test_tc_layer_forward_vs_oracle(tc, full_layer, M):
     dev, host, L = full_layer
