@@ -124,10 +124,11 @@ enum moe_option {
                                       rows streamed from HBM; 0 the ring-buffered GEMV.  Same
                                       results either way */
     MOE_OPT_DENSE_ONE_LAUNCH = 16  /* moe_q4_matmul_batchN on tensor cores for 1..16 tokens
-                                      (c_in % 256 == 0, c_out % 128 == 0): 1 (default) one kernel
-                                      that converts the tokens to fp16 itself and adds its split-K
-                                      partial sums in split order (the last CTA of a row tile);
-                                      0 the fp16 gather, the general GEMM and a reduction kernel */
+                                      (c_in % 256 == 0, c_in <= 8192, c_out % 128 == 0): 1 (default)
+                                      one kernel that converts the tokens to fp16 itself and adds
+                                      its split-K partial sums in split order (the splits of a row
+                                      tile are one thread block cluster); 0 the fp16 gather, the
+                                      general GEMM and a reduction kernel */
 };
 /* Expert-parallel forms of moe_layer_forward (no counterpart in the
  * single-process reference; see moe_ep_init).  Rank r of N owns the experts

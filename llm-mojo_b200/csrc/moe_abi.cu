@@ -42,7 +42,6 @@ struct Status {
 namespace {
 // Internal buffers of an expert evaluation for M tokens x K slots.
 constexpr int64_t kMaxSplitY = 4;  // split-K partials of the down projection kept in y
-constexpr int64_t kDenseTickets = 1024;  // row tiles of the one-launch projection (c_out <= 131072)
 struct ExpertBufs {
     int* slot_expert;
     float* slot_weight;
@@ -87,7 +86,6 @@ struct moe_ctx {
     int fused_route = 0;                 // MOE_OPT_FUSED_ROUTE
     bool gemv1 = true;                   // MOE_OPT_GEMV_ONE_TOKEN
     bool dense16 = true;                 // MOE_OPT_DENSE_ONE_LAUNCH
-    int* dense_tickets = nullptr;        // the one-launch projection's per-row-tile tickets (zero between launches)
     int dense_ksplit = 0;                // MOE_OPT_DENSE_KSPLIT (0: automatic)
     uint64_t device_timeout_ns = 4000000000ull;
     // profiling (moe_profile_enable)
@@ -620,16 +618,10 @@ size_t dense_bytes(int64_t batch, int64_t c_in, int64_t c_out) {
 bool dense_one_launch_ok(moe_ctx* ctx, const void* w, const void* sc, const void* xd, int64_t c_in, int64_t c_out,
                          int64_t batch) {
     return ctx->dense16 && moe::dense16_supported((int)std::min<int64_t>(batch, 1 << 20), c_in, c_out) &&
-           al16(w) && al16(sc) && al16(xd) && c_out / 128 <= kDenseTickets;
-}
-int dense_one_launch_splits(moe_ctx* ctx, int64_t c_in) {
-    const int nst = (int)(c_in / 256);
-    int ks = moe::dense16_splits(c_in);
-    if (ctx->dense_ksplit > 0) ks = (int)std::max<int64_t>(ks, std::min<int64_t>(ctx->dense_ksplit, nst));
-    return ks;
+           al16(w) && al16(sc) && al16(xd);
 }
 int dense_one_launch(moe_ctx* ctx, const void* w, const void* sc, const void* xd, void* od, int64_t c_in,
-                     int64_t c_out, int64_t batch, int ks, float* part) {
+                     int64_t c_out, int64_t batch) {
     moe::DenseArgs da;
     da.Ws = (const float*)sc;
     da.X = (const float*)xd;
@@ -639,13 +631,11 @@ int dense_one_launch(moe_ctx* ctx, const void* w, const void* sc, const void* xd
     da.R = c_out;
     da.out = (float*)od;
     da.out_stride = c_out;
-    da.part = part;
-    da.tickets = ctx->dense_tickets;
-    da.ks = ks;
+    da.ks = moe::dense16_splits(c_in, ctx->dense_ksplit);
     da.err_flag = ctx->err_flag;
     da.timeout_ns = ctx->device_timeout_ns;
     const int r = moe::launch_dense16((const uint8_t*)w, da, ctx->stream);
-    if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core projection setup failed");
+    if (r < 0) return fail(ctx, MOE_E_CUDA, "tensor-core projection launch failed");
     ctx->launches += r;
     return MOE_OK;
 }
@@ -659,14 +649,8 @@ int dense_q4(moe_ctx* ctx, const uint8_t* w, const float* sc, const float* xd, f
                     al8(sc) && (ctx->gemm_path == MOE_PATH_TC || batch >= ctx->dense_tc_min_tokens);
     if (tc && !exact_a && dense_one_launch_ok(ctx, w, sc, xd, c_in, c_out, batch)) {
         // 1..16 tokens: one launch (fp16 conversion and split-K sums inside)
-        const int ks = dense_one_launch_splits(ctx, c_in);
-        float* part = nullptr;
-        if (ks > 1) {
-            part = (float*)ws_take(ctx, (size_t)ks * batch * c_out * 4);
-            if (!part) return fail(ctx, MOE_E_NOMEM, "workspace exhausted");
-        }
         ProfScope ps(ctx, prof_name);
-        return dense_one_launch(ctx, w, sc, xd, od, c_in, c_out, batch, ks, part);
+        return dense_one_launch(ctx, w, sc, xd, od, c_in, c_out, batch);
     }
     if (tc) {
         __half* x16 = (__half*)ws_take(ctx, batch * c_in * 2);
@@ -742,9 +726,7 @@ int moe_ctx_create(int device, moe_ctx** out) {
         cudaMalloc(&ctx->err_flag, sizeof(int)) != cudaSuccess ||
         cudaMemset(ctx->err_flag, 0, sizeof(int)) != cudaSuccess ||
         cudaMalloc(&ctx->route_ticket, sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(ctx->route_ticket, 0, sizeof(unsigned)) != cudaSuccess ||
-        cudaMalloc(&ctx->dense_tickets, kDenseTickets * sizeof(int)) != cudaSuccess ||
-        cudaMemset(ctx->dense_tickets, 0, kDenseTickets * sizeof(int)) != cudaSuccess) {
+        cudaMemset(ctx->route_ticket, 0, sizeof(unsigned)) != cudaSuccess) {
         cudaGetLastError();
         delete ctx;
         return MOE_E_CUDA;
@@ -781,7 +763,6 @@ int moe_ctx_destroy(moe_ctx* ctx) {
     if (ctx->ep_host_cnt) cudaFreeHost(ctx->ep_host_cnt);
     if (ctx->err_flag) cudaFree(ctx->err_flag);
     if (ctx->route_ticket) cudaFree(ctx->route_ticket);
-    if (ctx->dense_tickets) cudaFree(ctx->dense_tickets);
     if (ctx->done) cudaEventDestroy(ctx->done);
     for (auto& r : ctx->prof_pending) {
         cudaEventDestroy(r.a);
@@ -2484,12 +2465,9 @@ int moe_q4_matmul_batchN_noalloc(moe_ctx* ctx, int64_t batch, const uint8_t* W, 
     }
     if (dense_one_launch_ok(ctx, w, sc, xd, c_in, c_out, batch)) {
         // the same kernel and split as moe_q4_matmul_batchN (the same bits);
-        // the partial sums in the fixed scratch
-        const int ks = dense_one_launch_splits(ctx, c_in);
-        if ((size_t)ks * batch * c_out * 4 <= kNoAllocScratchBytes) {
-            TRY(dense_one_launch(ctx, w, sc, xd, od, c_in, c_out, batch, ks, ks > 1 ? (float*)scratch : nullptr));
-            return finish(ctx);
-        }
+        // it needs no scratch
+        TRY(dense_one_launch(ctx, w, sc, xd, od, c_in, c_out, batch));
+        return finish(ctx);
     }
     __half* x16 = static_cast<__half*>(scratch);
     const size_t x16_bytes = al(batch * c_in * 2);

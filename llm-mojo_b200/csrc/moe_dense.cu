@@ -14,11 +14,12 @@
 //    stream kernel's arithmetic (one LOP3, one HSUB2, one HMUL2 per pair);
 //    warp 1 issues the tcgen05 MMAs (A in TMEM, B in shared memory, N = 16)
 //    into one fp32 accumulator;
-//   - with the K range split over several CTAs, each writes its partial sums
-//    and the last CTA of the row tile (a ticket taken after a threadfence)
-//    adds them in split order and writes the output, so one launch does the
-//    whole projection and the sum order is fixed.
-// Two CTAs fit per SM (94 KB shared memory, 256 TMEM columns each).  Every
+//   - with the K range split over several CTAs, those CTAs form one thread
+//    block cluster: each leaves its partial sums in its shared memory and
+//    split 0 adds them over distributed shared memory in split order and
+//    writes the output, so one launch does the whole projection and the sum
+//    order is fixed.
+// Two CTAs fit per SM (102 KB shared memory, 256 TMEM columns each).  Every
 // mbarrier wait is bounded; on expiry the kernel sets err_flag = 2, drains
 // what it issued and returns.
 #include <cuda.h>
@@ -43,13 +44,15 @@ constexpr int B_CHUNK = BN * 128;            // one 64-K chunk of the token tile
 constexpr int OFF_Q = 0;
 constexpr int OFF_S = OFF_Q + SQ * ST_Q;
 constexpr int OFF_B = OFF_S + SQ * ST_S;
-constexpr int OFF_BAR = OFF_B + MAXS * 4 * B_CHUNK;
+constexpr int OFF_P = OFF_B + MAXS * 4 * B_CHUNK;  // this split's partial sums [token][128 rows] fp32
+constexpr int OFF_BAR = OFF_P + BN * 128 * 4;
 constexpr int N_BAR = 2 * SQ + 2 * SA + 2;
 constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
 constexpr int TOTAL = OFF_MISC + 16 + 1024;  // + alignment slack
 constexpr int THREADS = 192;                 // producer, MMA issuer, four dequant / epilogue warps
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t ACOL = 32;                // A slots after the 16-column accumulator
+constexpr int MAX_SPLITS = 8;                // the K splits of a row tile form one cluster (portable size)
 }  // namespace dn
 
 template <int P>
@@ -76,7 +79,7 @@ __global__ void __launch_bounds__(dn::THREADS, 2)
     const uint32_t drain_bar = bar0 + 8u * (2 * SQ + 2 * SA + 1);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
-    volatile int* last_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
+    float* part_s = reinterpret_cast<float*>(smem + OFF_P);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nst = a.K / ST_K;
@@ -96,7 +99,6 @@ __global__ void __launch_bounds__(dn::THREADS, 2)
         mbar_init(acc_full, 1);
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
-        *last_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         prefetch_tmap(&qmap);
         prefetch_tmap(&smap);
@@ -281,9 +283,7 @@ __global__ void __launch_bounds__(dn::THREADS, 2)
                 tmem_ld<16>(tl, v);
             }
             // (loops over the 16 token columns are unrolled with a guard, so
-            // that v and acc stay in registers; the partial sums of a split
-            // are all requested before any is added: one L2 round trip per
-            // split, not per token)
+            // that v stays in registers)
             const int64_t r = row0 + t;
             if (a.ks == 1) {
                 if (ok) {
@@ -292,39 +292,36 @@ __global__ void __launch_bounds__(dn::THREADS, 2)
                         if (tok < a.M) a.out[(int64_t)tok * a.out_stride + r] = v[tok];
                 }
             } else {
-                if (ok) {
 #pragma unroll
-                    for (int tok = 0; tok < BN; ++tok)
-                        if (tok < a.M) a.part[((int64_t)ksi * a.M + tok) * a.R + r] = v[tok];
-                }
-                __threadfence();
-                asm volatile("bar.sync 2, 128;" ::: "memory");
-                if (threadIdx.x == 64) {
-                    const int old = atomicAdd(a.tickets + rt, 1);
-                    const int last = old == a.ks - 1;
-                    if (last) a.tickets[rt] = 0;  // every split has arrived: ready for the next call
-                    *last_flag = last;
-                }
-                asm volatile("bar.sync 2, 128;" ::: "memory");
-                if (*last_flag) {
-                    __threadfence();
-                    float acc[BN];
-#pragma unroll
-                    for (int tok = 0; tok < BN; ++tok) acc[tok] = 0.f;
-                    for (int k = 0; k < a.ks; ++k) {  // split order: the same sum on every call
-                        float pv[BN];
-                        const float* pk = a.part + (int64_t)k * a.M * a.R + r;
-#pragma unroll
-                        for (int tok = 0; tok < BN; ++tok) pv[tok] = tok < a.M ? __ldcg(pk + (int64_t)tok * a.R) : 0.f;
-#pragma unroll
-                        for (int tok = 0; tok < BN; ++tok) acc[tok] += pv[tok];
-                    }
-#pragma unroll
-                    for (int tok = 0; tok < BN; ++tok)
-                        if (tok < a.M) a.out[(int64_t)tok * a.out_stride + r] = acc[tok];
-                }
+                for (int tok = 0; tok < BN; ++tok) part_s[tok * 128 + t] = ok ? v[tok] : 0.f;
             }
         }
+    }
+    if (a.ks > 1) {
+        // The K splits of this row tile are the CTAs of one cluster: split 0
+        // adds the others' partial sums from their shared memory in split
+        // order (the same sum on every call), then every CTA waits until it
+        // is done before its shared memory goes away.
+        cl_sync();
+        if (ksi == 0 && warp >= 2) {
+            const int t = (warp & 3) * 32 + lane;
+            float acc[dn::BN];
+#pragma unroll
+            for (int tok = 0; tok < dn::BN; ++tok) acc[tok] = 0.f;
+            for (int k = 0; k < a.ks; ++k) {
+                const uint32_t base = cl_map(part_s, (uint32_t)k);
+                float pv[dn::BN];
+#pragma unroll
+                for (int tok = 0; tok < dn::BN; ++tok) pv[tok] = cl_ldf(base + (uint32_t)(tok * 128 + t) * 4u);
+#pragma unroll
+                for (int tok = 0; tok < dn::BN; ++tok) acc[tok] += pv[tok];
+            }
+            const int64_t r = row0 + t;
+#pragma unroll
+            for (int tok = 0; tok < dn::BN; ++tok)
+                if (tok < a.M) a.out[(int64_t)tok * a.out_stride + r] = acc[tok];
+        }
+        cl_sync();
     }
     tc_fence_before();
     __syncthreads();
@@ -337,20 +334,26 @@ __global__ void __launch_bounds__(dn::THREADS, 2)
 }  // namespace tc
 
 bool dense16_supported(int M, int64_t K, int64_t R) {
-    return M >= 1 && M <= tc::dn::BN && K % tc::dn::ST_K == 0 && R % 128 == 0 && K / tc::dn::ST_K >= 1;
+    // at most MAX_SPLITS splits of at most MAXS stages
+    return M >= 1 && M <= tc::dn::BN && K % tc::dn::ST_K == 0 && R % 128 == 0 && K / tc::dn::ST_K >= 1 &&
+           K / tc::dn::ST_K <= tc::dn::MAX_SPLITS * tc::dn::MAXS;
 }
 
-// Splits of the K range: about three stages per CTA (at most MAXS).
-int dense16_splits(int64_t K) {
+int dense16_splits(int64_t K, int requested) {
     const int nst = (int)(K / tc::dn::ST_K);
-    int ks = (nst + 2) / 3;
-    while ((nst + ks - 1) / ks > tc::dn::MAXS) ++ks;
+    const int lo = (nst + tc::dn::MAXS - 1) / tc::dn::MAXS;  // at most MAXS stages per split
+    const int hi = nst < tc::dn::MAX_SPLITS ? nst : tc::dn::MAX_SPLITS;
+    int ks = requested > 0 ? requested : (nst + 2) / 3;  // default: about three stages per split
+    if (ks < lo) ks = lo;
+    if (ks > hi) ks = hi;
     return ks < 1 ? 1 : ks;
 }
 
 int launch_dense16(const uint8_t* Wp, const DenseArgs& a, cudaStream_t s) {
     using namespace tc;
-    if (!dense16_supported(a.M, a.K, a.R) || a.ks < 1 || a.ks > a.K / dn::ST_K) return -1;
+    if (!dense16_supported(a.M, a.K, a.R) || a.ks < 1 || a.ks > a.K / dn::ST_K || a.ks > dn::MAX_SPLITS ||
+        (a.K / dn::ST_K + a.ks - 1) / a.ks > dn::MAXS)
+        return -1;
     if ((reinterpret_cast<uintptr_t>(Wp) & 15u) || (reinterpret_cast<uintptr_t>(a.Ws) & 15u) ||
         (reinterpret_cast<uintptr_t>(a.X) & 15u) || (a.x_stride % 4) != 0)
         return -1;
@@ -364,8 +367,21 @@ int launch_dense16(const uint8_t* Wp, const DenseArgs& a, cudaStream_t s) {
         return -1;
     if (cudaFuncSetAttribute(k_dense16, cudaFuncAttributeMaxDynamicSharedMemorySize, dn::TOTAL) != cudaSuccess)
         return -1;
-    const int grid = (int)(a.R / 128) * a.ks;
-    launch_k(k_dense16, dim3(grid), dim3(dn::THREADS), dn::TOTAL, s, qmap, smap, a);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((a.R / 128) * a.ks));
+    cfg.blockDim = dim3(dn::THREADS);
+    cfg.dynamicSmemBytes = dn::TOTAL;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)a.ks;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, k_dense16, qmap, smap, a) != cudaSuccess) return -1;
     return 1;
 }
 

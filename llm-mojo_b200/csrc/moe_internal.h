@@ -238,27 +238,25 @@ int launch_dgemv(int mode, const GemvArgs& a, int num_sms, cudaStream_t s);
 // One-token form (every expert has at most one token): one warp per row,
 // chunks streamed straight from HBM (moe_gemv.cu); same results as k_dgemv.
 // One-launch Q4 projection for 1..16 tokens (moe_dense.cu): fp32 tokens in,
-// fp32 out; the K range is split over `ks` CTAs per 128-row tile, whose
-// partial sums (`part`, ks * M * R floats) the last CTA of the tile adds in
-// split order.  `tickets` holds R / 128 zeroed ints; every launch leaves them
-// zero again.
+// fp32 out; the K range is split over `ks` CTAs per 128-row tile (one thread
+// block cluster), which add their partial sums in split order.
 struct DenseArgs {
     const float* Ws = nullptr;      // scales [R][K/32] (16-byte aligned)
     const float* X = nullptr;       // tokens [M][x_stride] fp32 (16-byte aligned)
     int64_t x_stride = 0;
     int M = 0;
-    int K = 0;                      // multiple of 256
+    int K = 0;                      // multiple of 256, at most 8192
     int64_t R = 0;                  // multiple of 128
     float* out = nullptr;           // [M][out_stride]
     int64_t out_stride = 0;
-    float* part = nullptr;
-    int* tickets = nullptr;
-    int ks = 1;
+    int ks = 1;                     // 1..8, at most 4 stages of 256 K per split
     int* err_flag = nullptr;
     uint64_t timeout_ns = 4000000000ull;
 };
 bool dense16_supported(int M, int64_t K, int64_t R);
-int dense16_splits(int64_t K);
+// The split count: about three stages per CTA, or `requested` (> 0) within
+// the kernel's limits.
+int dense16_splits(int64_t K, int requested);
 int launch_dense16(const uint8_t* Wp, const DenseArgs& a, cudaStream_t s);
 
 bool gemv1_supported(const GemvArgs& a);

@@ -56,8 +56,8 @@ def test_tc_dense_q4_matmul(tc, c_in, c_out, batch):
 def test_dense_one_launch(ctx, c_in, c_out, batch):
     """The one-launch projection (MOE_OPT_DENSE_ONE_LAUNCH, up to 16 tokens)
     against the oracle and against the three-kernel path, with its default
-    split of K and with one stage per CTA; each call twice in a row (the
-    last-CTA tickets must be back at zero)."""
+    split of K and with the most splits (a cluster of up to eight CTAs per
+    row tile); each call twice in a row, which must give the same bits."""
     import torch
     rng = np.random.default_rng(c_in * 3 + c_out + batch)
     W, S, _ = O.quantize_q4_0(rng.normal(0, 0.02, c_out * c_in).astype(np.float32))
