@@ -78,13 +78,22 @@ struct StLayout {
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_B = OFF_Q + SQ * ST_Q;
     static constexpr int OFF_S = OFF_B + SQ * B_BYTES;
-    static constexpr int OFF_BAR = OFF_S + SQ * ST_S;
-    static constexpr int N_BAR = 2 * SQ + 2 * SA + 4 + NG + 4 + 2 * SQ;
-    // item-scale mode (K % 128 == 64): the scale area holds two item buffers
-    static constexpr int ISCALE_BYTES = SQ * ST_S / 2;
+    // item-scale mode (K % 128 == 64): the scale area holds NIB item buffers
+    // of 128 rows x K/32 fp32 (K <= 768), as many as fit up to four: with two,
+    // the producer could not copy an item's scales (nor issue its stages)
+    // before the item two back was fully dequantised
+    static constexpr int ISCALE_BYTES = 12288;
+    static constexpr int NIB0 = (227 * 1024 - 3072 - WL_SMEM - 1024 - OFF_S) / ISCALE_BYTES;
+    static constexpr int NIB = NIB0 > 4 ? 4 : NIB0;
+    static_assert(NIB >= 2, "two item-scale buffers at least");
+    static constexpr int S_AREA = SQ * ST_S > NIB * ISCALE_BYTES ? SQ * ST_S : NIB * ISCALE_BYTES;
+    static constexpr int OFF_BAR = OFF_S + S_AREA;
+    static constexpr int BAR_IS = 2 * SQ + 2 * SA + 4 + NG;  // first item-scale barrier
+    static constexpr int N_BAR = BAR_IS + 2 * NIB + 2 * SQ;
     static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
     static constexpr int OFF_WL = OFF_MISC + 16;        // the work list (stage_worklist)
     static constexpr int TOTAL = OFF_WL + WL_SMEM + 1024;  // + alignment slack
+    static_assert(TOTAL <= 227 * 1024, "shared memory");
 };
 
 // fp16 pair (lo = element p, hi = element p + 4 of the word's 8-group) of
@@ -124,14 +133,15 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
     auto acc_empty = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + 2 + s); };
     auto drain_bar = [&](int j) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + j); };
     // item scales: all of an item's scale rows in one bulk copy (K % 128 == 64,
-    // where the 2-D scale tensor map cannot exist); buffers b = 0, 1
-    auto is_full = [&](int b) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + NG + b); };
-    auto is_empty = [&](int b) { return bar0 + 8u * (2 * SQ + 2 * SA + 4 + NG + 2 + b); };
+    // where the 2-D scale tensor map cannot exist); buffers b = 0 .. NIB-1
+    constexpr int NIB = L::NIB;
+    auto is_full = [&](int b) { return bar0 + 8u * (L::BAR_IS + b); };
+    auto is_empty = [&](int b) { return bar0 + 8u * (L::BAR_IS + NIB + b); };
     // activation tiles: same slot index as the stage, own barriers, so a
     // stage's weight bytes are released by the dequant group alone and the
     // tile stays until the stage's MMAs have read it
-    auto b_full = [&](int s) { return bar0 + 8u * (2 * SQ + 2 * SA + 8 + NG + s); };
-    auto b_empty = [&](int s) { return bar0 + 8u * (3 * SQ + 2 * SA + 8 + NG + s); };
+    auto b_full = [&](int s) { return bar0 + 8u * (L::BAR_IS + 2 * NIB + s); };
+    auto b_empty = [&](int s) { return bar0 + 8u * (L::BAR_IS + 2 * NIB + SQ + s); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -171,7 +181,7 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
             mbar_init(acc_empty(s), 4);
         }
         for (int j = 0; j < NG; ++j) mbar_init(drain_bar(j), 1);
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < NIB; ++b) {
             mbar_init(is_full(b), 1);
             mbar_init(is_empty(b), 4 * NG);  // every dequant warp
         }
@@ -214,8 +224,8 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
                 box_rows(it, row_a, row_b);
                 const int tok_row = it.s0 + it.tt * BN;
                 if (iscale) {
-                    const int b = (int)(ii & 1u);
-                    const uint32_t ph = (ii >> 1) & 1u;
+                    const int b = (int)(ii % NIB);
+                    const uint32_t ph = (ii / NIB) & 1u;
                     if (!(ok = mbar_wait(is_empty(b), ph ^ 1u, G))) break;
                     const uint32_t dst = smem_u32(smem + L::OFF_S + b * L::ISCALE_BYTES);
                     const uint32_t blk = (MODE == TC_ACT ? 64u : 128u) * (uint32_t)nb * 4u;
@@ -267,7 +277,7 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
                 if (q_armed & (1u << s)) mbar_wait(q_full(s), (q_par >> s) & 1u, Gd);
                 if (b_armed & (1u << s)) mbar_wait(b_full(s), (q_par >> s) & 1u, Gd);
             }
-            for (int b = 0; b < 2; ++b)
+            for (int b = 0; b < NIB; ++b)
                 if (is_armed & (1u << b)) mbar_wait(is_full(b), (is_par >> b) & 1u, Gd);
         }
         __syncwarp();
@@ -356,8 +366,8 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
             const int ns = s_end(it) - s_begin(it);
             const float* iscl = nullptr;  // item-scale mode: this row's scales
             if (iscale) {
-                const int b = (int)(ii & 1u);
-                if (!(ok = mbar_wait_warp(is_full(b), (ii >> 1) & 1u, G))) break;
+                const int b = (int)(ii % NIB);
+                if (!(ok = mbar_wait_warp(is_full(b), (ii / NIB) & 1u, G))) break;
                 iscl = reinterpret_cast<const float*>(smem + L::OFF_S + b * L::ISCALE_BYTES) + sr * nb;
             }
             for (int i = (grp - (int)(st % NG) + NG) % NG; i < ns && ok; i += NG) {
@@ -460,7 +470,7 @@ __global__ void __launch_bounds__(StLayout<BN>::THREADS, 1)
             if (!ok) break;
             if (iscale) {
                 __syncwarp();
-                if (lane == 0) mbar_arrive(is_empty((int)(ii & 1u)));
+                if (lane == 0) mbar_arrive(is_empty((int)(ii % NIB)));
             }
             st += (uint32_t)ns;
         }
