@@ -218,6 +218,30 @@ int ep_all_gather(EpComm& ep, const void* send, void* recv, size_t count, bool i
     return enqueued(ep, api, r, "ncclAllGather", timeout_ns, err);
 }
 
+int ep_all_gather_n(EpComm& ep, const EpGatherBuf* bufs, int n, cudaStream_t s, uint64_t timeout_ns,
+                    std::string& err) {
+    const NcclApi* api = nccl(err);
+    if (!api || !ep.comm) {
+        if (api) err = "no expert-parallel communicator";
+        return MOE_E_STATE;
+    }
+    ncclComm_t comm = static_cast<ncclComm_t>(ep.comm);
+    ncclResult_t r = api->group_start();
+    if (r != ncclSuccess) return enqueued(ep, api, r, "ncclGroupStart", timeout_ns, err);
+    for (int i = 0; i < n; ++i) {
+        r = api->all_gather(bufs[i].send, bufs[i].recv, bufs[i].count, bufs[i].is_float ? ncclFloat32 : ncclInt32,
+                            comm, s);
+        if (r != ncclSuccess && r != ncclInProgress) break;
+    }
+    const ncclResult_t r2 = api->group_end();
+    if (r != ncclSuccess && r != ncclInProgress) {
+        err = nccl_msg(api, "ncclAllGather", r);
+        ep_abort(ep);
+        return MOE_E_NCCL;
+    }
+    return enqueued(ep, api, r2, "ncclGroupEnd (all-gather)", timeout_ns, err);
+}
+
 int ep_reduce_scatter(EpComm& ep, const float* send, float* recv, size_t count, cudaStream_t s, uint64_t timeout_ns,
                       std::string& err) {
     const NcclApi* api = nccl(err);

@@ -25,6 +25,15 @@ int ep_all_reduce(EpComm& ep, float* buf, size_t count, cudaStream_t s, uint64_t
 // Gathers `count` elements (fp32 or int32) of every rank into `recv`, rank order.
 int ep_all_gather(EpComm& ep, const void* send, void* recv, size_t count, bool is_float, cudaStream_t s,
                   uint64_t timeout_ns, std::string& err);
+// Several all-gathers in one NCCL group.
+struct EpGatherBuf {
+    const void* send;
+    void* recv;
+    size_t count;   // elements per rank
+    bool is_float;  // fp32, else int32
+};
+int ep_all_gather_n(EpComm& ep, const EpGatherBuf* bufs, int n, cudaStream_t s, uint64_t timeout_ns,
+                    std::string& err);
 // Sums `send` [nranks * count] over the ranks; this rank receives its `count` slice.
 int ep_reduce_scatter(EpComm& ep, const float* send, float* recv, size_t count, cudaStream_t s, uint64_t timeout_ns,
                       std::string& err);
