@@ -334,9 +334,9 @@ def workload_config(args, M, par="replicas", ws=1):
 
 
 # ----------------------------------------------------------------- GPU leg
-PAR_HELP = ("N > 1: ep-gather (default for decode: each rank its own tokens, 128/N experts per rank, the "
-            "library all-gathers the tokens and reduce-scatters the partial outputs inside the layer call), "
-            "ep-a2a (default for prefill8k: each rank a shard of the tokens, routed rows to the expert owners "
+PAR_HELP = ("N > 1: ep-gather (default: each rank its own tokens, routed on that rank, 128/N experts per "
+            "rank, the library all-gathers the routed rows and reduce-scatters the partial outputs inside the "
+            "layer call), ep-a2a (each rank a shard of the workload's tokens, routed rows to the expert owners "
             "and back over NCCL inside the layer call), ep / ep-native (tokens replicated, NCCL all-reduce of "
             "partial outputs by torch.distributed / inside the library), or replicas")
 
@@ -416,7 +416,11 @@ def main():
 def fill_defaults(args, ws):
     wl = WORKLOADS[args.workload]
     if args.parallel is None:
-        args.parallel = ("ep-a2a" if wl.get("a2a") else "ep-gather") if ws > 1 else "replicas"
+        # the gather form for every workload: at 2 ranks it gave prefill8k
+        # 159.9k tokens/s and decode64 22.6k against the all-to-all form's
+        # 73.1k and 7.1k (one GPU: 98.1k and 10.1k); the all-to-all form moves
+        # up to K rows per token, the gather form one
+        args.parallel = "ep-gather" if ws > 1 else "replicas"
     if ws > 1 and not args.graph and args.parallel not in ("ep-gather",):
         # replaying graphs that hold NCCL calls was slower than eager launches
         # at 8 ranks for the replicated all-reduce form (825 us per step
