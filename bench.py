@@ -674,17 +674,21 @@ def measure(args, pg, ws, rank, local):
     if pg:
         pg.barrier()
 
-    # End to end through the public API with pinned host buffers: every call
-    # stages its host inputs (H2D) and copies its outputs back (D2H) on its
-    # context's stream; the calls are asynchronous (moe_set_async), the dense
-    # projections run on their own contexts' streams as in the device-timed
-    # step, and the step ends when the main stream has joined them.  A stack
-    # keeps its activations on the device between layers.
+    # End to end through the public API with pinned host buffers: the layer
+    # input x goes to the device once per step (the MoE layer and q/k/v read
+    # that copy), the o projection stages its own host input, and every call
+    # copies its outputs back to the host (D2H) on its context's stream; the
+    # calls are asynchronous (moe_set_async), the dense projections run on
+    # their own contexts' streams as in the device-timed step, and the step
+    # ends when the main stream has joined them.  A stack keeps its
+    # activations on the device between layers.
     x_h = [x.cpu().pin_memory() for x in xs]
     xo_h = x_o.cpu().pin_memory()
     out_h = torch.empty((max(M, 1), D)).pin_memory()
     dout_h = {n: torch.empty((M, co)).pin_memory() for n, (_, _, _, co) in dense.items()}
-    h2d = M * D * 4 + sum((M * (4096 if n == "o" else D) * 4) for n in dense)
+    # the layer input x crosses once per step (the MoE layer and q/k/v read its
+    # device copy); the o projection's input and every output cross as well
+    h2d = M * D * 4 + sum(M * 4096 * 4 for n in dense if n == "o")
     d2h = M * D * 4 + sum(M * co * 4 for (_, _, _, co) in dense.values())
     x_d = torch.empty((max(M, 1), D), device="cuda")
     h_d = torch.empty((max(M, 1), D), device="cuda")
@@ -707,6 +711,11 @@ def measure(args, pg, ws, rank, local):
         elif stack:
             for li in range(args.layers):
                 moe_layer(li, None, None)
+        elif M > 0 and dense:
+            # x once to the device; the layer and q/k/v read that copy
+            x_d[:M].copy_(xh, non_blocking=True)
+            fork.record(main)
+            ctx.layer_forward(descs[i % args.layers], M, x_d[:M], out_h[:M], MB.F_POST_NORM)
         elif M > 0:
             ctx.layer_forward(descs[i % args.layers], M, xh, out_h[:M], MB.F_POST_NORM)
         else:
@@ -714,7 +723,7 @@ def measure(args, pg, ws, rank, local):
         joins = []
         for name, (p, s, ci, co) in dense.items():
             dstream[name].wait_event(fork)
-            dctx[name].q4_matmul_batchN(M, p, s, xo_h if name == "o" else xh, dout_h[name], ci, co)
+            dctx[name].q4_matmul_batchN(M, p, s, xo_h if name == "o" else x_d[:M], dout_h[name], ci, co)
             ev = torch.cuda.Event()
             ev.record(dstream[name])
             joins.append(ev)
@@ -725,12 +734,40 @@ def measure(args, pg, ws, rank, local):
     for i in range(3):
         step_e2e(i)
     torch.cuda.synchronize()
+    # As the device-timed step, the end-to-end step replays CUDA graphs when
+    # the run uses them: the public calls with host buffers, captured with
+    # their copies from and to the pinned host buffers (each replay copies
+    # that step's inputs in and its results out), as a throughput-oriented
+    # caller would issue a decode loop.
+    e2e_graphs = []
+    if graphs:
+        cap2 = torch.cuda.Stream()
+        cap2.wait_stream(stream)
+        try:
+            ctx.set_stream(cap2.cuda_stream)
+            for gi in range(n_graphs):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=cap2):
+                    step_e2e(gi)
+                e2e_graphs.append(g)
+        except Exception as exc:  # capture refused: time the eager calls
+            print(f"e2e graph capture failed ({exc}); timing eager calls", file=sys.stderr)
+            e2e_graphs = []
+        finally:
+            ctx.set_stream(stream.cuda_stream)
+        for i in range(3):
+            if e2e_graphs:
+                e2e_graphs[i % n_graphs].replay()
+        torch.cuda.synchronize()
     if pg:
         pg.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(e2e_steps):
-        step_e2e(i)
+        if e2e_graphs:
+            e2e_graphs[i % n_graphs].replay()
+        else:
+            step_e2e(i)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -806,11 +843,12 @@ def measure(args, pg, ws, rank, local):
         "roofline": roof, "step_roofline": step_roof,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps, "cuda_graph": bool(e2e_graphs)},
         "gpu_launches": launches, "clocks": clk.summary(),
     }
     # graphs that hold NCCL calls must be gone before the process group is
     graphs.clear()
+    e2e_graphs.clear()
     import gc
     gc.collect()
     torch.cuda.synchronize()
