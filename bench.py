@@ -735,12 +735,14 @@ def measure(args, pg, ws, rank, local):
         step_e2e(i)
     torch.cuda.synchronize()
     # As the device-timed step, the end-to-end step replays CUDA graphs when
-    # the run uses them: the public calls with host buffers, captured with
-    # their copies from and to the pinned host buffers (each replay copies
-    # that step's inputs in and its results out), as a throughput-oriented
-    # caller would issue a decode loop.
+    # the run uses them, on one GPU: the public calls with host buffers,
+    # captured with their copies from and to the pinned host buffers (each
+    # replay copies that step's inputs in and its results out), as a
+    # throughput-oriented caller would issue a decode loop.  With several
+    # ranks (the layer call holding NCCL collectives) the capture of the
+    # host-buffer calls hung a 2-rank run, so there the calls run eagerly.
     e2e_graphs = []
-    if graphs:
+    if graphs and ws == 1:
         cap2 = torch.cuda.Stream()
         cap2.wait_stream(stream)
         try:
